@@ -1,0 +1,528 @@
+"""Parity checkers for the fastEmbedR optimizer hot path.
+
+TEST INFRASTRUCTURE ONLY.  Only ``tests/``, ``__graft_entry__.smoke`` and the
+CPU-baseline legs of ``bench.py`` may import this package; the product
+(``fastembedr_b200``) never does.
+
+Two checkers live here:
+
+* ``liboracle.so`` -- a C restatement of the reference algorithms
+  (``fe_oracle.c``; every function cites the reference routine it follows).
+* ``_ref/libferef.so`` -- the reference's *own* CPU sources
+  (``src/tsne_neighbors.cpp``, ``src/fast_knn_umap.cpp``) compiled unmodified
+  through a small Rcpp stand-in (``rcpp_shim/Rcpp.h``).  It pins the
+  restatement and is the CPU baseline.  It can only be rebuilt where the
+  reference sources exist; elsewhere a prebuilt copy is used if present.
+
+All embeddings are row-major ``float32[n, 2]``; KNN inputs are ``(n, k)``
+arrays (converted to R's column-major layout here).
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+from typing import Optional
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ORACLE_SO = os.path.join(HERE, "liboracle.so")
+REF_SO = os.path.join(HERE, "_ref", "libferef.so")
+
+_c_int_p = ctypes.POINTER(ctypes.c_int)
+_c_float_p = ctypes.POINTER(ctypes.c_float)
+_c_double_p = ctypes.POINTER(ctypes.c_double)
+
+_lib = None
+_ref = None
+
+
+def build(ref_src: Optional[str] = None) -> None:
+    """Compile the C restatement and, when the reference sources exist, ``_ref``."""
+    cmd = ["make", "-s", "-C", HERE]
+    if ref_src is not None:
+        cmd.append(f"REF_SRC={ref_src}")
+    subprocess.run(cmd, check=True)
+
+
+def _ptr(a: np.ndarray, ctype):
+    return a.ctypes.data_as(ctypes.POINTER(ctype))
+
+
+def lib() -> ctypes.CDLL:
+    global _lib
+    if _lib is None:
+        if not os.path.exists(ORACLE_SO):
+            build()
+        L = ctypes.CDLL(ORACLE_SO)
+        L.or_tsne_grid_size.restype = ctypes.c_int
+        L.or_tsne_build_p.restype = ctypes.c_longlong
+        L.or_tsne_kl.restype = ctypes.c_double
+        L.or_umap_powf.restype = ctypes.c_float
+        L.or_umap_powf.argtypes = [ctypes.c_float, ctypes.c_float]
+        L.or_umap_positive_samples.argtypes = [ctypes.c_float, ctypes.c_int]
+        L.or_umap_negative_samples.argtypes = [ctypes.c_float, ctypes.c_int, ctypes.c_int]
+        L.or_umap_negative_vertex.argtypes = [ctypes.c_int, ctypes.c_uint32, ctypes.c_int,
+                                              ctypes.c_int, ctypes.c_uint32, ctypes.c_int]
+        L.or_umap_graph.restype = ctypes.c_longlong
+        _lib = L
+    return _lib
+
+
+def ref_available() -> bool:
+    return os.path.exists(REF_SO)
+
+
+def ref() -> ctypes.CDLL:
+    """The reference's own CPU code (raises if it was never built)."""
+    global _ref
+    if _ref is None:
+        if not os.path.exists(REF_SO):
+            raise FileNotFoundError(f"{REF_SO} missing: build it where the reference sources exist")
+        R = ctypes.CDLL(REF_SO)
+        R.feref_tsne_last_error.restype = ctypes.c_char_p
+        R.feref_umap_last_error.restype = ctypes.c_char_p
+        R.feref_tsne_p_build.restype = ctypes.c_void_p
+        R.feref_tsne_p_build.argtypes = [_c_int_p, _c_float_p, ctypes.c_int, ctypes.c_int,
+                                         ctypes.c_double, ctypes.c_int]
+        R.feref_tsne_p_nnz.restype = ctypes.c_longlong
+        R.feref_tsne_p_nnz.argtypes = [ctypes.c_void_p]
+        R.feref_tsne_p_copy.argtypes = [ctypes.c_void_p, _c_int_p, _c_int_p, _c_float_p]
+        R.feref_tsne_p_free.argtypes = [ctypes.c_void_p]
+        R.feref_tsne_gradient_fft.argtypes = [_c_int_p, _c_int_p, _c_float_p, ctypes.c_int,
+                                              _c_float_p, ctypes.c_float, ctypes.c_int,
+                                              ctypes.c_int, _c_float_p]
+        R.feref_tsne_gradient_exact.argtypes = [_c_int_p, _c_int_p, _c_float_p, ctypes.c_int,
+                                                _c_float_p, ctypes.c_float, ctypes.c_int,
+                                                _c_float_p]
+        R.feref_tsne_attractive.argtypes = R.feref_tsne_gradient_exact.argtypes
+        R.feref_tsne_update.argtypes = [_c_float_p, _c_float_p, _c_float_p, _c_float_p,
+                                        ctypes.c_int, ctypes.c_float, ctypes.c_float,
+                                        ctypes.c_float, ctypes.c_float, ctypes.c_int]
+        R.feref_tsne_zero_mean.argtypes = [_c_float_p, ctypes.c_int]
+        R.feref_tsne_kl.argtypes = [_c_int_p, _c_int_p, _c_float_p, ctypes.c_int, _c_float_p,
+                                    ctypes.c_int, _c_double_p]
+        R.feref_tsne_run.argtypes = [_c_int_p, _c_float_p, ctypes.c_int, ctypes.c_int, _c_float_p,
+                                     ctypes.c_double, ctypes.c_int, ctypes.c_int, ctypes.c_double,
+                                     ctypes.c_double, ctypes.c_double, ctypes.c_int,
+                                     ctypes.c_double, ctypes.c_double, ctypes.c_double,
+                                     ctypes.c_double, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                     _c_float_p]
+        R.feref_tsne_grid_size.argtypes = [ctypes.c_int, ctypes.c_int]
+        R.feref_tsne_auto_parameters.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.c_double,
+                                                 ctypes.c_int, _c_double_p]
+        R.feref_umap_graph.restype = ctypes.c_void_p
+        R.feref_umap_graph.argtypes = [_c_int_p, _c_float_p, ctypes.c_int, ctypes.c_int,
+                                       ctypes.c_int]
+        R.feref_umap_graph_nnz.restype = ctypes.c_longlong
+        R.feref_umap_graph_nnz.argtypes = [ctypes.c_void_p]
+        R.feref_umap_graph_copy.argtypes = [ctypes.c_void_p, _c_int_p, _c_int_p, _c_float_p,
+                                            _c_float_p, _c_float_p]
+        R.feref_umap_graph_free.argtypes = [ctypes.c_void_p]
+        R.feref_umap_coo_replay.argtypes = [_c_int_p, _c_int_p, _c_float_p, _c_float_p,
+                                            _c_float_p, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                            ctypes.c_double, ctypes.c_int, ctypes.c_double,
+                                            ctypes.c_double, ctypes.c_int, ctypes.c_int,
+                                            ctypes.c_int, _c_float_p]
+        R.feref_umap_csr_optimize.argtypes = [_c_int_p, _c_int_p, _c_float_p, _c_float_p,
+                                              ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                              ctypes.c_double, ctypes.c_int, ctypes.c_double,
+                                              ctypes.c_double, ctypes.c_int, ctypes.c_int,
+                                              _c_float_p]
+        R.feref_umap_powf.restype = ctypes.c_float
+        R.feref_umap_powf.argtypes = [ctypes.c_float, ctypes.c_float]
+        R.feref_umap_positive_samples.argtypes = [ctypes.c_float, ctypes.c_int]
+        R.feref_umap_negative_samples.argtypes = [ctypes.c_float, ctypes.c_int, ctypes.c_int]
+        R.feref_umap_negative_vertex.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                                 ctypes.c_int, ctypes.c_longlong, ctypes.c_int]
+        R.feref_find_ab.argtypes = [ctypes.c_double, ctypes.c_double, _c_double_p, _c_double_p]
+        _ref = R
+    return _ref
+
+
+def _cm(a: np.ndarray, dtype) -> np.ndarray:
+    """(n, k) array -> R column-major buffer."""
+    return np.ascontiguousarray(np.asarray(a, dtype=dtype).T)
+
+
+def _f32(a) -> np.ndarray:
+    return np.ascontiguousarray(a, dtype=np.float32)
+
+
+def _i32(a) -> np.ndarray:
+    return np.ascontiguousarray(a, dtype=np.int32)
+
+
+class Csr:
+    """Symmetric t-SNE P (or a UMAP graph) in CSR form."""
+
+    def __init__(self, row_ptr, col, val):
+        self.row_ptr = _i32(row_ptr)
+        self.col = _i32(col)
+        self.val = _f32(val)
+
+    @property
+    def n(self) -> int:
+        return self.row_ptr.size - 1
+
+    @property
+    def nnz(self) -> int:
+        return int(self.row_ptr[-1])
+
+
+# ---------------------------------------------------------------- restatement
+
+
+def tsne_grid_size(n: int, grid_override: int = 0) -> int:
+    return lib().or_tsne_grid_size(n, grid_override)
+
+
+def tsne_build_p(idx: np.ndarray, dist: np.ndarray, perplexity: float, index_offset: int = 0) -> Csr:
+    n, k = idx.shape
+    idx_cm, dist_cm = _cm(idx, np.int32), _cm(dist, np.float32)
+    row_ptr = np.zeros(n + 1, np.int32)
+    col = np.zeros(2 * n * k, np.int32)
+    val = np.zeros(2 * n * k, np.float32)
+    nnz = lib().or_tsne_build_p(_ptr(idx_cm, ctypes.c_int), _ptr(dist_cm, ctypes.c_float),
+                                n, k, index_offset, ctypes.c_double(perplexity),
+                                _ptr(row_ptr, ctypes.c_int), _ptr(col, ctypes.c_int),
+                                _ptr(val, ctypes.c_float))
+    if nnz < 0:
+        raise ValueError("invalid KNN input for t-SNE affinities")
+    return Csr(row_ptr, col[:nnz].copy(), val[:nnz].copy())
+
+
+def tsne_gradient_fft(P: Csr, y: np.ndarray, exaggeration: float, grid_size: int,
+                      return_z: bool = False):
+    y = _f32(y)
+    grad = np.zeros_like(y)
+    z = ctypes.c_double(0.0)
+    lib().or_tsne_gradient_fft(_ptr(P.row_ptr, ctypes.c_int), _ptr(P.col, ctypes.c_int),
+                               _ptr(P.val, ctypes.c_float), P.n, _ptr(y, ctypes.c_float),
+                               ctypes.c_float(exaggeration), grid_size,
+                               _ptr(grad, ctypes.c_float), ctypes.byref(z))
+    return (grad, z.value) if return_z else grad
+
+
+def tsne_repulsive_fft(y: np.ndarray, grid_size: int):
+    y = _f32(y)
+    grad = np.zeros_like(y)
+    z = ctypes.c_double(0.0)
+    lib().or_tsne_repulsive_fft(_ptr(y, ctypes.c_float), y.shape[0], grid_size,
+                                _ptr(grad, ctypes.c_float), ctypes.byref(z))
+    return grad, z.value
+
+
+def tsne_attractive(P: Csr, y: np.ndarray, exaggeration: float) -> np.ndarray:
+    y = _f32(y)
+    grad = np.zeros_like(y)
+    lib().or_tsne_attractive(_ptr(P.row_ptr, ctypes.c_int), _ptr(P.col, ctypes.c_int),
+                             _ptr(P.val, ctypes.c_float), P.n, _ptr(y, ctypes.c_float),
+                             ctypes.c_float(exaggeration), _ptr(grad, ctypes.c_float))
+    return grad
+
+
+def tsne_gradient_exact(P: Csr, y: np.ndarray, exaggeration: float) -> np.ndarray:
+    y = _f32(y)
+    grad = np.zeros_like(y)
+    lib().or_tsne_gradient_exact(_ptr(P.row_ptr, ctypes.c_int), _ptr(P.col, ctypes.c_int),
+                                 _ptr(P.val, ctypes.c_float), P.n, _ptr(y, ctypes.c_float),
+                                 ctypes.c_float(exaggeration), _ptr(grad, ctypes.c_float))
+    return grad
+
+
+def tsne_update(y, update, gains, grad, learning_rate, momentum, min_gain=0.01, max_step_norm=5.0):
+    """One update + re-centering; returns new (y, update, gains)."""
+    y, update, gains, grad = (_f32(a).copy() for a in (y, update, gains, grad))
+    lib().or_tsne_update(_ptr(y, ctypes.c_float), _ptr(update, ctypes.c_float),
+                         _ptr(gains, ctypes.c_float), _ptr(grad, ctypes.c_float), y.shape[0],
+                         ctypes.c_float(learning_rate), ctypes.c_float(momentum),
+                         ctypes.c_float(min_gain), ctypes.c_float(max_step_norm))
+    return y, update, gains
+
+
+def tsne_zero_mean(y):
+    y = _f32(y).copy()
+    lib().or_tsne_zero_mean(_ptr(y, ctypes.c_float), y.shape[0])
+    return y
+
+
+def tsne_kl(P: Csr, y: np.ndarray) -> float:
+    y = _f32(y)
+    return float(lib().or_tsne_kl(_ptr(P.row_ptr, ctypes.c_int), _ptr(P.col, ctypes.c_int),
+                                  _ptr(P.val, ctypes.c_float), P.n, _ptr(y, ctypes.c_float)))
+
+
+def tsne_run(P: Csr, init: np.ndarray, early_exaggeration_iter=250, n_iter=500,
+             early_exaggeration=12.0, exaggeration=1.0, learning_rate=None,
+             initial_momentum=0.8, final_momentum=0.8, min_gain=0.01, max_step_norm=5.0,
+             grid_size: int = 0) -> np.ndarray:
+    init = _f32(init)
+    out = np.zeros_like(init)
+    n = init.shape[0]
+    g = grid_size or tsne_grid_size(n)
+    lr_auto = learning_rate is None
+    lib().or_tsne_run(_ptr(P.row_ptr, ctypes.c_int), _ptr(P.col, ctypes.c_int),
+                      _ptr(P.val, ctypes.c_float), n, _ptr(init, ctypes.c_float),
+                      early_exaggeration_iter, n_iter, ctypes.c_float(early_exaggeration),
+                      ctypes.c_float(exaggeration), ctypes.c_float(learning_rate or 0.0),
+                      int(lr_auto), ctypes.c_float(initial_momentum),
+                      ctypes.c_float(final_momentum), ctypes.c_float(min_gain),
+                      ctypes.c_float(max_step_norm), g, _ptr(out, ctypes.c_float))
+    return out
+
+
+def umap_powf(x: float, b: float) -> float:
+    return lib().or_umap_powf(x, b)
+
+
+def umap_positive_samples(period: float, epoch: int) -> int:
+    return lib().or_umap_positive_samples(period, epoch)
+
+
+def umap_negative_samples(period: float, nsr: int, epoch: int) -> int:
+    return lib().or_umap_negative_samples(period, nsr, epoch)
+
+
+def umap_negative_vertex(n, seed, epoch, head, key, sample) -> int:
+    return lib().or_umap_negative_vertex(n, seed & 0xFFFFFFFF, epoch, head, key & 0xFFFFFFFF, sample)
+
+
+def umap_find_ab(spread: float = 1.0, min_dist: float = 0.1):
+    a, b = ctypes.c_double(), ctypes.c_double()
+    lib().or_umap_find_ab(ctypes.c_double(spread), ctypes.c_double(min_dist),
+                          ctypes.byref(a), ctypes.byref(b))
+    return a.value, b.value
+
+
+class UmapGraph:
+    """Fuzzy-union CSR graph plus the COO view the CUDA optimizer consumes."""
+
+    def __init__(self, offsets, neighbors, weights, epochs_per_sample, max_weight):
+        self.offsets = _i32(offsets)
+        self.neighbors = _i32(neighbors)
+        self.weights = _f32(weights)
+        self.epochs_per_sample = _f32(epochs_per_sample)
+        self.max_weight = float(max_weight)
+
+    @property
+    def n(self) -> int:
+        return self.offsets.size - 1
+
+    def heads(self) -> np.ndarray:
+        """CSR -> COO head expansion (as src/embedding_cuda_bridge.cpp:343-376 does)."""
+        counts = np.diff(self.offsets)
+        return np.repeat(np.arange(self.n, dtype=np.int32), counts)
+
+
+def umap_graph(idx: np.ndarray, dist: np.ndarray, index_offset: int = 0) -> UmapGraph:
+    n, k = idx.shape
+    idx_cm, dist_cm = _cm(idx, np.int32), _cm(dist, np.float32)
+    offsets = np.zeros(n + 1, np.int32)
+    cap = 2 * n * k
+    nb = np.zeros(cap, np.int32)
+    w = np.zeros(cap, np.float32)
+    eps = np.zeros(cap, np.float32)
+    maxw = ctypes.c_float(0.0)
+    nnz = lib().or_umap_graph(_ptr(idx_cm, ctypes.c_int), _ptr(dist_cm, ctypes.c_float), n, k,
+                              index_offset, _ptr(offsets, ctypes.c_int), _ptr(nb, ctypes.c_int),
+                              _ptr(w, ctypes.c_float), _ptr(eps, ctypes.c_float), ctypes.byref(maxw))
+    if nnz < 0:
+        raise ValueError("invalid KNN input for the UMAP graph")
+    return UmapGraph(offsets, nb[:nnz].copy(), w[:nnz].copy(), eps[:nnz].copy(), maxw.value)
+
+
+def umap_epoch_delta(heads, tails, epochs_per_sample, layout, epoch, n_epochs,
+                     negative_sample_rate=5, learning_rate=1.0, a=1.5769434601962196,
+                     b=0.8950608781227859, repulsion_strength=1.0, seed=42,
+                     hash_key_is_tail=False, max_abs_coord=16.0) -> np.ndarray:
+    heads, tails, eps = _i32(heads), _i32(tails), _f32(epochs_per_sample)
+    y = _f32(layout).copy()
+    lib().or_umap_epoch_delta(_ptr(heads, ctypes.c_int), _ptr(tails, ctypes.c_int),
+                              _ptr(eps, ctypes.c_float), heads.size, _ptr(y, ctypes.c_float),
+                              y.shape[0], epoch, n_epochs, negative_sample_rate,
+                              ctypes.c_float(learning_rate), ctypes.c_float(a), ctypes.c_float(b),
+                              ctypes.c_float(repulsion_strength), ctypes.c_uint32(seed & 0xFFFFFFFF),
+                              int(hash_key_is_tail), ctypes.c_float(max_abs_coord))
+    return y
+
+
+def umap_replay_serial(heads, tails, epochs_per_sample, layout, epoch_begin, epoch_end, n_epochs,
+                       negative_sample_rate=5, learning_rate=1.0, a=1.5769434601962196,
+                       b=0.8950608781227859, repulsion_strength=1.0, seed=42,
+                       hash_key_is_tail=False, sanitize_each_epoch=True) -> np.ndarray:
+    heads, tails, eps = _i32(heads), _i32(tails), _f32(epochs_per_sample)
+    y = _f32(layout).copy()
+    lib().or_umap_replay_serial(_ptr(heads, ctypes.c_int), _ptr(tails, ctypes.c_int),
+                                _ptr(eps, ctypes.c_float), heads.size, _ptr(y, ctypes.c_float),
+                                y.shape[0], epoch_begin, epoch_end, n_epochs, negative_sample_rate,
+                                ctypes.c_float(learning_rate), ctypes.c_float(a),
+                                ctypes.c_float(b), ctypes.c_float(repulsion_strength),
+                                ctypes.c_uint32(seed & 0xFFFFFFFF), int(hash_key_is_tail),
+                                int(sanitize_each_epoch))
+    return y
+
+
+# ------------------------------------------------------------ the reference
+
+
+def _ref_check(rc: int, which: str = "tsne") -> None:
+    if rc != 0:
+        R = ref()
+        msg = (R.feref_tsne_last_error() if which == "tsne" else R.feref_umap_last_error())
+        raise RuntimeError(f"reference {which} call failed: {msg.decode()}")
+
+
+def ref_tsne_grid_size(n: int, grid_override: int = 0) -> int:
+    return ref().feref_tsne_grid_size(n, grid_override)
+
+
+def ref_tsne_build_p(idx: np.ndarray, dist: np.ndarray, perplexity: float, threads: int = 1) -> Csr:
+    n, k = idx.shape
+    idx_cm, dist_cm = _cm(idx, np.int32), _cm(dist, np.float32)
+    R = ref()
+    h = R.feref_tsne_p_build(_ptr(idx_cm, ctypes.c_int), _ptr(dist_cm, ctypes.c_float), n, k,
+                             perplexity, threads)
+    if not h:
+        raise RuntimeError("reference P build failed: " + R.feref_tsne_last_error().decode())
+    nnz = R.feref_tsne_p_nnz(h)
+    row_ptr = np.zeros(n + 1, np.int32)
+    col = np.zeros(nnz, np.int32)
+    val = np.zeros(nnz, np.float32)
+    R.feref_tsne_p_copy(h, _ptr(row_ptr, ctypes.c_int), _ptr(col, ctypes.c_int), _ptr(val, ctypes.c_float))
+    R.feref_tsne_p_free(h)
+    return Csr(row_ptr, col, val)
+
+
+def ref_tsne_gradient_fft(P: Csr, y, exaggeration, threads=1, grid_override=0) -> np.ndarray:
+    y = _f32(y)
+    grad = np.zeros_like(y)
+    _ref_check(ref().feref_tsne_gradient_fft(
+        _ptr(P.row_ptr, ctypes.c_int), _ptr(P.col, ctypes.c_int), _ptr(P.val, ctypes.c_float), P.n,
+        _ptr(y, ctypes.c_float), exaggeration, threads, grid_override, _ptr(grad, ctypes.c_float)))
+    return grad
+
+
+def ref_tsne_gradient_exact(P: Csr, y, exaggeration, threads=1) -> np.ndarray:
+    y = _f32(y)
+    grad = np.zeros_like(y)
+    _ref_check(ref().feref_tsne_gradient_exact(
+        _ptr(P.row_ptr, ctypes.c_int), _ptr(P.col, ctypes.c_int), _ptr(P.val, ctypes.c_float), P.n,
+        _ptr(y, ctypes.c_float), exaggeration, threads, _ptr(grad, ctypes.c_float)))
+    return grad
+
+
+def ref_tsne_update(y, update, gains, grad, learning_rate, momentum, min_gain=0.01,
+                    max_step_norm=5.0, threads=1):
+    y, update, gains, grad = (_f32(a).copy() for a in (y, update, gains, grad))
+    _ref_check(ref().feref_tsne_update(
+        _ptr(y, ctypes.c_float), _ptr(update, ctypes.c_float), _ptr(gains, ctypes.c_float),
+        _ptr(grad, ctypes.c_float), y.shape[0], learning_rate, momentum, min_gain,
+        max_step_norm, threads))
+    return y, update, gains
+
+
+def ref_tsne_kl(P: Csr, y, threads=1) -> float:
+    y = _f32(y)
+    out = ctypes.c_double(0.0)
+    _ref_check(ref().feref_tsne_kl(_ptr(P.row_ptr, ctypes.c_int), _ptr(P.col, ctypes.c_int),
+                                   _ptr(P.val, ctypes.c_float), P.n, _ptr(y, ctypes.c_float),
+                                   threads, ctypes.byref(out)))
+    return out.value
+
+
+def ref_tsne_run(idx, dist, init=None, perplexity=30.0, early_exaggeration_iter=250, n_iter=500,
+                 early_exaggeration=12.0, exaggeration=1.0, learning_rate=None,
+                 initial_momentum=0.8, final_momentum=0.8, min_gain=0.01, max_step_norm=5.0,
+                 threads=1, seed=42, grid_override=0) -> np.ndarray:
+    """knn_tsne_opentsne_float_cpp (the reference CPU backend of opentsne_knn)."""
+    n, k = idx.shape
+    idx_cm, dist_cm = _cm(idx, np.int32), _cm(dist, np.float32)
+    out = np.zeros((n, 2), np.float32)
+    init_p = None
+    if init is not None:
+        init = _f32(init)
+        init_p = _ptr(init, ctypes.c_float)
+    lr_auto = learning_rate is None
+    _ref_check(ref().feref_tsne_run(
+        _ptr(idx_cm, ctypes.c_int), _ptr(dist_cm, ctypes.c_float), n, k, init_p, perplexity,
+        early_exaggeration_iter, n_iter, early_exaggeration, exaggeration,
+        float(learning_rate or 0.0), int(lr_auto), initial_momentum, final_momentum, min_gain,
+        max_step_norm, threads, seed, grid_override, _ptr(out, ctypes.c_float)))
+    return out
+
+
+def ref_tsne_auto_parameters(n: int, k: int, perplexity: float = 30.0, perplexity_missing=False):
+    out = np.zeros(6, np.float64)
+    _ref_check(ref().feref_tsne_auto_parameters(n, k, perplexity, int(perplexity_missing),
+                                                _ptr(out, ctypes.c_double)))
+    keys = ("perplexity", "n_neighbors", "early_exaggeration", "learning_rate",
+            "early_exaggeration_iter", "n_iter")
+    return dict(zip(keys, out.tolist()))
+
+
+def ref_umap_graph(idx, dist, threads=1) -> UmapGraph:
+    n, k = idx.shape
+    idx_cm, dist_cm = _cm(idx, np.int32), _cm(dist, np.float32)
+    R = ref()
+    h = R.feref_umap_graph(_ptr(idx_cm, ctypes.c_int), _ptr(dist_cm, ctypes.c_float), n, k, threads)
+    if not h:
+        raise RuntimeError("reference UMAP graph failed: " + R.feref_umap_last_error().decode())
+    nnz = R.feref_umap_graph_nnz(h)
+    off = np.zeros(n + 1, np.int32)
+    nb = np.zeros(nnz, np.int32)
+    w = np.zeros(nnz, np.float32)
+    eps = np.zeros(nnz, np.float32)
+    maxw = ctypes.c_float(0.0)
+    R.feref_umap_graph_copy(h, _ptr(off, ctypes.c_int), _ptr(nb, ctypes.c_int),
+                            _ptr(w, ctypes.c_float), _ptr(eps, ctypes.c_float), ctypes.byref(maxw))
+    R.feref_umap_graph_free(h)
+    return UmapGraph(off, nb, w, eps, maxw.value)
+
+
+def ref_umap_coo_replay(heads, tails, weights, epochs_per_sample, init, n_epochs, min_dist=0.1,
+                        negative_sample_rate=5, learning_rate=1.0, repulsion_strength=1.0,
+                        threads=1, seed=42, sanitize_each_epoch=True) -> np.ndarray:
+    heads, tails, w, eps, init = _i32(heads), _i32(tails), _f32(weights), _f32(epochs_per_sample), _f32(init)
+    out = np.zeros_like(init)
+    _ref_check(ref().feref_umap_coo_replay(
+        _ptr(heads, ctypes.c_int), _ptr(tails, ctypes.c_int), _ptr(w, ctypes.c_float),
+        _ptr(eps, ctypes.c_float), _ptr(init, ctypes.c_float), init.shape[0], heads.size,
+        n_epochs, min_dist, negative_sample_rate, learning_rate, repulsion_strength, threads,
+        seed, int(sanitize_each_epoch), _ptr(out, ctypes.c_float)), "umap")
+    return out
+
+
+def ref_umap_csr_optimize(g: UmapGraph, init, n_epochs, min_dist=0.1, negative_sample_rate=5,
+                          learning_rate=1.0, repulsion_strength=1.0, threads=1, seed=42):
+    init = _f32(init)
+    out = np.zeros_like(init)
+    _ref_check(ref().feref_umap_csr_optimize(
+        _ptr(g.offsets, ctypes.c_int), _ptr(g.neighbors, ctypes.c_int), _ptr(g.weights, ctypes.c_float),
+        _ptr(init, ctypes.c_float), g.n, g.neighbors.size, n_epochs, min_dist,
+        negative_sample_rate, learning_rate, repulsion_strength, threads, seed,
+        _ptr(out, ctypes.c_float)), "umap")
+    return out
+
+
+def ref_umap_powf(x: float, b: float) -> float:
+    return ref().feref_umap_powf(x, b)
+
+
+def ref_umap_positive_samples(period, epoch) -> int:
+    return ref().feref_umap_positive_samples(period, epoch)
+
+
+def ref_umap_negative_samples(period, nsr, epoch) -> int:
+    return ref().feref_umap_negative_samples(period, nsr, epoch)
+
+
+def ref_umap_negative_vertex(n, seed, epoch, head, edge, sample) -> int:
+    return ref().feref_umap_negative_vertex(n, seed, epoch, head, edge, sample)
+
+
+def ref_find_ab(spread=1.0, min_dist=0.1):
+    a, b = ctypes.c_double(), ctypes.c_double()
+    ref().feref_find_ab(spread, min_dist, ctypes.byref(a), ctypes.byref(b))
+    return a.value, b.value

@@ -1,0 +1,371 @@
+"""Benchmark of the B200 embedding-optimizer backend.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload tsne_1m|tsne_70k|tsne_10k]
+
+A *step* is one openTSNE optimizer iteration (gradient + update) over the whole
+workload.  The default workload is configuration 3 of the benchmark set
+(N = 1,000,000 points, 20-component anisotropic Gaussian mixture in 50-D with
+Dirichlet weights, exact k = 90 KNN, perplexity 30, FFT grid repulsion) -- the
+configuration the headline metric (t-SNE iterations/s at N = 1M) is quoted on.
+
+Our arm (--impl ours) prints one JSON line with
+  value      iterations/s with P, layout and optimizer state resident in HBM
+  e2e        iterations/s of the full C-ABI call (fastembedr_cuda_opentsne_fft_from_knn_float)
+             from pinned host KNN to host layout: H2D, P build, 750 iterations, D2H
+  roofline   the fused gradient/update kernel: algorithmic bytes per launch over its
+             CUDA-event duration, against MEASURED_PEAKS.json's HBM copy bandwidth
+  cpu_baseline  the reference's own CPU loop (oracle/_ref) on a few iterations of the
+             same workload, all host threads
+The reference arm (--impl reference) times the reference's own CPU
+implementation of the same loop (rank 0 only).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import re
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+WORKLOADS = {
+    "tsne_1m": dict(spec="tsne_1m", k=90, perplexity=30.0),
+    "tsne_70k": dict(spec="tsne_70k", k=90, perplexity=30.0),
+    "tsne_10k": dict(spec="tsne_10k", k=90, perplexity=30.0),
+}
+EE_ITER, N_ITER, EE, EX, MOM = 250, 500, 12.0, 1.0, 0.8
+MIN_GAIN, MAX_STEP = 0.01, 5.0
+FALLBACK_HBM_GBS = 6650.0
+
+
+def log(*a):
+    print(*a, file=sys.stderr, flush=True)
+
+
+def dist_env():
+    return (int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1")),
+            int(os.environ.get("LOCAL_RANK", "0")))
+
+
+def peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    return FALLBACK_HBM_GBS, "fallback"
+
+
+def make_inputs(workload: str, device: str):
+    from fastembedr_b200 import synthetic as S
+
+    w = WORKLOADS[workload]
+    spec = S.CONFIGS[w["spec"]]
+    t0 = time.time()
+    x, _ = S.gaussian_mixture(spec)
+    idx, dist = S.exact_knn(x, w["k"], device=device)
+    log(f"[bench] {workload}: n={spec.n} k={w['k']} inputs in {time.time() - t0:.1f}s")
+    return idx, dist, S.tsne_init(spec.n, seed=0)
+
+
+def phase_params(i: int, n: int):
+    """Parameters of iteration i of the default schedule (250 early + 500 normal)."""
+    if (i % (EE_ITER + N_ITER)) < EE_ITER:
+        return EE, MOM, float(np.float32(n / EE))
+    return EX, MOM, float(np.float32(n / EX))
+
+
+def run_schedule(sess, start: int, count: int, n: int):
+    i = start
+    while i < start + count:
+        ex, mom, lr = phase_params(i, n)
+        cyc = i % (EE_ITER + N_ITER)
+        left = (EE_ITER - cyc) if cyc < EE_ITER else (EE_ITER + N_ITER - cyc)
+        step = min(left, start + count - i)
+        sess.iterate(step, ex, mom, lr, MIN_GAIN, MAX_STEP)
+        i += step
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except OSError:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = max(mx, float(parts[2]))
+            except ValueError:
+                continue
+            for nm, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(nm)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        return {"sm_mhz": float(np.median(sm)), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def profile_traffic(kernel: str, workload: str):
+    """DRAM bytes per launch from the committed ncu summary, if one exists."""
+    path = os.path.join(ROOT, "profiles", f"{kernel}_{workload}.md")
+    if not os.path.exists(path):
+        return None
+    m = re.search(r"traffic_bytes_per_launch:\s*([0-9.eE+]+)", open(path).read())
+    return float(m.group(1)) if m else None
+
+
+def cpu_baseline_tsne(idx, dist, perplexity, init, iters: int):
+    """The reference's own CPU loop on `iters` iterations of the workload."""
+    import oracle as O
+
+    threads = os.cpu_count() or 1
+    n = idx.shape[0]
+    ex, mom, lr = phase_params(0, n)
+    upd = np.zeros_like(init)
+    gains = np.ones_like(init)
+    if O.ref_available():
+        t0 = time.time()
+        P = O.ref_tsne_build_p(idx, dist, perplexity, threads=threads)
+        setup = time.time() - t0
+        _, _, _, secs = O.ref_tsne_iterate(P, O.tsne_zero_mean(init), upd, gains, iters, ex, mom, lr,
+                                           MIN_GAIN, MAX_STEP, threads=threads)
+        kind, cores = "reference", threads
+    else:
+        t0 = time.time()
+        P = O.tsne_build_p(idx, dist, perplexity)
+        setup = time.time() - t0
+        t0 = time.time()
+        O.tsne_iterate(P, O.tsne_zero_mean(init), upd, gains, iters, ex, mom, lr, MIN_GAIN, MAX_STEP)
+        secs = time.time() - t0
+        kind, cores = "port", 1
+    return {"value": iters / secs, "unit": "iterations/s", "cores": cores, "kind": kind,
+            "sample": f"{iters} optimizer iterations of the full n={n} workload "
+                      f"(P build {setup:.1f}s excluded), {cores} threads"}
+
+
+def bench_reference(args):
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return 0
+    w = WORKLOADS[args.workload]
+    device = "cuda" if _cuda_ok() else None
+    idx, dist, init = make_inputs(args.workload, device)
+    iters = max(1, min(args.steps, 40))
+    base = cpu_baseline_tsne(idx, dist, w["perplexity"], init, iters)
+    line = {
+        "impl": "reference", "metric": "tsne_iterations_per_second", "value": base["value"],
+        "unit": "iterations/s", "n_gpus": 0, "steps": iters, "warmup": 0,
+        "ms_per_step": 1000.0 / base["value"], "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": args.workload, "n": int(idx.shape[0]), "k": w["k"],
+                   "perplexity": w["perplexity"], "grid": "reference CPU policy"},
+        "cpu_baseline": {k: base[k] for k in ("value", "unit", "cores", "kind", "sample")},
+        "e2e": {"value": base["value"], "unit": "iterations/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def _cuda_ok():
+    try:
+        import torch
+
+        return torch.cuda.is_available()
+    except Exception:
+        return False
+
+
+def bench_ours(args):
+    import torch
+    import torch.distributed as tdist
+
+    from fastembedr_b200 import _lib, api
+
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    if world > 1:
+        tdist.init_process_group("nccl", init_method="env://", timeout=__import__("datetime").timedelta(seconds=300))
+    w = WORKLOADS[args.workload]
+    idx, dist, init = make_inputs(args.workload, f"cuda:{local}")
+    n, k = idx.shape
+    if not api.cuda_available():
+        raise RuntimeError("libfastembedr_b200 reports no usable B200")
+
+    # --- device-resident loop (value) ---
+    d_idx = torch.from_numpy(idx).cuda()
+    d_dist = torch.from_numpy(dist).cuda()
+    t0 = time.time()
+    sess = api.TsneSession.from_knn(d_idx, d_dist, perplexity=w["perplexity"], init=init)
+    info = sess.info()
+    log(f"[bench] rank {rank}: P nnz={info['nnz']} padded={info['nnz_padded']} G={info['grid']} "
+        f"(setup {time.time() - t0:.2f}s)")
+    del d_idx, d_dist
+    stream = torch.cuda.ExternalStream(sess.stream)
+    run_schedule(sess, 0, args.warmup, n)
+    torch.cuda.synchronize()
+    if world > 1:
+        tdist.barrier()
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        torch.cuda.synchronize()
+        start.record(stream)
+        run_schedule(sess, args.warmup, args.steps, n)
+        stop.record(stream)
+        torch.cuda.synchronize()
+    elapsed_ms = start.elapsed_time(stop)
+    if world > 1:
+        t = torch.tensor([elapsed_ms], device="cuda")
+        tdist.all_reduce(t, op=tdist.ReduceOp.MAX)
+        elapsed_ms = float(t.item())
+    ms_per_step = elapsed_ms / args.steps
+    value = world * args.steps / (elapsed_ms / 1000.0)
+
+    # --- per-kernel CUDA-event timing of the same loop (roofline) ---
+    sess.profile(True)
+    prof_iters = min(args.steps, 100)
+    run_schedule(sess, args.warmup + args.steps, prof_iters, n)
+    times = sess.kernel_times()
+    sess.profile(False)
+    grid = info["grid"]
+    nnz = info["nnz"]
+    # Algorithmic bytes of one grad_update launch: row_ptr, (col, val) per symmetric entry,
+    # layout read, update/gains read+write, layout write, potentials (4 floats per node).
+    alg_bytes = 4 * (n + 1) + 8 * nnz + 8 * n + 16 * n + 24 * n + 16 * grid * grid
+    gu_ms, gu_cnt = times["grad_update_kernel"]
+    gu_avg_s = gu_ms / max(gu_cnt, 1) / 1000.0
+    hbm, peak_kind = peaks()
+    achieved = alg_bytes / gu_avg_s / 1e9
+    total_ms = sum(v[0] for v in times.values())
+    kernel_share = {kname: round(v[0] / total_ms, 4) for kname, v in times.items()}
+
+    # --- end to end through the C ABI with pinned host buffers ---
+    e2e = None
+    if rank == 0 and not args.skip_e2e:
+        idx_cm = torch.from_numpy(np.ascontiguousarray(idx.T)).pin_memory()
+        dist_cm = torch.from_numpy(np.ascontiguousarray(dist.T)).pin_memory()
+        init_h = torch.from_numpy(init).pin_memory()
+        out_h = torch.empty((n, 2), dtype=torch.float32).pin_memory()
+        import ctypes
+
+        L = _lib.load()
+
+        def call():
+            rc = L.fastembedr_cuda_opentsne_fft_from_knn_float(
+                ctypes.c_void_p(idx_cm.data_ptr()), ctypes.c_void_p(dist_cm.data_ptr()),
+                ctypes.cast(init_h.data_ptr(), ctypes.POINTER(ctypes.c_float)), 1, n, k, 2,
+                w["perplexity"], EE_ITER, N_ITER, EE, EX, 0.0, 1, MOM, MOM, MIN_GAIN, MAX_STEP, 42, 0,
+                ctypes.cast(out_h.data_ptr(), ctypes.POINTER(ctypes.c_float)))
+            _lib.check(rc, "fastembedr_cuda_opentsne_fft_from_knn_float")
+
+        call()  # warm (first-call module load)
+        reps = 2
+        t0 = time.perf_counter()
+        for _ in range(reps):
+            call()
+        e2e_s = (time.perf_counter() - t0) / reps
+        e2e = {"value": (EE_ITER + N_ITER) / e2e_s, "unit": "iterations/s",
+               "h2d_bytes_per_step": int(idx_cm.numel() * 4 + dist_cm.numel() * 4 + init_h.numel() * 4),
+               "d2h_bytes_per_step": int(out_h.numel() * 4), "seconds_per_call": e2e_s,
+               "call": "fastembedr_cuda_opentsne_fft_from_knn_float (750 iterations, host KNN)"}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.skip_cpu:
+        cpu = cpu_baseline_tsne(idx, dist, w["perplexity"], init, args.cpu_iters)
+
+    sess.close()
+    if rank == 0:
+        line = {
+            "metric": "tsne_iterations_per_second", "value": value, "unit": "iterations/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
+            "higher_is_better": True, "scaling": "weak" if world > 1 else "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": args.workload, "n": int(n), "k": int(k), "perplexity": w["perplexity"],
+                       "grid": grid, "nnz": int(nnz), "schedule": "250 early (ex 12) + 500 normal, lr n/ex",
+                       "l2": "inputs larger than L2 (P is %.2f GB)" % ((8 * info["nnz_padded"]) / 1e9),
+                       "parallelism": "replicas" if world > 1 else "single"},
+            "roofline": {"kernel": "grad_update_kernel", "bound": "hbm", "achieved": achieved,
+                         "peak": hbm, "peak_kind": peak_kind, "unit": "GB/s", "frac": achieved / hbm,
+                         "algorithmic_bytes_per_launch": alg_bytes,
+                         "avg_launch_ms": gu_avg_s * 1000.0,
+                         "traffic": profile_traffic("grad_update_kernel", args.workload)},
+            "kernel_share": kernel_share,
+            "kernel_ms": {kname: v[0] / max(v[1], 1) for kname, v in times.items()},
+            "gpu_launches": 5 * args.steps,
+            "clocks": clocks.summary(),
+            "e2e": e2e,
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        tdist.barrier()
+        tdist.destroy_process_group()
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=1500)
+    ap.add_argument("--warmup", type=int, default=30)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="tsne_1m")
+    ap.add_argument("--cpu-iters", type=int, default=5)
+    ap.add_argument("--skip-e2e", action="store_true")
+    ap.add_argument("--skip-cpu", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be at least 3")
+    if args.impl == "reference":
+        return bench_reference(args)
+    return bench_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,387 @@
+"""Host-side mirror of the reference interface for the optimizer path.
+
+The reference reaches its CUDA optimizer from R: ``opentsne_knn(knn,
+backend = "cuda")`` and ``umap_knn(knn, backend = "cuda")`` resolve their
+parameters (R/tsne_affinity_dispatch.R, R/fast_knn_umap.R), then the C++
+wrapper (src/embedding_cuda_impl.cpp) converts matrices and calls the C ABI.
+R is not part of this build, so this module plays the wrapper's role for
+Python callers and tests: the same parameter policies, the same C-ABI calls,
+the same provenance strings, errors raised as exceptions.
+"""
+from __future__ import annotations
+
+import ctypes
+import math
+from dataclasses import dataclass, field
+from typing import Any, Dict, Optional, Tuple
+
+import numpy as np
+
+from . import _lib
+from ._lib import CudaBackendError, check
+
+# Provenance labels returned by the reference wrapper (src/embedding_cuda_impl.cpp:2194-2217),
+# asserted by the reference tests (tests/testthat/test-tsne.R:243-244).
+TSNE_OPTIMIZER_LABEL = "opentsne_fitsne_fft_grid_native_cuda"
+TSNE_REPULSION_LABEL = "fft_grid_cuda_cufft"
+UMAP_UPDATE_RULE_LABEL = "native_cuda_atomic_coo_umap_schedule"
+
+
+def _f32(a) -> np.ndarray:
+    return np.ascontiguousarray(a, dtype=np.float32)
+
+
+def _i32(a) -> np.ndarray:
+    return np.ascontiguousarray(a, dtype=np.int32)
+
+
+def _ptr(a: np.ndarray, ctype):
+    return a.ctypes.data_as(ctypes.POINTER(ctype))
+
+
+def cuda_available() -> bool:
+    return bool(_lib.load().fastembedr_cuda_available())
+
+
+def version() -> str:
+    return _lib.load().fe_b200_version().decode()
+
+
+# ------------------------------------------------------------------ parameter policy
+
+
+def tsne_auto_parameters(n: int, k: int, perplexity: Optional[float] = None) -> Dict[str, Any]:
+    """Restates tsne_auto_parameters_cpp (src/tsne_neighbors.cpp:1573-1618)."""
+    if n < 2:
+        raise ValueError("`n` must be at least 2.")
+    if k < 1:
+        raise ValueError("`k` must be positive.")
+    missing = perplexity is None or not math.isfinite(perplexity) or perplexity <= 0.0
+    max_n = max(1, (n - 1) // 3)
+    max_k = max(1, k // 3)
+    resolved = float(min(30, min(max_n, max_k))) if missing else float(perplexity)
+    max_resolved = min(max_n, max_k) if missing else max_n
+    resolved = max(1.0, min(resolved, float(max_resolved)))
+    ee = 12.0
+    return {
+        "perplexity": resolved,
+        "n_neighbors": max(1, min(n - 1, int(math.ceil(resolved)))),
+        "early_exaggeration": ee,
+        "exaggeration": 1.0,
+        "learning_rate": float(n) / ee,
+        "early_exaggeration_iter": 250,
+        "n_iter": 500,
+    }
+
+
+def find_ab_params(spread: float = 1.0, min_dist: float = 0.1) -> Tuple[float, float]:
+    """UMAP curve parameters a, b for (spread, min_dist).
+
+    Restates find_ab_params (src/fast_knn_umap.cpp:428-488, used by the CUDA
+    wrapper at src/embedding_cuda_impl.cpp:478-532): tabulated values for the
+    common settings, otherwise a coarse grid search refined by 80 gradient steps.
+    """
+    table = {(1.0, 0.01): (1.895605865596314, 0.8006377738365004),
+             (1.0, 0.1): (1.5769434601962196, 0.8950608781227859),
+             (1.0, 0.5): (0.5830300199018228, 1.3341669931033755)}
+    for (s, m), ab in table.items():
+        if abs(spread - s) < 1e-12 and abs(min_dist - m) < 1e-12:
+            return ab
+    xs = (spread * 3.0) * np.arange(300, dtype=np.float64) / 299.0
+    ys = np.where(xs < min_dist, 1.0, np.exp(-(xs - min_dist) / spread))
+    best = (1.5769434601962196, 0.8950608781227859)
+    best_loss = math.inf
+    loga = -4.0
+    while loga <= 4.0001:
+        b = 0.25
+        while b <= 2.0001:
+            a = math.exp(loga)
+            loss = 0.0
+            for x, y in zip(xs, ys):
+                e = 1.0 / (1.0 + a * math.pow(x, 2.0 * b)) - y
+                loss += e * e
+            if loss < best_loss:
+                best_loss, best = loss, (a, b)
+            b += 0.05
+        loga += 0.2
+    a, b = best
+    for _ in range(80):
+        ga = gb = 0.0
+        for x0, y in zip(xs, ys):
+            x = max(x0, 1e-6)
+            x2b = math.pow(x, 2.0 * b)
+            den = 1.0 + a * x2b
+            e = 1.0 / den - y
+            ga += e * (-x2b / (den * den))
+            gb += e * (-(a * x2b * 2.0 * math.log(x)) / (den * den))
+        a = max(1e-4, a - 0.01 * ga)
+        b = max(0.1, b - 0.01 * gb)
+    return a, b
+
+
+def resolve_index_offset(indices: np.ndarray) -> int:
+    """1 when every index lies in [1, n] (R's 1-based KNN), else 0
+    (src/embedding_cuda_impl.cpp:886-895)."""
+    n = indices.shape[0]
+    return 1 if indices.size and indices.min() >= 1 and indices.max() <= n else 0
+
+
+def column_major(a: np.ndarray, dtype) -> np.ndarray:
+    return np.ascontiguousarray(np.asarray(a, dtype=dtype).T)
+
+
+# ------------------------------------------------------------------ openTSNE
+
+
+@dataclass
+class EmbeddingResult:
+    Y: np.ndarray
+    config: Dict[str, Any] = field(default_factory=dict)
+
+
+def opentsne_knn(indices, distances, n_components: int = 2, perplexity: Optional[float] = 30.0,
+                 early_exaggeration_iter: int = 250, n_iter: int = 500,
+                 early_exaggeration: float = 12.0, exaggeration: float = 1.0,
+                 learning_rate="auto", initial_momentum: float = 0.8, final_momentum: float = 0.8,
+                 min_gain: float = 0.01, max_step_norm="auto", init: Optional[np.ndarray] = None,
+                 seed: int = 42, index_offset: Optional[int] = None) -> EmbeddingResult:
+    """openTSNE-style t-SNE from KNN on the B200 backend.
+
+    ``indices``/``distances`` are (n, k) host arrays (0- or 1-based indices,
+    self excluded) or CUDA tensors (then the device-KNN entry point is used and
+    nothing is copied).  Defaults follow R/fast_knn_tsne.R:39-60 and
+    R/tsne_affinity_dispatch.R (momentum 0.8/0.8, min_gain 0.01,
+    max_step_norm "auto" = 5, learning_rate "auto" = n / exaggeration).
+    """
+    on_device = hasattr(indices, "is_cuda") and indices.is_cuda
+    n, k = (int(indices.shape[0]), int(indices.shape[1]))
+    if perplexity is None:
+        perplexity = tsne_auto_parameters(n, k)["perplexity"]
+    lr_auto = isinstance(learning_rate, str)
+    lr = 0.0 if lr_auto else float(learning_rate)
+    msn = 5.0 if isinstance(max_step_norm, str) else float(max_step_norm)
+    out = np.zeros((n, 2), np.float32)
+    init_arr = None if init is None else _f32(init)
+    L = _lib.load()
+    if on_device:
+        import torch
+
+        idx_cm = indices.to(torch.int32).t().contiguous()
+        dist_cm = distances.to(torch.float32).t().contiguous()
+        off = index_offset if index_offset is not None else int(
+            bool((idx_cm.min() >= 1).item() and (idx_cm.max() <= n).item()))
+        rc = L.fastembedr_cuda_opentsne_fft_from_device_knn_float(
+            ctypes.c_void_p(idx_cm.data_ptr()), ctypes.c_void_p(dist_cm.data_ptr()),
+            None if init_arr is None else _ptr(init_arr, ctypes.c_float), int(init_arr is not None),
+            n, k, n_components, perplexity, early_exaggeration_iter, n_iter, early_exaggeration,
+            exaggeration, lr, int(lr_auto), initial_momentum, final_momentum, min_gain, msn,
+            seed & 0xFFFFFFFF, off, _ptr(out, ctypes.c_float))
+        entry = "fastembedr_cuda_opentsne_fft_from_device_knn_float"
+    else:
+        idx = np.asarray(indices)
+        off = index_offset if index_offset is not None else resolve_index_offset(idx)
+        idx_cm = column_major(idx, np.int32)
+        dist_cm = column_major(distances, np.float32)
+        rc = L.fastembedr_cuda_opentsne_fft_from_knn_float(
+            ctypes.c_void_p(idx_cm.ctypes.data), ctypes.c_void_p(dist_cm.ctypes.data),
+            None if init_arr is None else _ptr(init_arr, ctypes.c_float), int(init_arr is not None),
+            n, k, n_components, perplexity, early_exaggeration_iter, n_iter, early_exaggeration,
+            exaggeration, lr, int(lr_auto), initial_momentum, final_momentum, min_gain, msn,
+            seed & 0xFFFFFFFF, off, _ptr(out, ctypes.c_float))
+        entry = "fastembedr_cuda_opentsne_fft_from_knn_float"
+    if rc != 0:
+        raise CudaBackendError("CUDA openTSNE FFT-grid failed: " + _lib.last_error())
+    return EmbeddingResult(out, {
+        "optimizer": TSNE_OPTIMIZER_LABEL, "repulsion": TSNE_REPULSION_LABEL, "entry_point": entry,
+        "perplexity": perplexity, "learning_rate": "auto" if lr_auto else lr,
+        "max_step_norm": msn, "backend": "cuda", "device": "B200 (sm_100a)",
+    })
+
+
+class TsneSession:
+    """Device-resident t-SNE state (P, layout, gains, update) across calls."""
+
+    def __init__(self, handle: int, n: int):
+        self._h = ctypes.c_void_p(handle)
+        self.n = n
+
+    @classmethod
+    def from_knn(cls, indices, distances, perplexity: float = 30.0, init=None, seed: int = 42,
+                 grid_size: int = 0, index_offset: Optional[int] = None) -> "TsneSession":
+        L = _lib.load()
+        h = ctypes.c_void_p()
+        on_device = hasattr(indices, "is_cuda") and indices.is_cuda
+        n, k = int(indices.shape[0]), int(indices.shape[1])
+        init_arr = None if init is None else _f32(init)
+        keep = []
+        if on_device:
+            import torch
+
+            idx_cm = indices.to(torch.int32).t().contiguous()
+            dist_cm = distances.to(torch.float32).t().contiguous()
+            keep = [idx_cm, dist_cm]
+            off = 0 if index_offset is None else index_offset
+            ip, dp = ctypes.c_void_p(idx_cm.data_ptr()), ctypes.c_void_p(dist_cm.data_ptr())
+            init_dev = None
+            if init_arr is not None:
+                init_dev = torch.from_numpy(init_arr).cuda()
+                keep.append(init_dev)
+            init_p = None if init_dev is None else ctypes.cast(init_dev.data_ptr(), ctypes.POINTER(ctypes.c_float))
+        else:
+            idx = np.asarray(indices)
+            off = index_offset if index_offset is not None else resolve_index_offset(idx)
+            idx_cm = column_major(idx, np.int32)
+            dist_cm = column_major(distances, np.float32)
+            keep = [idx_cm, dist_cm]
+            ip, dp = ctypes.c_void_p(idx_cm.ctypes.data), ctypes.c_void_p(dist_cm.ctypes.data)
+            init_p = None if init_arr is None else _ptr(init_arr, ctypes.c_float)
+        check(L.fe_b200_tsne_create(ip, dp, n, k, off, perplexity, init_p, seed & 0xFFFFFFFF,
+                                    grid_size, int(on_device), ctypes.byref(h)), "fe_b200_tsne_create")
+        del keep
+        return cls(h.value, n)
+
+    @classmethod
+    def from_csr(cls, row_ptr, col, val, init, grid_size: int = 0) -> "TsneSession":
+        L = _lib.load()
+        rp, c, v, y = _i32(row_ptr), _i32(col), _f32(val), _f32(init)
+        h = ctypes.c_void_p()
+        check(L.fe_b200_tsne_create_csr(_ptr(rp, ctypes.c_int), _ptr(c, ctypes.c_int), _ptr(v, ctypes.c_float),
+                                        y.shape[0], _ptr(y, ctypes.c_float), grid_size, ctypes.byref(h)),
+              "fe_b200_tsne_create_csr")
+        return cls(h.value, y.shape[0])
+
+    def iterate(self, n_iter: int, exaggeration: float, momentum: float, learning_rate: float,
+                min_gain: float = 0.01, max_step_norm: float = 5.0) -> None:
+        check(_lib.load().fe_b200_tsne_iterate(self._h, n_iter, exaggeration, momentum, learning_rate,
+                                               min_gain, max_step_norm), "fe_b200_tsne_iterate")
+
+    def run(self, early_exaggeration_iter=250, n_iter=500, early_exaggeration=12.0, exaggeration=1.0,
+            learning_rate="auto", initial_momentum=0.8, final_momentum=0.8, min_gain=0.01,
+            max_step_norm=5.0) -> np.ndarray:
+        auto = isinstance(learning_rate, str)
+        lr_e = float(np.float32(self.n / early_exaggeration)) if auto else learning_rate
+        lr_n = float(np.float32(self.n / exaggeration)) if auto else learning_rate
+        self.iterate(early_exaggeration_iter, early_exaggeration, initial_momentum, lr_e, min_gain, max_step_norm)
+        self.iterate(n_iter, exaggeration, final_momentum, lr_n, min_gain, max_step_norm)
+        return self.layout()
+
+    def gradient(self, exaggeration: float) -> Tuple[np.ndarray, float]:
+        g = np.zeros((self.n, 2), np.float32)
+        z = ctypes.c_double(0.0)
+        check(_lib.load().fe_b200_tsne_gradient(self._h, exaggeration, _ptr(g, ctypes.c_float),
+                                                ctypes.byref(z)), "fe_b200_tsne_gradient")
+        return g, z.value
+
+    def layout(self) -> np.ndarray:
+        y = np.zeros((self.n, 2), np.float32)
+        check(_lib.load().fe_b200_tsne_get_layout(self._h, ctypes.c_void_p(y.ctypes.data), 0),
+              "fe_b200_tsne_get_layout")
+        return y
+
+    def set_layout(self, y, reset_state: bool = True) -> None:
+        y = _f32(y)
+        check(_lib.load().fe_b200_tsne_set_layout(self._h, ctypes.c_void_p(y.ctypes.data), 0,
+                                                  int(reset_state)), "fe_b200_tsne_set_layout")
+
+    def state(self) -> Tuple[np.ndarray, np.ndarray]:
+        u = np.zeros((self.n, 2), np.float32)
+        g = np.zeros((self.n, 2), np.float32)
+        check(_lib.load().fe_b200_tsne_get_state(self._h, _ptr(u, ctypes.c_float), _ptr(g, ctypes.c_float)),
+              "fe_b200_tsne_get_state")
+        return u, g
+
+    def set_state(self, update, gains) -> None:
+        u, g = _f32(update), _f32(gains)
+        check(_lib.load().fe_b200_tsne_set_state(self._h, _ptr(u, ctypes.c_float), _ptr(g, ctypes.c_float)),
+              "fe_b200_tsne_set_state")
+
+    def info(self) -> Dict[str, int]:
+        n, g = ctypes.c_int(), ctypes.c_int()
+        nnz, nnzp = ctypes.c_longlong(), ctypes.c_longlong()
+        check(_lib.load().fe_b200_tsne_info(self._h, ctypes.byref(n), ctypes.byref(g), ctypes.byref(nnz),
+                                            ctypes.byref(nnzp)), "fe_b200_tsne_info")
+        return {"n": n.value, "grid": g.value, "nnz": nnz.value, "nnz_padded": nnzp.value}
+
+    def p(self):
+        inf = self.info()
+        rp = np.zeros(inf["n"] + 1, np.int32)
+        c = np.zeros(inf["nnz_padded"], np.int32)
+        v = np.zeros(inf["nnz_padded"], np.float32)
+        check(_lib.load().fe_b200_tsne_get_p(self._h, _ptr(rp, ctypes.c_int), _ptr(c, ctypes.c_int),
+                                             _ptr(v, ctypes.c_float)), "fe_b200_tsne_get_p")
+        nnz = int(rp[-1])
+        return rp, c[:nnz].copy(), v[:nnz].copy()
+
+    @property
+    def stream(self) -> int:
+        return int(_lib.load().fe_b200_tsne_stream(self._h) or 0)
+
+    def profile(self, enable: bool) -> None:
+        check(_lib.load().fe_b200_tsne_profile(self._h, int(enable)), "fe_b200_tsne_profile")
+
+    def kernel_times(self) -> Dict[str, Tuple[float, int]]:
+        ms = np.zeros(5, np.float64)
+        cnt = np.zeros(5, np.int64)
+        L = _lib.load()
+        check(L.fe_b200_tsne_kernel_times(self._h, _ptr(ms, ctypes.c_double), _ptr(cnt, ctypes.c_longlong), 5),
+              "fe_b200_tsne_kernel_times")
+        return {L.fe_b200_tsne_kernel_name(i).decode(): (float(ms[i]), int(cnt[i])) for i in range(5)}
+
+    def close(self) -> None:
+        if self._h is not None and self._h.value:
+            _lib.load().fe_b200_tsne_destroy(self._h)
+        self._h = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+# ------------------------------------------------------------------ UMAP
+
+
+def umap_optimize_coo(heads, tails, weights, epochs_per_sample, init, n_epochs: int = 500,
+                      negative_sample_rate: int = 5, learning_rate: float = 1.0,
+                      min_dist: float = 0.1, repulsion_strength: float = 1.0, seed: int = 42,
+                      optimizer_mode: int = 0) -> np.ndarray:
+    """The CUDA COO UMAP optimizer (umap_cuda_optimize_coo_impl,
+    src/embedding_cuda_impl.cpp:1898-1957): a, b from min_dist, then the C ABI."""
+    h, t, w, e, y = _i32(heads), _i32(tails), _f32(weights), _f32(epochs_per_sample), _f32(init)
+    if not (h.size == t.size == w.size == e.size):
+        raise ValueError("COO heads, tails, weights, and epochs_per_sample must have the same length")
+    if y.ndim != 2 or y.shape[1] != 2:
+        raise ValueError("CUDA COO UMAP optimizer requires a two-dimensional initialization")
+    a, b = find_ab_params(1.0, min_dist)
+    out = np.zeros_like(y)
+    rc = _lib.load().fastembedr_cuda_umap_optimize_coo(
+        _ptr(h, ctypes.c_int), _ptr(t, ctypes.c_int), _ptr(w, ctypes.c_float), _ptr(e, ctypes.c_float),
+        _ptr(y, ctypes.c_float), y.shape[0], h.size, n_epochs, negative_sample_rate, learning_rate,
+        a, b, repulsion_strength, seed & 0xFFFFFFFF, optimizer_mode, _ptr(out, ctypes.c_float))
+    if rc != 0:
+        raise CudaBackendError("CUDA COO UMAP optimizer failed: " + _lib.last_error())
+    return out
+
+
+def umap_epochs(heads, tails, epochs_per_sample, layout, epoch_begin: int, epoch_end: int,
+                n_epochs: int, negative_sample_rate: int = 5, learning_rate: float = 1.0,
+                a: float = 1.5769434601962196, b: float = 0.8950608781227859,
+                repulsion_strength: float = 1.0, seed: int = 42, optimizer_mode: int = 1,
+                hash_key_is_tail: bool = False) -> Tuple[np.ndarray, int]:
+    """Runs epochs [epoch_begin, epoch_end) from ``layout``; returns (layout, positive samples)."""
+    h, t, e = _i32(heads), _i32(tails), _f32(epochs_per_sample)
+    y = _f32(layout).copy()
+    cnt = ctypes.c_longlong(0)
+    check(_lib.load().fe_b200_umap_epochs(
+        _ptr(h, ctypes.c_int), _ptr(t, ctypes.c_int), _ptr(e, ctypes.c_float), h.size,
+        _ptr(y, ctypes.c_float), y.shape[0], epoch_begin, epoch_end, n_epochs, negative_sample_rate,
+        learning_rate, a, b, repulsion_strength, seed & 0xFFFFFFFF, optimizer_mode,
+        int(hash_key_is_tail), ctypes.byref(cnt)), "fe_b200_umap_epochs")
+    return y, int(cnt.value)

@@ -1,0 +1,668 @@
+// extern "C" boundary of libfastembedr_b200.so (declared in include/fastembedr_b200.h).
+// The library is built with hidden visibility; only the declarations of the
+// public header are exported.
+#pragma GCC visibility push(default)
+#include "fastembedr_b200.h"
+#pragma GCC visibility pop
+#include "tsne.cuh"
+#include "umap.cuh"
+
+#include <cfloat>
+#include <cmath>
+#include <cstdlib>
+#include <cstring>
+#include <string>
+#include <vector>
+
+struct fe_b200_tsne {
+  fe::TsneSession* impl = nullptr;
+};
+
+namespace {
+
+using fe::set_error;
+
+const char* kOutOfScope = "not provided by the B200 backend (outside the optimizer hot path)";
+
+int out_of_scope(const char* name) {
+  set_error(std::string(name) + ": " + kOutOfScope);
+  return 1;
+}
+
+// Grid side: the reference CPU policy by default (the parity target);
+// FASTEMBEDR_B200_GRID_POLICY=cuda selects the reference CUDA sizes
+// (256 / 512 / 1024 by n, src/embedding_cuda_kernels.cpp:5496-5505).
+int resolve_grid(int n, int requested) {
+  if (requested > 0) {
+    int g = 4;
+    while (g < requested && g < 1024) g <<= 1;
+    return g;
+  }
+  const char* policy = std::getenv("FASTEMBEDR_B200_GRID_POLICY");
+  if (policy != nullptr && std::strcmp(policy, "cuda") == 0) {
+    int g = 512;
+    if (n < 20000) g = 256;
+    if (n >= 100000) g = 1024;
+    const int env = fe::env_int("FASTEMBEDR_TSNE_FFT_GRID", 0);
+    if (env == 128 || env == 256 || env == 512 || env == 1024) g = env;
+    return g;
+  }
+  return fe::default_grid_size(n);
+}
+
+struct DeviceCopy {
+  void* p = nullptr;
+  ~DeviceCopy() {
+    if (p) cudaFree(p);
+  }
+};
+
+int copy_to_device(const void* host, size_t bytes, DeviceCopy& dst, cudaStream_t stream, const char* what) {
+  FE_CUDA(cudaMalloc(&dst.p, bytes ? bytes : 1), what);
+  FE_CUDA(cudaMemcpyAsync(dst.p, host, bytes, cudaMemcpyHostToDevice, stream), what);
+  return 0;
+}
+
+// Shared by every openTSNE entry point (the reference's
+// fastembedr_cuda_opentsne_fft_from_knn_impl, src/embedding_cuda_kernels.cpp:5453-6008).
+int opentsne_impl(const int* indices, const void* distances, bool dist_double, const float* init,
+                  int has_init, int n, int k, int n_components, float perplexity,
+                  int early_exaggeration_iter, int n_iter, float early_exaggeration,
+                  float exaggeration, float learning_rate, int learning_rate_auto,
+                  float initial_momentum, float final_momentum, float min_gain,
+                  float max_step_norm, unsigned int seed, int index_offset, float* out,
+                  bool on_device) {
+  fe::clear_error();
+  if (indices == nullptr || distances == nullptr || out == nullptr || (has_init && init == nullptr)) {
+    set_error("null CUDA openTSNE input pointer");
+    return 1;
+  }
+  if (n < 2 || k < 1 || k > 256 || n_components != 2 || !(perplexity > 0.0f) ||
+      early_exaggeration_iter < 0 || n_iter < 0 || early_exaggeration_iter + n_iter < 1 ||
+      !(early_exaggeration > 0.0f) || !(exaggeration > 0.0f) ||
+      (!learning_rate_auto && !(learning_rate > 0.0f)) || initial_momentum < 0.0f ||
+      final_momentum < 0.0f || !(min_gain > 0.0f)) {
+    set_error("invalid CUDA openTSNE FFT-grid dimensions or parameters");
+    return 1;
+  }
+  cudaStream_t stream = nullptr;
+  FE_CUDA(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking), "cudaStreamCreate(openTSNE)");
+  struct StreamGuard {
+    cudaStream_t s;
+    ~StreamGuard() {
+      cudaStreamSynchronize(s);
+      cudaStreamDestroy(s);
+    }
+  } guard{stream};
+
+  const size_t items = static_cast<size_t>(n) * k;
+  int* row_ptr = nullptr;
+  int* col = nullptr;
+  float* val = nullptr;
+  long long nnz = 0, nnz_pad = 0;
+  {
+    DeviceCopy d_idx, d_dist;
+    const int* idx_dev = indices;
+    const void* dist_dev = distances;
+    if (!on_device) {
+      FE_TRY(copy_to_device(indices, items * sizeof(int), d_idx, stream, "H2D openTSNE indices"));
+      FE_TRY(copy_to_device(distances, items * (dist_double ? sizeof(double) : sizeof(float)), d_dist,
+                            stream, "H2D openTSNE distances"));
+      idx_dev = static_cast<const int*>(d_idx.p);
+      dist_dev = d_dist.p;
+    }
+    FE_TRY(fe::build_p_device(idx_dev, dist_dev, dist_double, n, k, index_offset, perplexity, stream,
+                              &row_ptr, &col, &val, &nnz, &nnz_pad));
+  }
+  fe::TsneSession* s = nullptr;
+  if (fe::session_create(&s, n, resolve_grid(n, 0), row_ptr, col, val, nnz, nnz_pad, stream)) {
+    cudaFree(row_ptr);
+    cudaFree(col);
+    cudaFree(val);
+    return 1;
+  }
+  struct SessionGuard {
+    fe::TsneSession* s;
+    ~SessionGuard() { fe::session_destroy(s); }
+  } sguard{s};
+  if (has_init) {
+    FE_TRY(fe::session_set_layout(s, init, true, true));
+  } else {
+    FE_TRY(fe::session_random_layout(s, seed));
+  }
+  // Learning rate per phase: n / exaggeration when automatic (src/tsne_neighbors.cpp:1734-1737).
+  const float lr_early = learning_rate_auto
+      ? static_cast<float>(static_cast<double>(n) / std::max(static_cast<double>(early_exaggeration), DBL_MIN))
+      : learning_rate;
+  const float lr_normal = learning_rate_auto
+      ? static_cast<float>(static_cast<double>(n) / std::max(static_cast<double>(exaggeration), DBL_MIN))
+      : learning_rate;
+  const float clip = std::isfinite(max_step_norm) ? max_step_norm : NAN;
+  FE_TRY(fe::session_iterate(s, early_exaggeration_iter, early_exaggeration, initial_momentum, lr_early,
+                             min_gain, clip));
+  FE_TRY(fe::session_iterate(s, n_iter, exaggeration, final_momentum, lr_normal, min_gain, clip));
+  FE_TRY(fe::session_get_layout(s, out, true));
+  return 0;
+}
+
+int umap_validate(const void* heads, const void* tails, const void* weights, const void* eps,
+                  const void* layout, int n, long long n_edges, int n_epochs, int nsr, float lr,
+                  float rep) {
+  if (heads == nullptr || tails == nullptr || weights == nullptr || eps == nullptr ||
+      layout == nullptr) {
+    set_error("null host pointer");
+    return 1;
+  }
+  if (n < 2 || n_edges < 1 || n_epochs < 1 || nsr < 0 || !(lr > 0.0f) || !(rep > 0.0f)) {
+    set_error("invalid CUDA COO UMAP optimization parameters");
+    return 1;
+  }
+  return 0;
+}
+
+int umap_hash_key_default() {
+  const char* v = std::getenv("FASTEMBEDR_B200_UMAP_NEGATIVE_KEY");
+  return (v != nullptr && std::strcmp(v, "tail") == 0) ? 1 : 0;
+}
+
+int umap_host_run(const int* heads, const int* tails, const float* eps, long long n_edges,
+                  const float* init, float* out, int n, int epoch_begin, int epoch_end, int n_epochs,
+                  int nsr, float lr, float a, float b, float rep, unsigned int seed, int mode,
+                  int hash_key_is_tail, long long* positive_samples) {
+  cudaStream_t stream = nullptr;
+  FE_CUDA(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking), "cudaStreamCreate(umap)");
+  struct StreamGuard {
+    cudaStream_t s;
+    ~StreamGuard() {
+      cudaStreamSynchronize(s);
+      cudaStreamDestroy(s);
+    }
+  } guard{stream};
+  fe::Arena arena;
+  int* d_heads = nullptr;
+  int* d_tails = nullptr;
+  float* d_eps = nullptr;
+  float2* d_layout = nullptr;
+  float2* d_delta = nullptr;
+  long long* d_count = nullptr;
+  const size_t e = static_cast<size_t>(n_edges);
+  for (int pass = 0; pass < 2; ++pass) {
+    if (pass == 0) arena.begin_plan();
+    else arena.rewind();
+    d_heads = arena.take<int>(e);
+    d_tails = arena.take<int>(e);
+    d_eps = arena.take<float>(e);
+    d_layout = arena.take<float2>(n);
+    d_delta = arena.take<float2>(mode == fe::kUmapDelta ? n : 0);
+    d_count = arena.take<long long>(1);
+    if (pass == 0) {
+      FE_TRY(fe::memory_preflight(arena.planned(), "CUDA COO UMAP optimizer allocation preflight"));
+      FE_TRY(arena.commit("COO UMAP workspace"));
+    }
+  }
+  FE_CUDA(cudaMemcpyAsync(d_heads, heads, e * sizeof(int), cudaMemcpyHostToDevice, stream), "H2D heads");
+  FE_CUDA(cudaMemcpyAsync(d_tails, tails, e * sizeof(int), cudaMemcpyHostToDevice, stream), "H2D tails");
+  FE_CUDA(cudaMemcpyAsync(d_eps, eps, e * sizeof(float), cudaMemcpyHostToDevice, stream), "H2D epochs_per_sample");
+  FE_CUDA(cudaMemcpyAsync(d_layout, init, sizeof(float2) * n, cudaMemcpyHostToDevice, stream), "H2D init");
+  FE_CUDA(cudaMemsetAsync(d_count, 0, sizeof(long long), stream), "memset count");
+  fe::UmapRun r;
+  r.params = fe::UmapParams{n, n_epochs, nsr, hash_key_is_tail, seed, lr, a, b, rep};
+  r.mode = mode;
+  r.heads = d_heads;
+  r.tails = d_tails;
+  r.periods = d_eps;
+  r.n_edges = n_edges;
+  r.layout = d_layout;
+  r.delta = mode == fe::kUmapDelta ? d_delta : nullptr;
+  r.positive_count = positive_samples != nullptr ? d_count : nullptr;
+  r.stream = stream;
+  r.edge_blocks = fe::umap_edge_blocks(n_edges);
+  r.use_graphs = fe::env_flag("FASTEMBEDR_CUDA_GRAPH_CAPTURE", true);
+  FE_TRY(fe::umap_run_epochs(&r, epoch_begin, epoch_end));
+  FE_CUDA(cudaMemcpyAsync(out, d_layout, sizeof(float2) * n, cudaMemcpyDeviceToHost, stream), "D2H layout");
+  if (positive_samples != nullptr) {
+    FE_CUDA(cudaMemcpyAsync(positive_samples, d_count, sizeof(long long), cudaMemcpyDeviceToHost, stream),
+            "D2H count");
+  }
+  FE_CUDA(cudaStreamSynchronize(stream), "cudaStreamSynchronize(umap)");
+  return 0;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* fe_b200_version(void) { return "fastembedr_b200 0.1.0 (sm_100a)"; }
+
+bool fastembedr_cuda_available(void) {
+  int count = 0;
+  if (cudaGetDeviceCount(&count) != cudaSuccess || count <= 0) {
+    cudaGetLastError();
+    return false;
+  }
+  int dev = 0, major = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  return major == 10;  // the library carries sm_100a code only
+}
+
+const char* fastembedr_cuda_embedding_last_error(void) { return fe::last_error(); }
+
+int fastembedr_cuda_opentsne_fft_from_knn(const int* indices, const double* distances,
+                                          const float* init, int has_init, int n, int k,
+                                          int n_components, float perplexity,
+                                          int early_exaggeration_iter, int n_iter,
+                                          float early_exaggeration, float exaggeration,
+                                          float learning_rate, int learning_rate_auto,
+                                          float initial_momentum, float final_momentum,
+                                          float min_gain, float max_step_norm, unsigned int seed,
+                                          int index_offset, float* out) {
+  return opentsne_impl(indices, distances, true, init, has_init, n, k, n_components, perplexity,
+                       early_exaggeration_iter, n_iter, early_exaggeration, exaggeration,
+                       learning_rate, learning_rate_auto, initial_momentum, final_momentum,
+                       min_gain, max_step_norm, seed, index_offset, out, false);
+}
+
+int fastembedr_cuda_opentsne_fft_from_knn_float(const int* indices, const float* distances,
+                                                const float* init, int has_init, int n, int k,
+                                                int n_components, float perplexity,
+                                                int early_exaggeration_iter, int n_iter,
+                                                float early_exaggeration, float exaggeration,
+                                                float learning_rate, int learning_rate_auto,
+                                                float initial_momentum, float final_momentum,
+                                                float min_gain, float max_step_norm,
+                                                unsigned int seed, int index_offset, float* out) {
+  return opentsne_impl(indices, distances, false, init, has_init, n, k, n_components, perplexity,
+                       early_exaggeration_iter, n_iter, early_exaggeration, exaggeration,
+                       learning_rate, learning_rate_auto, initial_momentum, final_momentum,
+                       min_gain, max_step_norm, seed, index_offset, out, false);
+}
+
+int fastembedr_cuda_opentsne_fft_from_device_knn_float(
+    const int* indices, const float* distances, const float* init, int has_init, int n, int k,
+    int n_components, float perplexity, int early_exaggeration_iter, int n_iter,
+    float early_exaggeration, float exaggeration, float learning_rate, int learning_rate_auto,
+    float initial_momentum, float final_momentum, float min_gain, float max_step_norm,
+    unsigned int seed, int index_offset, float* out) {
+  return opentsne_impl(indices, distances, false, init, has_init, n, k, n_components, perplexity,
+                       early_exaggeration_iter, n_iter, early_exaggeration, exaggeration,
+                       learning_rate, learning_rate_auto, initial_momentum, final_momentum,
+                       min_gain, max_step_norm, seed, index_offset, out, true);
+}
+
+int fastembedr_cuda_opentsne_fft_from_device_knn_float_pca_double(
+    const int*, const float*, const double*, int, int, int, int, float, int, int, float, float,
+    float, int, float, float, float, float, unsigned int, int, float*) {
+  set_error("CUDA device-resident PCA initialization requires RAPIDS RAFT/cuML TSVD support.");
+  return 1;
+}
+
+int fastembedr_cuda_opentsne_fft_from_device_knn_float_pca_float(
+    const int*, const float*, const float*, int, int, int, int, float, int, int, float, float,
+    float, int, float, float, float, float, unsigned int, int, float*) {
+  set_error("CUDA device-resident PCA initialization requires RAPIDS RAFT/cuML TSVD support.");
+  return 1;
+}
+
+int fastembedr_cuda_umap_optimize_coo(const int* heads, const int* tails, const float* weights,
+                                      const float* epochs_per_sample, const float* init, int n,
+                                      int n_edges_capacity, int n_epochs, int negative_sample_rate,
+                                      float learning_rate, float a, float b,
+                                      float repulsion_strength, unsigned int seed,
+                                      int optimizer_mode, float* out) {
+  fe::clear_error();
+  if (out == nullptr) {
+    set_error("null host pointer");
+    return 1;
+  }
+  FE_TRY(umap_validate(heads, tails, weights, epochs_per_sample, init, n, n_edges_capacity, n_epochs,
+                       negative_sample_rate, learning_rate, repulsion_strength));
+  const int mode = optimizer_mode == 1 ? fe::kUmapDelta : fe::kUmapInplace;
+  return umap_host_run(heads, tails, epochs_per_sample, n_edges_capacity, init, out, n, 0, n_epochs,
+                       n_epochs, negative_sample_rate, learning_rate, a, b, repulsion_strength, seed,
+                       mode, umap_hash_key_default(), nullptr);
+}
+
+int fe_b200_umap_epochs(const int* heads, const int* tails, const float* epochs_per_sample,
+                        long long n_edges, float* layout, int n, int epoch_begin, int epoch_end,
+                        int n_epochs, int negative_sample_rate, float learning_rate, float a,
+                        float b, float repulsion_strength, unsigned int seed, int optimizer_mode,
+                        int hash_key_is_tail, long long* positive_samples) {
+  fe::clear_error();
+  FE_TRY(umap_validate(heads, tails, epochs_per_sample, epochs_per_sample, layout, n, n_edges,
+                       n_epochs, negative_sample_rate, learning_rate, repulsion_strength));
+  if (epoch_begin < 0 || epoch_end < epoch_begin || epoch_end > n_epochs) {
+    set_error("invalid epoch range");
+    return 1;
+  }
+  const int mode = optimizer_mode == 1 ? fe::kUmapDelta : fe::kUmapInplace;
+  return umap_host_run(heads, tails, epochs_per_sample, n_edges, layout, layout, n, epoch_begin,
+                       epoch_end, n_epochs, negative_sample_rate, learning_rate, a, b,
+                       repulsion_strength, seed, mode, hash_key_is_tail, positive_samples);
+}
+
+// ---------------------------------------------------------------- t-SNE sessions
+
+int fe_b200_tsne_create(const int* indices, const float* distances, int n, int k, int index_offset,
+                        float perplexity, const float* init, unsigned int seed, int grid_size,
+                        int inputs_on_device, fe_b200_tsne** out) {
+  fe::clear_error();
+  if (out == nullptr || indices == nullptr || distances == nullptr) {
+    set_error("null CUDA openTSNE input pointer");
+    return 1;
+  }
+  *out = nullptr;
+  if (n < 2 || k < 1 || k > 256 || !(perplexity > 0.0f)) {
+    set_error("invalid CUDA openTSNE FFT-grid dimensions or parameters");
+    return 1;
+  }
+  cudaStream_t stream = nullptr;
+  FE_CUDA(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking), "cudaStreamCreate(session)");
+  int* row_ptr = nullptr;
+  int* col = nullptr;
+  float* val = nullptr;
+  long long nnz = 0, nnz_pad = 0;
+  int rc = 0;
+  {
+    DeviceCopy d_idx, d_dist;
+    const int* idx_dev = indices;
+    const float* dist_dev = distances;
+    const size_t items = static_cast<size_t>(n) * k;
+    if (!inputs_on_device) {
+      rc = copy_to_device(indices, items * sizeof(int), d_idx, stream, "H2D indices");
+      if (rc == 0) rc = copy_to_device(distances, items * sizeof(float), d_dist, stream, "H2D distances");
+      idx_dev = static_cast<const int*>(d_idx.p);
+      dist_dev = static_cast<const float*>(d_dist.p);
+    }
+    if (rc == 0) {
+      rc = fe::build_p_device(idx_dev, dist_dev, false, n, k, index_offset, perplexity, stream, &row_ptr,
+                              &col, &val, &nnz, &nnz_pad);
+    }
+  }
+  fe::TsneSession* s = nullptr;
+  if (rc == 0) rc = fe::session_create(&s, n, resolve_grid(n, grid_size), row_ptr, col, val, nnz, nnz_pad, nullptr);
+  if (rc != 0) {
+    if (s == nullptr) {
+      if (row_ptr) cudaFree(row_ptr);
+      if (col) cudaFree(col);
+      if (val) cudaFree(val);
+    }
+    cudaStreamDestroy(stream);
+    return 1;
+  }
+  cudaStreamSynchronize(stream);
+  cudaStreamDestroy(stream);
+  rc = init != nullptr ? fe::session_set_layout(s, init, !inputs_on_device, true)
+                       : fe::session_random_layout(s, seed);
+  if (rc != 0) {
+    fe::session_destroy(s);
+    return 1;
+  }
+  *out = new fe_b200_tsne{s};
+  return 0;
+}
+
+int fe_b200_tsne_create_csr(const int* row_ptr, const int* col, const float* val, int n,
+                            const float* init, int grid_size, fe_b200_tsne** out) {
+  fe::clear_error();
+  if (out == nullptr || row_ptr == nullptr || col == nullptr || val == nullptr || init == nullptr || n < 2) {
+    set_error("invalid CSR session arguments");
+    return 1;
+  }
+  *out = nullptr;
+  int* d_rp = nullptr;
+  int* d_col = nullptr;
+  float* d_val = nullptr;
+  long long nnz = 0, nnz_pad = 0;
+  FE_TRY(fe::upload_csr_padded(row_ptr, col, val, n, nullptr, &d_rp, &d_col, &d_val, &nnz, &nnz_pad));
+  fe::TsneSession* s = nullptr;
+  if (fe::session_create(&s, n, resolve_grid(n, grid_size), d_rp, d_col, d_val, nnz, nnz_pad, nullptr)) {
+    cudaFree(d_rp);
+    cudaFree(d_col);
+    cudaFree(d_val);
+    return 1;
+  }
+  if (fe::session_set_layout(s, init, true, true)) {
+    fe::session_destroy(s);
+    return 1;
+  }
+  *out = new fe_b200_tsne{s};
+  return 0;
+}
+
+int fe_b200_tsne_iterate(fe_b200_tsne* h, int n_iter, float exaggeration, float momentum,
+                         float learning_rate, float min_gain, float max_step_norm) {
+  fe::clear_error();
+  if (h == nullptr || n_iter < 0) {
+    set_error("invalid t-SNE session call");
+    return 1;
+  }
+  return fe::session_iterate(h->impl, n_iter, exaggeration, momentum, learning_rate, min_gain, max_step_norm);
+}
+
+int fe_b200_tsne_gradient(fe_b200_tsne* h, float exaggeration, float* grad, double* z) {
+  fe::clear_error();
+  if (h == nullptr || grad == nullptr) {
+    set_error("invalid t-SNE session call");
+    return 1;
+  }
+  // The gradient is evaluated at the stored layout exactly as given (no re-centring).
+  fe::TsneSession* s = h->impl;
+  FE_TRY(fe::launch_stats(s, 0));
+  FE_TRY(fe::session_gradient(s, exaggeration, grad, z));
+  return fe::launch_stats(s, 1);
+}
+
+int fe_b200_tsne_get_layout(fe_b200_tsne* h, float* out, int on_device) {
+  fe::clear_error();
+  if (h == nullptr || out == nullptr) {
+    set_error("invalid t-SNE session call");
+    return 1;
+  }
+  return fe::session_get_layout(h->impl, out, on_device == 0);
+}
+
+int fe_b200_tsne_set_layout(fe_b200_tsne* h, const float* y, int on_device, int reset_state) {
+  fe::clear_error();
+  if (h == nullptr || y == nullptr) {
+    set_error("invalid t-SNE session call");
+    return 1;
+  }
+  fe::TsneSession* s = h->impl;
+  FE_TRY(fe::session_set_layout(s, y, on_device == 0, true));
+  if (reset_state) {
+    std::vector<float> ones(static_cast<size_t>(s->n) * 2, 1.0f);
+    FE_CUDA(cudaMemsetAsync(s->update, 0, sizeof(float2) * s->n, s->stream), "memset update");
+    FE_CUDA(cudaMemcpyAsync(s->gains, ones.data(), sizeof(float2) * s->n, cudaMemcpyHostToDevice, s->stream),
+            "reset gains");
+    FE_CUDA(cudaStreamSynchronize(s->stream), "cudaStreamSynchronize(reset)");
+  }
+  return 0;
+}
+
+int fe_b200_tsne_get_state(fe_b200_tsne* h, float* update, float* gains) {
+  fe::clear_error();
+  if (h == nullptr || update == nullptr || gains == nullptr) {
+    set_error("invalid t-SNE session call");
+    return 1;
+  }
+  fe::TsneSession* s = h->impl;
+  FE_CUDA(cudaMemcpyAsync(update, s->update, sizeof(float2) * s->n, cudaMemcpyDeviceToHost, s->stream), "D2H update");
+  FE_CUDA(cudaMemcpyAsync(gains, s->gains, sizeof(float2) * s->n, cudaMemcpyDeviceToHost, s->stream), "D2H gains");
+  FE_CUDA(cudaStreamSynchronize(s->stream), "cudaStreamSynchronize(state)");
+  return 0;
+}
+
+int fe_b200_tsne_set_state(fe_b200_tsne* h, const float* update, const float* gains) {
+  fe::clear_error();
+  if (h == nullptr || update == nullptr || gains == nullptr) {
+    set_error("invalid t-SNE session call");
+    return 1;
+  }
+  fe::TsneSession* s = h->impl;
+  FE_CUDA(cudaMemcpyAsync(s->update, update, sizeof(float2) * s->n, cudaMemcpyHostToDevice, s->stream), "H2D update");
+  FE_CUDA(cudaMemcpyAsync(s->gains, gains, sizeof(float2) * s->n, cudaMemcpyHostToDevice, s->stream), "H2D gains");
+  FE_CUDA(cudaStreamSynchronize(s->stream), "cudaStreamSynchronize(state)");
+  return 0;
+}
+
+int fe_b200_tsne_info(fe_b200_tsne* h, int* n, int* grid, long long* nnz, long long* nnz_padded) {
+  if (h == nullptr) {
+    set_error("invalid t-SNE session call");
+    return 1;
+  }
+  if (n) *n = h->impl->n;
+  if (grid) *grid = h->impl->grid;
+  if (nnz) *nnz = h->impl->nnz;
+  if (nnz_padded) *nnz_padded = h->impl->nnz_pad;
+  return 0;
+}
+
+int fe_b200_tsne_get_p(fe_b200_tsne* h, int* row_ptr, int* col, float* val) {
+  fe::clear_error();
+  if (h == nullptr || row_ptr == nullptr || col == nullptr || val == nullptr) {
+    set_error("invalid t-SNE session call");
+    return 1;
+  }
+  fe::TsneSession* s = h->impl;
+  std::vector<int> rp(static_cast<size_t>(s->n) + 1);
+  std::vector<int> c(static_cast<size_t>(s->nnz_pad));
+  std::vector<float> v(static_cast<size_t>(s->nnz_pad));
+  FE_CUDA(cudaMemcpyAsync(rp.data(), s->row_ptr, sizeof(int) * rp.size(), cudaMemcpyDeviceToHost, s->stream), "D2H");
+  FE_CUDA(cudaMemcpyAsync(c.data(), s->col, sizeof(int) * c.size(), cudaMemcpyDeviceToHost, s->stream), "D2H");
+  FE_CUDA(cudaMemcpyAsync(v.data(), s->val, sizeof(float) * v.size(), cudaMemcpyDeviceToHost, s->stream), "D2H");
+  FE_CUDA(cudaStreamSynchronize(s->stream), "cudaStreamSynchronize(get_p)");
+  // Strip the (col = row, val = 0) padding entries at the end of each row.
+  long long w = 0;
+  row_ptr[0] = 0;
+  for (int r = 0; r < s->n; ++r) {
+    int end = rp[r + 1];
+    while (end > rp[r] && c[end - 1] == r && v[end - 1] == 0.0f) --end;
+    for (int t = rp[r]; t < end; ++t) {
+      col[w] = c[t];
+      val[w] = v[t];
+      ++w;
+    }
+    row_ptr[r + 1] = static_cast<int>(w);
+  }
+  return 0;
+}
+
+void* fe_b200_tsne_stream(fe_b200_tsne* h) { return h == nullptr ? nullptr : h->impl->stream; }
+
+int fe_b200_tsne_profile(fe_b200_tsne* h, int enable) {
+  if (h == nullptr) return 1;
+  h->impl->profile = enable != 0;
+  for (int k = 0; k < 8; ++k) {
+    h->impl->kernel_ms[k] = 0.0;
+    h->impl->kernel_launches[k] = 0;
+  }
+  return 0;
+}
+
+int fe_b200_tsne_kernel_times(fe_b200_tsne* h, double* ms, long long* launches, int kinds) {
+  if (h == nullptr) return 1;
+  for (int k = 0; k < kinds && k < fe::kKindCount; ++k) {
+    if (ms) ms[k] = h->impl->kernel_ms[k];
+    if (launches) launches[k] = h->impl->kernel_launches[k];
+  }
+  return 0;
+}
+
+const char* fe_b200_tsne_kernel_name(int kind) { return fe::kernel_kind_name(kind); }
+
+void fe_b200_tsne_destroy(fe_b200_tsne* h) {
+  if (h == nullptr) return;
+  fe::session_destroy(h->impl);
+  delete h;
+}
+
+// ---------------------------------------------------------------- UMAP from KNN (device graph)
+
+int fastembedr_cuda_umap_from_knn_spectral(const int*, const double*, int, int, int, int, float,
+                                           float, float, float, int, unsigned int, int, int, float*) {
+  return out_of_scope("fastembedr_cuda_umap_from_knn_spectral");
+}
+int fastembedr_cuda_umap_from_knn_spectral_float(const int*, const float*, int, int, int, int,
+                                                 float, float, float, float, int, unsigned int,
+                                                 int, int, float*) {
+  return out_of_scope("fastembedr_cuda_umap_from_knn_spectral_float");
+}
+int fastembedr_cuda_umap_from_device_knn_spectral_float(const int*, const float*, int, int, int,
+                                                        int, float, float, float, float, int,
+                                                        unsigned int, int, int, int, float*) {
+  return out_of_scope("fastembedr_cuda_umap_from_device_knn_spectral_float");
+}
+int fastembedr_cuda_umap_graph_dump_from_knn(const int*, const double*, int, int, int, int*, int*,
+                                             float*, float*, int*, int*) {
+  return out_of_scope("fastembedr_cuda_umap_graph_dump_from_knn");
+}
+
+// ---------------------------------------------------------------- out-of-scope symbols
+
+int fastembedr_cuda_embed(const int*, const float*, const float*, int, int, int, int, int, float,
+                          float, float, float, unsigned int, float*) {
+  return out_of_scope("fastembedr_cuda_embed");
+}
+int fastembedr_cuda_embed_from_knn(const int*, const double*, const float*, int, int, int, int, int,
+                                   float, float, float, unsigned int, int, float*) {
+  return out_of_scope("fastembedr_cuda_embed_from_knn");
+}
+int fastembedr_cuda_spectral_init_from_knn(const int*, const double*, int, int, int, unsigned int,
+                                           int, float*) {
+  return out_of_scope("fastembedr_cuda_spectral_init_from_knn");
+}
+int fastembedr_cuda_exact_tsne_from_knn(const int*, const double*, const float*, int, int, int,
+                                        float, float, int, int, float, float, float, unsigned int,
+                                        int, float*) {
+  return out_of_scope("fastembedr_cuda_exact_tsne_from_knn");
+}
+int fastembedr_cuda_landmark_tsne_from_device_knn(const int*, const float*, int, const float*,
+                                                  const float*, const float*, int, int, int, int,
+                                                  float, int, int, float, float, float, float, float,
+                                                  float, float, int, int, unsigned int, int, float,
+                                                  float, float*) {
+  return out_of_scope("fastembedr_cuda_landmark_tsne_from_device_knn");
+}
+int fastembedr_cuda_landmark_umap_from_device_knn(const int*, const float*, int, const float*,
+                                                  const float*, const float*, const int*, const int*,
+                                                  int, int, int, int, int, int, int, float, float,
+                                                  float, float, unsigned int, int, float, float,
+                                                  float*) {
+  return out_of_scope("fastembedr_cuda_landmark_umap_from_device_knn");
+}
+int fastembedr_cuda_standardize_matrix(const double*, int, int, double*, double*, double*) {
+  return out_of_scope("fastembedr_cuda_standardize_matrix");
+}
+int fastembedr_cuda_project_embedding(const double*, const int*, const double*, int, int, int, int,
+                                      double*) {
+  return out_of_scope("fastembedr_cuda_project_embedding");
+}
+int fastembedr_cuda_interpolate_landmark_layout(const double*, const int*, const int*, const double*,
+                                                int, int, int, int, double*) {
+  return out_of_scope("fastembedr_cuda_interpolate_landmark_layout");
+}
+int fastembedr_cuda_landmark_project_interpolate_knn_confidence(const double*, const double*,
+                                                                const double*, const int*, int, int,
+                                                                int, int, int, double*, int*,
+                                                                double*, double*) {
+  return out_of_scope("fastembedr_cuda_landmark_project_interpolate_knn_confidence");
+}
+int fastembedr_cuda_knn_structure_score(const double*, const int*, const int*, const int*, int, int,
+                                        int, int, int, int, int, double*) {
+  return out_of_scope("fastembedr_cuda_knn_structure_score");
+}
+int fastembedr_cuda_silhouette_score(const double*, const int*, const int*, int, int, double*) {
+  return out_of_scope("fastembedr_cuda_silhouette_score");
+}
+int fastembedr_cuda_matrix_multiply(const double*, const double*, int, int, int, int, double*) {
+  return out_of_scope("fastembedr_cuda_matrix_multiply");
+}
+int fastembedr_cuda_raft_tsvd_pca_init(const double*, int, int, int, float*) {
+  return out_of_scope("fastembedr_cuda_raft_tsvd_pca_init");
+}
+
+}  // extern "C"

@@ -1,0 +1,138 @@
+// Shared host/device plumbing for the B200 embedding-optimizer backend.
+//
+// Error convention (mirrors the reference C ABI, src/embedding_cuda_kernels.cpp:55-72):
+// every entry point returns 0 on success and 1 on failure, leaving a
+// thread-local message readable through fastembedr_cuda_embedding_last_error().
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstddef>
+#include <cstdint>
+#include <string>
+
+namespace fe {
+
+// ---------------------------------------------------------------- errors
+
+void set_error(const std::string& message);
+const char* last_error();
+void clear_error();
+
+inline int check_cuda(cudaError_t code, const char* where) {
+  if (code == cudaSuccess) return 0;
+  set_error(std::string(where) + ": " + cudaGetErrorString(code));
+  return 1;
+}
+
+#define FE_TRY(expr)          \
+  do {                        \
+    if ((expr) != 0) return 1; \
+  } while (0)
+
+#define FE_CUDA(call, where) FE_TRY(::fe::check_cuda((call), (where)))
+#define FE_LAUNCH(where) FE_TRY(::fe::check_cuda(cudaGetLastError(), (where)))
+
+// ---------------------------------------------------------------- memory
+
+constexpr std::size_t kAlign = 256;
+
+inline std::size_t align_up(std::size_t bytes, std::size_t a = kAlign) {
+  return (bytes + a - 1) & ~(a - 1);
+}
+
+// One device allocation carved into aligned sub-buffers.  Sizing is done by a
+// first "plan" pass (base == nullptr) that only accumulates offsets.
+class Arena {
+ public:
+  Arena() = default;
+  ~Arena() { release(); }
+  Arena(const Arena&) = delete;
+  Arena& operator=(const Arena&) = delete;
+
+  void begin_plan() {
+    planning_ = true;
+    offset_ = 0;
+  }
+  template <typename T>
+  T* take(std::size_t count) {
+    const std::size_t bytes = align_up(count * sizeof(T) + (count == 0 ? 1 : 0));
+    T* p = planning_ ? nullptr : reinterpret_cast<T*>(static_cast<char*>(base_) + offset_);
+    offset_ += bytes;
+    return p;
+  }
+  // Allocates the planned size; returns 0 on success.
+  int commit(const char* what);
+  // Adopts caller-owned device memory of at least planned() bytes (no allocation).
+  void adopt(void* base) {
+    base_ = base;
+    owned_ = false;
+    planning_ = false;
+    size_ = offset_;
+    offset_ = 0;
+  }
+  void rewind() { offset_ = 0; }
+  std::size_t planned() const { return offset_; }
+  std::size_t size() const { return size_; }
+  void release();
+
+ private:
+  void* base_ = nullptr;
+  bool owned_ = false;
+  bool planning_ = false;
+  std::size_t offset_ = 0;
+  std::size_t size_ = 0;
+};
+
+// Fails cleanly when a request exceeds 95% of free device memory
+// (the reference's preflight, src/embedding_cuda_kernels.cpp:224-241).
+int memory_preflight(std::size_t bytes, const char* where);
+
+// ---------------------------------------------------------------- launch shape
+
+// SM count of the current device (cached per device).
+int sm_count();
+
+// Environment helpers.
+int env_int(const char* name, int fallback);
+bool env_flag(const char* name, bool fallback);
+
+}  // namespace fe
+
+// ---------------------------------------------------------------- device helpers
+
+#ifdef __CUDACC__
+
+namespace fe {
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+__device__ __forceinline__ double warp_sum(double v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+__device__ __forceinline__ float warp_min(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fminf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// Streaming (evict-first) 16-byte loads for data read once per pass.
+__device__ __forceinline__ int4 ld_stream(const int4* p) { return __ldcs(p); }
+__device__ __forceinline__ float4 ld_stream(const float4* p) { return __ldcs(p); }
+
+}  // namespace fe
+
+#endif

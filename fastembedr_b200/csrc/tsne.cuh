@@ -1,0 +1,194 @@
+// openTSNE-style FFT-grid t-SNE optimizer for B200: data layout and kernels.
+//
+// Layout in HBM (one session = one embedding run):
+//   P        symmetric CSR (row_ptr int32[n+1], col int32[nnz_pad], val f32[nnz_pad]);
+//            every row is padded to a multiple of 4 entries with (col=row,
+//            val=0) so the attraction kernel streams 16-byte vectors.
+//   y[2]     float2[n] double-buffered layout (the gradient of iteration t
+//            reads y[cur] while the fused update writes y[cur^1]).
+//   update, gains  float2[n]
+//   charges  float4[G*G]   bilinear charges {1, x, y, 0} per grid node
+//   rowspec  float2[G][G+1][3]  x-half-spectra of the three charge planes
+//   krow     float2[G][G+1]     x-transforms of the q and q^2 kernel rows
+//   colspec  float2[G][G+1][4]  y-inverted products (q2, xq2, yq2, q)
+//   pot      float4[G*G]   potentials {phi_q2, phi_xq2, phi_yq2, phi_q}
+//   stats    LayoutStats   bounds/sums of the layout and the normaliser Z
+//
+// Per iteration: splat -> fft_rows_fwd -> fft_cols -> fft_rows_inv -> gradient+update.
+#pragma once
+
+#include "fe_common.cuh"
+
+#include <cuda_runtime.h>
+
+#include <vector>
+
+namespace fe {
+
+// Layout statistics carried between kernels (device resident).
+struct LayoutStats {
+  double sum_x, sum_y;        // sums of the raw (uncentred) layout
+  float min_x, max_x;         // bounds of the raw layout
+  float min_y, max_y;
+  int center;                 // 1: subtract the mean before use (iterations)
+  int pad0;
+  double z;                   // sum_i interp(phi_q)(y_i) - n
+  float inv_z;                // 1 / max(z, FLT_MIN)
+  unsigned int update_counter;  // last-block tickets
+  unsigned int fft_counter;
+  unsigned int stats_counter;
+};
+
+struct GridGeom {
+  float mean_x, mean_y;
+  float lower_x, lower_y;
+  float spacing, inv_spacing;
+};
+
+#ifdef __CUDACC__
+// Grid geometry of compute_gradient_fft_grid_f (src/tsne_neighbors.cpp:1084-1106),
+// evaluated on the centred layout.  Rounding is monotonic, so the bounds of the
+// centred layout equal the raw bounds minus the float mean, exactly.
+__device__ __forceinline__ GridGeom grid_geometry(const LayoutStats& s, int n, int g) {
+  GridGeom q;
+  if (s.center) {
+    q.mean_x = static_cast<float>(s.sum_x / static_cast<double>(n));
+    q.mean_y = static_cast<float>(s.sum_y / static_cast<double>(n));
+  } else {
+    q.mean_x = 0.0f;
+    q.mean_y = 0.0f;
+  }
+  const float min_x = s.min_x - q.mean_x, max_x = s.max_x - q.mean_x;
+  const float min_y = s.min_y - q.mean_y, max_y = s.max_y - q.mean_y;
+  const float cx = 0.5f * (min_x + max_x);
+  const float cy = 0.5f * (min_y + max_y);
+  float span = fmaxf(max_x - min_x, max_y - min_y);
+  if (!isfinite(span) || span <= 0.0f) span = 1.0f;
+  const float half = 0.55f * span + 1.0e-3f;
+  q.lower_x = cx - half;
+  q.lower_y = cy - half;
+  q.spacing = (2.0f * half) / static_cast<float>(g - 1);
+  q.inv_spacing = 1.0f / q.spacing;
+  return q;
+}
+
+// Clamped grid coordinates, cell origin and bilinear fractions of a point
+// (src/tsne_neighbors.cpp:1114-1128 and 760-775 use the same expressions).
+struct Cell {
+  int x0, y0;
+  float tx, ty;
+};
+__device__ __forceinline__ Cell grid_cell(float px, float py, const GridGeom& q, int g) {
+  const float raw_x = (px - q.lower_x) * q.inv_spacing;
+  const float raw_y = (py - q.lower_y) * q.inv_spacing;
+  const float gmax = static_cast<float>(g - 1);
+  const float cx = fmaxf(0.0f, fminf(gmax, raw_x));
+  const float cy = fmaxf(0.0f, fminf(gmax, raw_y));
+  Cell c;
+  c.x0 = max(0, min(g - 2, static_cast<int>(floorf(cx))));
+  c.y0 = max(0, min(g - 2, static_cast<int>(floorf(cy))));
+  c.tx = cx - static_cast<float>(c.x0);
+  c.ty = cy - static_cast<float>(c.y0);
+  return c;
+}
+#endif
+
+// Exactly one of these modes is run by the fused gradient kernel.
+enum GradMode { kGradUpdate = 0, kGradOnly = 1 };
+
+struct TsneSession {
+  int device = 0;
+  int n = 0;
+  int grid = 0;       // G
+  int fft = 0;        // M = 2G
+  int log_fft = 0;
+  long long nnz = 0;      // symmetric entries (both directions)
+  long long nnz_pad = 0;  // after 4-entry row padding
+  cudaStream_t stream = nullptr;
+  bool own_stream = false;
+  Arena arena;
+
+  int* row_ptr = nullptr;
+  int* col = nullptr;
+  float* val = nullptr;
+  float2* y[2] = {nullptr, nullptr};
+  int cur = 0;
+  float2* update = nullptr;
+  float2* gains = nullptr;
+  float2* grad_out = nullptr;  // kGradOnly target
+  LayoutStats* stats = nullptr;
+  double* update_partials = nullptr;  // 6 per block
+  double* z_partials = nullptr;       // one per grid row
+  float4* charges = nullptr;
+  float2* rowspec = nullptr;
+  float2* krow = nullptr;
+  float2* colspec = nullptr;
+  float4* pot = nullptr;
+  float2* twiddle = nullptr;  // exp(-2 pi i k / M), k < M/2
+
+  int update_blocks = 0;
+  int update_threads = 256;
+  int cols_per_block = 1;
+
+  // Optional per-kernel CUDA-event timing (bench / profiling).
+  bool profile = false;
+  std::vector<cudaEvent_t> events;
+  std::vector<int> event_kind;
+  double kernel_ms[8] = {0};
+  long long kernel_launches[8] = {0};
+  long long iterations_run = 0;
+
+  // CUDA graph of one iteration chunk (captured lazily per parameter set).
+  cudaGraphExec_t graph = nullptr;
+  int graph_iters = 0;
+  int graph_cur = 0;
+  float graph_params[5] = {0};
+  bool use_graphs = true;
+};
+
+enum KernelKind {
+  kKindSplat = 0,
+  kKindFftRows = 1,
+  kKindFftCols = 2,
+  kKindFftRowsInv = 3,
+  kKindGradUpdate = 4,
+  kKindCount = 5
+};
+const char* kernel_kind_name(int kind);
+
+// ---- P construction (tsne_affinity.cu) ----
+// Builds the padded symmetric CSR on the device from column-major KNN.
+// dist_is_double selects the element type of `dist`.  Temporaries are freed
+// before returning; the CSR arrays are allocated with cudaMalloc into *out_*.
+int build_p_device(const int* d_idx, const void* d_dist, bool dist_is_double, int n, int k,
+                   int index_offset, float perplexity, cudaStream_t stream, int** out_row_ptr,
+                   int** out_col, float** out_val, long long* out_nnz, long long* out_nnz_pad);
+
+// Pads and uploads a host CSR (parity hooks).
+int upload_csr_padded(const int* row_ptr, const int* col, const float* val, int n,
+                      cudaStream_t stream, int** out_row_ptr, int** out_col, float** out_val,
+                      long long* out_nnz, long long* out_nnz_pad);
+
+// ---- session (tsne_session.cu) ----
+int session_create(TsneSession** out, int n, int grid, int* d_row_ptr, int* d_col, float* d_val,
+                   long long nnz, long long nnz_pad, cudaStream_t stream);
+void session_destroy(TsneSession* s);
+int session_set_layout(TsneSession* s, const float* y, bool host, bool center);
+int session_random_layout(TsneSession* s, unsigned int seed);
+int session_iterate(TsneSession* s, int iters, float exaggeration, float momentum,
+                    float learning_rate, float min_gain, float max_step_norm);
+int session_gradient(TsneSession* s, float exaggeration, float* grad_host, double* z_out);
+int session_get_layout(TsneSession* s, float* out, bool host);
+
+// ---- kernels (tsne_kernels.cu) ----
+// Raises per-kernel dynamic shared-memory limits for this session's FFT size.
+int configure_kernels(TsneSession* s);
+int launch_stats(TsneSession* s, int center);
+int launch_iteration(TsneSession* s, GradMode mode, float exaggeration, float momentum,
+                     float learning_rate, float min_gain, float max_step_norm);
+int launch_center_output(TsneSession* s, float2* out);
+
+// CPU grid-size policy (tsne_fft_grid_size, src/tsne_neighbors.cpp:392-398).
+int default_grid_size(int n);
+
+}  // namespace fe

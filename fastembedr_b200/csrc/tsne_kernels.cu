@@ -1,0 +1,687 @@
+// Per-iteration kernels of the openTSNE FFT-grid optimizer.
+//
+// Algorithm (restating compute_gradient_fft_grid_f, src/tsne_neighbors.cpp:1076-1182,
+// and apply_open_tsne_update_f / zero_mean_f, :1196-1245):
+//   grad_i,d = -(y_i,d * phi_q2(y_i) - phi_dq2(y_i)) / Z + ex * sum_j P_ij q_ij (y_i,d - y_j,d)
+// where phi_* are the bilinear charges {1, x, y} on a GxG grid convolved
+// (linearly, zero-padded to 2G) with q = 1/(1+d^2) and q^2, and
+// Z = sum_i interp(phi_q)(y_i) - n.  Because spread and gather use the same
+// bilinear weights, Z = sum_nodes charge_1(node) * phi_q(node) - n, which the
+// inverse FFT pass reduces directly.
+//
+// Kernels (all on the session stream):
+//   splat_kernel           centres the layout in place and spreads {1,x,y}
+//                          with 16-byte vector atomics (red.global.add.v4.f32)
+//   fft_rows_fwd_kernel    x-direction real FFTs of the charge rows and of the
+//                          kernel rows (the kernels are even, so their
+//                          transforms are real)
+//   fft_cols_kernel        y-direction FFT, multiply by the real kernel
+//                          spectra, inverse y-FFT -- one column tile per block
+//   fft_rows_inv_kernel    inverse x-FFTs -> potentials, Z, and clears charges
+//   grad_update_kernel     CSR attraction (warp per row, 16-byte streaming
+//                          loads), repulsive gather, gains/momentum/step clip,
+//                          layout write and layout statistics for the next
+//                          iteration (last-block reduction, no second launch)
+#include "tsne.cuh"
+
+#include <cfloat>
+
+namespace fe {
+namespace {
+
+__device__ __forceinline__ float2 cmul(float2 a, float2 b) {
+  return make_float2(a.x * b.x - a.y * b.y, a.x * b.y + a.y * b.x);
+}
+__device__ __forceinline__ float2 cadd(float2 a, float2 b) { return make_float2(a.x + b.x, a.y + b.y); }
+__device__ __forceinline__ float2 csub(float2 a, float2 b) { return make_float2(a.x - b.x, a.y - b.y); }
+__device__ __forceinline__ float2 conjf2(float2 a) { return make_float2(a.x, -a.y); }
+__device__ __forceinline__ float2 cscale(float2 a, float s) { return make_float2(a.x * s, a.y * s); }
+
+// In-place radix-2 decimation-in-time FFT of `count` length-M sequences laid
+// out back to back in shared memory.  tw[k] = exp(-2 pi i k / M), k < M/2.
+// The inverse is unnormalised.
+__device__ void block_fft(float2* buf, int count, int m, int log_m, const float2* __restrict__ tw,
+                          bool inverse) {
+  const int total = count * m;
+  for (int t = threadIdx.x; t < total; t += blockDim.x) {
+    const int s = t >> log_m;
+    const int i = t & (m - 1);
+    const int j = static_cast<int>(__brev(static_cast<unsigned>(i)) >> (32 - log_m));
+    if (i < j) {
+      float2* base = buf + (s << log_m);
+      const float2 a = base[i];
+      base[i] = base[j];
+      base[j] = a;
+    }
+  }
+  __syncthreads();
+  const int half_total = count * (m >> 1);
+  for (int stage = 1; stage <= log_m; ++stage) {
+    const int half = 1 << (stage - 1);
+    const int tw_shift = log_m - stage;  // twiddle index = j * (M / len)
+    for (int t = threadIdx.x; t < half_total; t += blockDim.x) {
+      const int s = t >> (log_m - 1);
+      const int b = t & ((m >> 1) - 1);
+      const int grp = b >> (stage - 1);
+      const int j = b & (half - 1);
+      float2* base = buf + (s << log_m);
+      const int u = (grp << stage) + j;
+      const int v = u + half;
+      float2 w = __ldg(tw + (j << tw_shift));
+      if (inverse) w.y = -w.y;
+      const float2 x = cmul(base[v], w);
+      const float2 a = base[u];
+      base[v] = csub(a, x);
+      base[u] = cadd(a, x);
+    }
+    __syncthreads();
+  }
+}
+
+// Kernel value at integer offsets (dx, dy), formed in float exactly as
+// src/tsne_neighbors.cpp:912-920 forms it.
+__device__ __forceinline__ void kernel_values(int dx, int dy, float spacing, float* q, float* q2) {
+  const float x_off = static_cast<float>(dx) * spacing;
+  const float y_off = static_cast<float>(dy) * spacing;
+  const float d2 = x_off * x_off + y_off * y_off;
+  const float qq = 1.0f / (1.0f + d2);
+  *q = qq;
+  *q2 = qq * qq;
+}
+
+// ------------------------------------------------------------------ stats
+
+struct StatsAcc {
+  double sx, sy;
+  float mnx, mxx, mny, mxy;
+};
+
+__device__ __forceinline__ void stats_init(StatsAcc& a) {
+  a.sx = 0.0;
+  a.sy = 0.0;
+  a.mnx = FLT_MAX;
+  a.mxx = -FLT_MAX;
+  a.mny = FLT_MAX;
+  a.mxy = -FLT_MAX;
+}
+
+__device__ __forceinline__ void stats_add(StatsAcc& a, float2 p) {
+  a.sx += static_cast<double>(p.x);
+  a.sy += static_cast<double>(p.y);
+  a.mnx = fminf(a.mnx, p.x);
+  a.mxx = fmaxf(a.mxx, p.x);
+  a.mny = fminf(a.mny, p.y);
+  a.mxy = fmaxf(a.mxy, p.y);
+}
+
+// Block-reduces `a`, writes the block partial, and lets the last block to
+// finish fold all partials into *stats.  No block waits on another.
+__device__ void stats_block_finish(StatsAcc a, double* __restrict__ partials,
+                                   LayoutStats* __restrict__ stats, unsigned int* counter,
+                                   int center) {
+  __shared__ double s_d[2][32];
+  __shared__ float s_f[4][32];
+  __shared__ bool s_last;
+  a.sx = warp_sum(a.sx);
+  a.sy = warp_sum(a.sy);
+  a.mnx = warp_min(a.mnx);
+  a.mxx = warp_max(a.mxx);
+  a.mny = warp_min(a.mny);
+  a.mxy = warp_max(a.mxy);
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  if (lane == 0) {
+    s_d[0][wid] = a.sx;
+    s_d[1][wid] = a.sy;
+    s_f[0][wid] = a.mnx;
+    s_f[1][wid] = a.mxx;
+    s_f[2][wid] = a.mny;
+    s_f[3][wid] = a.mxy;
+  }
+  __syncthreads();
+  if (wid == 0) {
+    double sx = lane < nw ? s_d[0][lane] : 0.0;
+    double sy = lane < nw ? s_d[1][lane] : 0.0;
+    float mnx = lane < nw ? s_f[0][lane] : FLT_MAX;
+    float mxx = lane < nw ? s_f[1][lane] : -FLT_MAX;
+    float mny = lane < nw ? s_f[2][lane] : FLT_MAX;
+    float mxy = lane < nw ? s_f[3][lane] : -FLT_MAX;
+    sx = warp_sum(sx);
+    sy = warp_sum(sy);
+    mnx = warp_min(mnx);
+    mxx = warp_max(mxx);
+    mny = warp_min(mny);
+    mxy = warp_max(mxy);
+    if (lane == 0) {
+      double* p = partials + 6 * blockIdx.x;
+      p[0] = sx;
+      p[1] = sy;
+      p[2] = mnx;
+      p[3] = mxx;
+      p[4] = mny;
+      p[5] = mxy;
+      __threadfence();
+      const unsigned int ticket = atomicAdd(counter, 1u);
+      s_last = ticket == gridDim.x - 1;
+    }
+  }
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  StatsAcc t;
+  stats_init(t);
+  for (int b = threadIdx.x; b < static_cast<int>(gridDim.x); b += blockDim.x) {
+    const volatile double* p = partials + 6 * b;
+    t.sx += p[0];
+    t.sy += p[1];
+    t.mnx = fminf(t.mnx, static_cast<float>(p[2]));
+    t.mxx = fmaxf(t.mxx, static_cast<float>(p[3]));
+    t.mny = fminf(t.mny, static_cast<float>(p[4]));
+    t.mxy = fmaxf(t.mxy, static_cast<float>(p[5]));
+  }
+  t.sx = warp_sum(t.sx);
+  t.sy = warp_sum(t.sy);
+  t.mnx = warp_min(t.mnx);
+  t.mxx = warp_max(t.mxx);
+  t.mny = warp_min(t.mny);
+  t.mxy = warp_max(t.mxy);
+  __syncthreads();
+  if (lane == 0) {
+    s_d[0][wid] = t.sx;
+    s_d[1][wid] = t.sy;
+    s_f[0][wid] = t.mnx;
+    s_f[1][wid] = t.mxx;
+    s_f[2][wid] = t.mny;
+    s_f[3][wid] = t.mxy;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    StatsAcc r;
+    stats_init(r);
+    for (int w = 0; w < nw; ++w) {
+      r.sx += s_d[0][w];
+      r.sy += s_d[1][w];
+      r.mnx = fminf(r.mnx, s_f[0][w]);
+      r.mxx = fmaxf(r.mxx, s_f[1][w]);
+      r.mny = fminf(r.mny, s_f[2][w]);
+      r.mxy = fmaxf(r.mxy, s_f[3][w]);
+    }
+    stats->sum_x = r.sx;
+    stats->sum_y = r.sy;
+    stats->min_x = r.mnx;
+    stats->max_x = r.mxx;
+    stats->min_y = r.mny;
+    stats->max_y = r.mxy;
+    stats->center = center;
+    *counter = 0u;
+  }
+}
+
+__global__ void layout_stats_kernel(const float2* __restrict__ y, int n, double* partials,
+                                    LayoutStats* stats, int center) {
+  StatsAcc a;
+  stats_init(a);
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+    stats_add(a, y[i]);
+  }
+  stats_block_finish(a, partials, stats, &stats->stats_counter, center);
+}
+
+// ------------------------------------------------------------------ splat
+
+__global__ void splat_kernel(float2* __restrict__ y, const LayoutStats* __restrict__ stats, int n,
+                             int g, float4* __restrict__ charges) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const GridGeom q = grid_geometry(*stats, n, g);
+  float2 p = y[i];
+  if (stats->center) {
+    p.x -= q.mean_x;
+    p.y -= q.mean_y;
+    y[i] = p;
+  }
+  const Cell c = grid_cell(p.x, p.y, q, g);
+  const float w00 = (1.0f - c.tx) * (1.0f - c.ty);
+  const float w10 = c.tx * (1.0f - c.ty);
+  const float w01 = (1.0f - c.tx) * c.ty;
+  const float w11 = c.tx * c.ty;
+  float4* base = charges + static_cast<size_t>(c.y0) * g + c.x0;
+  atomicAdd(base, make_float4(w00, w00 * p.x, w00 * p.y, 0.0f));
+  atomicAdd(base + 1, make_float4(w10, w10 * p.x, w10 * p.y, 0.0f));
+  atomicAdd(base + g, make_float4(w01, w01 * p.x, w01 * p.y, 0.0f));
+  atomicAdd(base + g + 1, make_float4(w11, w11 * p.x, w11 * p.y, 0.0f));
+}
+
+// ------------------------------------------------------------------ FFT passes
+
+// Row r of the three charge planes and kernel row dy = r.  Packs
+// (m + i mx), (my + i Kq), (Kq2) into three complex length-M FFTs.
+__global__ void fft_rows_fwd_kernel(const float4* __restrict__ charges,
+                                    const LayoutStats* __restrict__ stats, int n, int g, int m,
+                                    int log_m, const float2* __restrict__ tw,
+                                    float2* __restrict__ rowspec, float2* __restrict__ krow) {
+  extern __shared__ float2 smem[];
+  float2* z0 = smem;
+  float2* z1 = smem + m;
+  float2* z2 = smem + 2 * m;
+  const int r = blockIdx.x;
+  const GridGeom q = grid_geometry(*stats, n, g);
+  for (int x = threadIdx.x; x < m; x += blockDim.x) {
+    float4 c = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (x < g) c = charges[static_cast<size_t>(r) * g + x];
+    float kq = 0.f, kq2 = 0.f;
+    if (x <= g - 1) {
+      kernel_values(x, r, q.spacing, &kq, &kq2);
+    } else if (x >= g + 1) {
+      kernel_values(x - m, r, q.spacing, &kq, &kq2);
+    }
+    z0[x] = make_float2(c.x, c.y);
+    z1[x] = make_float2(c.z, kq);
+    z2[x] = make_float2(kq2, 0.f);
+  }
+  __syncthreads();
+  block_fft(smem, 3, m, log_m, tw, false);
+  const int row_len = g + 1;
+  for (int k = threadIdx.x; k <= g; k += blockDim.x) {
+    const int km = (m - k) & (m - 1);
+    const float2 a = z0[k], ac = conjf2(z0[km]);
+    const float2 b = z1[k], bc = conjf2(z1[km]);
+    const float2 sum_a = cadd(a, ac), dif_a = csub(a, ac);
+    const float2 sum_b = cadd(b, bc), dif_b = csub(b, bc);
+    // X = (Z + Z*)/2, Y = (Z - Z*)/(2i)
+    const float2 xm = cscale(sum_a, 0.5f);
+    const float2 xmx = make_float2(0.5f * dif_a.y, -0.5f * dif_a.x);
+    const float2 xmy = cscale(sum_b, 0.5f);
+    const float kqx = 0.5f * dif_b.y;
+    const float kq2x = z2[k].x;
+    float2* out = rowspec + 3 * (static_cast<size_t>(r) * row_len + k);
+    out[0] = xm;
+    out[1] = xmx;
+    out[2] = xmy;
+    krow[static_cast<size_t>(r) * row_len + k] = make_float2(kqx, kq2x);
+  }
+}
+
+// Columns [k0, k0 + tk) of the half spectrum: y-FFT of three charge planes and
+// of the real, even kernel columns (Kq + i Kq2 packs two real spectra), product,
+// inverse y-FFT, keep rows [0, G).
+__global__ void fft_cols_kernel(const float2* __restrict__ rowspec, const float2* __restrict__ krow,
+                                int g, int m, int log_m, int tk, const float2* __restrict__ tw,
+                                float2* __restrict__ colspec) {
+  extern __shared__ float2 smem[];
+  const int row_len = g + 1;
+  const int k0 = blockIdx.x * tk;
+  const int cols = min(tk, row_len - k0);
+  // Buffer (c, p): column c, plane p in {0: m, 1: mx, 2: my, 3: kernel pack}.
+  for (int t = threadIdx.x; t < cols * m; t += blockDim.x) {
+    const int c = t >> log_m;
+    const int r = t & (m - 1);
+    const int k = k0 + c;
+    float2* b = smem + (static_cast<size_t>(c) * 4 << log_m);
+    float2 v0 = make_float2(0.f, 0.f), v1 = v0, v2 = v0, kk = v0;
+    if (r < g) {
+      const float2* src = rowspec + 3 * (static_cast<size_t>(r) * row_len + k);
+      v0 = src[0];
+      v1 = src[1];
+      v2 = src[2];
+    }
+    int dy = -1;
+    if (r <= g - 1) dy = r;
+    else if (r >= g + 1) dy = m - r;
+    if (dy >= 0) kk = krow[static_cast<size_t>(dy) * row_len + k];
+    b[r] = v0;
+    b[m + r] = v1;
+    b[2 * m + r] = v2;
+    b[3 * m + r] = kk;
+  }
+  __syncthreads();
+  block_fft(smem, cols * 4, m, log_m, tw, false);
+  for (int t = threadIdx.x; t < cols * m; t += blockDim.x) {
+    const int c = t >> log_m;
+    const int r = t & (m - 1);
+    float2* b = smem + (static_cast<size_t>(c) * 4 << log_m);
+    const float2 kk = b[3 * m + r];
+    const float kq = kk.x, kq2 = kk.y;
+    const float2 mm = b[r];
+    b[3 * m + r] = cscale(mm, kq);        // phi_q
+    b[r] = cscale(mm, kq2);               // phi_q2
+    b[m + r] = cscale(b[m + r], kq2);     // phi_xq2
+    b[2 * m + r] = cscale(b[2 * m + r], kq2);  // phi_yq2
+  }
+  __syncthreads();
+  block_fft(smem, cols * 4, m, log_m, tw, true);
+  for (int t = threadIdx.x; t < cols * g; t += blockDim.x) {
+    const int c = t / g;
+    const int r = t - c * g;
+    const int k = k0 + c;
+    const float2* b = smem + (static_cast<size_t>(c) * 4 << log_m);
+    float2* out = colspec + 4 * (static_cast<size_t>(r) * row_len + k);
+    out[0] = b[r];
+    out[1] = b[m + r];
+    out[2] = b[2 * m + r];
+    out[3] = b[3 * m + r];
+  }
+}
+
+// Output row r: inverse x-FFTs of (phi_q2 + i phi_xq2) and (phi_yq2 + i phi_q)
+// from their half spectra, potentials, this row's share of Z, and clearing of
+// the charges for the next splat.  The last block folds Z.
+__global__ void fft_rows_inv_kernel(const float2* __restrict__ colspec, float4* __restrict__ charges,
+                                    int n, int g, int m, int log_m, const float2* __restrict__ tw,
+                                    float4* __restrict__ pot, double* __restrict__ z_partials,
+                                    LayoutStats* __restrict__ stats) {
+  extern __shared__ float2 smem[];
+  float2* z0 = smem;
+  float2* z1 = smem + m;
+  const int r = blockIdx.x;
+  const int row_len = g + 1;
+  for (int k = threadIdx.x; k < m; k += blockDim.x) {
+    const bool mirror = k > g;
+    const int kk = mirror ? m - k : k;
+    const float2* src = colspec + 4 * (static_cast<size_t>(r) * row_len + kk);
+    float2 a = src[0], b = src[1], c = src[2], d = src[3];
+    if (mirror) {
+      a = conjf2(a);
+      b = conjf2(b);
+      c = conjf2(c);
+      d = conjf2(d);
+    }
+    z0[k] = make_float2(a.x - b.y, a.y + b.x);
+    z1[k] = make_float2(c.x - d.y, c.y + d.x);
+  }
+  __syncthreads();
+  block_fft(smem, 2, m, log_m, tw, true);
+  const float scale = 1.0f / (static_cast<float>(m) * static_cast<float>(m));
+  double zpart = 0.0;
+  for (int x = threadIdx.x; x < g; x += blockDim.x) {
+    const float2 a = z0[x], b = z1[x];
+    const float4 p = make_float4(a.x * scale, a.y * scale, b.x * scale, b.y * scale);
+    const size_t cell = static_cast<size_t>(r) * g + x;
+    pot[cell] = p;
+    const float4 ch = charges[cell];
+    zpart += static_cast<double>(ch.x) * static_cast<double>(p.w);
+    charges[cell] = make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  __shared__ double s_part[32];
+  __shared__ bool s_last;
+  zpart = warp_sum(zpart);
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  if (lane == 0) s_part[wid] = zpart;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    double v = 0.0;
+    for (int w = 0; w < static_cast<int>(blockDim.x >> 5); ++w) v += s_part[w];
+    z_partials[r] = v;
+    __threadfence();
+    const unsigned int ticket = atomicAdd(&stats->fft_counter, 1u);
+    s_last = ticket == gridDim.x - 1;
+  }
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  double acc = 0.0;
+  for (int b = threadIdx.x; b < static_cast<int>(gridDim.x); b += blockDim.x) {
+    acc += static_cast<const volatile double*>(z_partials)[b];
+  }
+  acc = warp_sum(acc);
+  __syncthreads();
+  if (lane == 0) s_part[wid] = acc;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    double z = 0.0;
+    for (int w = 0; w < static_cast<int>(blockDim.x >> 5); ++w) z += s_part[w];
+    z -= static_cast<double>(n);
+    stats->z = z;
+    stats->inv_z = static_cast<float>(1.0 / fmax(z, static_cast<double>(FLT_MIN)));
+    stats->fft_counter = 0u;
+  }
+}
+
+// ------------------------------------------------------------------ gradient + update
+
+struct UpdateParams {
+  int n;
+  int g;
+  float exaggeration;
+  float momentum;
+  float learning_rate;
+  float min_gain;
+  float max_step_norm;
+  int mode;
+};
+
+__device__ __forceinline__ float sign_f(float x) { return x == 0.0f ? 0.0f : (x < 0.0f ? -1.0f : 1.0f); }
+
+// bilinear_grid_value_t (src/tsne_neighbors.cpp:760-781) on three planes at once.
+__device__ __forceinline__ float3 gather_potentials(const float4* __restrict__ pot, const Cell& c, int g) {
+  const float4* base = pot + static_cast<size_t>(c.y0) * g + c.x0;
+  const float4 v00 = __ldg(base), v10 = __ldg(base + 1), v01 = __ldg(base + g), v11 = __ldg(base + g + 1);
+  const float a = (1.0f - c.tx) * (1.0f - c.ty);
+  const float b = c.tx * (1.0f - c.ty);
+  const float d = (1.0f - c.tx) * c.ty;
+  const float e = c.tx * c.ty;
+  float3 r;
+  r.x = a * v00.x + b * v10.x + d * v01.x + e * v11.x;
+  r.y = a * v00.y + b * v10.y + d * v01.y + e * v11.y;
+  r.z = a * v00.z + b * v10.z + d * v01.z + e * v11.z;
+  return r;
+}
+
+// One warp owns 32 consecutive rows: it sweeps their CSR rows one after the
+// other with all lanes (4 entries per lane per pass via 16-byte loads), keeps
+// row r's attraction in lane r, then every lane runs its row's epilogue.
+__global__ void __launch_bounds__(256) grad_update_kernel(
+    const int* __restrict__ row_ptr, const int4* __restrict__ col4, const float4* __restrict__ val4,
+    const float2* __restrict__ y, float2* __restrict__ y_next, float2* __restrict__ update,
+    float2* __restrict__ gains, float2* __restrict__ grad_out, const float4* __restrict__ pot,
+    LayoutStats* __restrict__ stats, double* __restrict__ partials, UpdateParams prm) {
+  const int lane = threadIdx.x & 31;
+  const int warps_per_block = blockDim.x >> 5;
+  const int warp_global = blockIdx.x * warps_per_block + (threadIdx.x >> 5);
+  const int n_warps = gridDim.x * warps_per_block;
+  const GridGeom q = grid_geometry(*stats, prm.n, prm.g);
+  const float inv_z = stats->inv_z;
+  StatsAcc acc;
+  stats_init(acc);
+
+  for (int row0 = warp_global * 32; row0 < prm.n; row0 += n_warps * 32) {
+    const int my_row = row0 + lane;
+    const bool active = my_row < prm.n;
+    const int my_beg = active ? row_ptr[my_row] : 0;
+    const int my_end = active ? row_ptr[my_row + 1] : 0;
+    const float2 my_y = active ? y[my_row] : make_float2(0.f, 0.f);
+    float my_ax = 0.f, my_ay = 0.f;
+    const int rows = min(32, prm.n - row0);
+    for (int r = 0; r < rows; ++r) {
+      const int beg = __shfl_sync(0xffffffffu, my_beg, r) >> 2;
+      const int end = __shfl_sync(0xffffffffu, my_end, r) >> 2;
+      const float yix = __shfl_sync(0xffffffffu, my_y.x, r);
+      const float yiy = __shfl_sync(0xffffffffu, my_y.y, r);
+      float ax = 0.f, ay = 0.f;
+      for (int e = beg + lane; e < end; e += 32) {
+        const int4 c = ld_stream(col4 + e);
+        const float4 v = ld_stream(val4 + e);
+        const float2 y0 = __ldg(y + c.x), y1 = __ldg(y + c.y), y2 = __ldg(y + c.z), y3 = __ldg(y + c.w);
+#define FE_ATTRACT(yj, pv)                                   \
+  {                                                          \
+    const float dx = yix - yj.x;                             \
+    const float dy = yiy - yj.y;                             \
+    const float d2 = dx * dx + dy * dy;                      \
+    const float qq = 1.0f / (1.0f + d2);                     \
+    const float w = prm.exaggeration * (pv) * qq;            \
+    ax += w * dx;                                            \
+    ay += w * dy;                                            \
+  }
+        FE_ATTRACT(y0, v.x)
+        FE_ATTRACT(y1, v.y)
+        FE_ATTRACT(y2, v.z)
+        FE_ATTRACT(y3, v.w)
+#undef FE_ATTRACT
+      }
+      ax = warp_sum(ax);
+      ay = warp_sum(ay);
+      if (lane == r) {
+        my_ax = ax;
+        my_ay = ay;
+      }
+    }
+    if (!active) continue;
+    // Repulsion from the potentials at this point's grid position.
+    const Cell c = grid_cell(my_y.x, my_y.y, q, prm.g);
+    const float3 ph = gather_potentials(pot, c, prm.g);
+    const float gx = -(my_y.x * ph.x - ph.y) * inv_z + my_ax;
+    const float gy = -(my_y.y * ph.x - ph.z) * inv_z + my_ay;
+    if (prm.mode == kGradOnly) {
+      grad_out[my_row] = make_float2(gx, gy);
+      continue;
+    }
+    // apply_open_tsne_update_f, src/tsne_neighbors.cpp:1213-1244.
+    float2 u = update[my_row];
+    float2 gn = gains[my_row];
+    if (sign_f(u.x) != sign_f(gx)) gn.x += 0.2f;
+    else gn.x = gn.x * 0.8f + prm.min_gain;
+    if (gn.x < prm.min_gain) gn.x = prm.min_gain;
+    u.x = prm.momentum * u.x - prm.learning_rate * gn.x * gx;
+    if (sign_f(u.y) != sign_f(gy)) gn.y += 0.2f;
+    else gn.y = gn.y * 0.8f + prm.min_gain;
+    if (gn.y < prm.min_gain) gn.y = prm.min_gain;
+    u.y = prm.momentum * u.y - prm.learning_rate * gn.y * gy;
+    float norm_sq = 0.0f;
+    norm_sq += u.x * u.x;
+    norm_sq += u.y * u.y;
+    float scale = 1.0f;
+    if (isfinite(prm.max_step_norm) && prm.max_step_norm > 0.0f &&
+        norm_sq > prm.max_step_norm * prm.max_step_norm) {
+      scale = prm.max_step_norm / sqrtf(fmaxf(norm_sq, FLT_MIN));
+    }
+    u.x *= scale;
+    u.y *= scale;
+    const float2 yn = make_float2(my_y.x + u.x, my_y.y + u.y);
+    update[my_row] = u;
+    gains[my_row] = gn;
+    y_next[my_row] = yn;
+    stats_add(acc, yn);
+  }
+  if (prm.mode == kGradUpdate) {
+    stats_block_finish(acc, partials, stats, &stats->update_counter, 1);
+  }
+}
+
+__global__ void center_copy_kernel(const float2* __restrict__ y, const LayoutStats* __restrict__ stats,
+                                   int n, float2* __restrict__ out) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  float2 p = y[i];
+  if (stats->center) {
+    const float mx = static_cast<float>(stats->sum_x / static_cast<double>(n));
+    const float my = static_cast<float>(stats->sum_y / static_cast<double>(n));
+    p.x -= mx;
+    p.y -= my;
+  }
+  out[i] = p;
+}
+
+}  // namespace
+
+const char* kernel_kind_name(int kind) {
+  switch (kind) {
+    case kKindSplat: return "splat_kernel";
+    case kKindFftRows: return "fft_rows_fwd_kernel";
+    case kKindFftCols: return "fft_cols_kernel";
+    case kKindFftRowsInv: return "fft_rows_inv_kernel";
+    case kKindGradUpdate: return "grad_update_kernel";
+    default: return "?";
+  }
+}
+
+int configure_kernels(TsneSession* s) {
+  const int m = s->fft;
+  const size_t cols_smem = static_cast<size_t>(s->cols_per_block) * 4 * m * sizeof(float2);
+  const size_t rows_smem = 3 * static_cast<size_t>(m) * sizeof(float2);
+  FE_CUDA(cudaFuncSetAttribute(fft_cols_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               static_cast<int>(cols_smem)), "cudaFuncSetAttribute(fft_cols_kernel)");
+  FE_CUDA(cudaFuncSetAttribute(fft_rows_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               static_cast<int>(rows_smem)), "cudaFuncSetAttribute(fft_rows_fwd_kernel)");
+  return 0;
+}
+
+int launch_stats(TsneSession* s, int center) {
+  const int blocks = std::min(1024, (s->n + 255) / 256);
+  layout_stats_kernel<<<blocks, 256, 0, s->stream>>>(s->y[s->cur], s->n, s->update_partials, s->stats, center);
+  FE_LAUNCH("layout_stats_kernel");
+  return 0;
+}
+
+namespace {
+
+struct ProfileScope {
+  TsneSession* s;
+  int kind;
+  ProfileScope(TsneSession* s_, int kind_) : s(s_), kind(kind_) {
+    if (!s->profile) return;
+    cudaEvent_t e;
+    cudaEventCreate(&e);
+    cudaEventRecord(e, s->stream);
+    s->events.push_back(e);
+  }
+  ~ProfileScope() {
+    if (!s->profile) return;
+    cudaEvent_t e;
+    cudaEventCreate(&e);
+    cudaEventRecord(e, s->stream);
+    s->events.push_back(e);
+    s->event_kind.push_back(kind);
+  }
+};
+
+}  // namespace
+
+int launch_iteration(TsneSession* s, GradMode mode, float exaggeration, float momentum,
+                     float learning_rate, float min_gain, float max_step_norm) {
+  const int g = s->grid, m = s->fft, lm = s->log_fft;
+  const int row_len = g + 1;
+  {
+    ProfileScope ps(s, kKindSplat);
+    splat_kernel<<<(s->n + 255) / 256, 256, 0, s->stream>>>(s->y[s->cur], s->stats, s->n, g, s->charges);
+    FE_LAUNCH("splat_kernel");
+  }
+  {
+    ProfileScope ps(s, kKindFftRows);
+    fft_rows_fwd_kernel<<<g, 256, 3 * m * sizeof(float2), s->stream>>>(
+        s->charges, s->stats, s->n, g, m, lm, s->twiddle, s->rowspec, s->krow);
+    FE_LAUNCH("fft_rows_fwd_kernel");
+  }
+  {
+    ProfileScope ps(s, kKindFftCols);
+    const int tk = s->cols_per_block;
+    const int blocks = (row_len + tk - 1) / tk;
+    fft_cols_kernel<<<blocks, 256, static_cast<size_t>(tk) * 4 * m * sizeof(float2), s->stream>>>(
+        s->rowspec, s->krow, g, m, lm, tk, s->twiddle, s->colspec);
+    FE_LAUNCH("fft_cols_kernel");
+  }
+  {
+    ProfileScope ps(s, kKindFftRowsInv);
+    fft_rows_inv_kernel<<<g, 256, 2 * m * sizeof(float2), s->stream>>>(
+        s->colspec, s->charges, s->n, g, m, lm, s->twiddle, s->pot, s->z_partials, s->stats);
+    FE_LAUNCH("fft_rows_inv_kernel");
+  }
+  {
+    ProfileScope ps(s, kKindGradUpdate);
+    UpdateParams prm{s->n, g, exaggeration, momentum, learning_rate, min_gain, max_step_norm,
+                     static_cast<int>(mode)};
+    grad_update_kernel<<<s->update_blocks, s->update_threads, 0, s->stream>>>(
+        s->row_ptr, reinterpret_cast<const int4*>(s->col), reinterpret_cast<const float4*>(s->val),
+        s->y[s->cur], s->y[s->cur ^ 1], s->update, s->gains, s->grad_out, s->pot, s->stats,
+        s->update_partials, prm);
+    FE_LAUNCH("grad_update_kernel");
+  }
+  if (mode == kGradUpdate) s->cur ^= 1;
+  return 0;
+}
+
+int launch_center_output(TsneSession* s, float2* out) {
+  center_copy_kernel<<<(s->n + 255) / 256, 256, 0, s->stream>>>(s->y[s->cur], s->stats, s->n, out);
+  FE_LAUNCH("center_copy_kernel");
+  return 0;
+}
+
+}  // namespace fe

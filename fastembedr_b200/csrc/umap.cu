@@ -1,0 +1,298 @@
+// UMAP edge-sampled SGD over a COO graph (objective 0, the UMAP cross entropy).
+//
+// Per epoch e and edge (h, t) with period p = epochs_per_sample:
+//   positives = floor(e/p) - floor((e-1)/p)  (0 at e = 0)
+//   each positive: d2 = max(eps, |y_h - y_t|^2), c = -2ab d2^(b-1) / (1 + a d2^b),
+//                  g = clip4(c (y_h - y_t)) * alpha;  y_h += g, y_t -= g
+//   negatives (count from the negative schedule): vertex from a counter-based
+//                  hash of (seed, epoch, head, key, sample); skip head/tail;
+//                  c = 2 gamma b / ((0.001 + d2)(1 + a d2^b)); y_h += clip4(c d) * alpha
+//   alpha = lr (1 - e / n_epochs); after the epoch: NaN -> 0, clamp to +-16.
+// This restates fast_knn_umap_coo_replay_cpp (src/fast_knn_umap.cpp:4904-5056)
+// and the reference kernels embed_epoch_coo_{atomic,delta}_kernel
+// (src/embedding_cuda_kernels.cpp:3066-3222).  d^b uses the reference's own
+// exponent-interpolation approximation (umap_powf_fast, src/fast_knn_umap.cpp:179-206).
+//
+// Modes:
+//   kUmapInplace (optimizer_mode 0): Hogwild.  Each edge reads its endpoints once,
+//     applies its own positive and negative updates sequentially to a local copy
+//     (the CPU replay's order within an edge), then adds the net displacement
+//     with one 8-byte vector atomic per endpoint (red.global.add.v2.f32).
+//   kUmapDelta (optimizer_mode 1): Jacobi.  Forces are evaluated against the
+//     layout frozen at epoch start and accumulated into a delta buffer, which a
+//     second kernel applies together with the sanitize step.
+// Head displacements of consecutive edges with the same head (COO built from
+// CSR is grouped by head) are summed across the warp before the atomic.
+#include "umap.cuh"
+
+#include <cfloat>
+#include <cmath>
+
+namespace fe {
+namespace {
+
+__device__ __forceinline__ float umap_pow(float x, float b) {
+  if (x <= 0.0f) return 0.0f;
+  const unsigned int bits = __float_as_uint(x);
+  const float bias_word = 1064866805.0f;
+  const int whole = static_cast<int>(b);
+  const float frac = b - static_cast<float>(whole);
+  const unsigned int interp = static_cast<unsigned int>(frac * (static_cast<float>(bits) - bias_word) + bias_word);
+  const float frac_pow = __uint_as_float(interp);
+  float int_pow = 1.0f;
+  float base = x;
+  int e = whole;
+  while (e > 0) {
+    if (e & 1) int_pow *= base;
+    base *= base;
+    e >>= 1;
+  }
+  return int_pow * frac_pow;
+}
+
+__device__ __forceinline__ int positive_samples(float period, int epoch) {
+  if (period <= 0.0f || !isfinite(period) || epoch == 0) return 0;
+  const float now = static_cast<float>(epoch);
+  const float prev = static_cast<float>(epoch - 1);
+  const int s = static_cast<int>(floorf(now / period)) - static_cast<int>(floorf(prev / period));
+  return s > 0 ? s : 0;
+}
+
+__device__ __forceinline__ int negative_samples(float period, int nsr, int epoch) {
+  if (nsr <= 0 || period <= 0.0f || !isfinite(period) || epoch == 0) return 0;
+  const float now = static_cast<float>(epoch);
+  const float prev = static_cast<float>(epoch - 1);
+  const int cur = static_cast<int>(floorf(now / period));
+  const int old = static_cast<int>(floorf(prev / period));
+  if (cur <= old) return 0;
+  const float neg_period = period / static_cast<float>(nsr);
+  if (neg_period <= 0.0f || !isfinite(neg_period)) return 0;
+  const int cur_total = static_cast<int>(floorf((now - neg_period) / neg_period));
+  int prev_total = 0;
+  if (cur > 1) {
+    const float prev_active = ceilf(static_cast<float>(cur - 1) * period);
+    prev_total = static_cast<int>(floorf((prev_active - neg_period) / neg_period));
+  }
+  const int s = cur_total - prev_total;
+  return s > 0 ? s : 0;
+}
+
+__device__ __forceinline__ unsigned int mix32(unsigned int x) {
+  x ^= x >> 16;
+  x *= 0x7feb352du;
+  x ^= x >> 15;
+  x *= 0x846ca68bu;
+  x ^= x >> 16;
+  return x;
+}
+
+__device__ __forceinline__ int negative_vertex(unsigned int n, unsigned int seed, int epoch, int head,
+                                               unsigned int key, int sample) {
+  unsigned int x = seed;
+  x ^= static_cast<unsigned int>(epoch) * 0x9e3779b9u;
+  x ^= (static_cast<unsigned int>(head) + 1u) * 0x85ebca6bu;
+  x ^= (key + 1u) * 0xc2b2ae35u;
+  x ^= (static_cast<unsigned int>(sample) + 1u) * 0x27d4eb2du;
+  return static_cast<int>(mix32(x) % n);
+}
+
+__device__ __forceinline__ float clip4(float v) { return v < -4.0f ? -4.0f : (v > 4.0f ? 4.0f : v); }
+
+template <int Mode>
+__global__ void __launch_bounds__(256) umap_epoch_kernel(const int* __restrict__ heads,
+                                                         const int* __restrict__ tails,
+                                                         const float* __restrict__ periods,
+                                                         long long n_edges, float2* layout,
+                                                         const float2* __restrict__ frozen,
+                                                         float2* __restrict__ delta, UmapParams p,
+                                                         int epoch, long long* positive_count) {
+  const float eps = 1.1920928955078125e-7f;
+  const float alpha = p.learning_rate * (1.0f - static_cast<float>(epoch) / fmaxf(1.0f, static_cast<float>(p.n_epochs)));
+  const float2* src = Mode == kUmapDelta ? frozen : layout;
+  float2* dst = Mode == kUmapDelta ? delta : layout;
+  const int lane = threadIdx.x & 31;
+  long long local_pos = 0;
+  const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
+  // Whole warps iterate together so the head-run reduction sees full warps.
+  const long long base0 = static_cast<long long>(blockIdx.x) * blockDim.x + (threadIdx.x & ~31);
+  for (long long base = base0; base < n_edges; base += stride) {
+    const long long gid = base + lane;
+    int h = -1, t = -1;
+    float gx_h = 0.f, gy_h = 0.f;
+    if (gid < n_edges) {
+      h = __ldcs(heads + gid);
+      t = __ldcs(tails + gid);
+      const float per = __ldcs(periods + gid);
+      const bool ok = h >= 0 && h < p.n && t >= 0 && t < p.n && h != t;
+      const int pos = ok ? positive_samples(per, epoch) : 0;
+      if (pos > 0) {
+        local_pos += pos;
+        const float2 yh0 = src[h];
+        const float2 yt0 = src[t];
+        const int neg = negative_samples(per, p.negative_sample_rate, epoch);
+        const unsigned int key = p.hash_key_is_tail ? static_cast<unsigned int>(t) : static_cast<unsigned int>(gid);
+        if (Mode == kUmapDelta) {
+          // Jacobi: every force at the frozen epoch-start positions.
+          float2 dh = make_float2(0.f, 0.f), dt = make_float2(0.f, 0.f);
+          for (int s = 0; s < pos; ++s) {
+            const float dx = yh0.x - yt0.x;
+            const float dy = yh0.y - yt0.y;
+            const float d2 = fmaxf(eps, dx * dx + dy * dy);
+            const float d2b = umap_pow(d2, p.b);
+            const float c = -2.0f * p.a * p.b * (d2b / d2) / (p.a * d2b + 1.0f);
+            const float gx = clip4(c * dx) * alpha;
+            const float gy = clip4(c * dy) * alpha;
+            dh.x += gx;
+            dh.y += gy;
+            dt.x -= gx;
+            dt.y -= gy;
+          }
+          for (int s = 0; s < neg; ++s) {
+            const int k = negative_vertex(static_cast<unsigned int>(p.n), p.seed, epoch, h, key, s);
+            if (k == h || k == t) continue;
+            const float2 yk = src[k];
+            const float dx = yh0.x - yk.x;
+            const float dy = yh0.y - yk.y;
+            const float d2 = fmaxf(eps, dx * dx + dy * dy);
+            const float d2b = umap_pow(d2, p.b);
+            const float c = p.repulsion_strength * 2.0f * p.b / ((0.001f + d2) * (p.a * d2b + 1.0f));
+            dh.x += clip4(c * dx) * alpha;
+            dh.y += clip4(c * dy) * alpha;
+          }
+          gx_h = dh.x;
+          gy_h = dh.y;
+          atomicAdd(dst + t, dt);
+        } else {
+          // In place: the edge's own updates are applied in the CPU replay's
+          // order to running copies of its endpoints.
+          float2 yh = yh0, yt = yt0;
+          for (int s = 0; s < pos; ++s) {
+            const float dx = yh.x - yt.x;
+            const float dy = yh.y - yt.y;
+            const float d2 = fmaxf(eps, dx * dx + dy * dy);
+            const float d2b = umap_pow(d2, p.b);
+            const float c = -2.0f * p.a * p.b * (d2b / d2) / (p.a * d2b + 1.0f);
+            const float gx = clip4(c * dx) * alpha;
+            const float gy = clip4(c * dy) * alpha;
+            yh.x += gx;
+            yh.y += gy;
+            yt.x += -gx;
+            yt.y += -gy;
+          }
+          for (int s = 0; s < neg; ++s) {
+            const int k = negative_vertex(static_cast<unsigned int>(p.n), p.seed, epoch, h, key, s);
+            if (k == h || k == t) continue;
+            const float2 yk = src[k];
+            const float dx = yh.x - yk.x;
+            const float dy = yh.y - yk.y;
+            const float d2 = fmaxf(eps, dx * dx + dy * dy);
+            const float d2b = umap_pow(d2, p.b);
+            const float c = p.repulsion_strength * 2.0f * p.b / ((0.001f + d2) * (p.a * d2b + 1.0f));
+            yh.x += clip4(c * dx) * alpha;
+            yh.y += clip4(c * dy) * alpha;
+          }
+          gx_h = yh.x - yh0.x;
+          gy_h = yh.y - yh0.y;
+          atomicAdd(dst + t, make_float2(yt.x - yt0.x, yt.y - yt0.y));
+        }
+      } else {
+        h = -1;
+      }
+    }
+    // Segmented sum of head displacements over lanes that share a head.
+    const unsigned int peers = __match_any_sync(0xffffffffu, h);
+    const int leader = __ffs(peers) - 1;
+    float sx = 0.f, sy = 0.f;
+    for (unsigned int m = peers; m; m &= m - 1) {
+      const int l = __ffs(m) - 1;
+      sx += __shfl_sync(peers, gx_h, l);
+      sy += __shfl_sync(peers, gy_h, l);
+    }
+    if (lane == leader && h >= 0) atomicAdd(dst + h, make_float2(sx, sy));
+  }
+  if (positive_count != nullptr) {
+    local_pos = warp_sum(static_cast<double>(local_pos));
+    if (lane == 0 && local_pos) atomicAdd(reinterpret_cast<unsigned long long*>(positive_count),
+                                          static_cast<unsigned long long>(local_pos));
+  }
+}
+
+__global__ void umap_sanitize_kernel(float2* layout, float2* delta, int n, float max_abs) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  float2 v = layout[i];
+  if (delta != nullptr) {
+    const float2 d = delta[i];
+    v.x += d.x;
+    v.y += d.y;
+    delta[i] = make_float2(0.f, 0.f);
+  }
+  if (!isfinite(v.x)) v.x = 0.0f;
+  if (!isfinite(v.y)) v.y = 0.0f;
+  v.x = fminf(max_abs, fmaxf(-max_abs, v.x));
+  v.y = fminf(max_abs, fmaxf(-max_abs, v.y));
+  layout[i] = v;
+}
+
+}  // namespace
+
+int umap_launch_epoch(UmapRun* r, int epoch) {
+  const UmapParams& p = r->params;
+  if (r->mode == kUmapDelta) {
+    umap_epoch_kernel<kUmapDelta><<<r->edge_blocks, 256, 0, r->stream>>>(
+        r->heads, r->tails, r->periods, r->n_edges, r->layout, r->layout, r->delta, p, epoch,
+        r->positive_count);
+  } else {
+    umap_epoch_kernel<kUmapInplace><<<r->edge_blocks, 256, 0, r->stream>>>(
+        r->heads, r->tails, r->periods, r->n_edges, r->layout, r->layout, nullptr, p, epoch,
+        r->positive_count);
+  }
+  FE_LAUNCH("umap_epoch_kernel");
+  umap_sanitize_kernel<<<(p.n + 255) / 256, 256, 0, r->stream>>>(
+      r->layout, r->mode == kUmapDelta ? r->delta : nullptr, p.n, 16.0f);
+  FE_LAUNCH("umap_sanitize_kernel");
+  return 0;
+}
+
+int umap_run_epochs(UmapRun* r, int epoch_begin, int epoch_end) {
+  if (r->mode == kUmapDelta && r->delta != nullptr) {
+    FE_CUDA(cudaMemsetAsync(r->delta, 0, sizeof(float2) * r->params.n, r->stream), "memset delta");
+  }
+  const bool graphs = r->use_graphs && (epoch_end - epoch_begin) > 8 && r->positive_count == nullptr;
+  if (!graphs) {
+    for (int e = epoch_begin; e < epoch_end; ++e) FE_TRY(umap_launch_epoch(r, e));
+    return 0;
+  }
+  // Capture chunks of epochs; the epoch index is a kernel argument, so each
+  // chunk is its own graph (instantiated once, launched once).
+  const int chunk = 50;
+  for (int e0 = epoch_begin; e0 < epoch_end; e0 += chunk) {
+    const int e1 = std::min(epoch_end, e0 + chunk);
+    cudaGraph_t g = nullptr;
+    FE_CUDA(cudaStreamBeginCapture(r->stream, cudaStreamCaptureModeThreadLocal), "cudaStreamBeginCapture(umap)");
+    int rc = 0;
+    for (int e = e0; e < e1 && rc == 0; ++e) rc = umap_launch_epoch(r, e);
+    const cudaError_t end = cudaStreamEndCapture(r->stream, &g);
+    if (rc != 0 || end != cudaSuccess) {
+      if (g) cudaGraphDestroy(g);
+      if (rc == 0) check_cuda(end, "cudaStreamEndCapture(umap)");
+      return 1;
+    }
+    cudaGraphExec_t exec = nullptr;
+    const cudaError_t inst = cudaGraphInstantiate(&exec, g, 0);
+    cudaGraphDestroy(g);
+    FE_CUDA(inst, "cudaGraphInstantiate(umap)");
+    const cudaError_t launch = cudaGraphLaunch(exec, r->stream);
+    cudaGraphExecDestroy(exec);
+    FE_CUDA(launch, "cudaGraphLaunch(umap)");
+  }
+  return 0;
+}
+
+int umap_edge_blocks(long long n_edges) {
+  const long long want = (n_edges + 255) / 256;
+  const long long cap = static_cast<long long>(sm_count()) * 8;
+  return static_cast<int>(std::max(1ll, std::min(want, cap)));
+}
+
+}  // namespace fe

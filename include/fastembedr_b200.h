@@ -1,0 +1,242 @@
+/*
+ * fastembedr_b200 -- B200-native drop-in for fastEmbedR's CUDA embedding optimizer.
+ *
+ * C ABI exported by libfastembedr_b200.so.  The first block reproduces, symbol
+ * for symbol and argument for argument, the prototypes that the reference's
+ * host wrapper src/embedding_cuda_impl.cpp declares (lines 24-380) and links
+ * against; the original definitions live in src/embedding_cuda_kernels.cpp.
+ * Conventions shared with the reference:
+ *   - return 0 on success, 1 on failure; the message is then available from
+ *     fastembedr_cuda_embedding_last_error() (thread-local);
+ *   - KNN inputs are R column-major n x k (entry j of row i at j*n + i), with
+ *     index_offset = 1 for 1-based indices;
+ *   - layouts (init, out) are row-major interleaved float[n*2], caller-owned;
+ *   - calls are synchronous and use the current CUDA device.
+ * Symbols outside the optimizer hot path (landmarks, metrics, exact t-SNE,
+ * legacy objectives, PCA/RAFT helpers) are exported so the wrapper links, and
+ * return 1 with "not provided by the B200 backend".
+ *
+ * The second block (fe_b200_*) is this backend's own interface: sessions that
+ * keep state resident on the device (benchmarks, checkpoint/resume), parity
+ * hooks and multi-GPU sharding.  They have no counterpart in the reference.
+ */
+#ifndef FASTEMBEDR_B200_H
+#define FASTEMBEDR_B200_H
+
+#include <stdbool.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ===================================================================== */
+/* Reference ABI (src/embedding_cuda_impl.cpp:24-380)                     */
+/* ===================================================================== */
+
+/* src/embedding_cuda_impl.cpp:25 */
+bool fastembedr_cuda_available(void);
+/* src/embedding_cuda_impl.cpp:26 */
+const char* fastembedr_cuda_embedding_last_error(void);
+
+/* openTSNE FFT-grid optimizer from host KNN with double distances.
+ * src/embedding_cuda_impl.cpp:79-99 (definition src/embedding_cuda_kernels.cpp:6010-6037). */
+int fastembedr_cuda_opentsne_fft_from_knn(const int* indices, const double* distances,
+                                          const float* init, int has_init, int n, int k,
+                                          int n_components, float perplexity,
+                                          int early_exaggeration_iter, int n_iter,
+                                          float early_exaggeration, float exaggeration,
+                                          float learning_rate, int learning_rate_auto,
+                                          float initial_momentum, float final_momentum,
+                                          float min_gain, float max_step_norm, unsigned int seed,
+                                          int index_offset, float* out);
+/* Same with float32 distances.  src/embedding_cuda_impl.cpp:100-120 (kernels.cpp:6039-6066). */
+int fastembedr_cuda_opentsne_fft_from_knn_float(const int* indices, const float* distances,
+                                                const float* init, int has_init, int n, int k,
+                                                int n_components, float perplexity,
+                                                int early_exaggeration_iter, int n_iter,
+                                                float early_exaggeration, float exaggeration,
+                                                float learning_rate, int learning_rate_auto,
+                                                float initial_momentum, float final_momentum,
+                                                float min_gain, float max_step_norm,
+                                                unsigned int seed, int index_offset, float* out);
+/* Device-resident KNN (the GPU-KNN object's borrowed pointers).
+ * src/embedding_cuda_impl.cpp:121-141 (kernels.cpp:6068-6095). */
+int fastembedr_cuda_opentsne_fft_from_device_knn_float(
+    const int* indices, const float* distances, const float* init, int has_init, int n, int k,
+    int n_components, float perplexity, int early_exaggeration_iter, int n_iter,
+    float early_exaggeration, float exaggeration, float learning_rate, int learning_rate_auto,
+    float initial_momentum, float final_momentum, float min_gain, float max_step_norm,
+    unsigned int seed, int index_offset, float* out);
+/* Device-KNN with device PCA init (RAFT TSVD in the reference; returns 1 here, as the
+ * reference does without RAFT).  src/embedding_cuda_impl.cpp:142-183. */
+int fastembedr_cuda_opentsne_fft_from_device_knn_float_pca_double(
+    const int* indices, const float* distances, const double* pca_init_values, int pca_init_p,
+    int n, int k, int n_components, float perplexity, int early_exaggeration_iter, int n_iter,
+    float early_exaggeration, float exaggeration, float learning_rate, int learning_rate_auto,
+    float initial_momentum, float final_momentum, float min_gain, float max_step_norm,
+    unsigned int seed, int index_offset, float* out);
+int fastembedr_cuda_opentsne_fft_from_device_knn_float_pca_float(
+    const int* indices, const float* distances, const float* pca_init_values, int pca_init_p,
+    int n, int k, int n_components, float perplexity, int early_exaggeration_iter, int n_iter,
+    float early_exaggeration, float exaggeration, float learning_rate, int learning_rate_auto,
+    float initial_momentum, float final_momentum, float min_gain, float max_step_norm,
+    unsigned int seed, int index_offset, float* out);
+
+/* UMAP over a host COO graph.  optimizer_mode 0: in-place (Hogwild) atomics;
+ * 1: Jacobi delta.  src/embedding_cuda_impl.cpp:243-258 (kernels.cpp:5325-5450). */
+int fastembedr_cuda_umap_optimize_coo(const int* heads, const int* tails, const float* weights,
+                                      const float* epochs_per_sample, const float* init, int n,
+                                      int n_edges_capacity, int n_epochs, int negative_sample_rate,
+                                      float learning_rate, float a, float b,
+                                      float repulsion_strength, unsigned int seed,
+                                      int optimizer_mode, float* out);
+
+/* UMAP from KNN with graph build and diffusion ("spectral") init on the device.
+ * src/embedding_cuda_impl.cpp:184-229 (kernels.cpp:5258-5323). */
+int fastembedr_cuda_umap_from_knn_spectral(const int* indices, const double* distances, int n,
+                                           int k, int n_epochs, int negative_sample_rate,
+                                           float learning_rate, float a, float b,
+                                           float repulsion_strength, int spectral_n_iter,
+                                           unsigned int seed, int index_offset,
+                                           int optimizer_mode, float* out);
+int fastembedr_cuda_umap_from_knn_spectral_float(const int* indices, const float* distances,
+                                                 int n, int k, int n_epochs,
+                                                 int negative_sample_rate, float learning_rate,
+                                                 float a, float b, float repulsion_strength,
+                                                 int spectral_n_iter, unsigned int seed,
+                                                 int index_offset, int optimizer_mode, float* out);
+int fastembedr_cuda_umap_from_device_knn_spectral_float(
+    const int* device_indices, const float* device_distances, int n, int k, int n_epochs,
+    int negative_sample_rate, float learning_rate, float a, float b, float repulsion_strength,
+    int spectral_n_iter, unsigned int seed, int index_offset, int optimizer_mode, int binary_graph,
+    float* out);
+/* Device graph dump (padded width x n COO).  src/embedding_cuda_impl.cpp:232-242. */
+int fastembedr_cuda_umap_graph_dump_from_knn(const int* indices, const double* distances, int n,
+                                             int k, int index_offset, int* out_heads,
+                                             int* out_tails, float* out_weights,
+                                             float* out_epochs_per_sample, int* out_width,
+                                             int* out_capacity);
+
+/* ---- out of scope: exported for linking, return 1 (src/embedding_cuda_impl.cpp:27-78, 259-379) ---- */
+int fastembedr_cuda_embed(const int* neighbors, const float* weights, const float* init, int n,
+                          int k, int objective, int n_epochs, int negative_sample_rate,
+                          float learning_rate, float a, float b, float max_weight,
+                          unsigned int seed, float* out);
+int fastembedr_cuda_embed_from_knn(const int* indices, const double* distances, const float* init,
+                                   int n, int k, int objective, int n_epochs,
+                                   int negative_sample_rate, float learning_rate, float a, float b,
+                                   unsigned int seed, int index_offset, float* out);
+int fastembedr_cuda_spectral_init_from_knn(const int* indices, const double* distances, int n,
+                                           int k, int spectral_n_iter, unsigned int seed,
+                                           int index_offset, float* out);
+int fastembedr_cuda_exact_tsne_from_knn(const int* indices, const double* distances,
+                                        const float* init, int n, int k, int n_epochs,
+                                        float perplexity, float learning_rate, int stop_lying_iter,
+                                        int mom_switch_iter, float momentum, float final_momentum,
+                                        float exaggeration_factor, unsigned int seed,
+                                        int index_offset, float* out);
+int fastembedr_cuda_landmark_tsne_from_device_knn(
+    const int* device_indices, const float* device_distances, int index_offset,
+    const float* reference_data, const float* query_data, const float* reference_layout,
+    int n_reference, int n_query, int n_features, int k, float perplexity, int n_iter,
+    int early_exaggeration_iter, float learning_rate, float early_exaggeration, float exaggeration,
+    float initial_momentum, float final_momentum, float max_grad_norm, float max_step_norm,
+    int n_negatives, int exact_repulsion_threshold, unsigned int seed, int affine_neighbors,
+    float affine_ridge, float max_extrapolation, float* out);
+int fastembedr_cuda_landmark_umap_from_device_knn(
+    const int* device_indices, const float* device_distances, int index_offset,
+    const float* reference_data, const float* query_data, const float* reference_layout,
+    const int* landmark_rows, const int* query_rows, int n_total, int n_reference, int n_query,
+    int n_features, int k, int n_epochs, int negative_sample_rate, float learning_rate, float a,
+    float b, float repulsion_strength, unsigned int seed, int affine_neighbors, float affine_ridge,
+    float max_extrapolation, float* out);
+int fastembedr_cuda_standardize_matrix(const double* values, int n, int p, double* out,
+                                       double* center, double* scale);
+int fastembedr_cuda_project_embedding(const double* reference_layout, const int* projection_indices,
+                                      const double* projection_distances, int n_reference,
+                                      int n_query, int k, int n_components, double* out);
+int fastembedr_cuda_interpolate_landmark_layout(const double* landmark_layout,
+                                                const int* landmark_indices,
+                                                const int* projection_indices,
+                                                const double* projection_distances,
+                                                int n_landmarks, int n, int k, int n_components,
+                                                double* out);
+int fastembedr_cuda_landmark_project_interpolate_knn_confidence(
+    const double* landmark_data, const double* query_data, const double* landmark_layout,
+    const int* landmark_indices, int n_landmarks, int n, int n_features, int k, int n_components,
+    double* out, int* projection_indices, double* projection_distances, double* confidence);
+int fastembedr_cuda_knn_structure_score(const double* layout, const int* indices, const int* keep,
+                                        const int* labels, int n, int index_rows,
+                                        int high_rank_limit, int preserve_k, int keep_n,
+                                        int compact_indices, int n_label_levels, double* totals);
+int fastembedr_cuda_silhouette_score(const double* layout, const int* labels, const int* counts,
+                                     int n, int n_label_levels, double* score);
+int fastembedr_cuda_matrix_multiply(const double* left, const double* right, int left_rows,
+                                    int left_cols, int right_cols, int transpose_left, double* out);
+int fastembedr_cuda_raft_tsvd_pca_init(const double* values, int n, int p, int n_components,
+                                       float* out);
+
+/* ===================================================================== */
+/* B200 backend extensions (no counterpart in the reference)              */
+/* ===================================================================== */
+
+/* Version string of this backend. */
+const char* fe_b200_version(void);
+
+/* ---- t-SNE sessions: device-resident state across calls ---- */
+typedef struct fe_b200_tsne fe_b200_tsne;
+
+/* Builds P on the device from column-major KNN (host or device pointers,
+ * float32 distances), uploads init (row-major float[n*2]; NULL = the reference
+ * CUDA path's hashed uniform init), and keeps everything resident.
+ * grid_size 0 selects the reference CPU policy (64/128/256 by n, env
+ * FASTEMBEDR_TSNE_FFT_GRID honoured). */
+int fe_b200_tsne_create(const int* indices, const float* distances, int n, int k,
+                        int index_offset, float perplexity, const float* init, unsigned int seed,
+                        int grid_size, int inputs_on_device, fe_b200_tsne** out);
+/* Same from an already symmetrised CSR P (host arrays; parity and resume). */
+int fe_b200_tsne_create_csr(const int* row_ptr, const int* col, const float* val, int n,
+                            const float* init, int grid_size, fe_b200_tsne** out);
+/* Runs n_iter optimizer iterations with fixed phase parameters. */
+int fe_b200_tsne_iterate(fe_b200_tsne* s, int n_iter, float exaggeration, float momentum,
+                         float learning_rate, float min_gain, float max_step_norm);
+/* Gradient at the current layout without updating it (grad: host float[n*2]). */
+int fe_b200_tsne_gradient(fe_b200_tsne* s, float exaggeration, float* grad, double* z);
+/* Current (centred) layout to host (on_device = 0) or device memory. */
+int fe_b200_tsne_get_layout(fe_b200_tsne* s, float* out, int on_device);
+/* Replaces the layout (and resets optimizer state when reset_state != 0). */
+int fe_b200_tsne_set_layout(fe_b200_tsne* s, const float* y, int on_device, int reset_state);
+/* Optimizer state (update, gains) to/from host, for checkpoint/resume. */
+int fe_b200_tsne_get_state(fe_b200_tsne* s, float* update, float* gains);
+int fe_b200_tsne_set_state(fe_b200_tsne* s, const float* update, const float* gains);
+/* Sizes: n, grid G, nnz (symmetric entries), padded nnz. */
+int fe_b200_tsne_info(fe_b200_tsne* s, int* n, int* grid, long long* nnz, long long* nnz_padded);
+/* Copies the (unpadded) CSR P to host arrays of size n+1 / nnz / nnz. */
+int fe_b200_tsne_get_p(fe_b200_tsne* s, int* row_ptr, int* col, float* val);
+/* The cudaStream_t the session launches on. */
+void* fe_b200_tsne_stream(fe_b200_tsne* s);
+/* Per-kernel CUDA-event timing: enable, then read per-kind totals
+ * (kinds: 0 splat, 1 fft rows, 2 fft cols, 3 fft rows inverse, 4 gradient+update). */
+int fe_b200_tsne_profile(fe_b200_tsne* s, int enable);
+int fe_b200_tsne_kernel_times(fe_b200_tsne* s, double* ms, long long* launches, int kinds);
+const char* fe_b200_tsne_kernel_name(int kind);
+void fe_b200_tsne_destroy(fe_b200_tsne* s);
+
+/* ---- UMAP parity hook ---- */
+/* Runs epochs [epoch_begin, epoch_end) of the COO optimizer on layout
+ * (row-major float[n*2], host, in/out).  hash_key_is_tail selects the
+ * negative-sample key (0: edge id as the CPU replay, 1: tail id as the
+ * reference CUDA kernels).  positive_samples (optional) receives the number of
+ * positive edge samples applied. */
+int fe_b200_umap_epochs(const int* heads, const int* tails, const float* epochs_per_sample,
+                        long long n_edges, float* layout, int n, int epoch_begin, int epoch_end,
+                        int n_epochs, int negative_sample_rate, float learning_rate, float a,
+                        float b, float repulsion_strength, unsigned int seed, int optimizer_mode,
+                        int hash_key_is_tail, long long* positive_samples);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FASTEMBEDR_B200_H */

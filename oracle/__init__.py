@@ -101,6 +101,10 @@ def ref() -> ctypes.CDLL:
                                         ctypes.c_int, ctypes.c_float, ctypes.c_float,
                                         ctypes.c_float, ctypes.c_float, ctypes.c_int]
         R.feref_tsne_zero_mean.argtypes = [_c_float_p, ctypes.c_int]
+        R.feref_tsne_iterate.argtypes = [_c_int_p, _c_int_p, _c_float_p, ctypes.c_int, _c_float_p,
+                                         _c_float_p, _c_float_p, ctypes.c_int, ctypes.c_float,
+                                         ctypes.c_float, ctypes.c_float, ctypes.c_float,
+                                         ctypes.c_float, ctypes.c_int, ctypes.c_int, _c_double_p]
         R.feref_tsne_kl.argtypes = [_c_int_p, _c_int_p, _c_float_p, ctypes.c_int, _c_float_p,
                                     ctypes.c_int, _c_double_p]
         R.feref_tsne_run.argtypes = [_c_int_p, _c_float_p, ctypes.c_int, ctypes.c_int, _c_float_p,
@@ -239,6 +243,19 @@ def tsne_update(y, update, gains, grad, learning_rate, momentum, min_gain=0.01, 
                          _ptr(gains, ctypes.c_float), _ptr(grad, ctypes.c_float), y.shape[0],
                          ctypes.c_float(learning_rate), ctypes.c_float(momentum),
                          ctypes.c_float(min_gain), ctypes.c_float(max_step_norm))
+    return y, update, gains
+
+
+def tsne_iterate(P: Csr, y, update, gains, iters, exaggeration, momentum, learning_rate,
+                 min_gain=0.01, max_step_norm=5.0, grid_size=0):
+    y, update, gains = (_f32(a).copy() for a in (y, update, gains))
+    g = grid_size or tsne_grid_size(P.n)
+    lib().or_tsne_iterate(_ptr(P.row_ptr, ctypes.c_int), _ptr(P.col, ctypes.c_int),
+                          _ptr(P.val, ctypes.c_float), P.n, _ptr(y, ctypes.c_float),
+                          _ptr(update, ctypes.c_float), _ptr(gains, ctypes.c_float), iters,
+                          ctypes.c_float(exaggeration), ctypes.c_float(momentum),
+                          ctypes.c_float(learning_rate), ctypes.c_float(min_gain),
+                          ctypes.c_float(max_step_norm), g)
     return y, update, gains
 
 
@@ -421,6 +438,19 @@ def ref_tsne_update(y, update, gains, grad, learning_rate, momentum, min_gain=0.
         _ptr(grad, ctypes.c_float), y.shape[0], learning_rate, momentum, min_gain,
         max_step_norm, threads))
     return y, update, gains
+
+
+def ref_tsne_iterate(P: Csr, y, update, gains, iters, exaggeration, momentum, learning_rate,
+                     min_gain=0.01, max_step_norm=5.0, threads=1, grid_override=0):
+    """The reference's own iteration loop; returns (y, update, gains, loop_seconds)."""
+    y, update, gains = (_f32(a).copy() for a in (y, update, gains))
+    secs = ctypes.c_double(0.0)
+    _ref_check(ref().feref_tsne_iterate(
+        _ptr(P.row_ptr, ctypes.c_int), _ptr(P.col, ctypes.c_int), _ptr(P.val, ctypes.c_float), P.n,
+        _ptr(y, ctypes.c_float), _ptr(update, ctypes.c_float), _ptr(gains, ctypes.c_float), iters,
+        exaggeration, momentum, learning_rate, min_gain, max_step_norm, threads, grid_override,
+        ctypes.byref(secs)))
+    return y, update, gains, secs.value
 
 
 def ref_tsne_kl(P: Csr, y, threads=1) -> float:

@@ -519,6 +519,17 @@ int or_tsne_run(const int* row_ptr, const int* col, const float* val, int n, con
   return 0;
 }
 
+void or_tsne_iterate(const int* row_ptr, const int* col, const float* val, int n, float* y,
+                     float* update, float* gains, int iters, float exaggeration, float momentum,
+                     float learning_rate, float min_gain, float max_step_norm, int grid_size) {
+  float* grad = (float*)calloc((size_t)n * 2, sizeof(float));
+  for (int it = 0; it < iters; ++it) {
+    or_tsne_gradient_fft(row_ptr, col, val, n, y, exaggeration, grid_size, grad, NULL);
+    or_tsne_update(y, update, gains, grad, n, learning_rate, momentum, min_gain, max_step_norm);
+  }
+  free(grad);
+}
+
 /* ------------------------------------------------------------------ */
 /* UMAP                                                                */
 /* ------------------------------------------------------------------ */

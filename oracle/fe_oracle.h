@@ -75,6 +75,11 @@ int or_tsne_run(const int* row_ptr, const int* col, const float* val, int n, con
                 float initial_momentum, float final_momentum, float min_gain,
                 float max_step_norm, int grid_size, float* out);
 
+/* The run_phase loop body for `iters` iterations from a given optimizer state. */
+void or_tsne_iterate(const int* row_ptr, const int* col, const float* val, int n, float* y,
+                     float* update, float* gains, int iters, float exaggeration, float momentum,
+                     float learning_rate, float min_gain, float max_step_norm, int grid_size);
+
 /* ---------------- UMAP ---------------- */
 
 /* umap_powf_fast, src/fast_knn_umap.cpp:179-206 (Schraudolph-style exponent interpolation). */

@@ -17,6 +17,7 @@
 
 #include FE_REF_TSNE_SRC
 
+#include <chrono>
 #include <cstdlib>
 #include <string>
 
@@ -180,6 +181,38 @@ int feref_tsne_update(float* y, float* update, float* gains, const float* grad, 
     ParallelExecutorScope scope(&executor);
     apply_open_tsne_update_f(yy, uu, gg, gr, n, 2, learning_rate, momentum, min_gain, max_step_norm, t);
     zero_mean_f(yy, n, 2);
+    std::copy(yy.begin(), yy.end(), y);
+    std::copy(uu.begin(), uu.end(), update);
+    std::copy(gg.begin(), gg.end(), gains);
+  });
+}
+
+// The reference's per-iteration loop body (run_phase, tsne_neighbors.cpp:1753-1771:
+// compute_gradient_f -> apply_open_tsne_update_f -> zero_mean_f) for `iters`
+// iterations with a persistent FFT workspace; *seconds receives the loop's
+// wall time only (no argument marshalling).  The CPU baseline of bench.py.
+int feref_tsne_iterate(const int* row_ptr, const int* col, const float* val, int n, float* y,
+                       float* update, float* gains, int iters, float exaggeration, float momentum,
+                       float learning_rate, float min_gain, float max_step_norm, int threads,
+                       int grid_override, double* seconds) {
+  return guarded([&]() {
+    GridOverride guard(grid_override);
+    SparseProbabilitiesF p = p_from_arrays(row_ptr, col, val, n);
+    const std::size_t m = static_cast<std::size_t>(n) * 2u;
+    std::vector<float> yy(y, y + m), uu(update, update + m), gg(gains, gains + m), grad(m, 0.0f);
+    const int t = resolve_threads(threads, n);
+    ParallelExecutor executor(t);
+    ParallelExecutorScope scope(&executor);
+    FftGridWorkspaceT<float> ws;
+    const auto start = std::chrono::steady_clock::now();
+    for (int it = 0; it < iters; ++it) {
+      compute_gradient_f(p, yy, n, 2, exaggeration, t, "fft_grid", &ws, grad);
+      apply_open_tsne_update_f(yy, uu, gg, grad, n, 2, learning_rate, momentum, min_gain,
+                               max_step_norm, t);
+      zero_mean_f(yy, n, 2);
+    }
+    const auto stop = std::chrono::steady_clock::now();
+    *seconds = std::chrono::duration<double>(stop - start).count();
     std::copy(yy.begin(), yy.end(), y);
     std::copy(uu.begin(), uu.end(), update);
     std::copy(gg.begin(), gg.end(), gains);

@@ -1,0 +1,36 @@
+"""Embedding quality metrics used by the end-to-end parity bars (GPU, via torch).
+
+knn_preservation and label_accuracy follow the definitions of the reference's
+knn_structure_score_cpp (src/embedding_utils.cpp:1386-1520): the mean fraction
+of each point's k high-dimensional neighbours found among its k nearest
+neighbours in the layout, and the mean fraction of those layout neighbours that
+share the point's label.  Evaluated over every point, in row blocks.
+"""
+import numpy as np
+
+
+def layout_knn(y, k, block=4096):
+    import torch
+
+    Y = torch.from_numpy(np.ascontiguousarray(y, np.float32)).cuda()
+    n = Y.shape[0]
+    out = np.empty((n, k), np.int64)
+    for s in range(0, n, block):
+        e = min(n, s + block)
+        d = torch.cdist(Y[s:e], Y)
+        d[torch.arange(e - s, device=Y.device), torch.arange(s, e, device=Y.device)] = float("inf")
+        out[s:e] = torch.topk(d, k, largest=False).indices.cpu().numpy()
+    return out
+
+
+def knn_preservation(y, idx, k=15):
+    nn = layout_knn(y, k)
+    hi = np.asarray(idx)[:, :k]
+    hits = (nn[:, :, None] == hi[:, None, :]).any(-1).sum(1)
+    return float(hits.mean() / k)
+
+
+def label_accuracy(y, labels, k=15):
+    nn = layout_knn(y, k)
+    lab = np.asarray(labels)
+    return float((lab[nn] == lab[:, None]).mean())

@@ -1,0 +1,175 @@
+"""CPU-only checks of the drop-in boundary and the host logic (no GPU needed).
+
+* the C-ABI library loads and exports every function include/fastembedr_b200.h
+  declares (which includes every symbol the reference wrapper links against);
+* calls that fail before touching a device return status 1 with the
+  reference's messages;
+* the host-side parameter policies match the reference.
+"""
+import ctypes
+import re
+
+import numpy as np
+import pytest
+
+import oracle as O
+from fastembedr_b200 import _lib, api
+
+REFERENCE_WRAPPER_SYMBOLS = [
+    # every prototype of the extern "C" block in src/embedding_cuda_impl.cpp:24-380
+    "fastembedr_cuda_available", "fastembedr_cuda_embedding_last_error", "fastembedr_cuda_embed",
+    "fastembedr_cuda_embed_from_knn", "fastembedr_cuda_spectral_init_from_knn",
+    "fastembedr_cuda_exact_tsne_from_knn", "fastembedr_cuda_opentsne_fft_from_knn",
+    "fastembedr_cuda_opentsne_fft_from_knn_float", "fastembedr_cuda_opentsne_fft_from_device_knn_float",
+    "fastembedr_cuda_opentsne_fft_from_device_knn_float_pca_double",
+    "fastembedr_cuda_opentsne_fft_from_device_knn_float_pca_float",
+    "fastembedr_cuda_umap_from_knn_spectral", "fastembedr_cuda_umap_from_knn_spectral_float",
+    "fastembedr_cuda_umap_from_device_knn_spectral_float", "fastembedr_cuda_umap_graph_dump_from_knn",
+    "fastembedr_cuda_umap_optimize_coo", "fastembedr_cuda_landmark_tsne_from_device_knn",
+    "fastembedr_cuda_landmark_umap_from_device_knn", "fastembedr_cuda_standardize_matrix",
+    "fastembedr_cuda_project_embedding", "fastembedr_cuda_interpolate_landmark_layout",
+    "fastembedr_cuda_landmark_project_interpolate_knn_confidence", "fastembedr_cuda_knn_structure_score",
+    "fastembedr_cuda_silhouette_score", "fastembedr_cuda_matrix_multiply",
+    "fastembedr_cuda_raft_tsvd_pca_init",
+]
+
+
+def exported_symbols():
+    import subprocess
+
+    out = subprocess.run(["nm", "-D", "--defined-only", _lib.LIB_PATH], capture_output=True, text=True,
+                         check=True).stdout
+    return {line.split()[-1] for line in out.splitlines() if line.strip()}
+
+
+def test_library_loads_and_exports_header():
+    L = _lib.load()
+    assert L is not None
+    declared = _lib.header_functions()
+    assert len(declared) >= 40
+    exported = exported_symbols()
+    missing = [f for f in declared if f not in exported]
+    assert not missing, missing
+    for f in declared:
+        assert hasattr(L, f)
+
+
+def test_header_covers_reference_wrapper():
+    declared = set(_lib.header_functions())
+    assert set(REFERENCE_WRAPPER_SYMBOLS) <= declared
+
+
+def test_only_the_c_abi_is_exported():
+    exported = exported_symbols()
+    ours = {s for s in exported if re.match(r"^(fastembedr_cuda_|fe_b200_)", s)}
+    assert ours == set(_lib.header_functions())
+    assert not any("fe6" in s or "TsneSession" in s for s in exported)
+
+
+def test_version_string():
+    assert "sm_100a" in api.version()
+
+
+def test_available_false_without_gpu():
+    import torch
+
+    if torch.cuda.is_available():
+        pytest.skip("a GPU is present")
+    assert api.cuda_available() is False
+
+
+@pytest.mark.parametrize("name,nargs", [
+    ("fastembedr_cuda_embed", 14), ("fastembedr_cuda_exact_tsne_from_knn", 16),
+    ("fastembedr_cuda_standardize_matrix", 6), ("fastembedr_cuda_silhouette_score", 6),
+    ("fastembedr_cuda_matrix_multiply", 7), ("fastembedr_cuda_raft_tsvd_pca_init", 5),
+])
+def test_out_of_scope_symbols_fail_cleanly(name, nargs):
+    fn = getattr(_lib.load(), name)
+    fn.restype = ctypes.c_int
+    args = [ctypes.c_void_p(0)] * nargs
+    assert fn(*args) == 1
+    assert "not provided by the B200 backend" in _lib.last_error()
+
+
+def test_pca_init_variant_reports_raft_requirement():
+    fn = _lib.load().fastembedr_cuda_opentsne_fft_from_device_knn_float_pca_float
+    fn.restype = ctypes.c_int
+    assert fn(*([ctypes.c_void_p(0)] * 21)) == 1
+    assert "RAFT" in _lib.last_error()
+
+
+def test_parameter_validation_precedes_device_work():
+    L = _lib.load()
+    out = np.zeros((10, 2), np.float32)
+    fout = out.ctypes.data_as(ctypes.POINTER(ctypes.c_float))
+    idx = np.zeros(30, np.int32)
+    dist = np.ones(30, np.float32)
+    base = [ctypes.c_void_p(idx.ctypes.data), ctypes.c_void_p(dist.ctypes.data), None, 0, 10, 3, 2, 1.0,
+            10, 10, 12.0, 1.0, 0.0, 1, 0.8, 0.8, 0.01, 5.0, 1, 0, fout]
+    cases = {4: 1, 5: 300, 6: 3, 7: 0.0, 8: -1, 10: 0.0, 16: 0.0}
+    for pos, bad in cases.items():
+        args = list(base)
+        args[pos] = bad
+        assert L.fastembedr_cuda_opentsne_fft_from_knn_float(*args) == 1
+        assert _lib.last_error() == "invalid CUDA openTSNE FFT-grid dimensions or parameters"
+    args = list(base)
+    args[0] = None
+    assert L.fastembedr_cuda_opentsne_fft_from_knn_float(*args) == 1
+    assert _lib.last_error() == "null CUDA openTSNE input pointer"
+    args = list(base)
+    args[3] = 1  # has_init without init
+    assert L.fastembedr_cuda_opentsne_fft_from_knn_float(*args) == 1
+
+
+def test_umap_validation_precedes_device_work():
+    with pytest.raises(api.CudaBackendError, match="invalid CUDA COO UMAP optimization parameters"):
+        api.umap_optimize_coo([0], [1], [1.0], [1.0], np.zeros((2, 2), np.float32), n_epochs=0)
+    with pytest.raises(api.CudaBackendError, match="invalid CUDA COO UMAP optimization parameters"):
+        api.umap_optimize_coo([0], [1], [1.0], [1.0], np.zeros((2, 2), np.float32), learning_rate=0.0)
+    with pytest.raises(ValueError):
+        api.umap_optimize_coo([0, 1], [1], [1.0], [1.0], np.zeros((2, 2), np.float32))
+
+
+def test_tsne_auto_parameters_policy():
+    # Values asserted by the reference's own tests (tests/testthat/test-tsne.R:31-56).
+    p = api.tsne_auto_parameters(150, 30, None)
+    assert p["perplexity"] == 10 and p["learning_rate"] == 150 / p["early_exaggeration"]
+    assert api.tsne_auto_parameters(70000, 90, None)["perplexity"] == 30
+    assert api.tsne_auto_parameters(10000, 90, 30.0)["learning_rate"] == pytest.approx(10000 / 12)
+
+
+@pytest.mark.skipif(not O.ref_available(), reason="compiled reference not present")
+@pytest.mark.parametrize("n,k,perp,missing", [(150, 30, 0.0, True), (70000, 90, 0.0, True),
+                                              (1000, 45, 15.0, False), (50, 200, 80.0, False)])
+def test_tsne_auto_parameters_against_reference(n, k, perp, missing):
+    ref = O.ref_tsne_auto_parameters(n, k, perp, missing)
+    ours = api.tsne_auto_parameters(n, k, None if missing else perp)
+    for key in ("perplexity", "n_neighbors", "early_exaggeration", "learning_rate",
+                "early_exaggeration_iter", "n_iter"):
+        assert ours[key] == pytest.approx(ref[key]), key
+
+
+def test_find_ab_params_matches_reference(umap_scalar_golden):
+    g = umap_scalar_golden
+    for md, (a, b) in zip(g["ab_min_dist"], g["ab"]):
+        ra, rb = api.find_ab_params(1.0, float(md))
+        assert ra == pytest.approx(a, rel=1e-12) and rb == pytest.approx(b, rel=1e-12)
+
+
+def test_index_offset_detection():
+    assert api.resolve_index_offset(np.array([[1, 2], [2, 1]])) == 1
+    assert api.resolve_index_offset(np.array([[0, 1], [1, 0]])) == 0
+    assert api.resolve_index_offset(np.array([[1, 3], [2, 1]])) == 0  # 3 > n
+
+
+def test_synthetic_configs_shapes():
+    from fastembedr_b200 import synthetic as S
+
+    x, lab = S.gaussian_mixture(S.MixtureSpec(n=500, components=5, dirichlet_weights=True, anisotropic=True))
+    assert x.shape == (500, 50) and x.dtype == np.float32 and lab.max() < 5
+    idx, dist = S.exact_knn(x, 10)
+    assert idx.shape == (500, 10) and (idx != np.arange(500)[:, None]).all()
+    assert (np.diff(dist, axis=1) >= 0).all()
+    d = np.linalg.norm(x[:, None, :].astype(np.float64) - x[None, :, :], axis=-1)
+    np.fill_diagonal(d, np.inf)
+    np.testing.assert_allclose(np.sort(d, axis=1)[:, :10], dist, rtol=1e-5)

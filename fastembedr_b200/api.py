@@ -305,8 +305,8 @@ class TsneSession:
     def p(self):
         inf = self.info()
         rp = np.zeros(inf["n"] + 1, np.int32)
-        c = np.zeros(inf["nnz_padded"], np.int32)
-        v = np.zeros(inf["nnz_padded"], np.float32)
+        c = np.zeros(inf["nnz"], np.int32)
+        v = np.zeros(inf["nnz"], np.float32)
         check(_lib.load().fe_b200_tsne_get_p(self._h, _ptr(rp, ctypes.c_int), _ptr(c, ctypes.c_int),
                                              _ptr(v, ctypes.c_float)), "fe_b200_tsne_get_p")
         nnz = int(rp[-1])

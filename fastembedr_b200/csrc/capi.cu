@@ -99,7 +99,7 @@ int opentsne_impl(const int* indices, const void* distances, bool dist_double, c
   int* row_ptr = nullptr;
   int* col = nullptr;
   float* val = nullptr;
-  long long nnz = 0, nnz_pad = 0;
+  long long nnz = 0;
   {
     DeviceCopy d_idx, d_dist;
     const int* idx_dev = indices;
@@ -112,10 +112,10 @@ int opentsne_impl(const int* indices, const void* distances, bool dist_double, c
       dist_dev = d_dist.p;
     }
     FE_TRY(fe::build_p_device(idx_dev, dist_dev, dist_double, n, k, index_offset, perplexity, stream,
-                              &row_ptr, &col, &val, &nnz, &nnz_pad));
+                              &row_ptr, &col, &val, &nnz));
   }
   fe::TsneSession* s = nullptr;
-  if (fe::session_create(&s, n, resolve_grid(n, 0), row_ptr, col, val, nnz, nnz_pad, stream)) {
+  if (fe::session_create(&s, n, resolve_grid(n, 0), row_ptr, col, val, nnz, stream)) {
     cudaFree(row_ptr);
     cudaFree(col);
     cudaFree(val);
@@ -364,7 +364,7 @@ int fe_b200_tsne_create(const int* indices, const float* distances, int n, int k
   int* row_ptr = nullptr;
   int* col = nullptr;
   float* val = nullptr;
-  long long nnz = 0, nnz_pad = 0;
+  long long nnz = 0;
   int rc = 0;
   {
     DeviceCopy d_idx, d_dist;
@@ -379,11 +379,11 @@ int fe_b200_tsne_create(const int* indices, const float* distances, int n, int k
     }
     if (rc == 0) {
       rc = fe::build_p_device(idx_dev, dist_dev, false, n, k, index_offset, perplexity, stream, &row_ptr,
-                              &col, &val, &nnz, &nnz_pad);
+                              &col, &val, &nnz);
     }
   }
   fe::TsneSession* s = nullptr;
-  if (rc == 0) rc = fe::session_create(&s, n, resolve_grid(n, grid_size), row_ptr, col, val, nnz, nnz_pad, nullptr);
+  if (rc == 0) rc = fe::session_create(&s, n, resolve_grid(n, grid_size), row_ptr, col, val, nnz, nullptr);
   if (rc != 0) {
     if (s == nullptr) {
       if (row_ptr) cudaFree(row_ptr);
@@ -416,10 +416,10 @@ int fe_b200_tsne_create_csr(const int* row_ptr, const int* col, const float* val
   int* d_rp = nullptr;
   int* d_col = nullptr;
   float* d_val = nullptr;
-  long long nnz = 0, nnz_pad = 0;
-  FE_TRY(fe::upload_csr_padded(row_ptr, col, val, n, nullptr, &d_rp, &d_col, &d_val, &nnz, &nnz_pad));
+  long long nnz = 0;
+  FE_TRY(fe::upload_csr(row_ptr, col, val, n, nullptr, &d_rp, &d_col, &d_val, &nnz));
   fe::TsneSession* s = nullptr;
-  if (fe::session_create(&s, n, resolve_grid(n, grid_size), d_rp, d_col, d_val, nnz, nnz_pad, nullptr)) {
+  if (fe::session_create(&s, n, resolve_grid(n, grid_size), d_rp, d_col, d_val, nnz, nullptr)) {
     cudaFree(d_rp);
     cudaFree(d_col);
     cudaFree(d_val);
@@ -449,11 +449,7 @@ int fe_b200_tsne_gradient(fe_b200_tsne* h, float exaggeration, float* grad, doub
     set_error("invalid t-SNE session call");
     return 1;
   }
-  // The gradient is evaluated at the stored layout exactly as given (no re-centring).
-  fe::TsneSession* s = h->impl;
-  FE_TRY(fe::launch_stats(s, 0));
-  FE_TRY(fe::session_gradient(s, exaggeration, grad, z));
-  return fe::launch_stats(s, 1);
+  return fe::session_gradient(h->impl, exaggeration, grad, z);
 }
 
 int fe_b200_tsne_get_layout(fe_b200_tsne* h, float* out, int on_device) {
@@ -471,16 +467,8 @@ int fe_b200_tsne_set_layout(fe_b200_tsne* h, const float* y, int on_device, int 
     set_error("invalid t-SNE session call");
     return 1;
   }
-  fe::TsneSession* s = h->impl;
-  FE_TRY(fe::session_set_layout(s, y, on_device == 0, true));
-  if (reset_state) {
-    std::vector<float> ones(static_cast<size_t>(s->n) * 2, 1.0f);
-    FE_CUDA(cudaMemsetAsync(s->update, 0, sizeof(float2) * s->n, s->stream), "memset update");
-    FE_CUDA(cudaMemcpyAsync(s->gains, ones.data(), sizeof(float2) * s->n, cudaMemcpyHostToDevice, s->stream),
-            "reset gains");
-    FE_CUDA(cudaStreamSynchronize(s->stream), "cudaStreamSynchronize(reset)");
-  }
-  return 0;
+  FE_TRY(fe::session_set_layout(h->impl, y, on_device == 0, true));
+  return reset_state ? fe::session_reset_state(h->impl) : 0;
 }
 
 int fe_b200_tsne_get_state(fe_b200_tsne* h, float* update, float* gains) {
@@ -489,11 +477,7 @@ int fe_b200_tsne_get_state(fe_b200_tsne* h, float* update, float* gains) {
     set_error("invalid t-SNE session call");
     return 1;
   }
-  fe::TsneSession* s = h->impl;
-  FE_CUDA(cudaMemcpyAsync(update, s->update, sizeof(float2) * s->n, cudaMemcpyDeviceToHost, s->stream), "D2H update");
-  FE_CUDA(cudaMemcpyAsync(gains, s->gains, sizeof(float2) * s->n, cudaMemcpyDeviceToHost, s->stream), "D2H gains");
-  FE_CUDA(cudaStreamSynchronize(s->stream), "cudaStreamSynchronize(state)");
-  return 0;
+  return fe::session_get_state(h->impl, update, gains, true);
 }
 
 int fe_b200_tsne_set_state(fe_b200_tsne* h, const float* update, const float* gains) {
@@ -502,11 +486,7 @@ int fe_b200_tsne_set_state(fe_b200_tsne* h, const float* update, const float* ga
     set_error("invalid t-SNE session call");
     return 1;
   }
-  fe::TsneSession* s = h->impl;
-  FE_CUDA(cudaMemcpyAsync(s->update, update, sizeof(float2) * s->n, cudaMemcpyHostToDevice, s->stream), "H2D update");
-  FE_CUDA(cudaMemcpyAsync(s->gains, gains, sizeof(float2) * s->n, cudaMemcpyHostToDevice, s->stream), "H2D gains");
-  FE_CUDA(cudaStreamSynchronize(s->stream), "cudaStreamSynchronize(state)");
-  return 0;
+  return fe::session_set_state(h->impl, update, gains, true);
 }
 
 int fe_b200_tsne_info(fe_b200_tsne* h, int* n, int* grid, long long* nnz, long long* nnz_padded) {
@@ -517,7 +497,7 @@ int fe_b200_tsne_info(fe_b200_tsne* h, int* n, int* grid, long long* nnz, long l
   if (n) *n = h->impl->n;
   if (grid) *grid = h->impl->grid;
   if (nnz) *nnz = h->impl->nnz;
-  if (nnz_padded) *nnz_padded = h->impl->nnz_pad;
+  if (nnz_padded) *nnz_padded = 4 * h->impl->csr4_groups;
   return 0;
 }
 
@@ -527,28 +507,7 @@ int fe_b200_tsne_get_p(fe_b200_tsne* h, int* row_ptr, int* col, float* val) {
     set_error("invalid t-SNE session call");
     return 1;
   }
-  fe::TsneSession* s = h->impl;
-  std::vector<int> rp(static_cast<size_t>(s->n) + 1);
-  std::vector<int> c(static_cast<size_t>(s->nnz_pad));
-  std::vector<float> v(static_cast<size_t>(s->nnz_pad));
-  FE_CUDA(cudaMemcpyAsync(rp.data(), s->row_ptr, sizeof(int) * rp.size(), cudaMemcpyDeviceToHost, s->stream), "D2H");
-  FE_CUDA(cudaMemcpyAsync(c.data(), s->col, sizeof(int) * c.size(), cudaMemcpyDeviceToHost, s->stream), "D2H");
-  FE_CUDA(cudaMemcpyAsync(v.data(), s->val, sizeof(float) * v.size(), cudaMemcpyDeviceToHost, s->stream), "D2H");
-  FE_CUDA(cudaStreamSynchronize(s->stream), "cudaStreamSynchronize(get_p)");
-  // Strip the (col = row, val = 0) padding entries at the end of each row.
-  long long w = 0;
-  row_ptr[0] = 0;
-  for (int r = 0; r < s->n; ++r) {
-    int end = rp[r + 1];
-    while (end > rp[r] && c[end - 1] == r && v[end - 1] == 0.0f) --end;
-    for (int t = rp[r]; t < end; ++t) {
-      col[w] = c[t];
-      val[w] = v[t];
-      ++w;
-    }
-    row_ptr[r + 1] = static_cast<int>(w);
-  }
-  return 0;
+  return fe::session_get_p(h->impl, row_ptr, col, val);
 }
 
 void* fe_b200_tsne_stream(fe_b200_tsne* h) { return h == nullptr ? nullptr : h->impl->stream; }

@@ -83,6 +83,15 @@ int env_int(const char* name, int fallback) {
   return static_cast<int>(v);
 }
 
+int env_int_nonneg(const char* name, int fallback) {
+  const char* raw = std::getenv(name);
+  if (raw == nullptr || raw[0] == '\0') return fallback;
+  char* end = nullptr;
+  const long v = std::strtol(raw, &end, 10);
+  if (end == raw || v < 0 || v > 1 << 30) return fallback;
+  return static_cast<int>(v);
+}
+
 bool env_flag(const char* name, bool fallback) {
   const char* raw = std::getenv(name);
   if (raw == nullptr || raw[0] == '\0') return fallback;

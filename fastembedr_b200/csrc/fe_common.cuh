@@ -94,7 +94,8 @@ int memory_preflight(std::size_t bytes, const char* where);
 int sm_count();
 
 // Environment helpers.
-int env_int(const char* name, int fallback);
+int env_int(const char* name, int fallback);         // positive values only
+int env_int_nonneg(const char* name, int fallback);  // zero allowed
 bool env_flag(const char* name, bool fallback);
 
 }  // namespace fe

@@ -1,13 +1,13 @@
 // openTSNE-style FFT-grid t-SNE optimizer for B200: data layout and kernels.
 //
 // Layout in HBM (one session = one embedding run):
-//   P        symmetric CSR (row_ptr int32[n+1], col int32[nnz_pad], val f32[nnz_pad]);
-//            every row is padded to a multiple of 4 entries with (col=row,
-//            val=0) so the attraction kernel streams 16-byte vectors.
+//   P        symmetric CSR in the caller's order (row_ptr int32[n+1], col int32[nnz],
+//            val f32[nnz]) and a copy in the internal (spatial) order with rows
+//            padded to groups of four entries, streamed as int4 / float4.
 //   y[2]     float2[n] double-buffered layout (the gradient of iteration t
 //            reads y[cur] while the fused update writes y[cur^1]).
 //   update, gains  float2[n]
-//   charges  float4[G*G]   bilinear charges {1, x, y, 0} per grid node
+//   charges  ChargeCell[G*G]  bilinear charges {1, x, y} per grid node, 64-bit fixed point
 //   rowspec  float2[G][G+1][3]  x-half-spectra of the three charge planes
 //   krow     float2[G][G+1]     x-transforms of the q and q^2 kernel rows
 //   colspec  float2[G][G+1][4]  y-inverted products (q2, xq2, yq2, q)
@@ -26,6 +26,11 @@
 namespace fe {
 
 // Layout statistics carried between kernels (device resident).
+// One grid node's charges {sum w, sum w x, sum w y} in fixed point (+ pad to 32 B).
+struct ChargeCell {
+  unsigned long long m, mx, my, pad;
+};
+
 struct LayoutStats {
   double sum_x, sum_y;        // sums of the raw (uncentred) layout
   float min_x, max_x;         // bounds of the raw layout
@@ -72,6 +77,30 @@ __device__ __forceinline__ GridGeom grid_geometry(const LayoutStats& s, int n, i
   return q;
 }
 
+// Charges are accumulated in signed 64-bit fixed point, so the splat's
+// atomics are associative and the result does not depend on their order
+// (runs are bit-reproducible).  Scales are powers of two chosen so that the
+// largest possible node total stays below 2^62: sum of weights <= n, and
+// |x|, |y| <= the grid box half extent.
+struct ChargeScales {
+  double m;   // weight scale
+  double xy;  // coordinate-weighted scale
+};
+__device__ __forceinline__ double pow2_scale_for(double max_total) {
+  int e = 0;
+  frexp(fmax(max_total, 1.0), &e);  // max_total < 2^e
+  return ldexp(1.0, 62 - e);
+}
+__device__ __forceinline__ ChargeScales charge_scales(const GridGeom& q, int n, int g) {
+  const float extent = q.spacing * static_cast<float>(g - 1);
+  const double xmax = fmax(fmax(fabs(static_cast<double>(q.lower_x)), fabs(static_cast<double>(q.lower_x) + extent)),
+                           fmax(fabs(static_cast<double>(q.lower_y)), fabs(static_cast<double>(q.lower_y) + extent)));
+  ChargeScales c;
+  c.m = pow2_scale_for(static_cast<double>(n));
+  c.xy = pow2_scale_for(static_cast<double>(n) * (xmax + 1.0));
+  return c;
+}
+
 // Clamped grid coordinates, cell origin and bilinear fractions of a point
 // (src/tsne_neighbors.cpp:1114-1128 and 760-775 use the same expressions).
 struct Cell {
@@ -103,14 +132,23 @@ struct TsneSession {
   int fft = 0;        // M = 2G
   int log_fft = 0;
   long long nnz = 0;      // symmetric entries (both directions)
-  long long nnz_pad = 0;  // after 4-entry row padding
   cudaStream_t stream = nullptr;
   bool own_stream = false;
   Arena arena;
 
+  // P in the caller's point order: unpadded CSR, columns ascending (the
+  // reference's CSR exactly).  Canonical copy; never permuted.
   int* row_ptr = nullptr;
   int* col = nullptr;
   float* val = nullptr;
+  // P in the internal point order, rows contiguous and padded to whole groups
+  // of four entries with (col = row, val = 0): row r occupies groups
+  // row_ptr4[r] .. row_ptr4[r+1]-1 of csr4_col / csr4_val (int4 / float4).
+  int* row_ptr4 = nullptr;         // n + 1 offsets, in 16-byte groups
+  int4* csr4_col = nullptr;
+  float4* csr4_val = nullptr;
+  long long csr4_groups = 0;       // groups in use
+  long long csr4_capacity = 0;     // groups allocated
   float2* y[2] = {nullptr, nullptr};
   int cur = 0;
   float2* update = nullptr;
@@ -119,7 +157,7 @@ struct TsneSession {
   LayoutStats* stats = nullptr;
   double* update_partials = nullptr;  // 6 per block
   double* z_partials = nullptr;       // one per grid row
-  float4* charges = nullptr;
+  ChargeCell* charges = nullptr;
   float2* rowspec = nullptr;
   float2* krow = nullptr;
   float2* colspec = nullptr;
@@ -144,6 +182,14 @@ struct TsneSession {
   int graph_cur = 0;
   float graph_params[5] = {0};
   bool use_graphs = true;
+
+  // Spatial ordering: internal point r is the caller's point perm[r], and
+  // caller point i is internal point rank[i].
+  int* perm = nullptr;
+  int* rank = nullptr;
+  bool identity_perm = true;
+  int reorder_every = 0;          // iterations between reorders (0 = never)
+  long long next_reorder = 0;
 };
 
 enum KernelKind {
@@ -157,21 +203,21 @@ enum KernelKind {
 const char* kernel_kind_name(int kind);
 
 // ---- P construction (tsne_affinity.cu) ----
-// Builds the padded symmetric CSR on the device from column-major KNN.
-// dist_is_double selects the element type of `dist`.  Temporaries are freed
-// before returning; the CSR arrays are allocated with cudaMalloc into *out_*.
+// Builds the symmetric CSR (caller order, columns ascending) on the device
+// from column-major KNN.  dist_is_double selects the element type of `dist`.
+// Temporaries are freed before returning; the CSR arrays are allocated with
+// cudaMalloc into *out_*.
 int build_p_device(const int* d_idx, const void* d_dist, bool dist_is_double, int n, int k,
                    int index_offset, float perplexity, cudaStream_t stream, int** out_row_ptr,
-                   int** out_col, float** out_val, long long* out_nnz, long long* out_nnz_pad);
+                   int** out_col, float** out_val, long long* out_nnz);
 
-// Pads and uploads a host CSR (parity hooks).
-int upload_csr_padded(const int* row_ptr, const int* col, const float* val, int n,
-                      cudaStream_t stream, int** out_row_ptr, int** out_col, float** out_val,
-                      long long* out_nnz, long long* out_nnz_pad);
+// Validates and uploads a host CSR (parity hooks, resume).
+int upload_csr(const int* row_ptr, const int* col, const float* val, int n, cudaStream_t stream,
+               int** out_row_ptr, int** out_col, float** out_val, long long* out_nnz);
 
 // ---- session (tsne_session.cu) ----
 int session_create(TsneSession** out, int n, int grid, int* d_row_ptr, int* d_col, float* d_val,
-                   long long nnz, long long nnz_pad, cudaStream_t stream);
+                   long long nnz, cudaStream_t stream);
 void session_destroy(TsneSession* s);
 int session_set_layout(TsneSession* s, const float* y, bool host, bool center);
 int session_random_layout(TsneSession* s, unsigned int seed);
@@ -179,6 +225,21 @@ int session_iterate(TsneSession* s, int iters, float exaggeration, float momentu
                     float learning_rate, float min_gain, float max_step_norm);
 int session_gradient(TsneSession* s, float exaggeration, float* grad_host, double* z_out);
 int session_get_layout(TsneSession* s, float* out, bool host);
+// Optimizer state in the caller's point order.
+int session_set_state(TsneSession* s, const float* update, const float* gains, bool host);
+int session_get_state(TsneSession* s, float* update, float* gains, bool host);
+int session_reset_state(TsneSession* s);
+// Unpadded CSR P in the caller's point order, columns ascending.
+int session_get_p(TsneSession* s, int* row_ptr, int* col, float* val);
+
+// ---- ordering and the internal copy of P (tsne_reorder.cu) ----
+// Chooses the internal point order -- Morton order of the current layout when
+// by_layout, else the caller's order -- permutes the point arrays, and
+// rebuilds the internal-order, group-padded copy of P from the caller CSR.
+int session_reorder(TsneSession* s, bool by_layout);
+// out[perm[r]] = in[r] (internal -> caller order) and out[r] = in[perm[r]].
+int launch_unpermute(TsneSession* s, const float2* in, float2* out);
+int launch_permute_in(TsneSession* s, const float2* in, float2* out);
 
 // ---- kernels (tsne_kernels.cu) ----
 // Raises per-kernel dynamic shared-memory limits for this session's FFT size.

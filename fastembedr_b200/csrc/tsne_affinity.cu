@@ -155,38 +155,10 @@ __global__ void row_bounds_kernel(const unsigned long long* __restrict__ keys, l
   for (int t = rp + 1; t <= r; ++t) row_start[t] = static_cast<int>(i);
 }
 
-__global__ void padded_lengths_kernel(const int* __restrict__ row_start, int n,
-                                      int* __restrict__ plen) {
-  const int r = blockIdx.x * blockDim.x + threadIdx.x;
-  if (r >= n) return;
-  const int len = row_start[r + 1] - row_start[r];
-  plen[r] = (len + 3) & ~3;
-}
-
-__global__ void scatter_padded_kernel(const unsigned long long* __restrict__ keys,
-                                      const float* __restrict__ vals, long long m,
-                                      const int* __restrict__ row_start,
-                                      const int* __restrict__ row_ptr_pad, int* __restrict__ col,
-                                      float* __restrict__ val) {
+__global__ void split_keys_kernel(const unsigned long long* __restrict__ keys, long long m,
+                                  int* __restrict__ col) {
   const long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x;
-  if (i >= m) return;
-  const int r = static_cast<int>(keys[i] >> 32);
-  const int dst = row_ptr_pad[r] + static_cast<int>(i - row_start[r]);
-  col[dst] = static_cast<int>(keys[i] & 0xffffffffull);
-  val[dst] = vals[i];
-}
-
-__global__ void fill_padding_kernel(const int* __restrict__ row_start,
-                                    const int* __restrict__ row_ptr_pad, int n,
-                                    int* __restrict__ col, float* __restrict__ val) {
-  const int r = blockIdx.x * blockDim.x + threadIdx.x;
-  if (r >= n) return;
-  const int len = row_start[r + 1] - row_start[r];
-  const int beg = row_ptr_pad[r];
-  for (int t = len; t < row_ptr_pad[r + 1] - beg; ++t) {
-    col[beg + t] = r;
-    val[beg + t] = 0.0f;
-  }
+  if (i < m) col[i] = static_cast<int>(keys[i] & 0xffffffffull);
 }
 
 template <typename T>
@@ -209,44 +181,20 @@ inline unsigned blocks_for(long long m, int threads) {
   return static_cast<unsigned>((m + threads - 1) / threads);
 }
 
-// Sorted (row, col) entry list -> padded CSR.
-int assemble_padded(const unsigned long long* d_keys, const float* d_vals, long long m, int n,
-                    cudaStream_t stream, int** out_row_ptr, int** out_col, float** out_val,
-                    long long* out_nnz_pad) {
-  DevBuf<int> row_start, plen, row_ptr;
-  FE_TRY(row_start.alloc(n + 1, "cudaMalloc(row_start)"));
-  FE_TRY(plen.alloc(n + 1, "cudaMalloc(padded lengths)"));
+// Sorted (row, col) entry list -> CSR; the values array is adopted as is.
+int assemble_csr(const unsigned long long* d_keys, float* d_vals, long long m, int n,
+                 cudaStream_t stream, int** out_row_ptr, int** out_col) {
+  DevBuf<int> row_ptr, col;
   FE_TRY(row_ptr.alloc(n + 1, "cudaMalloc(row_ptr)"));
-  row_bounds_kernel<<<blocks_for(m + 1, 256), 256, 0, stream>>>(d_keys, m, n, row_start.p);
+  FE_TRY(col.alloc(m, "cudaMalloc(P col)"));
+  row_bounds_kernel<<<blocks_for(m + 1, 256), 256, 0, stream>>>(d_keys, m, n, row_ptr.p);
   FE_LAUNCH("row_bounds_kernel");
-  padded_lengths_kernel<<<blocks_for(n, 256), 256, 0, stream>>>(row_start.p, n, plen.p);
-  FE_LAUNCH("padded_lengths_kernel");
-  FE_CUDA(cudaMemsetAsync(plen.p + n, 0, sizeof(int), stream), "cudaMemsetAsync(plen tail)");
-  size_t temp_bytes = 0;
-  FE_CUDA(cub::DeviceScan::ExclusiveSum(nullptr, temp_bytes, plen.p, row_ptr.p, n + 1, stream),
-          "cub::DeviceScan(sizing)");
-  DevBuf<unsigned char> temp;
-  FE_TRY(temp.alloc(temp_bytes, "cudaMalloc(scan temp)"));
-  FE_CUDA(cub::DeviceScan::ExclusiveSum(temp.p, temp_bytes, plen.p, row_ptr.p, n + 1, stream),
-          "cub::DeviceScan(padded row_ptr)");
-  int nnz_pad = 0;
-  FE_CUDA(cudaMemcpyAsync(&nnz_pad, row_ptr.p + n, sizeof(int), cudaMemcpyDeviceToHost, stream),
-          "cudaMemcpyAsync(nnz_pad)");
-  FE_CUDA(cudaStreamSynchronize(stream), "cudaStreamSynchronize(assemble)");
-  DevBuf<int> col;
-  DevBuf<float> val;
-  FE_TRY(col.alloc(static_cast<size_t>(nnz_pad), "cudaMalloc(P col)"));
-  FE_TRY(val.alloc(static_cast<size_t>(nnz_pad), "cudaMalloc(P val)"));
-  scatter_padded_kernel<<<blocks_for(m, 256), 256, 0, stream>>>(d_keys, d_vals, m, row_start.p,
-                                                                row_ptr.p, col.p, val.p);
-  FE_LAUNCH("scatter_padded_kernel");
-  fill_padding_kernel<<<blocks_for(n, 256), 256, 0, stream>>>(row_start.p, row_ptr.p, n, col.p, val.p);
-  FE_LAUNCH("fill_padding_kernel");
-  FE_CUDA(cudaStreamSynchronize(stream), "cudaStreamSynchronize(P scatter)");
+  split_keys_kernel<<<blocks_for(m, 256), 256, 0, stream>>>(d_keys, m, col.p);
+  FE_LAUNCH("split_keys_kernel");
+  FE_CUDA(cudaStreamSynchronize(stream), "cudaStreamSynchronize(P assemble)");
   *out_row_ptr = row_ptr.release();
   *out_col = col.release();
-  *out_val = val.release();
-  *out_nnz_pad = nnz_pad;
+  (void)d_vals;
   return 0;
 }
 
@@ -254,7 +202,7 @@ int assemble_padded(const unsigned long long* d_keys, const float* d_vals, long 
 
 int build_p_device(const int* d_idx, const void* d_dist, bool dist_is_double, int n, int k,
                    int index_offset, float perplexity, cudaStream_t stream, int** out_row_ptr,
-                   int** out_col, float** out_val, long long* out_nnz, long long* out_nnz_pad) {
+                   int** out_col, float** out_val, long long* out_nnz) {
   const long long m = static_cast<long long>(n) * k;
   if (m >= (1ll << 31) - 1) {
     set_error("t-SNE affinities: n*k exceeds the 32-bit entry range");
@@ -359,56 +307,44 @@ int build_p_device(const int* d_idx, const void* d_dist, bool dist_is_double, in
             "cub::DeviceRadixSort(directed keys)");
     FE_CUDA(cudaStreamSynchronize(stream), "cudaStreamSynchronize(directed sort)");
   }
-  FE_TRY(assemble_padded(k2s.p, v2s.p, m2, n, stream, out_row_ptr, out_col, out_val, out_nnz_pad));
+  FE_TRY(assemble_csr(k2s.p, v2s.p, m2, n, stream, out_row_ptr, out_col));
+  *out_val = v2s.release();
   *out_nnz = m2;
   return 0;
 }
 
-int upload_csr_padded(const int* row_ptr, const int* col, const float* val, int n,
-                      cudaStream_t stream, int** out_row_ptr, int** out_col, float** out_val,
-                      long long* out_nnz, long long* out_nnz_pad) {
-  std::vector<int> rp(static_cast<size_t>(n) + 1, 0);
+int upload_csr(const int* row_ptr, const int* col, const float* val, int n, cudaStream_t stream,
+               int** out_row_ptr, int** out_col, float** out_val, long long* out_nnz) {
+  if (row_ptr[0] != 0) {
+    set_error("CSR row_ptr must start at 0");
+    return 1;
+  }
   for (int r = 0; r < n; ++r) {
-    const int len = row_ptr[r + 1] - row_ptr[r];
-    if (len < 0) {
+    if (row_ptr[r + 1] < row_ptr[r]) {
       set_error("CSR row_ptr is not monotone");
       return 1;
     }
-    rp[r + 1] = rp[r] + ((len + 3) & ~3);
   }
-  const size_t nnz_pad = static_cast<size_t>(rp[n]);
-  std::vector<int> c(nnz_pad);
-  std::vector<float> v(nnz_pad);
-  for (int r = 0; r < n; ++r) {
-    const int len = row_ptr[r + 1] - row_ptr[r];
-    for (int t = 0; t < len; ++t) {
-      const int j = col[row_ptr[r] + t];
-      if (j < 0 || j >= n) {
-        set_error("CSR column index out of range");
-        return 1;
-      }
-      c[rp[r] + t] = j;
-      v[rp[r] + t] = val[row_ptr[r] + t];
-    }
-    for (int t = len; t < rp[r + 1] - rp[r]; ++t) {
-      c[rp[r] + t] = r;
-      v[rp[r] + t] = 0.0f;
+  const size_t nnz = static_cast<size_t>(row_ptr[n]);
+  for (size_t t = 0; t < nnz; ++t) {
+    if (col[t] < 0 || col[t] >= n) {
+      set_error("CSR column index out of range");
+      return 1;
     }
   }
   DevBuf<int> d_rp, d_c;
   DevBuf<float> d_v;
   FE_TRY(d_rp.alloc(n + 1, "cudaMalloc(row_ptr)"));
-  FE_TRY(d_c.alloc(nnz_pad, "cudaMalloc(col)"));
-  FE_TRY(d_v.alloc(nnz_pad, "cudaMalloc(val)"));
-  FE_CUDA(cudaMemcpyAsync(d_rp.p, rp.data(), sizeof(int) * (n + 1), cudaMemcpyHostToDevice, stream), "H2D row_ptr");
-  FE_CUDA(cudaMemcpyAsync(d_c.p, c.data(), sizeof(int) * nnz_pad, cudaMemcpyHostToDevice, stream), "H2D col");
-  FE_CUDA(cudaMemcpyAsync(d_v.p, v.data(), sizeof(float) * nnz_pad, cudaMemcpyHostToDevice, stream), "H2D val");
+  FE_TRY(d_c.alloc(nnz, "cudaMalloc(col)"));
+  FE_TRY(d_v.alloc(nnz, "cudaMalloc(val)"));
+  FE_CUDA(cudaMemcpyAsync(d_rp.p, row_ptr, sizeof(int) * (n + 1), cudaMemcpyHostToDevice, stream), "H2D row_ptr");
+  FE_CUDA(cudaMemcpyAsync(d_c.p, col, sizeof(int) * nnz, cudaMemcpyHostToDevice, stream), "H2D col");
+  FE_CUDA(cudaMemcpyAsync(d_v.p, val, sizeof(float) * nnz, cudaMemcpyHostToDevice, stream), "H2D val");
   FE_CUDA(cudaStreamSynchronize(stream), "cudaStreamSynchronize(csr upload)");
   *out_row_ptr = d_rp.release();
   *out_col = d_c.release();
   *out_val = d_v.release();
-  *out_nnz = row_ptr[n];
-  *out_nnz_pad = static_cast<long long>(nnz_pad);
+  *out_nnz = static_cast<long long>(nnz);
   return 0;
 }
 

@@ -10,16 +10,18 @@
 // inverse FFT pass reduces directly.
 //
 // Kernels (all on the session stream):
-//   splat_kernel           centres the layout in place and spreads {1,x,y}
-//                          with 16-byte vector atomics (red.global.add.v4.f32)
+//   splat_kernel           centres the layout in place and spreads {1,x,y};
+//                          lanes sharing a cell combine first, then 64-bit
+//                          fixed-point atomics (order-independent, reproducible)
 //   fft_rows_fwd_kernel    x-direction real FFTs of the charge rows and of the
 //                          kernel rows (the kernels are even, so their
 //                          transforms are real)
 //   fft_cols_kernel        y-direction FFT, multiply by the real kernel
 //                          spectra, inverse y-FFT -- one column tile per block
 //   fft_rows_inv_kernel    inverse x-FFTs -> potentials, Z, and clears charges
-//   grad_update_kernel     CSR attraction (warp per row, 16-byte streaming
-//                          loads), repulsive gather, gains/momentum/step clip,
+//   grad_update_kernel     attraction (8 lanes per row, 16-byte streaming
+//                          loads, next pass prefetched), repulsive gather,
+//                          gains / momentum / step clip,
 //                          layout write and layout statistics for the next
 //                          iteration (last-block reduction, no second launch)
 #include "tsne.cuh"
@@ -228,34 +230,79 @@ __global__ void layout_stats_kernel(const float2* __restrict__ y, int n, double*
 
 // ------------------------------------------------------------------ splat
 
+__device__ __forceinline__ void add_fixed(unsigned long long* dst, float v, double scale) {
+  const long long q = __double2ll_rn(static_cast<double>(v) * scale);
+  if (q != 0) atomicAdd(dst, static_cast<unsigned long long>(q));
+}
+
+// One thread per point.  Lanes of a warp whose points share a grid cell
+// (common: the layout is compact early on, and points are stored in Morton
+// order later) first sum their 12 contributions in lane order, then the
+// lowest such lane adds the sums with 64-bit integer atomics.
 __global__ void splat_kernel(float2* __restrict__ y, const LayoutStats* __restrict__ stats, int n,
-                             int g, float4* __restrict__ charges) {
+                             int g, ChargeCell* __restrict__ charges) {
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= n) return;
+  const int lane = threadIdx.x & 31;
   const GridGeom q = grid_geometry(*stats, n, g);
-  float2 p = y[i];
-  if (stats->center) {
-    p.x -= q.mean_x;
-    p.y -= q.mean_y;
-    y[i] = p;
+  int key = -1;
+  float v[12];
+#pragma unroll
+  for (int t = 0; t < 12; ++t) v[t] = 0.0f;
+  if (i < n) {
+    float2 p = y[i];
+    if (stats->center) {
+      p.x -= q.mean_x;
+      p.y -= q.mean_y;
+      y[i] = p;
+    }
+    const Cell c = grid_cell(p.x, p.y, q, g);
+    key = c.y0 * g + c.x0;
+    const float w[4] = {(1.0f - c.tx) * (1.0f - c.ty), c.tx * (1.0f - c.ty), (1.0f - c.tx) * c.ty,
+                        c.tx * c.ty};
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      v[3 * k] = w[k];
+      v[3 * k + 1] = w[k] * p.x;
+      v[3 * k + 2] = w[k] * p.y;
+    }
   }
-  const Cell c = grid_cell(p.x, p.y, q, g);
-  const float w00 = (1.0f - c.tx) * (1.0f - c.ty);
-  const float w10 = c.tx * (1.0f - c.ty);
-  const float w01 = (1.0f - c.tx) * c.ty;
-  const float w11 = c.tx * c.ty;
-  float4* base = charges + static_cast<size_t>(c.y0) * g + c.x0;
-  atomicAdd(base, make_float4(w00, w00 * p.x, w00 * p.y, 0.0f));
-  atomicAdd(base + 1, make_float4(w10, w10 * p.x, w10 * p.y, 0.0f));
-  atomicAdd(base + g, make_float4(w01, w01 * p.x, w01 * p.y, 0.0f));
-  atomicAdd(base + g + 1, make_float4(w11, w11 * p.x, w11 * p.y, 0.0f));
+  const unsigned int peers = __match_any_sync(0xffffffffu, key);
+  const int leader = __ffs(peers) - 1;
+  if (__popc(peers) > 1) {
+    float s[12];
+#pragma unroll
+    for (int t = 0; t < 12; ++t) s[t] = 0.0f;
+    for (unsigned int m = peers; m; m &= m - 1) {
+      const int src = __ffs(m) - 1;
+#pragma unroll
+      for (int t = 0; t < 12; ++t) s[t] += __shfl_sync(peers, v[t], src);
+    }
+#pragma unroll
+    for (int t = 0; t < 12; ++t) v[t] = s[t];
+  }
+  if (key < 0 || lane != leader) return;
+  const ChargeScales sc = charge_scales(q, n, g);
+  const int corner[4] = {key, key + 1, key + g, key + g + 1};
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    ChargeCell* cell = charges + corner[k];
+    add_fixed(&cell->m, v[3 * k], sc.m);
+    add_fixed(&cell->mx, v[3 * k + 1], sc.xy);
+    add_fixed(&cell->my, v[3 * k + 2], sc.xy);
+  }
+}
+
+__device__ __forceinline__ float3 read_charge(const ChargeCell& c, const ChargeScales& sc) {
+  return make_float3(static_cast<float>(static_cast<double>(static_cast<long long>(c.m)) / sc.m),
+                     static_cast<float>(static_cast<double>(static_cast<long long>(c.mx)) / sc.xy),
+                     static_cast<float>(static_cast<double>(static_cast<long long>(c.my)) / sc.xy));
 }
 
 // ------------------------------------------------------------------ FFT passes
 
 // Row r of the three charge planes and kernel row dy = r.  Packs
 // (m + i mx), (my + i Kq), (Kq2) into three complex length-M FFTs.
-__global__ void fft_rows_fwd_kernel(const float4* __restrict__ charges,
+__global__ void fft_rows_fwd_kernel(const ChargeCell* __restrict__ charges,
                                     const LayoutStats* __restrict__ stats, int n, int g, int m,
                                     int log_m, const float2* __restrict__ tw,
                                     float2* __restrict__ rowspec, float2* __restrict__ krow) {
@@ -265,9 +312,10 @@ __global__ void fft_rows_fwd_kernel(const float4* __restrict__ charges,
   float2* z2 = smem + 2 * m;
   const int r = blockIdx.x;
   const GridGeom q = grid_geometry(*stats, n, g);
+  const ChargeScales sc = charge_scales(q, n, g);
   for (int x = threadIdx.x; x < m; x += blockDim.x) {
-    float4 c = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (x < g) c = charges[static_cast<size_t>(r) * g + x];
+    float3 c = make_float3(0.f, 0.f, 0.f);
+    if (x < g) c = read_charge(charges[static_cast<size_t>(r) * g + x], sc);
     float kq = 0.f, kq2 = 0.f;
     if (x <= g - 1) {
       kernel_values(x, r, q.spacing, &kq, &kq2);
@@ -365,7 +413,7 @@ __global__ void fft_cols_kernel(const float2* __restrict__ rowspec, const float2
 // Output row r: inverse x-FFTs of (phi_q2 + i phi_xq2) and (phi_yq2 + i phi_q)
 // from their half spectra, potentials, this row's share of Z, and clearing of
 // the charges for the next splat.  The last block folds Z.
-__global__ void fft_rows_inv_kernel(const float2* __restrict__ colspec, float4* __restrict__ charges,
+__global__ void fft_rows_inv_kernel(const float2* __restrict__ colspec, ChargeCell* __restrict__ charges,
                                     int n, int g, int m, int log_m, const float2* __restrict__ tw,
                                     float4* __restrict__ pot, double* __restrict__ z_partials,
                                     LayoutStats* __restrict__ stats) {
@@ -374,6 +422,7 @@ __global__ void fft_rows_inv_kernel(const float2* __restrict__ colspec, float4* 
   float2* z1 = smem + m;
   const int r = blockIdx.x;
   const int row_len = g + 1;
+  const double inv_scale_m = 1.0 / charge_scales(grid_geometry(*stats, n, g), n, g).m;
   for (int k = threadIdx.x; k < m; k += blockDim.x) {
     const bool mirror = k > g;
     const int kk = mirror ? m - k : k;
@@ -397,9 +446,9 @@ __global__ void fft_rows_inv_kernel(const float2* __restrict__ colspec, float4* 
     const float4 p = make_float4(a.x * scale, a.y * scale, b.x * scale, b.y * scale);
     const size_t cell = static_cast<size_t>(r) * g + x;
     pot[cell] = p;
-    const float4 ch = charges[cell];
-    zpart += static_cast<double>(ch.x) * static_cast<double>(p.w);
-    charges[cell] = make_float4(0.f, 0.f, 0.f, 0.f);
+    const double mass = static_cast<double>(static_cast<long long>(charges[cell].m)) * inv_scale_m;
+    zpart += mass * static_cast<double>(p.w);
+    charges[cell] = ChargeCell{0ull, 0ull, 0ull, 0ull};
   }
   __shared__ double s_part[32];
   __shared__ bool s_last;
@@ -466,77 +515,125 @@ __device__ __forceinline__ float3 gather_potentials(const float4* __restrict__ p
   return r;
 }
 
-// One warp owns 32 consecutive rows: it sweeps their CSR rows one after the
-// other with all lanes (4 entries per lane per pass via 16-byte loads), keeps
-// row r's attraction in lane r, then every lane runs its row's epilogue.
-__global__ void __launch_bounds__(256) grad_update_kernel(
-    const int* __restrict__ row_ptr, const int4* __restrict__ col4, const float4* __restrict__ val4,
+// Attraction over the internal-order P, eight lanes per row: a warp takes a
+// block of 32 rows in 8 rounds of 4 rows.  Each pass a lane streams two
+// 16-byte groups of columns and two of values (stride 8 groups within its
+// row), gathers the eight y_j and accumulates; the next pass's loads are
+// issued before the current pass's gathers (FE_ATTRACT_PREFETCH).  Three xor
+// shuffles reduce a row's eight partial sums, and the row's sum is parked in
+// one lane so that the epilogue -- repulsive gather, gains/momentum/step clip,
+// layout write, statistics for the next iteration -- runs 32 rows wide.
+#ifndef FE_ATTRACT_PREFETCH
+#define FE_ATTRACT_PREFETCH 1
+#endif
+
+__device__ __forceinline__ void attract4(float yix, float yiy, int4 c, float4 v, float ex,
+                                         const float2* __restrict__ y, float& ax, float& ay) {
+  const float2 g0 = __ldg(y + c.x), g1 = __ldg(y + c.y), g2 = __ldg(y + c.z), g3 = __ldg(y + c.w);
+  const float2 g[4] = {g0, g1, g2, g3};
+  const float pv[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const float dx = yix - g[q].x;
+    const float dy = yiy - g[q].y;
+    float d2 = 0.0f;
+    d2 += dx * dx;
+    d2 += dy * dy;
+    const float qq = 1.0f / (1.0f + d2);
+    const float w = ex * pv[q] * qq;
+    ax += w * dx;
+    ay += w * dy;
+  }
+}
+
+// 64 registers (4 blocks of 256 per SM): measured faster than the unbounded
+// 78-register build despite a few spilled bytes.
+__global__ void __launch_bounds__(256, 4) grad_update_kernel(
+    const int* __restrict__ row_ptr4, const int4* __restrict__ col4, const float4* __restrict__ val4,
     const float2* __restrict__ y, float2* __restrict__ y_next, float2* __restrict__ update,
     float2* __restrict__ gains, float2* __restrict__ grad_out, const float4* __restrict__ pot,
     LayoutStats* __restrict__ stats, double* __restrict__ partials, UpdateParams prm) {
   const int lane = threadIdx.x & 31;
+  const int sub = lane >> 3;  // which of the 4 rows of a round
+  const int sl = lane & 7;    // lane within the row
   const int warps_per_block = blockDim.x >> 5;
   const int warp_global = blockIdx.x * warps_per_block + (threadIdx.x >> 5);
   const int n_warps = gridDim.x * warps_per_block;
-  const GridGeom q = grid_geometry(*stats, prm.n, prm.g);
-  const float inv_z = stats->inv_z;
+  const float ex = prm.exaggeration;
+  const int4 zero_c = make_int4(0, 0, 0, 0);
+  const float4 zero_v = make_float4(0.f, 0.f, 0.f, 0.f);
   StatsAcc acc;
   stats_init(acc);
-
   for (int row0 = warp_global * 32; row0 < prm.n; row0 += n_warps * 32) {
-    const int my_row = row0 + lane;
-    const bool active = my_row < prm.n;
-    const int my_beg = active ? row_ptr[my_row] : 0;
-    const int my_end = active ? row_ptr[my_row + 1] : 0;
-    const float2 my_y = active ? y[my_row] : make_float2(0.f, 0.f);
     float my_ax = 0.f, my_ay = 0.f;
-    const int rows = min(32, prm.n - row0);
-    for (int r = 0; r < rows; ++r) {
-      const int beg = __shfl_sync(0xffffffffu, my_beg, r) >> 2;
-      const int end = __shfl_sync(0xffffffffu, my_end, r) >> 2;
-      const float yix = __shfl_sync(0xffffffffu, my_y.x, r);
-      const float yiy = __shfl_sync(0xffffffffu, my_y.y, r);
+#pragma unroll 1
+    for (int it = 0; it < 8; ++it) {
+      const int row = row0 + 4 * it + sub;
+      const bool rv = row < prm.n;
+      const int beg = rv ? __ldg(row_ptr4 + row) : 0;
+      const int end = rv ? __ldg(row_ptr4 + row + 1) : 0;
+      const float2 yi = rv ? y[row] : make_float2(0.f, 0.f);
+      int passes = (end - beg + 15) >> 4;
+      passes = max(passes, __shfl_xor_sync(0xffffffffu, passes, 8));
+      passes = max(passes, __shfl_xor_sync(0xffffffffu, passes, 16));
       float ax = 0.f, ay = 0.f;
-      for (int e = beg + lane; e < end; e += 32) {
-        const int4 c = ld_stream(col4 + e);
-        const float4 v = ld_stream(val4 + e);
-        const float2 y0 = __ldg(y + c.x), y1 = __ldg(y + c.y), y2 = __ldg(y + c.z), y3 = __ldg(y + c.w);
-#define FE_ATTRACT(yj, pv)                                   \
-  {                                                          \
-    const float dx = yix - yj.x;                             \
-    const float dy = yiy - yj.y;                             \
-    const float d2 = dx * dx + dy * dy;                      \
-    const float qq = 1.0f / (1.0f + d2);                     \
-    const float w = prm.exaggeration * (pv) * qq;            \
-    ax += w * dx;                                            \
-    ay += w * dy;                                            \
-  }
-        FE_ATTRACT(y0, v.x)
-        FE_ATTRACT(y1, v.y)
-        FE_ATTRACT(y2, v.z)
-        FE_ATTRACT(y3, v.w)
-#undef FE_ATTRACT
+      int e = beg + sl;
+#if FE_ATTRACT_PREFETCH
+      int4 c0 = e < end ? ld_stream(col4 + e) : zero_c;
+      float4 v0 = e < end ? ld_stream(val4 + e) : zero_v;
+      int4 c1 = e + 8 < end ? ld_stream(col4 + e + 8) : zero_c;
+      float4 v1 = e + 8 < end ? ld_stream(val4 + e + 8) : zero_v;
+      for (int p = 0; p < passes; ++p) {
+        const int en = e + 16;
+        const int4 nc0 = en < end ? ld_stream(col4 + en) : zero_c;
+        const float4 nv0 = en < end ? ld_stream(val4 + en) : zero_v;
+        const int4 nc1 = en + 8 < end ? ld_stream(col4 + en + 8) : zero_c;
+        const float4 nv1 = en + 8 < end ? ld_stream(val4 + en + 8) : zero_v;
+        attract4(yi.x, yi.y, c0, v0, ex, y, ax, ay);
+        attract4(yi.x, yi.y, c1, v1, ex, y, ax, ay);
+        c0 = nc0;
+        v0 = nv0;
+        c1 = nc1;
+        v1 = nv1;
+        e = en;
       }
-      ax = warp_sum(ax);
-      ay = warp_sum(ay);
-      if (lane == r) {
+#else
+      for (int p = 0; p < passes; ++p, e += 16) {
+        const int4 c0 = e < end ? ld_stream(col4 + e) : zero_c;
+        const float4 v0 = e < end ? ld_stream(val4 + e) : zero_v;
+        const int4 c1 = e + 8 < end ? ld_stream(col4 + e + 8) : zero_c;
+        const float4 v1 = e + 8 < end ? ld_stream(val4 + e + 8) : zero_v;
+        attract4(yi.x, yi.y, c0, v0, ex, y, ax, ay);
+        attract4(yi.x, yi.y, c1, v1, ex, y, ax, ay);
+      }
+#endif
+#pragma unroll
+      for (int o = 4; o > 0; o >>= 1) {
+        ax += __shfl_xor_sync(0xffffffffu, ax, o);
+        ay += __shfl_xor_sync(0xffffffffu, ay, o);
+      }
+      if (sl == it) {
         my_ax = ax;
         my_ay = ay;
       }
     }
-    if (!active) continue;
-    // Repulsion from the potentials at this point's grid position.
-    const Cell c = grid_cell(my_y.x, my_y.y, q, prm.g);
+    // Epilogue: lane L finishes row row0 + 4 (L % 8) + L / 8.
+    const int row = row0 + 4 * sl + sub;
+    if (row >= prm.n) continue;
+    const float2 yi = y[row];
+    const GridGeom q = grid_geometry(*stats, prm.n, prm.g);
+    const Cell c = grid_cell(yi.x, yi.y, q, prm.g);
     const float3 ph = gather_potentials(pot, c, prm.g);
-    const float gx = -(my_y.x * ph.x - ph.y) * inv_z + my_ax;
-    const float gy = -(my_y.y * ph.x - ph.z) * inv_z + my_ay;
+    const float inv_z = stats->inv_z;
+    const float gx = -(yi.x * ph.x - ph.y) * inv_z + my_ax;
+    const float gy = -(yi.y * ph.x - ph.z) * inv_z + my_ay;
     if (prm.mode == kGradOnly) {
-      grad_out[my_row] = make_float2(gx, gy);
+      grad_out[row] = make_float2(gx, gy);
       continue;
     }
     // apply_open_tsne_update_f, src/tsne_neighbors.cpp:1213-1244.
-    float2 u = update[my_row];
-    float2 gn = gains[my_row];
+    float2 u = update[row];
+    float2 gn = gains[row];
     if (sign_f(u.x) != sign_f(gx)) gn.x += 0.2f;
     else gn.x = gn.x * 0.8f + prm.min_gain;
     if (gn.x < prm.min_gain) gn.x = prm.min_gain;
@@ -548,17 +645,26 @@ __global__ void __launch_bounds__(256) grad_update_kernel(
     float norm_sq = 0.0f;
     norm_sq += u.x * u.x;
     norm_sq += u.y * u.y;
-    float scale = 1.0f;
     if (isfinite(prm.max_step_norm) && prm.max_step_norm > 0.0f &&
         norm_sq > prm.max_step_norm * prm.max_step_norm) {
-      scale = prm.max_step_norm / sqrtf(fmaxf(norm_sq, FLT_MIN));
+      if (isfinite(norm_sq)) {
+        const float scale = prm.max_step_norm / sqrtf(fmaxf(norm_sq, FLT_MIN));
+        u.x *= scale;
+        u.y *= scale;
+      } else {
+        // An infinite step (Z collapsed to FLT_MIN): the reference's clip would
+        // form inf * 0; keep the step's direction at the maximum length instead.
+        const float sx = isinf(u.x) ? copysignf(1.0f, u.x) : 0.0f;
+        const float sy = isinf(u.y) ? copysignf(1.0f, u.y) : 0.0f;
+        const float len = sqrtf(sx * sx + sy * sy);
+        u.x = len > 0.0f ? sx / len * prm.max_step_norm : 0.0f;
+        u.y = len > 0.0f ? sy / len * prm.max_step_norm : 0.0f;
+      }
     }
-    u.x *= scale;
-    u.y *= scale;
-    const float2 yn = make_float2(my_y.x + u.x, my_y.y + u.y);
-    update[my_row] = u;
-    gains[my_row] = gn;
-    y_next[my_row] = yn;
+    const float2 yn = make_float2(yi.x + u.x, yi.y + u.y);
+    update[row] = u;
+    gains[row] = gn;
+    y_next[row] = yn;
     stats_add(acc, yn);
   }
   if (prm.mode == kGradUpdate) {
@@ -669,9 +775,8 @@ int launch_iteration(TsneSession* s, GradMode mode, float exaggeration, float mo
     UpdateParams prm{s->n, g, exaggeration, momentum, learning_rate, min_gain, max_step_norm,
                      static_cast<int>(mode)};
     grad_update_kernel<<<s->update_blocks, s->update_threads, 0, s->stream>>>(
-        s->row_ptr, reinterpret_cast<const int4*>(s->col), reinterpret_cast<const float4*>(s->val),
-        s->y[s->cur], s->y[s->cur ^ 1], s->update, s->gains, s->grad_out, s->pot, s->stats,
-        s->update_partials, prm);
+        s->row_ptr4, s->csr4_col, s->csr4_val, s->y[s->cur], s->y[s->cur ^ 1], s->update,
+        s->gains, s->grad_out, s->pot, s->stats, s->update_partials, prm);
     FE_LAUNCH("grad_update_kernel");
   }
   if (mode == kGradUpdate) s->cur ^= 1;

@@ -1,0 +1,223 @@
+// Internal point order and the internal copy of P.
+//
+// The optimizer's arithmetic does not depend on the order in which points are
+// stored; its memory behaviour does.  The attraction kernel gathers y_j for
+// every entry of P, the splat scatters into the grid and the repulsion gathers
+// potentials.  Storing points in Morton (Z-curve) order of their grid position
+// makes all three local -- KNN neighbours end up close in the layout, hence
+// close in memory -- so y_j gathers hit L1/L2 and lanes of a warp touch
+// neighbouring grid nodes.
+//
+// P is kept twice: the caller-order CSR (canonical, never permuted) and an
+// internal-order copy, rows padded to whole 16-byte groups, that the
+// attraction kernel streams.  A reorder
+//   1. sorts points by a 30-bit Morton key of the current layout (or keeps the
+//      caller's order for the first build),
+//   2. permutes the layout, optimizer state and permutation arrays,
+//   3. rebuilds the internal copy from the caller-order CSR: internal row r is
+//      caller row perm[r], with columns renamed through rank.
+#include "tsne.cuh"
+
+#include <cub/cub.cuh>
+
+#include <algorithm>
+
+namespace fe {
+namespace {
+
+__device__ __forceinline__ unsigned int spread_bits_15(unsigned int v) {
+  v &= 0x7fffu;
+  v = (v | (v << 8)) & 0x00ff00ffu;
+  v = (v | (v << 4)) & 0x0f0f0f0fu;
+  v = (v | (v << 2)) & 0x33333333u;
+  v = (v | (v << 1)) & 0x55555555u;
+  return v;
+}
+
+__global__ void morton_keys_kernel(const float2* __restrict__ y, const LayoutStats* __restrict__ stats,
+                                   int n, int g, int by_layout, unsigned int* __restrict__ keys,
+                                   int* __restrict__ idx) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  idx[i] = i;
+  if (!by_layout) {
+    keys[i] = 0u;  // a stable sort keeps the current order
+    return;
+  }
+  const GridGeom q = grid_geometry(*stats, n, g);
+  float2 p = y[i];
+  p.x -= q.mean_x;
+  p.y -= q.mean_y;
+  const float extent = q.spacing * static_cast<float>(g - 1);
+  const float sx = fminf(fmaxf((p.x - q.lower_x) / extent, 0.0f), 1.0f);
+  const float sy = fminf(fmaxf((p.y - q.lower_y) / extent, 0.0f), 1.0f);
+  const unsigned int ix = min(32767u, static_cast<unsigned int>(sx * 32767.0f));
+  const unsigned int iy = min(32767u, static_cast<unsigned int>(sy * 32767.0f));
+  keys[i] = spread_bits_15(ix) | (spread_bits_15(iy) << 1);
+}
+
+// order[r] = old internal index now at r.  New perm/rank, point arrays and the
+// padded row lengths (in groups of four entries).
+__global__ void permute_points_kernel(const int* __restrict__ order, int n, const int* __restrict__ perm_in,
+                                      int* __restrict__ perm_out, int* __restrict__ rank_out,
+                                      const int* __restrict__ row_ptr, int* __restrict__ groups,
+                                      const float2* __restrict__ y_in, float2* __restrict__ y_out,
+                                      const float2* __restrict__ u_in, float2* __restrict__ u_out,
+                                      const float2* __restrict__ g_in, float2* __restrict__ g_out) {
+  const int r = blockIdx.x * blockDim.x + threadIdx.x;
+  if (r >= n) return;
+  const int o = order[r];
+  const int caller = perm_in[o];
+  perm_out[r] = caller;
+  rank_out[caller] = r;
+  groups[r] = (row_ptr[caller + 1] - row_ptr[caller] + 3) >> 2;
+  y_out[r] = y_in[o];
+  u_out[r] = u_in[o];
+  g_out[r] = g_in[o];
+}
+
+// One warp per internal row: coalesced copy of caller row perm[r] with renamed
+// columns, padded with (own row, 0) to a whole group.
+__global__ void fill_rows_kernel(const int* __restrict__ perm, const int* __restrict__ rank,
+                                 const int* __restrict__ row_ptr, const int* __restrict__ col,
+                                 const float* __restrict__ val, int n, const int* __restrict__ row_ptr4,
+                                 int* __restrict__ out_col, float* __restrict__ out_val) {
+  const long long gid = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int r = static_cast<int>(gid >> 5);
+  const int lane = static_cast<int>(gid & 31);
+  if (r >= n) return;
+  const int caller = perm[r];
+  const int beg = row_ptr[caller];
+  const int len = row_ptr[caller + 1] - beg;
+  const long long dst = static_cast<long long>(row_ptr4[r]) * 4;
+  const int padded = (row_ptr4[r + 1] - row_ptr4[r]) * 4;
+  for (int e = lane; e < padded; e += 32) {
+    if (e < len) {
+      out_col[dst + e] = rank[col[beg + e]];
+      out_val[dst + e] = val[beg + e];
+    } else {
+      out_col[dst + e] = r;
+      out_val[dst + e] = 0.0f;
+    }
+  }
+}
+
+__global__ void unpermute_kernel(const float2* __restrict__ in, const int* __restrict__ perm, int n,
+                                 float2* __restrict__ out) {
+  const int r = blockIdx.x * blockDim.x + threadIdx.x;
+  if (r < n) out[perm[r]] = in[r];
+}
+
+__global__ void permute_in_kernel(const float2* __restrict__ in, const int* __restrict__ perm, int n,
+                                  float2* __restrict__ out) {
+  const int r = blockIdx.x * blockDim.x + threadIdx.x;
+  if (r < n) out[r] = in[perm[r]];
+}
+
+}  // namespace
+
+int session_reorder(TsneSession* s, bool by_layout) {
+  const int n = s->n;
+  const unsigned blocks = static_cast<unsigned>((n + 255) / 256);
+  cudaStream_t st = s->stream;
+
+  // Scratch (freed on return): keys, indices, order, new perm/rank, lengths,
+  // point temporaries, CUB temp.
+  size_t sort_bytes = 0, scan_bytes = 0;
+  FE_CUDA(cub::DeviceRadixSort::SortPairs(nullptr, sort_bytes, static_cast<unsigned int*>(nullptr),
+                                          static_cast<unsigned int*>(nullptr), static_cast<int*>(nullptr),
+                                          static_cast<int*>(nullptr), n, 0, 30, st),
+          "cub::DeviceRadixSort(sizing)");
+  FE_CUDA(cub::DeviceScan::ExclusiveSum(nullptr, scan_bytes, static_cast<int*>(nullptr),
+                                        static_cast<int*>(nullptr), n + 1, st),
+          "cub::DeviceScan(sizing)");
+  const size_t temp_bytes = std::max(sort_bytes, scan_bytes);
+  const size_t need = 2 * align_up(sizeof(unsigned int) * n) + 4 * align_up(sizeof(int) * n) +
+                      align_up(sizeof(int) * (n + 1)) + 2 * align_up(sizeof(float2) * n) +
+                      align_up(temp_bytes);
+  void* scratch = nullptr;
+  FE_CUDA(cudaMalloc(&scratch, need), "cudaMalloc(reorder scratch)");
+  struct Free {
+    void* q;
+    ~Free() { cudaFree(q); }
+  } free_scratch{scratch};
+  char* p = static_cast<char*>(scratch);
+  auto carve = [&p](size_t bytes) {
+    char* q = p;
+    p += align_up(bytes);
+    return q;
+  };
+  unsigned int* keys = reinterpret_cast<unsigned int*>(carve(sizeof(unsigned int) * n));
+  unsigned int* keys_sorted = reinterpret_cast<unsigned int*>(carve(sizeof(unsigned int) * n));
+  int* idx = reinterpret_cast<int*>(carve(sizeof(int) * n));
+  int* order = reinterpret_cast<int*>(carve(sizeof(int) * n));
+  int* perm_new = reinterpret_cast<int*>(carve(sizeof(int) * n));
+  int* rank_new = reinterpret_cast<int*>(carve(sizeof(int) * n));
+  int* groups = reinterpret_cast<int*>(carve(sizeof(int) * (n + 1)));
+  float2* u_tmp = reinterpret_cast<float2*>(carve(sizeof(float2) * n));
+  float2* g_tmp = reinterpret_cast<float2*>(carve(sizeof(float2) * n));
+  void* temp = carve(temp_bytes);
+
+  const int cur = s->cur;
+  morton_keys_kernel<<<blocks, 256, 0, st>>>(s->y[cur], s->stats, n, s->grid, by_layout ? 1 : 0, keys, idx);
+  FE_LAUNCH("morton_keys_kernel");
+  size_t tb = temp_bytes;
+  FE_CUDA(cub::DeviceRadixSort::SortPairs(temp, tb, keys, keys_sorted, idx, order, n, 0, 30, st),
+          "cub::DeviceRadixSort(morton)");
+  float2* y_new = s->y[cur ^ 1];
+  permute_points_kernel<<<blocks, 256, 0, st>>>(order, n, s->perm, perm_new, rank_new, s->row_ptr, groups,
+                                                s->y[cur], y_new, s->update, u_tmp, s->gains, g_tmp);
+  FE_LAUNCH("permute_points_kernel");
+  FE_CUDA(cudaMemcpyAsync(s->update, u_tmp, sizeof(float2) * n, cudaMemcpyDeviceToDevice, st), "permute update");
+  FE_CUDA(cudaMemcpyAsync(s->gains, g_tmp, sizeof(float2) * n, cudaMemcpyDeviceToDevice, st), "permute gains");
+  FE_CUDA(cudaMemcpyAsync(s->perm, perm_new, sizeof(int) * n, cudaMemcpyDeviceToDevice, st), "permute perm");
+  FE_CUDA(cudaMemcpyAsync(s->rank, rank_new, sizeof(int) * n, cudaMemcpyDeviceToDevice, st), "permute rank");
+  s->cur = cur ^ 1;
+  FE_CUDA(cudaMemsetAsync(groups + n, 0, sizeof(int), st), "memset");
+  tb = temp_bytes;
+  FE_CUDA(cub::DeviceScan::ExclusiveSum(temp, tb, groups, s->row_ptr4, n + 1, st), "cub::DeviceScan(row_ptr4)");
+  int total = 0;
+  FE_CUDA(cudaMemcpyAsync(&total, s->row_ptr4 + n, sizeof(int), cudaMemcpyDeviceToHost, st), "D2H");
+  FE_CUDA(cudaStreamSynchronize(st), "cudaStreamSynchronize(reorder)");
+  if (total < 0) {
+    set_error("padded P exceeds the 32-bit group range");
+    return 1;
+  }
+  if (total > s->csr4_capacity) {
+    if (s->csr4_col) cudaFree(s->csr4_col);
+    if (s->csr4_val) cudaFree(s->csr4_val);
+    s->csr4_col = nullptr;
+    s->csr4_val = nullptr;
+    FE_TRY(memory_preflight(static_cast<size_t>(total) * 32, "padded P preflight"));
+    FE_CUDA(cudaMalloc(&s->csr4_col, sizeof(int4) * static_cast<size_t>(total)), "cudaMalloc(P cols)");
+    FE_CUDA(cudaMalloc(&s->csr4_val, sizeof(float4) * static_cast<size_t>(total)), "cudaMalloc(P vals)");
+    s->csr4_capacity = total;
+  }
+  s->csr4_groups = total;
+  const unsigned warp_blocks = static_cast<unsigned>((static_cast<long long>(n) * 32 + 255) / 256);
+  fill_rows_kernel<<<warp_blocks, 256, 0, st>>>(s->perm, s->rank, s->row_ptr, s->col, s->val, n, s->row_ptr4,
+                                                reinterpret_cast<int*>(s->csr4_col),
+                                                reinterpret_cast<float*>(s->csr4_val));
+  FE_LAUNCH("fill_rows_kernel");
+  FE_CUDA(cudaStreamSynchronize(st), "cudaStreamSynchronize(fill rows)");
+  s->identity_perm = false;
+  if (s->graph) {
+    cudaGraphExecDestroy(s->graph);
+    s->graph = nullptr;
+  }
+  return 0;
+}
+
+int launch_unpermute(TsneSession* s, const float2* in, float2* out) {
+  unpermute_kernel<<<(s->n + 255) / 256, 256, 0, s->stream>>>(in, s->perm, s->n, out);
+  FE_LAUNCH("unpermute_kernel");
+  return 0;
+}
+
+int launch_permute_in(TsneSession* s, const float2* in, float2* out) {
+  permute_in_kernel<<<(s->n + 255) / 256, 256, 0, s->stream>>>(in, s->perm, s->n, out);
+  FE_LAUNCH("permute_in_kernel");
+  return 0;
+}
+
+}  // namespace fe

@@ -1,9 +1,12 @@
 // t-SNE session: owns the device state of one optimisation run and drives the
-// per-iteration kernel sequence (optionally as a CUDA graph per phase chunk).
+// per-iteration kernel sequence (as CUDA graphs of iteration chunks), the
+// periodic spatial reordering, and the caller-order views of its state.
 #include "tsne.cuh"
 
+#include <algorithm>
 #include <cmath>
 #include <cstring>
+#include <utility>
 #include <vector>
 
 namespace fe {
@@ -39,10 +42,40 @@ __global__ void fill_float2_kernel(float2* p, int n, float2 v) {
   if (i < n) p[i] = v;
 }
 
+__global__ void iota_kernel(int* p, int n) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) p[i] = i;
+}
+
 int ilog2(int v) {
   int l = 0;
   while ((1 << l) < v) ++l;
   return l;
+}
+
+// Copies a caller-order float2 array (host or device) into internal order at dst.
+int load_caller_order(TsneSession* s, const float* src, bool host, float2* dst, float2* scratch) {
+  const size_t bytes = sizeof(float2) * s->n;
+  const cudaMemcpyKind kind = host ? cudaMemcpyHostToDevice : cudaMemcpyDeviceToDevice;
+  if (s->identity_perm) {
+    FE_CUDA(cudaMemcpyAsync(dst, src, bytes, kind, s->stream), "copy in");
+    return 0;
+  }
+  FE_CUDA(cudaMemcpyAsync(scratch, src, bytes, kind, s->stream), "copy in");
+  return launch_permute_in(s, scratch, dst);
+}
+
+// Copies an internal-order device array into caller order at dst (host or device).
+int store_caller_order(TsneSession* s, const float2* src, bool host, float* dst, float2* scratch) {
+  const size_t bytes = sizeof(float2) * s->n;
+  const cudaMemcpyKind kind = host ? cudaMemcpyDeviceToHost : cudaMemcpyDeviceToDevice;
+  if (!s->identity_perm) {
+    FE_TRY(launch_unpermute(s, src, scratch));
+    src = scratch;
+  }
+  FE_CUDA(cudaMemcpyAsync(dst, src, bytes, kind, s->stream), "copy out");
+  FE_CUDA(cudaStreamSynchronize(s->stream), "cudaStreamSynchronize(copy out)");
+  return 0;
 }
 
 }  // namespace
@@ -56,7 +89,7 @@ int default_grid_size(int n) {
 }
 
 int session_create(TsneSession** out, int n, int grid, int* d_row_ptr, int* d_col, float* d_val,
-                   long long nnz, long long nnz_pad, cudaStream_t stream) {
+                   long long nnz, cudaStream_t stream) {
   *out = nullptr;
   if (grid < 4 || (grid & (grid - 1)) != 0 || grid > 1024) {
     set_error("t-SNE FFT grid size must be a power of two in [4, 1024]");
@@ -69,11 +102,14 @@ int session_create(TsneSession** out, int n, int grid, int* d_row_ptr, int* d_co
   s->fft = grid * 2;
   s->log_fft = ilog2(s->fft);
   s->nnz = nnz;
-  s->nnz_pad = nnz_pad;
   s->row_ptr = d_row_ptr;
   s->col = d_col;
   s->val = d_val;
   s->use_graphs = env_flag("FASTEMBEDR_CUDA_GRAPH_CAPTURE", true);
+  // Spatial reordering pays once gathers start missing the caches.
+  s->reorder_every = env_int_nonneg("FASTEMBEDR_B200_REORDER_EVERY", n >= 4096 ? 50 : 0);
+  if (!env_flag("FASTEMBEDR_B200_REORDER", true)) s->reorder_every = 0;
+  s->next_reorder = s->reorder_every;
   if (stream == nullptr) {
     if (check_cuda(cudaStreamCreateWithFlags(&s->stream, cudaStreamNonBlocking), "cudaStreamCreate")) {
       delete s;
@@ -84,10 +120,10 @@ int session_create(TsneSession** out, int n, int grid, int* d_row_ptr, int* d_co
     s->stream = stream;
   }
 
-  // Launch shape of the fused gradient/update kernel: persistent blocks sized
-  // to the measured occupancy on this device.
+  // Fused gradient/update kernel: a warp per block of 32 rows, persistent
+  // blocks of 8 warps, 8 blocks per SM.
   s->update_threads = 256;
-  s->update_blocks = sm_count() * 8;  // 2048 resident threads per SM
+  s->update_blocks = sm_count() * 8;
   s->update_blocks = std::max(1, std::min(s->update_blocks, (n + 255) / 256));
   const int m = s->fft;
   s->cols_per_block = std::max(1, std::min(16, 2048 / m));
@@ -110,10 +146,13 @@ int session_create(TsneSession** out, int n, int grid, int* d_row_ptr, int* d_co
     s->update = a.take<float2>(n);
     s->gains = a.take<float2>(n);
     s->grad_out = a.take<float2>(n);
+    s->perm = a.take<int>(n);
+    s->rank = a.take<int>(n);
+    s->row_ptr4 = a.take<int>(static_cast<size_t>(n) + 1);
     s->stats = a.take<LayoutStats>(1);
     s->update_partials = a.take<double>(6 * static_cast<size_t>(stat_blocks));
     s->z_partials = a.take<double>(g);
-    s->charges = a.take<float4>(cells);
+    s->charges = a.take<ChargeCell>(cells);
     s->rowspec = a.take<float2>(3 * spec);
     s->krow = a.take<float2>(spec);
     s->colspec = a.take<float2>(4 * spec);
@@ -134,14 +173,17 @@ int session_create(TsneSession** out, int n, int grid, int* d_row_ptr, int* d_co
   if (check_cuda(cudaMemcpyAsync(s->twiddle, tw.data(), sizeof(float2) * tw.size(),
                                  cudaMemcpyHostToDevice, s->stream), "H2D twiddles") ||
       check_cuda(cudaMemsetAsync(s->stats, 0, sizeof(LayoutStats), s->stream), "memset stats") ||
-      check_cuda(cudaMemsetAsync(s->charges, 0, sizeof(float4) * cells, s->stream), "memset charges") ||
-      check_cuda(cudaMemsetAsync(s->update, 0, sizeof(float2) * n, s->stream), "memset update") ||
-      check_cuda(cudaStreamSynchronize(s->stream), "cudaStreamSynchronize(session)")) {
+      check_cuda(cudaMemsetAsync(s->charges, 0, sizeof(ChargeCell) * cells, s->stream), "memset charges") ||
+      check_cuda(cudaMemsetAsync(s->update, 0, sizeof(float2) * n, s->stream), "memset update")) {
     session_destroy(s);
     return 1;
   }
   fill_float2_kernel<<<(n + 255) / 256, 256, 0, s->stream>>>(s->gains, n, make_float2(1.0f, 1.0f));
-  if (check_cuda(cudaGetLastError(), "fill gains")) {
+  iota_kernel<<<(n + 255) / 256, 256, 0, s->stream>>>(s->perm, n);
+  iota_kernel<<<(n + 255) / 256, 256, 0, s->stream>>>(s->rank, n);
+  if (check_cuda(cudaGetLastError(), "session init kernels") ||
+      check_cuda(cudaStreamSynchronize(s->stream), "cudaStreamSynchronize(session)") ||
+      session_reorder(s, false)) {
     session_destroy(s);
     return 1;
   }
@@ -157,6 +199,8 @@ void session_destroy(TsneSession* s) {
   if (s->row_ptr) cudaFree(s->row_ptr);
   if (s->col) cudaFree(s->col);
   if (s->val) cudaFree(s->val);
+  if (s->csr4_col) cudaFree(s->csr4_col);
+  if (s->csr4_val) cudaFree(s->csr4_val);
   s->arena.release();
   if (s->own_stream && s->stream) cudaStreamDestroy(s->stream);
   delete s;
@@ -164,17 +208,43 @@ void session_destroy(TsneSession* s) {
 
 int session_set_layout(TsneSession* s, const float* y, bool host, bool center) {
   s->cur = 0;
-  FE_CUDA(cudaMemcpyAsync(s->y[0], y, sizeof(float2) * s->n,
-                          host ? cudaMemcpyHostToDevice : cudaMemcpyDeviceToDevice, s->stream),
-          "copy layout");
+  FE_TRY(load_caller_order(s, y, host, s->y[0], s->y[1]));
   return launch_stats(s, center ? 1 : 0);
 }
 
 int session_random_layout(TsneSession* s, unsigned int seed) {
   s->cur = 0;
-  random_layout_kernel<<<(s->n + 255) / 256, 256, 0, s->stream>>>(s->y[0], s->n, seed);
+  // The hashed init is keyed on the caller's row index.
+  random_layout_kernel<<<(s->n + 255) / 256, 256, 0, s->stream>>>(s->y[1], s->n, seed);
   FE_LAUNCH("random_layout_kernel");
+  if (s->identity_perm) {
+    FE_CUDA(cudaMemcpyAsync(s->y[0], s->y[1], sizeof(float2) * s->n, cudaMemcpyDeviceToDevice, s->stream),
+            "copy init");
+  } else {
+    FE_TRY(launch_permute_in(s, s->y[1], s->y[0]));
+  }
   return launch_stats(s, 1);
+}
+
+int session_set_state(TsneSession* s, const float* update, const float* gains, bool host) {
+  FE_TRY(load_caller_order(s, update, host, s->update, s->grad_out));
+  FE_TRY(load_caller_order(s, gains, host, s->gains, s->grad_out));
+  FE_CUDA(cudaStreamSynchronize(s->stream), "cudaStreamSynchronize(set state)");
+  return 0;
+}
+
+int session_get_state(TsneSession* s, float* update, float* gains, bool host) {
+  FE_TRY(store_caller_order(s, s->update, host, update, s->grad_out));
+  FE_TRY(store_caller_order(s, s->gains, host, gains, s->grad_out));
+  return 0;
+}
+
+int session_reset_state(TsneSession* s) {
+  FE_CUDA(cudaMemsetAsync(s->update, 0, sizeof(float2) * s->n, s->stream), "memset update");
+  fill_float2_kernel<<<(s->n + 255) / 256, 256, 0, s->stream>>>(s->gains, s->n, make_float2(1.0f, 1.0f));
+  FE_LAUNCH("fill gains");
+  FE_CUDA(cudaStreamSynchronize(s->stream), "cudaStreamSynchronize(reset)");
+  return 0;
 }
 
 namespace {
@@ -195,56 +265,54 @@ int collect_profile(TsneSession* s) {
   return 0;
 }
 
-}  // namespace
-
-int session_iterate(TsneSession* s, int iters, float exaggeration, float momentum,
-                    float learning_rate, float min_gain, float max_step_norm) {
+// Runs `iters` iterations with one parameter set and no reorder in between.
+int iterate_block(TsneSession* s, int iters, float exaggeration, float momentum, float learning_rate,
+                  float min_gain, float max_step_norm) {
   if (iters <= 0) return 0;
   const bool graphs = s->use_graphs && !s->profile && iters > 1;
   if (!graphs) {
     for (int it = 0; it < iters; ++it) {
       FE_TRY(launch_iteration(s, kGradUpdate, exaggeration, momentum, learning_rate, min_gain,
                               max_step_norm));
-      s->iterations_run += 1;
       if (s->profile && s->events.size() > 4000) FE_TRY(collect_profile(s));
     }
     return collect_profile(s);
   }
-  // One captured chunk of up to 25 iterations per parameter set (the chunk
-  // length the reference uses, src/embedding_cuda_kernels.cpp:5902-5985).
-  // Capturing an even number of iterations keeps the y double-buffer parity.
-  const int chunk = std::min(iters, 24);
+  // One captured chunk of up to 24 iterations per parameter set (the reference
+  // captures chunks of 25, src/embedding_cuda_kernels.cpp:5902-5985).  An even
+  // chunk returns the y double buffer to the parity it was captured with.
+  const int chunk = std::min(iters, 24) & ~1;
   const float key[5] = {exaggeration, momentum, learning_rate, min_gain, max_step_norm};
-  const bool reuse = s->graph != nullptr && s->graph_iters == chunk && s->graph_cur == s->cur &&
-                     std::memcmp(key, s->graph_params, sizeof(key)) == 0 && (chunk % 2 == 0);
-  if (!reuse && chunk % 2 == 0) {
-    if (s->graph) {
-      cudaGraphExecDestroy(s->graph);
-      s->graph = nullptr;
-    }
-    const int saved_cur = s->cur;
-    cudaGraph_t g = nullptr;
-    FE_CUDA(cudaStreamBeginCapture(s->stream, cudaStreamCaptureModeThreadLocal), "cudaStreamBeginCapture");
-    int rc = 0;
-    for (int it = 0; it < chunk && rc == 0; ++it) {
-      rc = launch_iteration(s, kGradUpdate, exaggeration, momentum, learning_rate, min_gain, max_step_norm);
-    }
-    const cudaError_t end = cudaStreamEndCapture(s->stream, &g);
-    s->cur = saved_cur;
-    if (rc != 0 || end != cudaSuccess) {
-      if (g) cudaGraphDestroy(g);
-      if (rc == 0) check_cuda(end, "cudaStreamEndCapture");
-      return 1;
-    }
-    const cudaError_t inst = cudaGraphInstantiate(&s->graph, g, 0);
-    cudaGraphDestroy(g);
-    FE_CUDA(inst, "cudaGraphInstantiate");
-    s->graph_iters = chunk;
-    s->graph_cur = saved_cur;
-    std::memcpy(s->graph_params, key, sizeof(key));
-  }
   int done = 0;
-  if (chunk % 2 == 0) {
+  if (chunk >= 2) {
+    const bool reuse = s->graph != nullptr && s->graph_iters == chunk && s->graph_cur == s->cur &&
+                       std::memcmp(key, s->graph_params, sizeof(key)) == 0;
+    if (!reuse) {
+      if (s->graph) {
+        cudaGraphExecDestroy(s->graph);
+        s->graph = nullptr;
+      }
+      const int saved_cur = s->cur;
+      cudaGraph_t g = nullptr;
+      FE_CUDA(cudaStreamBeginCapture(s->stream, cudaStreamCaptureModeThreadLocal), "cudaStreamBeginCapture");
+      int rc = 0;
+      for (int it = 0; it < chunk && rc == 0; ++it) {
+        rc = launch_iteration(s, kGradUpdate, exaggeration, momentum, learning_rate, min_gain, max_step_norm);
+      }
+      const cudaError_t end = cudaStreamEndCapture(s->stream, &g);
+      s->cur = saved_cur;
+      if (rc != 0 || end != cudaSuccess) {
+        if (g) cudaGraphDestroy(g);
+        if (rc == 0) check_cuda(end, "cudaStreamEndCapture");
+        return 1;
+      }
+      const cudaError_t inst = cudaGraphInstantiate(&s->graph, g, 0);
+      cudaGraphDestroy(g);
+      FE_CUDA(inst, "cudaGraphInstantiate");
+      s->graph_iters = chunk;
+      s->graph_cur = saved_cur;
+      std::memcpy(s->graph_params, key, sizeof(key));
+    }
     while (iters - done >= chunk) {
       FE_CUDA(cudaGraphLaunch(s->graph, s->stream), "cudaGraphLaunch(t-SNE chunk)");
       done += chunk;
@@ -253,28 +321,52 @@ int session_iterate(TsneSession* s, int iters, float exaggeration, float momentu
   for (; done < iters; ++done) {
     FE_TRY(launch_iteration(s, kGradUpdate, exaggeration, momentum, learning_rate, min_gain, max_step_norm));
   }
-  s->iterations_run += iters;
+  return 0;
+}
+
+}  // namespace
+
+int session_iterate(TsneSession* s, int iters, float exaggeration, float momentum,
+                    float learning_rate, float min_gain, float max_step_norm) {
+  while (iters > 0) {
+    if (s->reorder_every > 0 && s->iterations_run >= s->next_reorder) {
+      FE_TRY(session_reorder(s, true));
+      s->next_reorder = s->iterations_run + s->reorder_every;
+    }
+    long long block = iters;
+    if (s->reorder_every > 0) block = std::min<long long>(block, s->next_reorder - s->iterations_run);
+    FE_TRY(iterate_block(s, static_cast<int>(block), exaggeration, momentum, learning_rate, min_gain,
+                         max_step_norm));
+    s->iterations_run += block;
+    iters -= static_cast<int>(block);
+  }
   return 0;
 }
 
 int session_gradient(TsneSession* s, float exaggeration, float* grad_host, double* z_out) {
+  // Evaluated at the stored layout exactly as given (no re-centring).
+  FE_TRY(launch_stats(s, 0));
   FE_TRY(launch_iteration(s, kGradOnly, exaggeration, 0.f, 0.f, 0.f, 0.f));
-  FE_CUDA(cudaMemcpyAsync(grad_host, s->grad_out, sizeof(float2) * s->n, cudaMemcpyDeviceToHost, s->stream),
-          "D2H gradient");
   LayoutStats st;
   FE_CUDA(cudaMemcpyAsync(&st, s->stats, sizeof(st), cudaMemcpyDeviceToHost, s->stream), "D2H stats");
-  FE_CUDA(cudaStreamSynchronize(s->stream), "cudaStreamSynchronize(gradient)");
+  FE_TRY(store_caller_order(s, s->grad_out, true, grad_host, s->y[s->cur ^ 1]));
   if (z_out) *z_out = st.z;
-  return 0;
+  return launch_stats(s, 1);
 }
 
 int session_get_layout(TsneSession* s, float* out, bool host) {
-  // The newest layout is uncentred until the next splat; centre into grad_out.
+  // The newest layout is uncentred until the next splat: centre into grad_out.
   FE_TRY(launch_center_output(s, s->grad_out));
-  FE_CUDA(cudaMemcpyAsync(out, s->grad_out, sizeof(float2) * s->n,
-                          host ? cudaMemcpyDeviceToHost : cudaMemcpyDeviceToDevice, s->stream),
-          "copy layout out");
-  FE_CUDA(cudaStreamSynchronize(s->stream), "cudaStreamSynchronize(layout)");
+  return store_caller_order(s, s->grad_out, host, out, s->y[s->cur ^ 1]);
+}
+
+int session_get_p(TsneSession* s, int* row_ptr, int* col, float* val) {
+  // The caller-order CSR is kept as is; copy it out.
+  const size_t nnz = static_cast<size_t>(s->nnz);
+  FE_CUDA(cudaMemcpyAsync(row_ptr, s->row_ptr, sizeof(int) * (s->n + 1), cudaMemcpyDeviceToHost, s->stream), "D2H");
+  FE_CUDA(cudaMemcpyAsync(col, s->col, sizeof(int) * nnz, cudaMemcpyDeviceToHost, s->stream), "D2H");
+  FE_CUDA(cudaMemcpyAsync(val, s->val, sizeof(float) * nnz, cudaMemcpyDeviceToHost, s->stream), "D2H");
+  FE_CUDA(cudaStreamSynchronize(s->stream), "cudaStreamSynchronize(get_p)");
   return 0;
 }
 

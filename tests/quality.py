@@ -34,3 +34,27 @@ def label_accuracy(y, labels, k=15):
     nn = layout_knn(y, k)
     lab = np.asarray(labels)
     return float((lab[nn] == lab[:, None]).mean())
+
+
+def tsne_kl(row_ptr, col, val, y, block=4096):
+    """Exact KL(P || Q) of a t-SNE layout, as evaluate_kl_f
+    (src/tsne_neighbors.cpp:1247-1276): Z over all ordered pairs i != j in
+    double, per-entry p log((p + 1e-9) / (q + 1e-9))."""
+    import torch
+
+    Y = torch.from_numpy(np.ascontiguousarray(y, np.float32)).cuda().double()
+    n = Y.shape[0]
+    z = 0.0
+    for s in range(0, n, block):
+        e = min(n, s + block)
+        d2 = torch.cdist(Y[s:e], Y) ** 2
+        q = 1.0 / (1.0 + d2)
+        q[torch.arange(e - s, device=Y.device), torch.arange(s, e, device=Y.device)] = 0.0
+        z += float(q.sum())
+    rows = torch.repeat_interleave(torch.arange(n, device=Y.device),
+                                   torch.from_numpy(np.diff(row_ptr)).cuda())
+    cols = torch.from_numpy(np.asarray(col, np.int64)).cuda()
+    p = torch.from_numpy(np.asarray(val, np.float64)).cuda()
+    d2 = ((Y[rows] - Y[cols]) ** 2).sum(1)
+    qn = (1.0 / (1.0 + d2)) / z
+    return float((p * torch.log((p + 1e-9) / (qn + 1e-9))).sum())

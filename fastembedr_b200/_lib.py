@@ -34,6 +34,8 @@ _SIGNATURES = {
                                               F, F, F, F, U, I, c_float_p]),
     "fe_b200_umap_epochs": (I, [c_int_p, c_int_p, c_float_p, LL, c_float_p, I, I, I, I, I, F, F, F, F, U, I, I,
                                 c_ll_p]),
+    "fe_b200_umap_epochs_noalloc": (I, [c_void_p, c_void_p, c_void_p, LL, c_void_p, I, I, I, I, I, F, F, F, F,
+                                        U, I, c_void_p]),
     "fe_b200_tsne_create": (I, [c_void_p, c_void_p, I, I, I, F, c_float_p, U, I, I, ctypes.POINTER(c_void_p)]),
     "fe_b200_tsne_create_csr": (I, [c_int_p, c_int_p, c_float_p, I, c_float_p, I, ctypes.POINTER(c_void_p)]),
     "fe_b200_tsne_iterate": (I, [c_void_p, I, F, F, F, F, F]),

@@ -235,6 +235,30 @@ int fe_b200_umap_epochs(const int* heads, const int* tails, const float* epochs_
                         float b, float repulsion_strength, unsigned int seed, int optimizer_mode,
                         int hash_key_is_tail, long long* positive_samples);
 
+/* ---- UMAP epochs without any device allocation ----
+ * No counterpart in the reference.  For callers that cannot let a library
+ * allocate device memory (a framework that owns the device heap through its
+ * own allocator or pool, real-time loops where cudaMalloc/cudaFree would
+ * synchronise the device, embedders with a fixed memory budget): runs epochs
+ * [epoch_begin, epoch_end) of the COO optimizer in Jacobi (delta) mode --
+ * optimizer_mode 1 of fe_b200_umap_epochs, same results -- entirely on
+ * caller-owned DEVICE buffers (heads, tails, epochs_per_sample: n_edges each;
+ * layout: row-major float[n*2], updated in place), on `stream`
+ * (cudaStream_t; NULL = the legacy default stream), and returns after the work
+ * has finished.  It calls no cudaMalloc, cudaFree or allocating library
+ * routine: its only scratch, one float2 per vertex, is a fixed 8 MiB static
+ * device array that every GPU loading this library holds until exit, so n is
+ * limited to 1,048,576 vertices (larger n returns 1 with a message).  The
+ * first call on a device looks up the array's address on that device; make
+ * that first call before any stream capture.  All calls share the array and
+ * clear it on entry; calls that overlap on the GPU race on it. */
+int fe_b200_umap_epochs_noalloc(const int* heads, const int* tails,
+                                const float* epochs_per_sample, long long n_edges, float* layout,
+                                int n, int epoch_begin, int epoch_end, int n_epochs,
+                                int negative_sample_rate, float learning_rate, float a, float b,
+                                float repulsion_strength, unsigned int seed, int hash_key_is_tail,
+                                void* stream);
+
 #ifdef __cplusplus
 }
 #endif

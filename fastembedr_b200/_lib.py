@@ -32,6 +32,14 @@ _SIGNATURES = {
     "fastembedr_cuda_opentsne_fft_from_device_knn_float": (I, _TSNE_KNN_ARGS),
     "fastembedr_cuda_umap_optimize_coo": (I, [c_int_p, c_int_p, c_float_p, c_float_p, c_float_p, I, I, I, I,
                                               F, F, F, F, U, I, c_float_p]),
+    "fastembedr_cuda_umap_from_knn_spectral": (I, [c_void_p, c_void_p, I, I, I, I, F, F, F, F, I, U, I, I,
+                                                   c_float_p]),
+    "fastembedr_cuda_umap_from_knn_spectral_float": (I, [c_void_p, c_void_p, I, I, I, I, F, F, F, F, I, U, I, I,
+                                                         c_float_p]),
+    "fastembedr_cuda_umap_from_device_knn_spectral_float": (I, [c_void_p, c_void_p, I, I, I, I, F, F, F, F, I, U,
+                                                                I, I, I, c_float_p]),
+    "fastembedr_cuda_umap_graph_dump_from_knn": (I, [c_void_p, c_void_p, I, I, I, c_int_p, c_int_p, c_float_p,
+                                                     c_float_p, c_int_p, c_int_p]),
     "fe_b200_umap_epochs": (I, [c_int_p, c_int_p, c_float_p, LL, c_float_p, I, I, I, I, I, F, F, F, F, U, I, I,
                                 c_ll_p]),
     "fe_b200_umap_epochs_noalloc": (I, [c_void_p, c_void_p, c_void_p, LL, c_void_p, I, I, I, I, I, F, F, F, F,

@@ -348,6 +348,106 @@ class TsneSession:
 # ------------------------------------------------------------------ UMAP
 
 
+def umap_config(n: int, k: int) -> Dict[str, Any]:
+    """Size rules of the reference's UMAP defaults (fast_knn_umap_config,
+    R/fast_knn_umap.R:1191-1224)."""
+    if n >= 10000:
+        return {"n_epochs": 200, "min_dist": 0.01, "negative_sample_rate": 5,
+                "spectral_n_iter": 30 if k <= 15 else 20, "learning_rate": 1.0, "repulsion_strength": 1.0}
+    return {"n_epochs": 500, "min_dist": 0.01, "negative_sample_rate": 5,
+            "spectral_n_iter": 60 if n >= 500 else 50, "learning_rate": 1.0, "repulsion_strength": 1.0}
+
+
+def umap_knn(indices, distances, n_epochs: Optional[int] = None, negative_sample_rate: Optional[int] = None,
+             learning_rate: Optional[float] = None, min_dist: Optional[float] = None,
+             repulsion_strength: Optional[float] = None, spectral_n_iter: Optional[int] = None,
+             seed: int = 42, optimizer_mode: int = 0, graph_mode: str = "fuzzy",
+             index_offset: Optional[int] = None) -> EmbeddingResult:
+    """UMAP from KNN on the B200 backend: device fuzzy graph, diffusion start and
+    COO edge SGD in one call (the fused path of umap_knn(backend = "cuda"),
+    src/embedding_cuda_impl.cpp:1566-1768).
+
+    ``indices``/``distances`` are (n, k) host arrays (0- or 1-based, self
+    excluded) or CUDA tensors (device-KNN entry point, nothing copied).
+    ``graph_mode="binary"`` sets every graph weight to 1; the reference offers it
+    on the device-KNN entry point only, so host inputs are moved to the device
+    for it.  Unset parameters follow the reference's size rules (umap_config).
+    """
+    on_device = hasattr(indices, "is_cuda") and indices.is_cuda
+    n, k = (int(indices.shape[0]), int(indices.shape[1]))
+    cfg = umap_config(n, k)
+    n_epochs = cfg["n_epochs"] if n_epochs is None else int(n_epochs)
+    nsr = cfg["negative_sample_rate"] if negative_sample_rate is None else int(negative_sample_rate)
+    lr = cfg["learning_rate"] if learning_rate is None else float(learning_rate)
+    md = cfg["min_dist"] if min_dist is None else float(min_dist)
+    rep = cfg["repulsion_strength"] if repulsion_strength is None else float(repulsion_strength)
+    sni = cfg["spectral_n_iter"] if spectral_n_iter is None else int(spectral_n_iter)
+    if graph_mode not in ("fuzzy", "binary"):
+        raise ValueError("graph_mode must be 'fuzzy' or 'binary'")
+    binary = graph_mode == "binary"
+    a, b = find_ab_params(1.0, md)
+    out = np.zeros((n, 2), np.float32)
+    L = _lib.load()
+    if binary and not on_device:
+        import torch
+
+        indices = torch.as_tensor(np.asarray(indices), dtype=torch.int32, device="cuda")
+        distances = torch.as_tensor(np.asarray(distances), dtype=torch.float32, device="cuda")
+        on_device = True
+    if on_device:
+        import torch
+
+        idx_cm = indices.to(torch.int32).t().contiguous()
+        dist_cm = distances.to(torch.float32).t().contiguous()
+        off = index_offset if index_offset is not None else int(
+            bool((idx_cm.min() >= 1).item() and (idx_cm.max() <= n).item()))
+        rc = L.fastembedr_cuda_umap_from_device_knn_spectral_float(
+            ctypes.c_void_p(idx_cm.data_ptr()), ctypes.c_void_p(dist_cm.data_ptr()), n, k, n_epochs, nsr, lr, a,
+            b, rep, sni, seed & 0xFFFFFFFF, off, optimizer_mode, int(binary), _ptr(out, ctypes.c_float))
+        entry = "fastembedr_cuda_umap_from_device_knn_spectral_float"
+    else:
+        idx = np.asarray(indices)
+        off = index_offset if index_offset is not None else resolve_index_offset(idx)
+        idx_cm = column_major(idx, np.int32)
+        dist_cm = column_major(distances, np.float32)
+        rc = L.fastembedr_cuda_umap_from_knn_spectral_float(
+            ctypes.c_void_p(idx_cm.ctypes.data), ctypes.c_void_p(dist_cm.ctypes.data), n, k, n_epochs, nsr, lr,
+            a, b, rep, sni, seed & 0xFFFFFFFF, off, optimizer_mode, _ptr(out, ctypes.c_float))
+        entry = "fastembedr_cuda_umap_from_knn_spectral_float"
+    if rc != 0:
+        raise CudaBackendError("CUDA fused UMAP failed: " + _lib.last_error())
+    return EmbeddingResult(out, {
+        "entry_point": entry, "n_epochs": n_epochs, "negative_sample_rate": nsr, "learning_rate": lr,
+        "min_dist": md, "a": a, "b": b, "spectral_n_iter": sni, "graph_mode": graph_mode,
+        "optimizer_mode": optimizer_mode, "backend": "cuda", "device": "B200 (sm_100a)",
+    })
+
+
+def umap_graph_dump(indices, distances, index_offset: Optional[int] = None) -> Dict[str, Any]:
+    """The device-KNN fuzzy graph as a rank-major COO list
+    (fastembedr_cuda_umap_graph_dump_from_knn; umap_cuda_graph_dump_impl,
+    src/embedding_cuda_impl.cpp:1838-1896)."""
+    idx = np.asarray(indices)
+    n, k = idx.shape
+    off = index_offset if index_offset is not None else resolve_index_offset(idx)
+    width = min(256, 2 * k)
+    cap = n * width
+    idx_cm = column_major(idx, np.int32)
+    dist_cm = column_major(distances, np.float64)
+    heads, tails = np.full(cap, -1, np.int32), np.full(cap, -1, np.int32)
+    weights, eps = np.zeros(cap, np.float32), np.zeros(cap, np.float32)
+    w_out, c_out = ctypes.c_int(0), ctypes.c_int(0)
+    rc = _lib.load().fastembedr_cuda_umap_graph_dump_from_knn(
+        ctypes.c_void_p(idx_cm.ctypes.data), ctypes.c_void_p(dist_cm.ctypes.data), n, k, off,
+        _ptr(heads, ctypes.c_int), _ptr(tails, ctypes.c_int), _ptr(weights, ctypes.c_float),
+        _ptr(eps, ctypes.c_float), ctypes.byref(w_out), ctypes.byref(c_out))
+    if rc != 0:
+        raise CudaBackendError("CUDA UMAP graph dump failed: " + _lib.last_error())
+    m = c_out.value
+    return {"heads": heads[:m].copy(), "tails": tails[:m].copy(), "weights": weights[:m].copy(),
+            "epochs_per_sample": eps[:m].copy(), "width": w_out.value, "capacity": m}
+
+
 def umap_optimize_coo(heads, tails, weights, epochs_per_sample, init, n_epochs: int = 500,
                       negative_sample_rate: int = 5, learning_rate: float = 1.0,
                       min_dist: float = 0.1, repulsion_strength: float = 1.0, seed: int = 42,

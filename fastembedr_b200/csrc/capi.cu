@@ -228,6 +228,113 @@ int umap_host_run(const int* heads, const int* tails, const float* eps, long lon
   return 0;
 }
 
+// Device bytes of the graph build at its peak plus the COO list and layouts.
+size_t umap_graph_bytes(int n, int k) {
+  const size_t nk = static_cast<size_t>(n) * k;
+  const size_t slots = static_cast<size_t>(n) * fe::umap_graph_width(k);
+  return 64 * nk + 24 * slots + 32 * static_cast<size_t>(n) + (64u << 20);
+}
+
+// The device-KNN UMAP path (fastembedr_cuda_umap_from_device_knn_spectral_impl,
+// src/embedding_cuda_kernels.cpp:4967-5199): graph, diffusion start, rank-major
+// COO list, then the epochs.  Negatives are keyed on the tail vertex, as the
+// reference's COO kernels key them (:3109-3118).  The edge order matters to the
+// in-place (Hogwild) mode: rank-major order puts a vertex's edges far apart in
+// time, so each sees its earlier moves, as in the reference; grouped by head
+// they would all start from the same stale position.
+int umap_fused_impl(const int* idx, const void* dist, bool dist_double, bool on_device, int n, int k,
+                    int n_epochs, int nsr, float lr, float a, float b, float rep, int spectral_n_iter,
+                    unsigned int seed, int index_offset, int optimizer_mode, bool binary, float* out) {
+  if (n_epochs < 1 || nsr < 0 || lr <= 0.0f || spectral_n_iter < 1) {
+    set_error("invalid fused CUDA UMAP dimensions or parameters");
+    return 1;
+  }
+  FE_TRY(fe::memory_preflight(umap_graph_bytes(n, k) +
+                                  (on_device ? 0 : static_cast<size_t>(n) * k * (dist_double ? 12 : 8)),
+                              "CUDA fused UMAP allocation preflight"));
+  cudaStream_t stream = nullptr;
+  FE_CUDA(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking), "cudaStreamCreate(fused umap)");
+  struct StreamGuard {
+    cudaStream_t s;
+    ~StreamGuard() {
+      cudaStreamSynchronize(s);
+      cudaStreamDestroy(s);
+    }
+  } guard{stream};
+  fe::UmapDenseGraph g;
+  {
+    DeviceCopy d_idx, d_dist;
+    const int* idx_dev = idx;
+    const void* dist_dev = dist;
+    if (!on_device) {
+      const size_t items = static_cast<size_t>(n) * k;
+      FE_TRY(copy_to_device(idx, items * sizeof(int), d_idx, stream, "H2D fused umap indices"));
+      FE_TRY(copy_to_device(dist, items * (dist_double ? sizeof(double) : sizeof(float)), d_dist, stream,
+                            "H2D fused umap distances"));
+      idx_dev = static_cast<const int*>(d_idx.p);
+      dist_dev = d_dist.p;
+    }
+    FE_TRY(fe::umap_graph_build(idx_dev, dist_dev, dist_double, n, k, index_offset, binary, stream, &g));
+  }
+  fe::Arena arena;
+  const size_t slots = static_cast<size_t>(n) * g.width;
+  int* heads = nullptr;
+  int* tails = nullptr;
+  float* periods = nullptr;
+  float2* layout = nullptr;
+  float2* delta = nullptr;
+  const int mode = optimizer_mode == 1 ? fe::kUmapDelta : fe::kUmapInplaceSample;
+  for (int pass = 0; pass < 2; ++pass) {
+    if (pass == 0) arena.begin_plan();
+    else arena.rewind();
+    heads = arena.take<int>(slots);
+    tails = arena.take<int>(slots);
+    periods = arena.take<float>(slots);
+    layout = arena.take<float2>(n);
+    delta = arena.take<float2>(mode == fe::kUmapDelta ? n : 0);
+    if (pass == 0) FE_TRY(arena.commit("fused UMAP workspace"));
+  }
+  FE_TRY(fe::umap_diffusion_init(g, seed, spectral_n_iter, layout, stream));
+  long long n_edges = 0;
+  FE_TRY(fe::umap_graph_pack(g, true, heads, tails, nullptr, periods, &n_edges, stream));
+  if (n_edges < 1 || n_edges > static_cast<long long>(slots)) {
+    set_error("invalid fused CUDA UMAP graph edge count");
+    return 1;
+  }
+  fe::UmapRun r;
+  r.params = fe::UmapParams{n, n_epochs, nsr, 1, seed, lr, a, b, rep};
+  r.mode = mode;
+  r.heads = heads;
+  r.tails = tails;
+  r.periods = periods;
+  r.n_edges = n_edges;
+  r.layout = layout;
+  r.delta = mode == fe::kUmapDelta ? delta : nullptr;
+  r.stream = stream;
+  r.edge_blocks = fe::umap_edge_blocks(n_edges);
+  r.use_graphs = fe::env_flag("FASTEMBEDR_CUDA_GRAPH_CAPTURE", true);
+  FE_TRY(fe::umap_run_epochs(&r, 0, n_epochs));
+  FE_CUDA(cudaMemcpyAsync(out, layout, sizeof(float2) * n, cudaMemcpyDeviceToHost, stream), "D2H fused umap layout");
+  FE_CUDA(cudaStreamSynchronize(stream), "cudaStreamSynchronize(fused umap)");
+  return 0;
+}
+
+int umap_fused_host(const int* idx, const void* dist, bool dist_double, int n, int k, int n_epochs, int nsr,
+                    float lr, float a, float b, float rep, int spectral_n_iter, unsigned int seed,
+                    int index_offset, int optimizer_mode, float* out) {
+  fe::clear_error();
+  if (idx == nullptr || dist == nullptr || out == nullptr) {
+    set_error("null host pointer");
+    return 1;
+  }
+  if (n < 2 || k < 1 || k > 256) {
+    set_error("invalid host CUDA UMAP dimensions");
+    return 1;
+  }
+  return umap_fused_impl(idx, dist, dist_double, false, n, k, n_epochs, nsr, lr, a, b, rep, spectral_n_iter,
+                         seed, index_offset, optimizer_mode, false, out);
+}
+
 }  // namespace
 
 extern "C" {
@@ -541,23 +648,114 @@ void fe_b200_tsne_destroy(fe_b200_tsne* h) {
 
 // ---------------------------------------------------------------- UMAP from KNN (device graph)
 
-int fastembedr_cuda_umap_from_knn_spectral(const int*, const double*, int, int, int, int, float,
-                                           float, float, float, int, unsigned int, int, int, float*) {
-  return out_of_scope("fastembedr_cuda_umap_from_knn_spectral");
+int fastembedr_cuda_umap_from_knn_spectral(const int* indices, const double* distances, int n, int k,
+                                           int n_epochs, int negative_sample_rate, float learning_rate,
+                                           float a, float b, float repulsion_strength, int spectral_n_iter,
+                                           unsigned int seed, int index_offset, int optimizer_mode,
+                                           float* out) {
+  return umap_fused_host(indices, distances, true, n, k, n_epochs, negative_sample_rate, learning_rate, a, b,
+                         repulsion_strength, spectral_n_iter, seed, index_offset, optimizer_mode, out);
 }
-int fastembedr_cuda_umap_from_knn_spectral_float(const int*, const float*, int, int, int, int,
-                                                 float, float, float, float, int, unsigned int,
-                                                 int, int, float*) {
-  return out_of_scope("fastembedr_cuda_umap_from_knn_spectral_float");
+
+int fastembedr_cuda_umap_from_knn_spectral_float(const int* indices, const float* distances, int n, int k,
+                                                 int n_epochs, int negative_sample_rate, float learning_rate,
+                                                 float a, float b, float repulsion_strength,
+                                                 int spectral_n_iter, unsigned int seed, int index_offset,
+                                                 int optimizer_mode, float* out) {
+  return umap_fused_host(indices, distances, false, n, k, n_epochs, negative_sample_rate, learning_rate, a, b,
+                         repulsion_strength, spectral_n_iter, seed, index_offset, optimizer_mode, out);
 }
-int fastembedr_cuda_umap_from_device_knn_spectral_float(const int*, const float*, int, int, int,
-                                                        int, float, float, float, float, int,
-                                                        unsigned int, int, int, int, float*) {
-  return out_of_scope("fastembedr_cuda_umap_from_device_knn_spectral_float");
+
+int fastembedr_cuda_umap_from_device_knn_spectral_float(const int* device_indices,
+                                                        const float* device_distances, int n, int k,
+                                                        int n_epochs, int negative_sample_rate,
+                                                        float learning_rate, float a, float b,
+                                                        float repulsion_strength, int spectral_n_iter,
+                                                        unsigned int seed, int index_offset,
+                                                        int optimizer_mode, int binary_graph, float* out) {
+  fe::clear_error();
+  if (device_indices == nullptr || device_distances == nullptr || out == nullptr) {
+    set_error("null device pointer");
+    return 1;
+  }
+  if (n < 2 || k < 1 || k > 256) {
+    set_error("invalid fused CUDA UMAP dimensions or parameters");
+    return 1;
+  }
+  return umap_fused_impl(device_indices, device_distances, false, true, n, k, n_epochs, negative_sample_rate,
+                         learning_rate, a, b, repulsion_strength, spectral_n_iter, seed, index_offset,
+                         optimizer_mode, binary_graph != 0, out);
 }
-int fastembedr_cuda_umap_graph_dump_from_knn(const int*, const double*, int, int, int, int*, int*,
-                                             float*, float*, int*, int*) {
-  return out_of_scope("fastembedr_cuda_umap_graph_dump_from_knn");
+
+// fastembedr_cuda_umap_graph_dump_from_knn_impl (src/embedding_cuda_kernels.cpp:4804-4948):
+// the device graph as a rank-major COO list; the caller's buffers hold n * width entries.
+int fastembedr_cuda_umap_graph_dump_from_knn(const int* indices, const double* distances, int n, int k,
+                                             int index_offset, int* out_heads, int* out_tails,
+                                             float* out_weights, float* out_epochs_per_sample, int* out_width,
+                                             int* out_capacity) {
+  fe::clear_error();
+  if (indices == nullptr || distances == nullptr || out_heads == nullptr || out_tails == nullptr ||
+      out_weights == nullptr || out_epochs_per_sample == nullptr || out_width == nullptr ||
+      out_capacity == nullptr) {
+    set_error("null host pointer");
+    return 1;
+  }
+  if (n < 2 || k < 1 || k > 256) {
+    set_error("invalid CUDA UMAP graph dump dimensions");
+    return 1;
+  }
+  FE_TRY(fe::memory_preflight(umap_graph_bytes(n, k) + static_cast<size_t>(n) * k * 12,
+                              "CUDA UMAP graph dump allocation preflight"));
+  cudaStream_t stream = nullptr;
+  FE_CUDA(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking), "cudaStreamCreate(umap graph dump)");
+  struct StreamGuard {
+    cudaStream_t s;
+    ~StreamGuard() {
+      cudaStreamSynchronize(s);
+      cudaStreamDestroy(s);
+    }
+  } guard{stream};
+  fe::UmapDenseGraph g;
+  {
+    DeviceCopy d_idx, d_dist;
+    const size_t items = static_cast<size_t>(n) * k;
+    FE_TRY(copy_to_device(indices, items * sizeof(int), d_idx, stream, "H2D umap dump indices"));
+    FE_TRY(copy_to_device(distances, items * sizeof(double), d_dist, stream, "H2D umap dump distances"));
+    FE_TRY(fe::umap_graph_build(static_cast<const int*>(d_idx.p), d_dist.p, true, n, k, index_offset, false,
+                                stream, &g));
+  }
+  const size_t slots = static_cast<size_t>(n) * g.width;
+  fe::Arena arena;
+  int* heads = nullptr;
+  int* tails = nullptr;
+  float* weights = nullptr;
+  float* periods = nullptr;
+  for (int pass = 0; pass < 2; ++pass) {
+    if (pass == 0) arena.begin_plan();
+    else arena.rewind();
+    heads = arena.take<int>(slots);
+    tails = arena.take<int>(slots);
+    weights = arena.take<float>(slots);
+    periods = arena.take<float>(slots);
+    if (pass == 0) FE_TRY(arena.commit("UMAP graph dump workspace"));
+  }
+  long long n_edges = 0;
+  FE_TRY(fe::umap_graph_pack(g, true, heads, tails, weights, periods, &n_edges, stream));
+  if (n_edges < 1 || n_edges > static_cast<long long>(slots)) {
+    set_error("invalid CUDA UMAP graph edge count");
+    return 1;
+  }
+  const size_t e = static_cast<size_t>(n_edges);
+  FE_CUDA(cudaMemcpyAsync(out_heads, heads, e * sizeof(int), cudaMemcpyDeviceToHost, stream), "D2H dump heads");
+  FE_CUDA(cudaMemcpyAsync(out_tails, tails, e * sizeof(int), cudaMemcpyDeviceToHost, stream), "D2H dump tails");
+  FE_CUDA(cudaMemcpyAsync(out_weights, weights, e * sizeof(float), cudaMemcpyDeviceToHost, stream),
+          "D2H dump weights");
+  FE_CUDA(cudaMemcpyAsync(out_epochs_per_sample, periods, e * sizeof(float), cudaMemcpyDeviceToHost, stream),
+          "D2H dump epochs_per_sample");
+  FE_CUDA(cudaStreamSynchronize(stream), "cudaStreamSynchronize(umap graph dump)");
+  *out_width = g.width;
+  *out_capacity = static_cast<int>(n_edges);
+  return 0;
 }
 
 // ---------------------------------------------------------------- out-of-scope symbols

@@ -134,6 +134,23 @@ __device__ __forceinline__ float warp_max(float v) {
 __device__ __forceinline__ int4 ld_stream(const int4* p) { return __ldcs(p); }
 __device__ __forceinline__ float4 ld_stream(const float4* p) { return __ldcs(p); }
 
+// The reference's counter-based uniform in [-1, 1] for coordinate `col` of
+// point `row` (deterministic_unit, src/embedding_cuda_kernels.cpp:266-274):
+// a 32-bit finaliser over the seed mixed with (row + 1) and (col + 1), whose
+// low 24 bits are scaled.  The constants are the reference's, so that random
+// starts agree with it point for point.
+__device__ __forceinline__ float hashed_unit(unsigned int seed, int row, int col) {
+  unsigned int x = seed;
+  x ^= (static_cast<unsigned int>(row) + 1u) * 0x9e3779b9u;
+  x ^= (static_cast<unsigned int>(col) + 1u) * 0x85ebca6bu;
+  x ^= x >> 16;
+  x *= 0x7feb352du;
+  x ^= x >> 15;
+  x *= 0x846ca68bu;
+  x ^= x >> 16;
+  return static_cast<float>(x & 0x00ffffffu) / 8388607.5f - 1.0f;
+}
+
 }  // namespace fe
 
 #endif

@@ -13,28 +13,11 @@ namespace fe {
 namespace {
 
 // Random init of the reference CUDA path when no init is passed
-// (random_init_kernel + deterministic_unit, src/embedding_cuda_kernels.cpp:266-274, 1162-1167).
-__device__ __forceinline__ unsigned int mix_unit(unsigned int x) {
-  x ^= x >> 16;
-  x *= 0x7feb352du;
-  x ^= x >> 15;
-  x *= 0x846ca68bu;
-  x ^= x >> 16;
-  return x;
-}
-
+// (random_init_kernel, src/embedding_cuda_kernels.cpp:1162-1167).
 __global__ void random_layout_kernel(float2* y, int n, unsigned int seed) {
   const int row = blockIdx.x * blockDim.x + threadIdx.x;
   if (row >= n) return;
-  float v[2];
-  for (unsigned int col = 0; col < 2; ++col) {
-    unsigned int x = seed;
-    x ^= (static_cast<unsigned int>(row) + 1u) * 0x9e3779b9u;
-    x ^= (col + 1u) * 0x85ebca6bu;
-    const unsigned int bits = mix_unit(x);
-    v[col] = static_cast<float>(bits & 0x00ffffffu) / 8388607.5f - 1.0f;
-  }
-  y[row] = make_float2(v[0], v[1]);
+  y[row] = make_float2(hashed_unit(seed, row, 0), hashed_unit(seed, row, 1));
 }
 
 __global__ void fill_float2_kernel(float2* p, int n, float2 v) {

@@ -13,16 +13,26 @@
 // (src/embedding_cuda_kernels.cpp:3066-3222).  d^b uses the reference's own
 // exponent-interpolation approximation (umap_powf_fast, src/fast_knn_umap.cpp:179-206).
 //
-// Modes:
-//   kUmapInplace (optimizer_mode 0): Hogwild.  Each edge reads its endpoints once,
-//     applies its own positive and negative updates sequentially to a local copy
-//     (the CPU replay's order within an edge), then adds the net displacement
-//     with one 8-byte vector atomic per endpoint (red.global.add.v2.f32).
-//   kUmapDelta (optimizer_mode 1): Jacobi.  Forces are evaluated against the
-//     layout frozen at epoch start and accumulated into a delta buffer, which a
-//     second kernel applies together with the sanitize step.
-// Head displacements of consecutive edges with the same head (COO built from
-// CSR is grouped by head) are summed across the warp before the atomic.
+// Modes (optimizer_mode 0 is Hogwild, 1 Jacobi, as in the reference):
+//   kUmapInplace: Hogwild at edge granularity.  Each edge reads its endpoints
+//     once, applies its positive and negative samples in turn to running copies
+//     (the CPU replay's order within an edge), then adds its net move with one
+//     8-byte vector atomic per endpoint (red.global.add.v2.f32); head moves of
+//     consecutive edges sharing a head are first summed across the warp.  The
+//     COO entry point uses it: its parity target is the CPU replay, and on the
+//     70k configuration (CPU graph, COO grouped by head) it reaches 0.00773 kNN
+//     preservation against the CPU replay's 0.00791 (sample granularity: 0.00725,
+//     the reference CUDA kernel: 0.00708; means of 3 seeds).
+//   kUmapInplaceSample: Hogwild at sample granularity, as
+//     embed_epoch_coo_atomic_kernel: every sample reads its endpoints afresh from
+//     L2 (ld.global.cg, so moves made since by this and concurrent edges are
+//     seen) and applies its move at once with vector atomics.  The device-KNN
+//     path uses it: its only reference is that CUDA kernel, and with its
+//     rank-major edges and small diffusion start the edge-granularity form lost
+//     7-11% kNN preservation against it on 50-D mixtures.
+//   kUmapDelta: Jacobi.  Forces are evaluated against the layout frozen at epoch
+//     start and accumulated into a delta buffer, which a second kernel applies
+//     together with the sanitize step; head moves are combined as above.
 #include "umap.cuh"
 
 #include <cfloat>
@@ -102,8 +112,8 @@ template <int Mode>
 __global__ void __launch_bounds__(256) umap_epoch_kernel(const int* __restrict__ heads,
                                                          const int* __restrict__ tails,
                                                          const float* __restrict__ periods,
-                                                         long long n_edges, float2* layout,
-                                                         const float2* __restrict__ frozen,
+                                                         long long edge_begin, long long edge_end,
+                                                         float2* layout, const float2* __restrict__ frozen,
                                                          float2* __restrict__ delta, UmapParams p,
                                                          int epoch, long long* positive_count) {
   const float eps = 1.1920928955078125e-7f;
@@ -114,12 +124,12 @@ __global__ void __launch_bounds__(256) umap_epoch_kernel(const int* __restrict__
   long long local_pos = 0;
   const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
   // Whole warps iterate together so the head-run reduction sees full warps.
-  const long long base0 = static_cast<long long>(blockIdx.x) * blockDim.x + (threadIdx.x & ~31);
-  for (long long base = base0; base < n_edges; base += stride) {
+  const long long base0 = edge_begin + static_cast<long long>(blockIdx.x) * blockDim.x + (threadIdx.x & ~31);
+  for (long long base = base0; base < edge_end; base += stride) {
     const long long gid = base + lane;
     int h = -1, t = -1;
     float gx_h = 0.f, gy_h = 0.f;
-    if (gid < n_edges) {
+    if (gid < edge_end) {
       h = __ldcs(heads + gid);
       t = __ldcs(tails + gid);
       const float per = __ldcs(periods + gid);
@@ -162,9 +172,8 @@ __global__ void __launch_bounds__(256) umap_epoch_kernel(const int* __restrict__
           gx_h = dh.x;
           gy_h = dh.y;
           atomicAdd(dst + t, dt);
-        } else {
-          // In place: the edge's own updates are applied in the CPU replay's
-          // order to running copies of its endpoints.
+        } else if (Mode == kUmapInplace) {
+          // The edge's samples in the CPU replay's order on running copies.
           float2 yh = yh0, yt = yt0;
           for (int s = 0; s < pos; ++s) {
             const float dx = yh.x - yt.x;
@@ -194,6 +203,35 @@ __global__ void __launch_bounds__(256) umap_epoch_kernel(const int* __restrict__
           gx_h = yh.x - yh0.x;
           gy_h = yh.y - yh0.y;
           atomicAdd(dst + t, make_float2(yt.x - yt0.x, yt.y - yt0.y));
+        } else {
+          // Each sample reads fresh positions and applies its move at once.
+          float2 yh, yt;
+          for (int s = 0; s < pos; ++s) {
+            yh = __ldcg(layout + h);
+            yt = __ldcg(layout + t);
+            const float dx = yh.x - yt.x;
+            const float dy = yh.y - yt.y;
+            const float d2 = fmaxf(eps, dx * dx + dy * dy);
+            const float d2b = umap_pow(d2, p.b);
+            const float c = -2.0f * p.a * p.b * (d2b / d2) / (p.a * d2b + 1.0f);
+            const float gx = clip4(c * dx) * alpha;
+            const float gy = clip4(c * dy) * alpha;
+            atomicAdd(layout + h, make_float2(gx, gy));
+            atomicAdd(layout + t, make_float2(-gx, -gy));
+          }
+          for (int s = 0; s < neg; ++s) {
+            const int k = negative_vertex(static_cast<unsigned int>(p.n), p.seed, epoch, h, key, s);
+            if (k == h || k == t) continue;
+            yh = __ldcg(layout + h);
+            const float2 yk = __ldcg(layout + k);
+            const float dx = yh.x - yk.x;
+            const float dy = yh.y - yk.y;
+            const float d2 = fmaxf(eps, dx * dx + dy * dy);
+            const float d2b = umap_pow(d2, p.b);
+            const float c = p.repulsion_strength * 2.0f * p.b / ((0.001f + d2) * (p.a * d2b + 1.0f));
+            atomicAdd(layout + h, make_float2(clip4(c * dx) * alpha, clip4(c * dy) * alpha));
+          }
+          h = -1;  // moves already applied; nothing to combine across the warp
         }
       } else {
         h = -1;
@@ -240,14 +278,21 @@ int umap_launch_epoch(UmapRun* r, int epoch) {
   const UmapParams& p = r->params;
   if (r->mode == kUmapDelta) {
     umap_epoch_kernel<kUmapDelta><<<r->edge_blocks, 256, 0, r->stream>>>(
-        r->heads, r->tails, r->periods, r->n_edges, r->layout, r->layout, r->delta, p, epoch,
+        r->heads, r->tails, r->periods, 0, r->n_edges, r->layout, r->layout, r->delta, p, epoch,
         r->positive_count);
+    FE_LAUNCH("umap_epoch_kernel");
   } else {
-    umap_epoch_kernel<kUmapInplace><<<r->edge_blocks, 256, 0, r->stream>>>(
-        r->heads, r->tails, r->periods, r->n_edges, r->layout, r->layout, nullptr, p, epoch,
-        r->positive_count);
+    if (r->mode == kUmapInplaceSample) {
+      umap_epoch_kernel<kUmapInplaceSample><<<r->edge_blocks, 256, 0, r->stream>>>(
+          r->heads, r->tails, r->periods, 0, r->n_edges, r->layout, r->layout, nullptr, p, epoch,
+          r->positive_count);
+    } else {
+      umap_epoch_kernel<kUmapInplace><<<r->edge_blocks, 256, 0, r->stream>>>(
+          r->heads, r->tails, r->periods, 0, r->n_edges, r->layout, r->layout, nullptr, p, epoch,
+          r->positive_count);
+    }
+    FE_LAUNCH("umap_epoch_kernel");
   }
-  FE_LAUNCH("umap_epoch_kernel");
   umap_sanitize_kernel<<<(p.n + 255) / 256, 256, 0, r->stream>>>(
       r->layout, r->mode == kUmapDelta ? r->delta : nullptr, p.n, 16.0f);
   FE_LAUNCH("umap_sanitize_kernel");

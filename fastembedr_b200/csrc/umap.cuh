@@ -10,7 +10,10 @@
 
 namespace fe {
 
-enum UmapMode { kUmapInplace = 0, kUmapDelta = 1 };
+// kUmapInplace: Hogwild at edge granularity (the CPU replay's order within an
+// edge); kUmapDelta: Jacobi; kUmapInplaceSample: Hogwild at sample granularity
+// (the reference CUDA kernel's).  umap.cu says which entry point uses which.
+enum UmapMode { kUmapInplace = 0, kUmapDelta = 1, kUmapInplaceSample = 2 };
 
 struct UmapParams {
   int n;
@@ -42,5 +45,42 @@ struct UmapRun {
 int umap_launch_epoch(UmapRun* r, int epoch);
 int umap_run_epochs(UmapRun* r, int epoch_begin, int epoch_end);
 int umap_edge_blocks(long long n_edges);
+
+// ---------------------------------------------------------------- graph from KNN
+
+// The fuzzy KNN graph of the device-KNN path as dense rows: row i holds up to
+// `width` = min(256, 2k) (neighbour, weight) slots, empty slots are (i, 0).
+// Slots 0..out-1 hold row i's own KNN entries in rank order, the rest the
+// incoming-only neighbours in ascending order.
+struct UmapDenseGraph {
+  int n = 0;
+  int k = 0;
+  int width = 0;
+  int* nbr = nullptr;   // device, n * width
+  float* w = nullptr;   // device, n * width
+  ~UmapDenseGraph();
+  UmapDenseGraph() = default;
+  UmapDenseGraph(const UmapDenseGraph&) = delete;
+  UmapDenseGraph& operator=(const UmapDenseGraph&) = delete;
+};
+
+// Row capacity of the reference's device graph, min(256, max(k, 2k))
+// (src/embedding_cuda_kernels.cpp:4996).
+inline int umap_graph_width(int k) { return 2 * k < 256 ? 2 * k : 256; }
+
+// Builds the graph from column-major device KNN (entry j of row i at j*n+i).
+int umap_graph_build(const int* d_idx, const void* d_dist, bool dist_is_double, int n, int k,
+                     int index_offset, bool binary, cudaStream_t stream, UmapDenseGraph* g);
+
+// Packs the non-empty slots into COO arrays (device, capacity n * width):
+// rank-major (all rows' slot 0, then slot 1, ...) or row-major (grouped by
+// head).  epochs_per_sample = 1 / max(w, 1e-6).
+int umap_graph_pack(const UmapDenseGraph& g, bool rank_major, int* heads, int* tails, float* weights,
+                    float* epochs_per_sample, long long* n_edges, cudaStream_t stream);
+
+// Diffusion start: hashed uniform start, whitened, then `iters` rounds of
+// weighted neighbour averaging, each followed by whitening.
+int umap_diffusion_init(const UmapDenseGraph& g, unsigned int seed, int iters, float2* layout,
+                        cudaStream_t stream);
 
 }  // namespace fe

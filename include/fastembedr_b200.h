@@ -111,7 +111,10 @@ int fastembedr_cuda_umap_from_device_knn_spectral_float(
     int negative_sample_rate, float learning_rate, float a, float b, float repulsion_strength,
     int spectral_n_iter, unsigned int seed, int index_offset, int optimizer_mode, int binary_graph,
     float* out);
-/* Device graph dump (padded width x n COO).  src/embedding_cuda_impl.cpp:232-242. */
+/* The device-KNN fuzzy graph as a rank-major COO list (every row's slot 0, then
+ * slot 1, ...).  The out arrays hold n * min(256, 2k) entries; *out_width gets
+ * min(256, 2k) and *out_capacity the number of edges written.
+ * src/embedding_cuda_impl.cpp:232-242 (kernels.cpp:4804-4964). */
 int fastembedr_cuda_umap_graph_dump_from_knn(const int* indices, const double* distances, int n,
                                              int k, int index_offset, int* out_heads,
                                              int* out_tails, float* out_weights,

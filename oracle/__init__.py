@@ -66,6 +66,7 @@ def lib() -> ctypes.CDLL:
         L.or_umap_negative_vertex.argtypes = [ctypes.c_int, ctypes.c_uint32, ctypes.c_int,
                                               ctypes.c_int, ctypes.c_uint32, ctypes.c_int]
         L.or_umap_graph.restype = ctypes.c_longlong
+        L.or_umap_pack_coo.restype = ctypes.c_longlong
         _lib = L
     return _lib
 
@@ -350,6 +351,43 @@ def umap_graph(idx: np.ndarray, dist: np.ndarray, index_offset: int = 0) -> Umap
     return UmapGraph(offsets, nb[:nnz].copy(), w[:nnz].copy(), eps[:nnz].copy(), maxw.value)
 
 
+def umap_device_graph(idx: np.ndarray, dist: np.ndarray, index_offset: int = 0, binary: bool = False):
+    """The device-KNN path's dense fuzzy graph: (nbr, w), each (n, width)."""
+    n, k = idx.shape
+    width = lib().or_umap_graph_width(k)
+    idx_cm, dist_cm = _cm(idx, np.int32), _cm(dist, np.float32)
+    nbr = np.zeros((n, width), np.int32)
+    w = np.zeros((n, width), np.float32)
+    rc = lib().or_umap_device_graph(_ptr(idx_cm, ctypes.c_int), _ptr(dist_cm, ctypes.c_float), n, k,
+                                    index_offset, int(binary), _ptr(nbr, ctypes.c_int), _ptr(w, ctypes.c_float))
+    if rc < 0:
+        raise MemoryError("or_umap_device_graph")
+    return nbr, w
+
+
+def umap_pack_coo(nbr: np.ndarray, w: np.ndarray, rank_major: bool = True) -> dict:
+    """Non-empty slots of a dense graph as COO arrays."""
+    nbr, w = _i32(nbr), _f32(w)
+    n, width = nbr.shape
+    cap = n * width
+    heads, tails = np.zeros(cap, np.int32), np.zeros(cap, np.int32)
+    weights, eps = np.zeros(cap, np.float32), np.zeros(cap, np.float32)
+    m = lib().or_umap_pack_coo(_ptr(nbr, ctypes.c_int), _ptr(w, ctypes.c_float), n, width, int(rank_major),
+                               _ptr(heads, ctypes.c_int), _ptr(tails, ctypes.c_int),
+                               _ptr(weights, ctypes.c_float), _ptr(eps, ctypes.c_float))
+    return {"heads": heads[:m].copy(), "tails": tails[:m].copy(), "weights": weights[:m].copy(),
+            "epochs_per_sample": eps[:m].copy()}
+
+
+def umap_diffusion_init(nbr: np.ndarray, w: np.ndarray, seed: int, iters: int) -> np.ndarray:
+    nbr, w = _i32(nbr), _f32(w)
+    n, width = nbr.shape
+    out = np.zeros((n, 2), np.float32)
+    lib().or_umap_diffusion_init(_ptr(nbr, ctypes.c_int), _ptr(w, ctypes.c_float), n, width,
+                                 ctypes.c_uint32(seed & 0xFFFFFFFF), iters, _ptr(out, ctypes.c_float))
+    return out
+
+
 def umap_epoch_delta(heads, tails, epochs_per_sample, layout, epoch, n_epochs,
                      negative_sample_rate=5, learning_rate=1.0, a=1.5769434601962196,
                      b=0.8950608781227859, repulsion_strength=1.0, seed=42,
@@ -556,3 +594,76 @@ def ref_find_ab(spread=1.0, min_dist=0.1):
     a, b = ctypes.c_double(), ctypes.c_double()
     ref().feref_find_ab(spread, min_dist, ctypes.byref(a), ctypes.byref(b))
     return a.value, b.value
+
+
+# ------------------------------------------------- the reference's CUDA backend
+
+REF_CUDA_SO = os.path.join(HERE, "_ref", "libferef_cuda.so")
+_ref_cuda = None
+
+
+def ref_cuda_available() -> bool:
+    return os.path.exists(REF_CUDA_SO)
+
+
+def ref_cuda() -> ctypes.CDLL:
+    """The reference's own CUDA backend, src/embedding_cuda_kernels.cpp (needs a GPU to run)."""
+    global _ref_cuda
+    if _ref_cuda is None:
+        if not os.path.exists(REF_CUDA_SO):
+            raise FileNotFoundError(f"{REF_CUDA_SO} missing: build it where the reference sources exist")
+        C = ctypes.CDLL(REF_CUDA_SO)
+        I, F, U = ctypes.c_int, ctypes.c_float, ctypes.c_uint
+        C.fastembedr_cuda_embedding_last_error.restype = ctypes.c_char_p
+        C.fastembedr_cuda_available.restype = ctypes.c_bool
+        C.fastembedr_cuda_umap_graph_dump_from_knn.argtypes = [
+            _c_int_p, _c_double_p, I, I, I, _c_int_p, _c_int_p, _c_float_p, _c_float_p, _c_int_p, _c_int_p]
+        C.fastembedr_cuda_umap_from_knn_spectral_float.argtypes = [
+            _c_int_p, _c_float_p, I, I, I, I, F, F, F, F, I, U, I, I, _c_float_p]
+        C.fastembedr_cuda_umap_optimize_coo.argtypes = [
+            _c_int_p, _c_int_p, _c_float_p, _c_float_p, _c_float_p, I, I, I, I, F, F, F, F, U, I, _c_float_p]
+        C.fastembedr_cuda_opentsne_fft_from_knn_float.argtypes = [
+            _c_int_p, _c_float_p, _c_float_p, I, I, I, I, F, I, I, F, F, F, I, F, F, F, F, U, I, _c_float_p]
+        _ref_cuda = C
+    return _ref_cuda
+
+
+def _ref_cuda_check(rc: int, what: str) -> None:
+    if rc != 0:
+        raise RuntimeError(f"reference CUDA {what} failed: "
+                           f"{ref_cuda().fastembedr_cuda_embedding_last_error().decode()}")
+
+
+def ref_cuda_umap_graph_dump(idx: np.ndarray, dist: np.ndarray, index_offset: int = 0) -> dict:
+    """fastembedr_cuda_umap_graph_dump_from_knn of the reference (rank-major COO)."""
+    n, k = idx.shape
+    width = min(256, 2 * k)
+    cap = n * width
+    idx_cm, dist_cm = _cm(idx, np.int32), _cm(dist, np.float64)
+    heads, tails = np.full(cap, -1, np.int32), np.full(cap, -1, np.int32)
+    weights, eps = np.zeros(cap, np.float32), np.zeros(cap, np.float32)
+    w_out, c_out = ctypes.c_int(0), ctypes.c_int(0)
+    rc = ref_cuda().fastembedr_cuda_umap_graph_dump_from_knn(
+        _ptr(idx_cm, ctypes.c_int), _ptr(dist_cm, ctypes.c_double), n, k, index_offset,
+        _ptr(heads, ctypes.c_int), _ptr(tails, ctypes.c_int), _ptr(weights, ctypes.c_float),
+        _ptr(eps, ctypes.c_float), ctypes.byref(w_out), ctypes.byref(c_out))
+    _ref_cuda_check(rc, "UMAP graph dump")
+    m = c_out.value
+    return {"heads": heads[:m].copy(), "tails": tails[:m].copy(), "weights": weights[:m].copy(),
+            "epochs_per_sample": eps[:m].copy(), "width": w_out.value, "capacity": m}
+
+
+def ref_cuda_umap_fused(idx: np.ndarray, dist: np.ndarray, n_epochs: int, negative_sample_rate: int = 5,
+                        learning_rate: float = 1.0, a: float = 1.5769434601962196, b: float = 0.8950608781227859,
+                        repulsion_strength: float = 1.0, spectral_n_iter: int = 30, seed: int = 42,
+                        index_offset: int = 0, optimizer_mode: int = 0) -> np.ndarray:
+    """fastembedr_cuda_umap_from_knn_spectral_float of the reference."""
+    n, k = idx.shape
+    idx_cm, dist_cm = _cm(idx, np.int32), _cm(dist, np.float32)
+    out = np.zeros((n, 2), np.float32)
+    rc = ref_cuda().fastembedr_cuda_umap_from_knn_spectral_float(
+        _ptr(idx_cm, ctypes.c_int), _ptr(dist_cm, ctypes.c_float), n, k, n_epochs, negative_sample_rate,
+        learning_rate, a, b, repulsion_strength, spectral_n_iter, seed & 0xFFFFFFFF, index_offset,
+        optimizer_mode, _ptr(out, ctypes.c_float))
+    _ref_cuda_check(rc, "fused UMAP")
+    return out

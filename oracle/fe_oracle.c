@@ -911,3 +911,224 @@ long long or_umap_graph(const int* idx_cm, const float* dist_cm, int n, int k, i
   *max_weight_out = maxw;
   return (long long)out;
 }
+
+/* ---------------- UMAP: device-KNN path ---------------- */
+
+int or_umap_graph_width(int k) { return 2 * k < 256 ? 2 * k : 256; }
+
+int or_umap_device_graph(const int* idx_cm, const float* dist_cm, int n, int k, int index_offset,
+                         int binary, int* nbr, float* w) {
+  const int width = or_umap_graph_width(k);
+  const size_t nk = (size_t)n * k;
+  int* nbr_k = (int*)malloc(nk * sizeof(int));
+  float* w_k = (float*)malloc(nk * sizeof(float));
+  int* slot_k = (int*)malloc(nk * sizeof(int));
+  int* own = (int*)calloc((size_t)n, sizeof(int));
+  if (!nbr_k || !w_k || !slot_k || !own) {
+    free(nbr_k); free(w_k); free(slot_k); free(own);
+    return -1;
+  }
+  /* prepare_directed_knn_kernel, src/embedding_cuda_kernels.cpp:1004-1058. */
+  for (int i = 0; i < n; ++i) {
+    float rho = INFINITY;
+    for (int j = 0; j < k; ++j) {
+      const float d = dist_cm[(size_t)j * n + i];
+      if (d > 0.0f && d < rho) rho = d;
+    }
+    if (!isfinite(rho)) rho = 0.0f;
+    const float target = log2f((float)(k < 2 ? 2 : k));
+    float lo = 0.0f, hi = INFINITY, sigma = 1.0f;
+    for (int step = 0; step < 48; ++step) {
+      float psum = 0.0f;
+      for (int j = 0; j < k; ++j) {
+        const float d = dist_cm[(size_t)j * n + i] - rho;
+        psum += d <= 0.0f ? 1.0f : expf(-d / sigma);
+      }
+      if (fabsf(psum - target) < 1.0e-5f) break;
+      if (psum > target) {
+        hi = sigma;
+        sigma = 0.5f * (lo + hi);
+      } else {
+        lo = sigma;
+        sigma = isinf(hi) ? sigma * 2.0f : 0.5f * (lo + hi);
+      }
+    }
+    sigma = fmaxf(sigma, 1.0e-6f);
+    for (int j = 0; j < k; ++j) {
+      const int nb = idx_cm[(size_t)j * n + i] - index_offset;
+      const float d = dist_cm[(size_t)j * n + i];
+      const int valid = nb >= 0 && nb < n && nb != i;
+      const float wt = valid ? (d <= rho ? 1.0f : expf(-(d - rho) / sigma)) : 0.0f;
+      const size_t e = (size_t)i * k + j;
+      nbr_k[e] = valid ? nb : -1;
+      w_k[e] = wt;
+      slot_k[e] = (valid && !(wt <= 0.0f)) ? own[i]++ : -1;
+    }
+  }
+  for (size_t s = 0; s < (size_t)n * width; ++s) {
+    nbr[s] = (int)(s / width);
+    w[s] = 0.0f;
+  }
+  /* Own entries: add_umap_outgoing_kernel (:1111-1135); the reverse weight is
+   * that of the first entry of the target row naming this row (:1060-1071). */
+  for (int i = 0; i < n; ++i) {
+    for (int t = 0; t < k; ++t) {
+      const size_t e = (size_t)i * k + t;
+      if (slot_k[e] < 0) continue;
+      const int j = nbr_k[e];
+      float r = 0.0f;
+      for (int u = 0; u < k; ++u) {
+        if (nbr_k[(size_t)j * k + u] == i) {
+          r = w_k[(size_t)j * k + u];
+          break;
+        }
+      }
+      const float f = w_k[e];
+      nbr[(size_t)i * width + slot_k[e]] = j;
+      w[(size_t)i * width + slot_k[e]] = f + r - f * r;
+    }
+  }
+  /* Incoming-only entries: add_umap_incoming_kernel (:1137-1160), appended in
+   * ascending (source row, rank) order while the row has room. */
+  int* fill = (int*)malloc((size_t)n * sizeof(int));
+  for (int i = 0; i < n; ++i) fill[i] = own[i];
+  for (int j = 0; j < n; ++j) {
+    for (int t = 0; t < k; ++t) {
+      const size_t e = (size_t)j * k + t;
+      const int i = nbr_k[e];
+      if (i < 0 || w_k[e] <= 0.0f) continue;
+      int named = 0;
+      for (int u = 0; u < k && !named; ++u) named = nbr_k[(size_t)i * k + u] == j;
+      if (named) continue;
+      if (fill[i] < width) {
+        nbr[(size_t)i * width + fill[i]] = j;
+        w[(size_t)i * width + fill[i]] = w_k[e];
+      }
+      ++fill[i];
+    }
+  }
+  if (binary) {
+    /* binary_graph_weights_kernel, :1099-1109. */
+    for (size_t s = 0; s < (size_t)n * width; ++s) {
+      const int row = (int)(s / width);
+      w[s] = (nbr[s] >= 0 && nbr[s] < n && nbr[s] != row) ? 1.0f : 0.0f;
+    }
+  }
+  free(fill);
+  free(nbr_k);
+  free(w_k);
+  free(slot_k);
+  free(own);
+  return width;
+}
+
+long long or_umap_pack_coo(const int* nbr, const float* w, int n, int width, int rank_major, int* heads,
+                           int* tails, float* weights, float* epochs_per_sample) {
+  long long out = 0;
+  const long long slots = (long long)n * width;
+  for (long long id = 0; id < slots; ++id) {
+    int row, slot;
+    if (rank_major) {
+      slot = (int)(id / n);
+      row = (int)(id - (long long)slot * n);
+    } else {
+      row = (int)(id / width);
+      slot = (int)(id - (long long)row * width);
+    }
+    const size_t dense = (size_t)row * width + slot;
+    const int nb = nbr[dense];
+    const float wt = w[dense];
+    if (!(nb >= 0 && nb < n && nb != row && wt > 0.0f)) continue;
+    heads[out] = row;
+    tails[out] = nb;
+    weights[out] = wt;
+    epochs_per_sample[out] = 1.0f / fmaxf(wt, 1.0e-6f);
+    ++out;
+  }
+  return out;
+}
+
+/* deterministic_unit, src/embedding_cuda_kernels.cpp:266-274. */
+static float hashed_unit(uint32_t seed, int row, int col) {
+  uint32_t x = seed;
+  x ^= ((uint32_t)row + 1u) * 0x9e3779b9u;
+  x ^= ((uint32_t)col + 1u) * 0x85ebca6bu;
+  return (float)(mix32(x) & 0x00ffffffu) / 8388607.5f - 1.0f;
+}
+
+/* reduce/finalize_init_stats_kernel, :1198-1306. */
+static void whiten_stats(const float* y, int n, double st[5]) {
+  double sx = 0.0, sy = 0.0, sxx = 0.0, sxy = 0.0, syy = 0.0;
+  for (int i = 0; i < n; ++i) {
+    const double x = y[2 * i], v = y[2 * i + 1];
+    sx += x;
+    sy += v;
+    sxx += x * x;
+    sxy += x * v;
+    syy += v * v;
+  }
+  const double dn = (double)(n > 1 ? n : 1);
+  const double x_ss = fmax(sxx - sx * sx / dn, 1.0e-24);
+  const double y_ss = fmax(syy - sy * sy / dn, 1.0e-24);
+  const double xy = sxy - sx * sy / dn;
+  const double norm_x = sqrt(x_ss);
+  const double proj = xy / norm_x;
+  const double resid = fmax(y_ss - proj * proj, 1.0e-24);
+  st[0] = sx / dn;
+  st[1] = sy / dn;
+  st[2] = 1.0 / norm_x;
+  st[3] = proj;
+  st[4] = 1.0 / sqrt(resid);
+}
+
+/* normalize_init_kernel, :1308-1319. */
+static void whiten_value(const float* v, const double st[5], float* out) {
+  const double x = ((double)v[0] - st[0]) * st[2];
+  const double yc = (double)v[1] - st[1];
+  const double y = (yc - st[3] * x) * st[4];
+  out[0] = (float)x;
+  out[1] = (float)y;
+}
+
+void or_umap_diffusion_init(const int* nbr, const float* w, int n, int width, uint32_t seed, int iters,
+                            float* out) {
+  float* cur = (float*)malloc((size_t)n * 2 * sizeof(float));
+  float* next = (float*)malloc((size_t)n * 2 * sizeof(float));
+  for (int i = 0; i < n; ++i) {
+    cur[2 * i] = hashed_unit(seed, i, 0);
+    cur[2 * i + 1] = hashed_unit(seed, i, 1);
+  }
+  /* random_init_kernel (:1162-1167), whitened. */
+  double st[5];
+  whiten_stats(cur, n, st);
+  for (int i = 0; i < n; ++i) whiten_value(cur + 2 * i, st, cur + 2 * i);
+  /* diffuse_init_kernel, :1169-1196, each round followed by whitening. */
+  for (int it = 0; it < iters; ++it) {
+    for (int i = 0; i < n; ++i) {
+      float sx = 0.0f, sy = 0.0f, sw = 0.0f;
+      for (int j = 0; j < width; ++j) {
+        const int nb = nbr[(size_t)i * width + j];
+        const float wt = w[(size_t)i * width + j];
+        if (nb < 0 || nb >= n || nb == i || wt <= 0.0f) continue;
+        sx += wt * cur[2 * nb];
+        sy += wt * cur[2 * nb + 1];
+        sw += wt;
+      }
+      if (sw <= 0.0f) {
+        next[2 * i] = cur[2 * i];
+        next[2 * i + 1] = cur[2 * i + 1];
+      } else {
+        next[2 * i] = sx / sw;
+        next[2 * i + 1] = sy / sw;
+      }
+    }
+    whiten_stats(next, n, st);
+    for (int i = 0; i < n; ++i) whiten_value(next + 2 * i, st, next + 2 * i);
+    float* t = cur;
+    cur = next;
+    next = t;
+  }
+  memcpy(out, cur, (size_t)n * 2 * sizeof(float));
+  free(cur);
+  free(next);
+}

@@ -127,6 +127,32 @@ long long or_umap_graph(const int* idx_cm, const float* dist_cm, int n, int k, i
                         int* offsets, int* neighbors, float* weights, float* epochs_per_sample,
                         float* max_weight);
 
+/* Row capacity of the device-KNN graph, min(256, 2k) (src/embedding_cuda_kernels.cpp:4996). */
+int or_umap_graph_width(int k);
+
+/* The device-KNN path's fuzzy graph (prepare_device_knn_graph,
+ * src/embedding_cuda_kernels.cpp:3241-3321, kernels :1004-1160) as dense rows
+ * nbr/w[n * width]; empty slots hold (row, 0).  The reference fills slots with
+ * atomics; this restatement fixes the order the B200 library uses: own
+ * entries in rank order, then incoming-only entries in ascending (source row,
+ * rank) order, dropped once the row is full.  Returns width (or -1). */
+int or_umap_device_graph(const int* idx_cm, const float* dist_cm, int n, int k, int index_offset,
+                         int binary, int* nbr, float* w);
+
+/* Non-empty slots as COO (mark_valid_graph_entries_rank_major_kernel and
+ * pack_coo_graph_from_selected_rank_major_kernel, :2983-3022): rank-major
+ * (rank_major = 1) or grouped by head.  epochs_per_sample = 1 / max(w, 1e-6).
+ * Outputs hold n * width.  Returns the edge count. */
+long long or_umap_pack_coo(const int* nbr, const float* w, int n, int width, int rank_major, int* heads,
+                           int* tails, float* weights, float* epochs_per_sample);
+
+/* Diffusion start layout of the device-KNN path (random_init_kernel,
+ * diffuse_init_kernel, normalize_device_init, :1162-1319, 3323-3337): hashed
+ * uniform start, whitened, then `iters` rounds of weighted neighbour averaging,
+ * each whitened.  Moments are summed in double in row order. */
+void or_umap_diffusion_init(const int* nbr, const float* w, int n, int width, uint32_t seed, int iters,
+                            float* out);
+
 #ifdef __cplusplus
 }
 #endif

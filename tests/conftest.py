@@ -33,3 +33,8 @@ def umap_golden():
 @pytest.fixture(scope="session")
 def umap_scalar_golden():
     return golden("umap_scalar.npz")
+
+
+@pytest.fixture(scope="session")
+def umap_device_golden():
+    return golden("umap_device_small.npz")

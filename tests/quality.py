@@ -36,6 +36,18 @@ def label_accuracy(y, labels, k=15):
     return float((lab[nn] == lab[:, None]).mean())
 
 
+def within_reference(ours, ref, rel=0.02, z=2.0):
+    """Seed-averaged bar for Hogwild runs, whose quality moves from seed to seed
+    by about as much as the bar itself: mean(ours) must reach (1 - rel) *
+    mean(ref) minus z standard errors of the difference of the two means.
+    Returns (passed, message)."""
+    a, b = np.asarray(ours, np.float64), np.asarray(ref, np.float64)
+    se = float(np.sqrt(a.var(ddof=1) / a.size + b.var(ddof=1) / b.size))
+    floor = (1.0 - rel) * b.mean() - z * se
+    msg = f"mean {a.mean():.5f} vs reference {b.mean():.5f} (se of difference {se:.5f}, floor {floor:.5f})"
+    return bool(a.mean() >= floor), msg
+
+
 def tsne_kl(row_ptr, col, val, y, block=4096):
     """Exact KL(P || Q) of a t-SNE layout, as evaluate_kl_f
     (src/tsne_neighbors.cpp:1247-1276): Z over all ordered pairs i != j in

@@ -130,6 +130,47 @@ def test_umap_validation_precedes_device_work():
         api.umap_optimize_coo([0, 1], [1], [1.0], [1.0], np.zeros((2, 2), np.float32))
 
 
+def test_fused_umap_validation_precedes_device_work():
+    """The reference's checks and messages (src/embedding_cuda_kernels.cpp:4984-4992,
+    5217-5224, 4817-4825), before any CUDA call."""
+    L = _lib.load()
+    idx = np.zeros(40, np.int32)
+    dist = np.ones(40, np.float32)
+    out = np.zeros((10, 2), np.float32)
+    fout = out.ctypes.data_as(ctypes.POINTER(ctypes.c_float))
+    base = [ctypes.c_void_p(idx.ctypes.data), ctypes.c_void_p(dist.ctypes.data), 10, 4, 20, 5, 1.0, 1.5, 0.9, 1.0,
+            30, 42, 0, 0, fout]
+    for pos, bad, msg in ((3, 300, "invalid host CUDA UMAP dimensions"), (2, 1, "invalid host CUDA UMAP dimensions"),
+                          (4, 0, "invalid fused CUDA UMAP dimensions or parameters"),
+                          (6, 0.0, "invalid fused CUDA UMAP dimensions or parameters"),
+                          (10, 0, "invalid fused CUDA UMAP dimensions or parameters"),
+                          (0, None, "null host pointer")):
+        args = list(base)
+        args[pos] = bad
+        assert L.fastembedr_cuda_umap_from_knn_spectral_float(*args) == 1
+        assert _lib.last_error() == msg
+    dev = base[:14] + [0, fout]
+    dev[0] = None
+    assert L.fastembedr_cuda_umap_from_device_knn_spectral_float(*dev) == 1
+    assert _lib.last_error() == "null device pointer"
+    i_out = np.zeros(400, np.int32)
+    f_out = np.zeros(400, np.float32)
+    w_out, c_out = ctypes.c_int(0), ctypes.c_int(0)
+    ip = i_out.ctypes.data_as(ctypes.POINTER(ctypes.c_int))
+    fp = f_out.ctypes.data_as(ctypes.POINTER(ctypes.c_float))
+    assert L.fastembedr_cuda_umap_graph_dump_from_knn(
+        ctypes.c_void_p(idx.ctypes.data), ctypes.c_void_p(dist.ctypes.data), 10, 0, 0, ip, ip, fp, fp,
+        ctypes.byref(w_out), ctypes.byref(c_out)) == 1
+    assert _lib.last_error() == "invalid CUDA UMAP graph dump dimensions"
+
+
+def test_umap_config_size_rules():
+    assert api.umap_config(20000, 15)["n_epochs"] == 200 and api.umap_config(20000, 15)["spectral_n_iter"] == 30
+    assert api.umap_config(20000, 30)["spectral_n_iter"] == 20
+    assert api.umap_config(1000, 15)["n_epochs"] == 500 and api.umap_config(1000, 15)["spectral_n_iter"] == 60
+    assert api.umap_config(100, 15)["spectral_n_iter"] == 50
+
+
 def test_tsne_auto_parameters_policy():
     # Values asserted by the reference's own tests (tests/testthat/test-tsne.R:31-56).
     p = api.tsne_auto_parameters(150, 30, None)

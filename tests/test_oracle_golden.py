@@ -121,6 +121,63 @@ def test_umap_scalar_helpers(umap_scalar_golden):
         assert O.umap_find_ab(1.0, float(md)) == (a, b)
 
 
+# ------------------------------------------- device-KNN UMAP path (reference CUDA golden vectors)
+
+
+def _row_lists(heads, tails, weights, n):
+    order = np.lexsort((tails, heads))
+    h, t, w = heads[order], tails[order], weights[order]
+    bounds = np.searchsorted(h, np.arange(n + 1))
+    return [(t[bounds[i]:bounds[i + 1]], w[bounds[i]:bounds[i + 1]]) for i in range(n)]
+
+
+def test_umap_device_graph_against_reference_cuda(umap_device_golden, umap_golden):
+    """The restated device graph against the reference's dump, row by row.  The
+    low-dimensional graph has no full row, so every row must agree; in the hub
+    graph full rows keep an arbitrary subset of incoming edges in the reference,
+    so only their size and own KNN entries are compared.  Weights within 1e-4
+    relative: the C library's expf differs from CUDA's in the last bits."""
+    g = umap_device_golden
+    for key, idx, dist in (("lowd", g["lowd_idx"], g["lowd_dist"]), ("hub", umap_golden["idx"], umap_golden["dist"])):
+        n, k = idx.shape
+        width = 2 * k
+        nbr, w = O.umap_device_graph(idx, dist)
+        coo = O.umap_pack_coo(nbr, w, rank_major=True)
+        ours = _row_lists(coo["heads"], coo["tails"], coo["weights"], n)
+        ref = _row_lists(g[f"{key}_heads"], g[f"{key}_tails"], g[f"{key}_weights"], n)
+        full = 0
+        for i, ((t, wt), (tr, wr)) in enumerate(zip(ours, ref)):
+            if tr.size < width:
+                np.testing.assert_array_equal(t, tr)
+                np.testing.assert_allclose(wt, wr, rtol=1e-4)
+            else:
+                full += 1
+                assert t.size == width
+                own = np.unique(idx[i][idx[i] != i])
+                assert np.isin(own, t).all() and np.isin(own, tr).all()
+        assert (full == 0) == (key == "lowd")
+        np.testing.assert_allclose(coo["epochs_per_sample"], 1.0 / np.maximum(coo["weights"], 1e-6), rtol=1e-6)
+
+
+def test_umap_diffusion_start_against_reference_cuda(umap_device_golden):
+    g = umap_device_golden
+    for binary, key in ((False, "lowd_start"), (True, "lowd_start_binary")):
+        nbr, w = O.umap_device_graph(g["lowd_idx"], g["lowd_dist"], binary=binary)
+        y = O.umap_diffusion_init(nbr, w, int(g["seed"]), int(g["spectral_n_iter"]))
+        np.testing.assert_allclose(y, g[key], atol=1e-6)
+
+
+def test_umap_fused_jacobi_epochs_against_reference_cuda(umap_device_golden):
+    """The reference's fused Jacobi run (3 epochs) replayed by the restatement on
+    the reference's own edge list and start layout."""
+    g = umap_device_golden
+    y = g["lowd_start"].copy()
+    for e in range(3):
+        y = O.umap_epoch_delta(g["lowd_heads"], g["lowd_tails"], g["lowd_epochs_per_sample"], y, e, 3,
+                               seed=int(g["seed"]), hash_key_is_tail=True)
+    np.testing.assert_allclose(y, g["lowd_delta3"], atol=1e-3)
+
+
 @pytest.mark.skipif(not O.ref_available(), reason="compiled reference not present")
 def test_restatement_against_live_reference_fresh_seed():
     from fastembedr_b200 import synthetic as S

@@ -95,26 +95,33 @@ def test_inplace_tracks_sequential_replay_golden(umap_golden):
 def test_end_to_end_quality_vs_reference_cpu(cfg1, mode):
     """Default (in-place) mode: kNN preservation and label accuracy within 2% of
     the reference's CPU replay of the same COO schedule
-    (fast_knn_umap_coo_replay_cpp, all host threads).  The Jacobi mode is a
-    different update order (all forces from the epoch-start layout); it is held
-    to the label-accuracy bar and a looser preservation floor."""
-    from quality import knn_preservation, label_accuracy
+    (fast_knn_umap_coo_replay_cpp, all host threads), as means over four random
+    starts (both runs are Hogwild; see quality.within_reference).  The Jacobi
+    mode is a different update order (all forces from the epoch-start layout);
+    it is held to the label-accuracy bar and a looser preservation floor."""
+    from quality import knn_preservation, label_accuracy, within_reference
 
     idx, dist, g, labels = cfg1
     heads, tails, w, eps = _coo(g)
     n = idx.shape[0]
-    init = S.umap_random_init(n, seed=3)
-    y = api.umap_optimize_coo(heads, tails, w, eps, init, n_epochs=500, min_dist=0.1, optimizer_mode=mode)
-    assert np.isfinite(y).all() and np.abs(y).max() <= 16.0
-    if O.ref_available():
-        yr = O.ref_umap_coo_replay(heads, tails, w, eps, init, 500, min_dist=0.1, threads=8)
-    else:
-        yr = O.umap_replay_serial(heads, tails, eps, init, 0, 500, 500, a=A, b=B)
-    q, qr = knn_preservation(y, idx), knn_preservation(yr, idx)
-    la, lar = label_accuracy(y, labels), label_accuracy(yr, labels)
-    print(f"mode {mode}: knn preservation {q:.4f} vs ref {qr:.4f}; label acc {la:.4f} vs ref {lar:.4f}")
-    assert la >= lar * 0.98, (la, lar)
-    assert q >= qr * (0.98 if mode == 0 else 0.75), (q, qr)
+    q, qr, la, lar = [], [], [], []
+    for seed in (3, 4, 5, 6):
+        init = S.umap_random_init(n, seed=seed)
+        y = api.umap_optimize_coo(heads, tails, w, eps, init, n_epochs=500, min_dist=0.1, optimizer_mode=mode)
+        assert np.isfinite(y).all() and np.abs(y).max() <= 16.0
+        if O.ref_available():
+            yr = O.ref_umap_coo_replay(heads, tails, w, eps, init, 500, min_dist=0.1, threads=8)
+        else:
+            yr = O.umap_replay_serial(heads, tails, eps, init, 0, 500, 500, a=A, b=B)
+        q.append(knn_preservation(y, idx))
+        qr.append(knn_preservation(yr, idx))
+        la.append(label_accuracy(y, labels))
+        lar.append(label_accuracy(yr, labels))
+    ok_q, msg_q = within_reference(q, qr, rel=0.02 if mode == 0 else 0.25)
+    ok_l, msg_l = within_reference(la, lar)
+    print(f"mode {mode}: knn preservation {msg_q}; label acc {msg_l}")
+    assert ok_l, msg_l
+    assert ok_q, msg_q
 
 
 def test_reference_default_key_is_edge_id(umap_golden, monkeypatch):

@@ -279,6 +279,14 @@ class TsneSession:
         return y
 
     def set_layout(self, y, reset_state: bool = True) -> None:
+        """Sets the layout from a host array or a CUDA tensor of shape (n, 2)."""
+        if hasattr(y, "is_cuda") and y.is_cuda:
+            import torch
+
+            y = y.to(torch.float32).contiguous()
+            check(_lib.load().fe_b200_tsne_set_layout(self._h, ctypes.c_void_p(y.data_ptr()), 1,
+                                                      int(reset_state)), "fe_b200_tsne_set_layout")
+            return
         y = _f32(y)
         check(_lib.load().fe_b200_tsne_set_layout(self._h, ctypes.c_void_p(y.ctypes.data), 0,
                                                   int(reset_state)), "fe_b200_tsne_set_layout")

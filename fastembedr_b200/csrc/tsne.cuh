@@ -176,12 +176,32 @@ struct TsneSession {
   long long kernel_launches[8] = {0};
   long long iterations_run = 0;
 
-  // CUDA graph of one iteration chunk (captured lazily per parameter set).
-  cudaGraphExec_t graph = nullptr;
-  int graph_iters = 0;
-  int graph_cur = 0;
-  float graph_params[5] = {0};
+  // Captured iteration chunks, keyed by chunk length, parameter set and the
+  // layout double-buffer parity they start from (least recently used evicted).
+  struct GraphEntry {
+    cudaGraphExec_t exec;
+    int iters;
+    int cur;
+    float params[5];
+    unsigned long long used;
+  };
+  std::vector<GraphEntry> graphs;
+  unsigned long long graph_clock = 0;
   bool use_graphs = true;
+
+  // Reorder scratch, carved from the session arena so that a periodic
+  // reorder neither allocates nor synchronises with the host.
+  unsigned int* ro_keys = nullptr;
+  unsigned int* ro_keys_sorted = nullptr;
+  int* ro_idx = nullptr;
+  int* ro_order = nullptr;
+  int* ro_perm = nullptr;
+  int* ro_rank = nullptr;
+  int* ro_groups = nullptr;
+  float2* ro_update = nullptr;
+  float2* ro_gains = nullptr;
+  void* ro_temp = nullptr;
+  size_t ro_temp_bytes = 0;
 
   // Spatial ordering: internal point r is the caller's point perm[r], and
   // caller point i is internal point rank[i].
@@ -236,7 +256,13 @@ int session_get_p(TsneSession* s, int* row_ptr, int* col, float* val);
 // Chooses the internal point order -- Morton order of the current layout when
 // by_layout, else the caller's order -- permutes the point arrays, and
 // rebuilds the internal-order, group-padded copy of P from the caller CSR.
+// Only the first call (from session_create) sizes the padded copy and waits
+// for the device; later calls are asynchronous on the session stream.
 int session_reorder(TsneSession* s, bool by_layout);
+// CUB temporary storage the reorder needs for n points.
+int reorder_temp_bytes(int n, size_t* bytes);
+// Drops every captured iteration chunk.
+void drop_graphs(TsneSession* s);
 // out[perm[r]] = in[r] (internal -> caller order) and out[r] = in[perm[r]].
 int launch_unpermute(TsneSession* s, const float2* in, float2* out);
 int launch_permute_in(TsneSession* s, const float2* in, float2* out);

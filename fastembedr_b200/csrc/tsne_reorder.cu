@@ -116,95 +116,74 @@ __global__ void permute_in_kernel(const float2* __restrict__ in, const int* __re
 
 }  // namespace
 
+int reorder_temp_bytes(int n, size_t* bytes) {
+  size_t sort_bytes = 0, scan_bytes = 0;
+  FE_CUDA(cub::DeviceRadixSort::SortPairs(nullptr, sort_bytes, static_cast<unsigned int*>(nullptr),
+                                          static_cast<unsigned int*>(nullptr), static_cast<int*>(nullptr),
+                                          static_cast<int*>(nullptr), n, 0, 30),
+          "cub::DeviceRadixSort(sizing)");
+  FE_CUDA(cub::DeviceScan::ExclusiveSum(nullptr, scan_bytes, static_cast<int*>(nullptr),
+                                        static_cast<int*>(nullptr), n + 1),
+          "cub::DeviceScan(sizing)");
+  *bytes = std::max(sort_bytes, scan_bytes);
+  return 0;
+}
+
 int session_reorder(TsneSession* s, bool by_layout) {
   const int n = s->n;
   const unsigned blocks = static_cast<unsigned>((n + 255) / 256);
   cudaStream_t st = s->stream;
-
-  // Scratch (freed on return): keys, indices, order, new perm/rank, lengths,
-  // point temporaries, CUB temp.
-  size_t sort_bytes = 0, scan_bytes = 0;
-  FE_CUDA(cub::DeviceRadixSort::SortPairs(nullptr, sort_bytes, static_cast<unsigned int*>(nullptr),
-                                          static_cast<unsigned int*>(nullptr), static_cast<int*>(nullptr),
-                                          static_cast<int*>(nullptr), n, 0, 30, st),
-          "cub::DeviceRadixSort(sizing)");
-  FE_CUDA(cub::DeviceScan::ExclusiveSum(nullptr, scan_bytes, static_cast<int*>(nullptr),
-                                        static_cast<int*>(nullptr), n + 1, st),
-          "cub::DeviceScan(sizing)");
-  const size_t temp_bytes = std::max(sort_bytes, scan_bytes);
-  const size_t need = 2 * align_up(sizeof(unsigned int) * n) + 4 * align_up(sizeof(int) * n) +
-                      align_up(sizeof(int) * (n + 1)) + 2 * align_up(sizeof(float2) * n) +
-                      align_up(temp_bytes);
-  void* scratch = nullptr;
-  FE_CUDA(cudaMalloc(&scratch, need), "cudaMalloc(reorder scratch)");
-  struct Free {
-    void* q;
-    ~Free() { cudaFree(q); }
-  } free_scratch{scratch};
-  char* p = static_cast<char*>(scratch);
-  auto carve = [&p](size_t bytes) {
-    char* q = p;
-    p += align_up(bytes);
-    return q;
-  };
-  unsigned int* keys = reinterpret_cast<unsigned int*>(carve(sizeof(unsigned int) * n));
-  unsigned int* keys_sorted = reinterpret_cast<unsigned int*>(carve(sizeof(unsigned int) * n));
-  int* idx = reinterpret_cast<int*>(carve(sizeof(int) * n));
-  int* order = reinterpret_cast<int*>(carve(sizeof(int) * n));
-  int* perm_new = reinterpret_cast<int*>(carve(sizeof(int) * n));
-  int* rank_new = reinterpret_cast<int*>(carve(sizeof(int) * n));
-  int* groups = reinterpret_cast<int*>(carve(sizeof(int) * (n + 1)));
-  float2* u_tmp = reinterpret_cast<float2*>(carve(sizeof(float2) * n));
-  float2* g_tmp = reinterpret_cast<float2*>(carve(sizeof(float2) * n));
-  void* temp = carve(temp_bytes);
-
   const int cur = s->cur;
-  morton_keys_kernel<<<blocks, 256, 0, st>>>(s->y[cur], s->stats, n, s->grid, by_layout ? 1 : 0, keys, idx);
+
+  morton_keys_kernel<<<blocks, 256, 0, st>>>(s->y[cur], s->stats, n, s->grid, by_layout ? 1 : 0, s->ro_keys,
+                                             s->ro_idx);
   FE_LAUNCH("morton_keys_kernel");
-  size_t tb = temp_bytes;
-  FE_CUDA(cub::DeviceRadixSort::SortPairs(temp, tb, keys, keys_sorted, idx, order, n, 0, 30, st),
+  size_t tb = s->ro_temp_bytes;
+  FE_CUDA(cub::DeviceRadixSort::SortPairs(s->ro_temp, tb, s->ro_keys, s->ro_keys_sorted, s->ro_idx, s->ro_order,
+                                          n, 0, 30, st),
           "cub::DeviceRadixSort(morton)");
+  // The permuted layout lands in the free half of the double buffer and is
+  // copied back, so the buffer parity (and every captured graph) is unchanged.
   float2* y_new = s->y[cur ^ 1];
-  permute_points_kernel<<<blocks, 256, 0, st>>>(order, n, s->perm, perm_new, rank_new, s->row_ptr, groups,
-                                                s->y[cur], y_new, s->update, u_tmp, s->gains, g_tmp);
+  permute_points_kernel<<<blocks, 256, 0, st>>>(s->ro_order, n, s->perm, s->ro_perm, s->ro_rank, s->row_ptr,
+                                                s->ro_groups, s->y[cur], y_new, s->update, s->ro_update,
+                                                s->gains, s->ro_gains);
   FE_LAUNCH("permute_points_kernel");
-  FE_CUDA(cudaMemcpyAsync(s->update, u_tmp, sizeof(float2) * n, cudaMemcpyDeviceToDevice, st), "permute update");
-  FE_CUDA(cudaMemcpyAsync(s->gains, g_tmp, sizeof(float2) * n, cudaMemcpyDeviceToDevice, st), "permute gains");
-  FE_CUDA(cudaMemcpyAsync(s->perm, perm_new, sizeof(int) * n, cudaMemcpyDeviceToDevice, st), "permute perm");
-  FE_CUDA(cudaMemcpyAsync(s->rank, rank_new, sizeof(int) * n, cudaMemcpyDeviceToDevice, st), "permute rank");
-  s->cur = cur ^ 1;
-  FE_CUDA(cudaMemsetAsync(groups + n, 0, sizeof(int), st), "memset");
-  tb = temp_bytes;
-  FE_CUDA(cub::DeviceScan::ExclusiveSum(temp, tb, groups, s->row_ptr4, n + 1, st), "cub::DeviceScan(row_ptr4)");
-  int total = 0;
-  FE_CUDA(cudaMemcpyAsync(&total, s->row_ptr4 + n, sizeof(int), cudaMemcpyDeviceToHost, st), "D2H");
-  FE_CUDA(cudaStreamSynchronize(st), "cudaStreamSynchronize(reorder)");
-  if (total < 0) {
-    set_error("padded P exceeds the 32-bit group range");
-    return 1;
-  }
-  if (total > s->csr4_capacity) {
-    if (s->csr4_col) cudaFree(s->csr4_col);
-    if (s->csr4_val) cudaFree(s->csr4_val);
-    s->csr4_col = nullptr;
-    s->csr4_val = nullptr;
+  FE_CUDA(cudaMemcpyAsync(s->y[cur], y_new, sizeof(float2) * n, cudaMemcpyDeviceToDevice, st), "permute layout");
+  FE_CUDA(cudaMemcpyAsync(s->update, s->ro_update, sizeof(float2) * n, cudaMemcpyDeviceToDevice, st),
+          "permute update");
+  FE_CUDA(cudaMemcpyAsync(s->gains, s->ro_gains, sizeof(float2) * n, cudaMemcpyDeviceToDevice, st),
+          "permute gains");
+  FE_CUDA(cudaMemcpyAsync(s->perm, s->ro_perm, sizeof(int) * n, cudaMemcpyDeviceToDevice, st), "permute perm");
+  FE_CUDA(cudaMemcpyAsync(s->rank, s->ro_rank, sizeof(int) * n, cudaMemcpyDeviceToDevice, st), "permute rank");
+  FE_CUDA(cudaMemsetAsync(s->ro_groups + n, 0, sizeof(int), st), "memset");
+  tb = s->ro_temp_bytes;
+  FE_CUDA(cub::DeviceScan::ExclusiveSum(s->ro_temp, tb, s->ro_groups, s->row_ptr4, n + 1, st),
+          "cub::DeviceScan(row_ptr4)");
+  if (s->csr4_capacity == 0) {
+    // First build: size the padded copy.  The total of padded groups does not
+    // depend on the point order, so later reorders reuse this allocation.
+    int total = 0;
+    FE_CUDA(cudaMemcpyAsync(&total, s->row_ptr4 + n, sizeof(int), cudaMemcpyDeviceToHost, st), "D2H");
+    FE_CUDA(cudaStreamSynchronize(st), "cudaStreamSynchronize(reorder)");
+    if (total < 0) {
+      set_error("padded P exceeds the 32-bit group range");
+      return 1;
+    }
     FE_TRY(memory_preflight(static_cast<size_t>(total) * 32, "padded P preflight"));
-    FE_CUDA(cudaMalloc(&s->csr4_col, sizeof(int4) * static_cast<size_t>(total)), "cudaMalloc(P cols)");
-    FE_CUDA(cudaMalloc(&s->csr4_val, sizeof(float4) * static_cast<size_t>(total)), "cudaMalloc(P vals)");
+    const size_t groups = std::max<size_t>(1, static_cast<size_t>(total));
+    FE_CUDA(cudaMalloc(&s->csr4_col, sizeof(int4) * groups), "cudaMalloc(P cols)");
+    FE_CUDA(cudaMalloc(&s->csr4_val, sizeof(float4) * groups), "cudaMalloc(P vals)");
     s->csr4_capacity = total;
+    s->csr4_groups = total;
+    drop_graphs(s);
   }
-  s->csr4_groups = total;
   const unsigned warp_blocks = static_cast<unsigned>((static_cast<long long>(n) * 32 + 255) / 256);
   fill_rows_kernel<<<warp_blocks, 256, 0, st>>>(s->perm, s->rank, s->row_ptr, s->col, s->val, n, s->row_ptr4,
                                                 reinterpret_cast<int*>(s->csr4_col),
                                                 reinterpret_cast<float*>(s->csr4_val));
   FE_LAUNCH("fill_rows_kernel");
-  FE_CUDA(cudaStreamSynchronize(st), "cudaStreamSynchronize(fill rows)");
   s->identity_perm = false;
-  if (s->graph) {
-    cudaGraphExecDestroy(s->graph);
-    s->graph = nullptr;
-  }
   return 0;
 }
 

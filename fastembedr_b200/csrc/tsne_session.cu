@@ -63,6 +63,11 @@ int store_caller_order(TsneSession* s, const float2* src, bool host, float* dst,
 
 }  // namespace
 
+void drop_graphs(TsneSession* s) {
+  for (TsneSession::GraphEntry& e : s->graphs) cudaGraphExecDestroy(e.exec);
+  s->graphs.clear();
+}
+
 int default_grid_size(int n) {
   const int fallback = n >= 50000 ? 256 : (n >= 10000 ? 128 : 64);
   const int requested = env_int("FASTEMBEDR_TSNE_FFT_GRID", fallback);
@@ -116,6 +121,11 @@ int session_create(TsneSession** out, int n, int grid, int* d_row_ptr, int* d_co
     return 1;
   }
 
+  if (reorder_temp_bytes(n, &s->ro_temp_bytes)) {
+    if (s->own_stream) cudaStreamDestroy(s->stream);
+    delete s;
+    return 1;
+  }
   const int g = grid;
   const size_t cells = static_cast<size_t>(g) * g;
   const size_t spec = static_cast<size_t>(g) * (g + 1);
@@ -141,6 +151,16 @@ int session_create(TsneSession** out, int n, int grid, int* d_row_ptr, int* d_co
     s->colspec = a.take<float2>(4 * spec);
     s->pot = a.take<float4>(cells);
     s->twiddle = a.take<float2>(m / 2);
+    s->ro_keys = a.take<unsigned int>(n);
+    s->ro_keys_sorted = a.take<unsigned int>(n);
+    s->ro_idx = a.take<int>(n);
+    s->ro_order = a.take<int>(n);
+    s->ro_perm = a.take<int>(n);
+    s->ro_rank = a.take<int>(n);
+    s->ro_groups = a.take<int>(static_cast<size_t>(n) + 1);
+    s->ro_update = a.take<float2>(n);
+    s->ro_gains = a.take<float2>(n);
+    s->ro_temp = a.take<char>(s->ro_temp_bytes);
     if (pass == 0) {
       if (memory_preflight(a.planned(), "t-SNE workspace preflight") || a.commit("t-SNE workspace")) {
         session_destroy(s);
@@ -177,7 +197,7 @@ int session_create(TsneSession** out, int n, int grid, int* d_row_ptr, int* d_co
 void session_destroy(TsneSession* s) {
   if (s == nullptr) return;
   if (s->stream) cudaStreamSynchronize(s->stream);
-  if (s->graph) cudaGraphExecDestroy(s->graph);
+  drop_graphs(s);
   for (cudaEvent_t e : s->events) cudaEventDestroy(e);
   if (s->row_ptr) cudaFree(s->row_ptr);
   if (s->col) cudaFree(s->col);
@@ -226,7 +246,6 @@ int session_reset_state(TsneSession* s) {
   FE_CUDA(cudaMemsetAsync(s->update, 0, sizeof(float2) * s->n, s->stream), "memset update");
   fill_float2_kernel<<<(s->n + 255) / 256, 256, 0, s->stream>>>(s->gains, s->n, make_float2(1.0f, 1.0f));
   FE_LAUNCH("fill gains");
-  FE_CUDA(cudaStreamSynchronize(s->stream), "cudaStreamSynchronize(reset)");
   return 0;
 }
 
@@ -248,6 +267,53 @@ int collect_profile(TsneSession* s) {
   return 0;
 }
 
+// The captured chunk of `iters` iterations for this parameter set starting at
+// the current buffer parity; captured on first use.  Capturing only records
+// launches, so it can overlap device work already queued on the stream.
+cudaGraphExec_t chunk_graph(TsneSession* s, int iters, const float key[5]) {
+  for (TsneSession::GraphEntry& e : s->graphs) {
+    if (e.iters == iters && e.cur == s->cur && std::memcmp(key, e.params, sizeof(e.params)) == 0) {
+      e.used = ++s->graph_clock;
+      return e.exec;
+    }
+  }
+  constexpr size_t kMaxGraphs = 8;
+  if (s->graphs.size() >= kMaxGraphs) {
+    auto lru = std::min_element(s->graphs.begin(), s->graphs.end(),
+                                [](const TsneSession::GraphEntry& a, const TsneSession::GraphEntry& b) {
+                                  return a.used < b.used;
+                                });
+    cudaGraphExecDestroy(lru->exec);
+    s->graphs.erase(lru);
+  }
+  const int saved_cur = s->cur;
+  cudaGraph_t g = nullptr;
+  if (check_cuda(cudaStreamBeginCapture(s->stream, cudaStreamCaptureModeThreadLocal), "cudaStreamBeginCapture")) {
+    return nullptr;
+  }
+  int rc = 0;
+  for (int it = 0; it < iters && rc == 0; ++it) {
+    rc = launch_iteration(s, kGradUpdate, key[0], key[1], key[2], key[3], key[4]);
+  }
+  const cudaError_t end = cudaStreamEndCapture(s->stream, &g);
+  s->cur = saved_cur;
+  if (rc != 0 || end != cudaSuccess) {
+    if (g) cudaGraphDestroy(g);
+    if (rc == 0) check_cuda(end, "cudaStreamEndCapture");
+    return nullptr;
+  }
+  TsneSession::GraphEntry e{};
+  const cudaError_t inst = cudaGraphInstantiate(&e.exec, g, 0);
+  cudaGraphDestroy(g);
+  if (check_cuda(inst, "cudaGraphInstantiate")) return nullptr;
+  e.iters = iters;
+  e.cur = saved_cur;
+  std::memcpy(e.params, key, sizeof(e.params));
+  e.used = ++s->graph_clock;
+  s->graphs.push_back(e);
+  return e.exec;
+}
+
 // Runs `iters` iterations with one parameter set and no reorder in between.
 int iterate_block(TsneSession* s, int iters, float exaggeration, float momentum, float learning_rate,
                   float min_gain, float max_step_norm) {
@@ -261,45 +327,17 @@ int iterate_block(TsneSession* s, int iters, float exaggeration, float momentum,
     }
     return collect_profile(s);
   }
-  // One captured chunk of up to 24 iterations per parameter set (the reference
-  // captures chunks of 25, src/embedding_cuda_kernels.cpp:5902-5985).  An even
-  // chunk returns the y double buffer to the parity it was captured with.
-  const int chunk = std::min(iters, 24) & ~1;
+  // Captured chunks of up to 24 iterations (the reference captures chunks of
+  // 25, src/embedding_cuda_kernels.cpp:5902-5985).  Chunks have an even length,
+  // so a chunk returns the layout double buffer to the parity it started from.
   const float key[5] = {exaggeration, momentum, learning_rate, min_gain, max_step_norm};
   int done = 0;
-  if (chunk >= 2) {
-    const bool reuse = s->graph != nullptr && s->graph_iters == chunk && s->graph_cur == s->cur &&
-                       std::memcmp(key, s->graph_params, sizeof(key)) == 0;
-    if (!reuse) {
-      if (s->graph) {
-        cudaGraphExecDestroy(s->graph);
-        s->graph = nullptr;
-      }
-      const int saved_cur = s->cur;
-      cudaGraph_t g = nullptr;
-      FE_CUDA(cudaStreamBeginCapture(s->stream, cudaStreamCaptureModeThreadLocal), "cudaStreamBeginCapture");
-      int rc = 0;
-      for (int it = 0; it < chunk && rc == 0; ++it) {
-        rc = launch_iteration(s, kGradUpdate, exaggeration, momentum, learning_rate, min_gain, max_step_norm);
-      }
-      const cudaError_t end = cudaStreamEndCapture(s->stream, &g);
-      s->cur = saved_cur;
-      if (rc != 0 || end != cudaSuccess) {
-        if (g) cudaGraphDestroy(g);
-        if (rc == 0) check_cuda(end, "cudaStreamEndCapture");
-        return 1;
-      }
-      const cudaError_t inst = cudaGraphInstantiate(&s->graph, g, 0);
-      cudaGraphDestroy(g);
-      FE_CUDA(inst, "cudaGraphInstantiate");
-      s->graph_iters = chunk;
-      s->graph_cur = saved_cur;
-      std::memcpy(s->graph_params, key, sizeof(key));
-    }
-    while (iters - done >= chunk) {
-      FE_CUDA(cudaGraphLaunch(s->graph, s->stream), "cudaGraphLaunch(t-SNE chunk)");
-      done += chunk;
-    }
+  while (iters - done >= 2) {
+    const int chunk = std::min(iters - done, 24) & ~1;
+    cudaGraphExec_t exec = chunk_graph(s, chunk, key);
+    if (exec == nullptr) return 1;
+    FE_CUDA(cudaGraphLaunch(exec, s->stream), "cudaGraphLaunch(t-SNE chunk)");
+    done += chunk;
   }
   for (; done < iters; ++done) {
     FE_TRY(launch_iteration(s, kGradUpdate, exaggeration, momentum, learning_rate, min_gain, max_step_norm));

@@ -228,6 +228,30 @@ def _cuda_ok():
         return False
 
 
+def shared_inputs(args, rank: int, world: int, local: int):
+    """The workload's KNN and init, made on rank 0 and broadcast, so that every
+    rank of a sharded run holds identical inputs."""
+    import torch
+    import torch.distributed as tdist
+
+    if world == 1:
+        return make_inputs(args.workload, f"cuda:{local}")
+    from fastembedr_b200 import synthetic as S
+
+    w = WORKLOADS[args.workload]
+    n, k = S.CONFIGS[w["spec"]].n, w["k"]
+    if rank == 0:
+        idx, dist, init = make_inputs(args.workload, f"cuda:{local}")
+        t = [torch.from_numpy(idx).cuda(), torch.from_numpy(dist).cuda(), torch.from_numpy(init).cuda()]
+    else:
+        t = [torch.empty((n, k), dtype=torch.int32, device="cuda"),
+             torch.empty((n, k), dtype=torch.float32, device="cuda"),
+             torch.empty((n, 2), dtype=torch.float32, device="cuda")]
+    for x in t:
+        tdist.broadcast(x, 0)
+    return tuple(x.cpu().numpy() for x in t)
+
+
 def bench_ours(args):
     import torch
     import torch.distributed as tdist
@@ -237,9 +261,10 @@ def bench_ours(args):
     rank, world, local = dist_env()
     torch.cuda.set_device(local)
     if world > 1:
-        tdist.init_process_group("nccl", init_method="env://", timeout=__import__("datetime").timedelta(seconds=300))
+        tdist.init_process_group("nccl", init_method="env://", timeout=__import__("datetime").timedelta(seconds=300),
+                                 device_id=torch.device("cuda", local))
     w = WORKLOADS[args.workload]
-    idx, dist, init = make_inputs(args.workload, f"cuda:{local}")
+    idx, dist, init = shared_inputs(args, rank, world, local)
     n, k = idx.shape
     if not api.cuda_available():
         raise RuntimeError("libfastembedr_b200 reports no usable B200")
@@ -249,6 +274,10 @@ def bench_ours(args):
     d_dist = torch.from_numpy(dist).cuda()
     t0 = time.time()
     sess = api.TsneSession.from_knn(d_idx, d_dist, perplexity=w["perplexity"], init=init)
+    if world > 1:
+        # One process per GPU: each rank owns 1/world of the points (rows of P),
+        # the charge grid is all-reduced and the layout all-gathered per iteration.
+        sess.shard_over()
     info = sess.info()
     log(f"[bench] rank {rank}: P nnz={info['nnz']} padded={info['nnz_padded']} G={info['grid']} "
         f"(setup {time.time() - t0:.2f}s)")
@@ -258,6 +287,8 @@ def bench_ours(args):
     torch.cuda.synchronize()
     run_schedule(sess, 0, args.warmup, n)
     sess.set_layout(init_dev, reset_state=True)  # the timed region starts a fresh standard run
+    for i in (0, EE_ITER):  # both phases' iteration graphs are captured before timing
+        sess.prepare(*phase_params(i, n), MIN_GAIN, MAX_STEP)
     torch.cuda.synchronize()
     if world > 1:
         tdist.barrier()
@@ -274,20 +305,24 @@ def bench_ours(args):
         tdist.all_reduce(t, op=tdist.ReduceOp.MAX)
         elapsed_ms = float(t.item())
     ms_per_step = elapsed_ms / args.steps
-    value = world * args.steps / (elapsed_ms / 1000.0)
+    # The whole job advances one iteration per step on every rank together.
+    value = args.steps / (elapsed_ms / 1000.0)
 
     # --- per-kernel CUDA-event timing of one full standard run (roofline) ---
-    sess.set_layout(init, reset_state=True)
+    sess.set_layout(init_dev, reset_state=True)
     sess.profile(True)
     prof_iters = EE_ITER + N_ITER
-    run_schedule(sess, 0, prof_iters, n, init)
+    run_schedule(sess, 0, prof_iters, n, init_dev)
     times = sess.kernel_times()
     sess.profile(False)
     grid = info["grid"]
     nnz = info["nnz"]
     # Algorithmic bytes of one grad_update launch: row_ptr, (col, val) per symmetric entry,
     # layout read, update/gains read+write, layout write, potentials (4 floats per node).
-    alg_bytes = 4 * (n + 1) + 8 * nnz + 8 * n + 16 * n + 24 * n + 16 * grid * grid
+    # A shard streams its own rows: 1/world of the points and (rows are interleaved
+    # in Morton order) about 1/world of P.
+    rows = n / world
+    alg_bytes = 4 * (rows + 1) + 8 * nnz / world + 8 * rows + 16 * rows + 24 * rows + 16 * grid * grid
     gu_ms, gu_cnt = times["grad_update_kernel"]
     gu_avg_s = gu_ms / max(gu_cnt, 1) / 1000.0
     hbm, peak_kind = peaks()
@@ -295,9 +330,9 @@ def bench_ours(args):
     total_ms = sum(v[0] for v in times.values())
     kernel_share = {kname: round(v[0] / total_ms, 4) for kname, v in times.items()}
 
-    # --- end to end through the C ABI with pinned host buffers ---
+    # --- end to end through the public API with pinned host buffers ---
     e2e = None
-    if rank == 0 and not args.skip_e2e:
+    if not args.skip_e2e and world == 1:
         idx_cm = torch.from_numpy(np.ascontiguousarray(idx.T)).pin_memory()
         dist_cm = torch.from_numpy(np.ascontiguousarray(dist.T)).pin_memory()
         init_h = torch.from_numpy(init).pin_memory()
@@ -324,6 +359,33 @@ def bench_ours(args):
                "h2d_bytes_per_step": int(idx_cm.numel() * 4 + dist_cm.numel() * 4 + init_h.numel() * 4),
                "d2h_bytes_per_step": int(out_h.numel() * 4), "seconds_per_call": e2e_s,
                "call": "fastembedr_cuda_opentsne_fft_from_knn_float (750 iterations, host KNN)"}
+    elif not args.skip_e2e:
+        # Every rank: pinned host KNN -> device, P build, shard (communicator set-up
+        # included), 750 iterations, layout back to the host.  Max over ranks.
+        idx_h = torch.from_numpy(idx).pin_memory()
+        dist_h = torch.from_numpy(dist).pin_memory()
+        out_h = torch.empty((n, 2), dtype=torch.float32).pin_memory()
+
+        def call():
+            d_i = idx_h.cuda(non_blocking=True)
+            d_d = dist_h.cuda(non_blocking=True)
+            torch.cuda.synchronize()
+            with api.TsneSession.from_knn(d_i, d_d, perplexity=w["perplexity"], init=init) as s2:
+                s2.shard_over()
+                s2.run(EE_ITER, N_ITER, EE, EX, "auto", MOM, MOM, MIN_GAIN, MAX_STEP)
+
+        call()
+        tdist.barrier()
+        t0 = time.perf_counter()
+        call()
+        e2e_s = time.perf_counter() - t0
+        t = torch.tensor([e2e_s], device="cuda")
+        tdist.all_reduce(t, op=tdist.ReduceOp.MAX)
+        e2e_s = float(t.item())
+        e2e = {"value": (EE_ITER + N_ITER) / e2e_s, "unit": "iterations/s",
+               "h2d_bytes_per_step": int(idx_h.numel() * 4 + dist_h.numel() * 4 + init.size * 4),
+               "d2h_bytes_per_step": int(out_h.numel() * 4), "seconds_per_call": e2e_s,
+               "call": "TsneSession.from_knn + shard_over + run (750 iterations, pinned host KNN), every rank"}
 
     cpu = None
     if rank == 0 and world == 1 and not args.skip_cpu:
@@ -331,25 +393,28 @@ def bench_ours(args):
 
     sess.close()
     if rank == 0:
+        per_iter = 5 if world == 1 else 6  # sharded: + layout statistics (NCCL kernels not counted)
         line = {
             "metric": "tsne_iterations_per_second", "value": value, "unit": "iterations/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
-            "higher_is_better": True, "scaling": "weak" if world > 1 else "weak",
+            "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "config": {"workload": args.workload, "n": int(n), "k": int(k), "perplexity": w["perplexity"],
                        "grid": grid, "nnz": int(nnz), "schedule": "250 early (ex 12) + 500 normal, lr n/ex",
                        "l2": "inputs larger than L2 (P is %.2f GB)" % ((8 * info["nnz_padded"]) / 1e9),
-                       "parallelism": "replicas" if world > 1 else "single"},
+                       "parallelism": f"points sharded over {world} GPUs (NCCL all-reduce of the charge grid "
+                                      f"+ all-gather of the layout per iteration)" if world > 1 else "single"},
             "roofline": {"kernel": "grad_update_kernel", "bound": "hbm", "achieved": achieved,
                          "peak": hbm, "peak_kind": peak_kind, "unit": "GB/s", "frac": achieved / hbm,
                          "algorithmic_bytes_per_launch": alg_bytes,
                          "avg_launch_ms": gu_avg_s * 1000.0,
-                         "traffic": profile_traffic("grad_update_kernel", args.workload)},
+                         "traffic": profile_traffic("grad_update_kernel", args.workload) if world == 1 else None},
             "kernel_share": kernel_share,
             "kernel_ms": {kname: v[0] / max(v[1], 1) for kname, v in times.items()},
-            # 5 kernels per iteration; 5 per spatial reorder (every 50 iterations at
-            # n >= 50k; CUB sort/scan kernels not counted); 2 per run restart.
-            "gpu_launches": 5 * args.steps + (5 * (args.steps // 50) if n >= 50000 else 0)
+            # per iteration: splat, 3 FFT passes, gradient/update (+ statistics when
+            # sharded); 5 per spatial reorder (every 50 iterations at n >= 4096;
+            # CUB sort/scan kernels not counted); 2 per run restart.
+            "gpu_launches": per_iter * args.steps + (5 * (args.steps // 50) if n >= 4096 else 0)
                             + 2 * ((args.steps - 1) // (EE_ITER + N_ITER)),
             "clocks": clocks.summary(),
             "e2e": e2e,

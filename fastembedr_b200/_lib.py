@@ -47,6 +47,7 @@ _SIGNATURES = {
     "fe_b200_tsne_create": (I, [c_void_p, c_void_p, I, I, I, F, c_float_p, U, I, I, ctypes.POINTER(c_void_p)]),
     "fe_b200_tsne_create_csr": (I, [c_int_p, c_int_p, c_float_p, I, c_float_p, I, ctypes.POINTER(c_void_p)]),
     "fe_b200_tsne_iterate": (I, [c_void_p, I, F, F, F, F, F]),
+    "fe_b200_tsne_prepare": (I, [c_void_p, F, F, F, F, F]),
     "fe_b200_tsne_gradient": (I, [c_void_p, F, c_float_p, c_double_p]),
     "fe_b200_tsne_get_layout": (I, [c_void_p, c_void_p, I]),
     "fe_b200_tsne_set_layout": (I, [c_void_p, c_void_p, I, I]),
@@ -59,6 +60,8 @@ _SIGNATURES = {
     "fe_b200_tsne_kernel_times": (I, [c_void_p, c_double_p, c_ll_p, I]),
     "fe_b200_tsne_kernel_name": (ctypes.c_char_p, [I]),
     "fe_b200_tsne_destroy": (None, [c_void_p]),
+    "fe_b200_nccl_unique_id": (I, [c_void_p, I]),
+    "fe_b200_tsne_shard": (I, [c_void_p, c_void_p, I, I, I]),
 }
 
 _lib = None

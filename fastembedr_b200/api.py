@@ -255,6 +255,12 @@ class TsneSession:
         check(_lib.load().fe_b200_tsne_iterate(self._h, n_iter, exaggeration, momentum, learning_rate,
                                                min_gain, max_step_norm), "fe_b200_tsne_iterate")
 
+    def prepare(self, exaggeration: float, momentum: float, learning_rate: float, min_gain: float = 0.01,
+                max_step_norm: float = 5.0) -> None:
+        """Captures the iteration graphs for this parameter set ahead of iterate()."""
+        check(_lib.load().fe_b200_tsne_prepare(self._h, exaggeration, momentum, learning_rate, min_gain,
+                                               max_step_norm), "fe_b200_tsne_prepare")
+
     def run(self, early_exaggeration_iter=250, n_iter=500, early_exaggeration=12.0, exaggeration=1.0,
             learning_rate="auto", initial_momentum=0.8, final_momentum=0.8, min_gain=0.01,
             max_step_norm=5.0) -> np.ndarray:
@@ -328,12 +334,33 @@ class TsneSession:
         check(_lib.load().fe_b200_tsne_profile(self._h, int(enable)), "fe_b200_tsne_profile")
 
     def kernel_times(self) -> Dict[str, Tuple[float, int]]:
-        ms = np.zeros(5, np.float64)
-        cnt = np.zeros(5, np.int64)
+        """Per-kind CUDA-event totals (ms, launches) since profiling was enabled;
+        the collective kinds appear only for sharded sessions."""
+        kinds = 8
+        ms = np.zeros(kinds, np.float64)
+        cnt = np.zeros(kinds, np.int64)
         L = _lib.load()
-        check(L.fe_b200_tsne_kernel_times(self._h, _ptr(ms, ctypes.c_double), _ptr(cnt, ctypes.c_longlong), 5),
-              "fe_b200_tsne_kernel_times")
-        return {L.fe_b200_tsne_kernel_name(i).decode(): (float(ms[i]), int(cnt[i])) for i in range(5)}
+        check(L.fe_b200_tsne_kernel_times(self._h, _ptr(ms, ctypes.c_double), _ptr(cnt, ctypes.c_longlong),
+                                          kinds), "fe_b200_tsne_kernel_times")
+        return {L.fe_b200_tsne_kernel_name(i).decode(): (float(ms[i]), int(cnt[i]))
+                for i in range(kinds) if i < 5 or cnt[i] > 0}
+
+    def shard(self, unique_id: bytes, nranks: int, rank: int) -> None:
+        """Makes this session rank `rank` of an nranks-way sharded run (one
+        process per GPU).  Every rank must hold an identical session and make
+        the same calls from then on; see fe_b200_tsne_shard."""
+        uid = (ctypes.c_ubyte * len(unique_id)).from_buffer_copy(unique_id)
+        check(_lib.load().fe_b200_tsne_shard(self._h, uid, len(unique_id), nranks, rank), "fe_b200_tsne_shard")
+
+    def shard_over(self, group=None) -> None:
+        """Shards over a torch.distributed process group (any backend): rank 0
+        makes the communicator id and the group broadcasts it."""
+        import torch.distributed as dist
+
+        box = [nccl_unique_id() if dist.get_rank(group) == 0 else None]
+        dist.broadcast_object_list(box, src=dist.get_global_rank(group, 0) if group is not None else 0,
+                                   group=group)
+        self.shard(box[0], dist.get_world_size(group), dist.get_rank(group))
 
     def close(self) -> None:
         if self._h is not None and self._h.value:
@@ -351,6 +378,23 @@ class TsneSession:
             self.close()
         except Exception:
             pass
+
+
+def nccl_unique_id() -> bytes:
+    """A new NCCL communicator id (128 bytes) for TsneSession.shard."""
+    buf = (ctypes.c_ubyte * 128)()
+    check(_lib.load().fe_b200_nccl_unique_id(buf, 128), "fe_b200_nccl_unique_id")
+    return bytes(buf)
+
+
+def shard_rows(n: int, nranks: int, rank: int) -> Tuple[int, int]:
+    """Internal rows [begin, end) that `rank` owns in an nranks-way sharded
+    t-SNE session: blocks of ceil(n / nranks) rows rounded up to whole warps
+    (32 rows), the last block short (mirrors session_shard)."""
+    per = -(-n // nranks)
+    per = (per + 31) & ~31
+    begin = min(n, rank * per)
+    return begin, min(n, begin + per)
 
 
 # ------------------------------------------------------------------ UMAP

@@ -24,9 +24,9 @@ INCLUDE = os.path.join(ROOT, "include")
 LIB = os.path.join(PKG, "libfastembedr_b200.so")
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 
-SOURCES = ["common.cu", "tsne_affinity.cu", "tsne_kernels.cu", "tsne_session.cu", "tsne_reorder.cu", "umap.cu",
-           "umap_graph.cu", "umap_noalloc.cu", "capi.cu"]
-HEADERS = ["fe_common.cuh", "tsne.cuh", "umap.cuh"]
+SOURCES = ["common.cu", "nccl_loader.cu", "tsne_affinity.cu", "tsne_kernels.cu", "tsne_session.cu",
+           "tsne_reorder.cu", "tsne_shard.cu", "umap.cu", "umap_graph.cu", "umap_noalloc.cu", "capi.cu"]
+HEADERS = ["fe_common.cuh", "nccl_loader.cuh", "tsne.cuh", "umap.cuh"]
 
 NVCC_FLAGS = [
     "-std=c++17", "-O3", "-lineinfo", "--fmad=false",
@@ -78,7 +78,7 @@ def build(force: bool = False, verbose: bool = False, jobs: int = 0) -> str:
         raise RuntimeError("nvcc compilation failed")
     # Export only the public C ABI: every extern "C" symbol is marked default
     # visibility by the header's linkage; internal C++ stays hidden.
-    link = [NVCC, "-shared", "-gencode", "arch=compute_100a,code=sm_100a", *objs, "-o", LIB + ".tmp"]
+    link = [NVCC, "-shared", "-gencode", "arch=compute_100a,code=sm_100a", *objs, "-ldl", "-o", LIB + ".tmp"]
     subprocess.run(link, check=True)
     os.replace(LIB + ".tmp", LIB)
     return LIB

@@ -4,6 +4,7 @@
 #pragma GCC visibility push(default)
 #include "fastembedr_b200.h"
 #pragma GCC visibility pop
+#include "nccl_loader.cuh"
 #include "tsne.cuh"
 #include "umap.cuh"
 
@@ -550,6 +551,16 @@ int fe_b200_tsne_iterate(fe_b200_tsne* h, int n_iter, float exaggeration, float 
   return fe::session_iterate(h->impl, n_iter, exaggeration, momentum, learning_rate, min_gain, max_step_norm);
 }
 
+int fe_b200_tsne_prepare(fe_b200_tsne* h, float exaggeration, float momentum, float learning_rate,
+                         float min_gain, float max_step_norm) {
+  fe::clear_error();
+  if (h == nullptr) {
+    set_error("invalid t-SNE session call");
+    return 1;
+  }
+  return fe::session_prepare(h->impl, exaggeration, momentum, learning_rate, min_gain, max_step_norm);
+}
+
 int fe_b200_tsne_gradient(fe_b200_tsne* h, float exaggeration, float* grad, double* z) {
   fe::clear_error();
   if (h == nullptr || grad == nullptr) {
@@ -644,6 +655,29 @@ void fe_b200_tsne_destroy(fe_b200_tsne* h) {
   if (h == nullptr) return;
   fe::session_destroy(h->impl);
   delete h;
+}
+
+int fe_b200_nccl_unique_id(unsigned char* id, int id_bytes) {
+  fe::clear_error();
+  if (id == nullptr || id_bytes < static_cast<int>(sizeof(ncclUniqueId))) {
+    set_error("fe_b200_nccl_unique_id: need a buffer of at least 128 bytes");
+    return 1;
+  }
+  const fe::NcclApi* api = fe::nccl_api();
+  if (api == nullptr) return 1;
+  ncclUniqueId uid;
+  FE_TRY(fe::check_nccl(api->GetUniqueId(&uid), "ncclGetUniqueId"));
+  std::memcpy(id, &uid, sizeof(uid));
+  return 0;
+}
+
+int fe_b200_tsne_shard(fe_b200_tsne* h, const unsigned char* id, int id_bytes, int nranks, int rank) {
+  fe::clear_error();
+  if (h == nullptr || id == nullptr || id_bytes < static_cast<int>(sizeof(ncclUniqueId))) {
+    set_error("invalid t-SNE shard call");
+    return 1;
+  }
+  return fe::session_shard(h->impl, id, nranks, rank);
 }
 
 // ---------------------------------------------------------------- UMAP from KNN (device graph)

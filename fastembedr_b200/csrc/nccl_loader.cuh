@@ -1,0 +1,33 @@
+// NCCL, resolved at run time.
+//
+// The library does not link NCCL: single-GPU callers never need it, and a
+// process that already holds a libnccl.so.2 (PyTorch bundles one) must not
+// load a second copy.  The first sharded call opens "libnccl.so.2" (or the
+// path in FASTEMBEDR_B200_NCCL_LIB) with dlopen, which returns the copy
+// already loaded in the process when there is one, and resolves the handful of
+// entry points used below.  Types and enum values come from nccl.h; they are
+// part of NCCL's stable C ABI.
+#pragma once
+
+#include <nccl.h>
+
+namespace fe {
+
+struct NcclApi {
+  ncclResult_t (*GetUniqueId)(ncclUniqueId*);
+  ncclResult_t (*CommInitRank)(ncclComm_t*, int, ncclUniqueId, int);
+  ncclResult_t (*CommDestroy)(ncclComm_t);
+  ncclResult_t (*CommAbort)(ncclComm_t);
+  ncclResult_t (*AllReduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
+                            cudaStream_t);
+  ncclResult_t (*AllGather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t, cudaStream_t);
+  const char* (*GetErrorString)(ncclResult_t);
+};
+
+// The resolved table, or nullptr with the error text set.
+const NcclApi* nccl_api();
+
+// 0 on ncclSuccess; otherwise sets "<where>: <NCCL message>" and returns 1.
+int check_nccl(ncclResult_t code, const char* where);
+
+}  // namespace fe

@@ -39,8 +39,8 @@ struct LayoutStats {
   int pad0;
   double z;                   // sum_i interp(phi_q)(y_i) - n
   float inv_z;                // 1 / max(z, FLT_MIN)
-  unsigned int update_counter;  // last-block tickets
-  unsigned int fft_counter;
+  unsigned int row_groups_taken;  // grad_update_kernel work counter
+  unsigned int fft_counter;       // last-block tickets
   unsigned int stats_counter;
 };
 
@@ -202,6 +202,33 @@ struct TsneSession {
   float2* ro_gains = nullptr;
   void* ro_temp = nullptr;
   size_t ro_temp_bytes = 0;
+  // The order in which grad_update_kernel's warps take 32-row groups: most
+  // expensive first (longest-processing-time first), so the groups holding
+  // hub rows -- rows of P with thousands of entries -- start early and
+  // overlap with the many short ones instead of forming the kernel's tail.
+  // Rebuilt with the internal order.
+  int* group_order = nullptr;
+  unsigned int* group_cost = nullptr;
+  unsigned int* group_cost_sorted = nullptr;
+  int* group_ids = nullptr;
+
+  // Sharding across processes, one per GPU (session_shard).  Every rank holds
+  // the whole layout; rank r owns internal rows [row_begin, row_end), the r-th
+  // block of rows_per_rank rows: it splats, attracts and updates only those,
+  // the charge grid is summed with one all-reduce and the updated rows are
+  // all-gathered, in place, once per iteration.  Blocks are whole multiples
+  // of 32 rows, so a warp never straddles two ranks and the splat combines the
+  // same lanes as an unsharded run; point arrays have room for the padding of
+  // the last block (kPadRows).
+  static constexpr int kMaxRanks = 256;
+  static constexpr int kPadRows = 32 * kMaxRanks;
+  bool sharded = false;
+  int shard_ranks = 1;
+  int shard_rank = 0;
+  int rows_per_rank = 0;
+  int row_begin = 0;
+  int row_end = 0;
+  void* comm = nullptr;  // ncclComm_t
 
   // Spatial ordering: internal point r is the caller's point perm[r], and
   // caller point i is internal point rank[i].
@@ -218,7 +245,10 @@ enum KernelKind {
   kKindFftCols = 2,
   kKindFftRowsInv = 3,
   kKindGradUpdate = 4,
-  kKindCount = 5
+  kKindChargeSum = 5,     // sharded: all-reduce of the charge grid
+  kKindLayoutGather = 6,  // sharded: all-gather of the updated rows
+  kKindLayoutStats = 7,   // statistics of the new layout
+  kKindCount = 8
 };
 const char* kernel_kind_name(int kind);
 
@@ -244,6 +274,10 @@ int session_random_layout(TsneSession* s, unsigned int seed);
 int session_iterate(TsneSession* s, int iters, float exaggeration, float momentum,
                     float learning_rate, float min_gain, float max_step_norm);
 int session_gradient(TsneSession* s, float exaggeration, float* grad_host, double* z_out);
+// Captures the iteration chunks of one parameter set now, so that a later
+// session_iterate with these parameters launches without capturing.
+int session_prepare(TsneSession* s, float exaggeration, float momentum, float learning_rate, float min_gain,
+                    float max_step_norm);
 int session_get_layout(TsneSession* s, float* out, bool host);
 // Optimizer state in the caller's point order.
 int session_set_state(TsneSession* s, const float* update, const float* gains, bool host);
@@ -251,6 +285,18 @@ int session_get_state(TsneSession* s, float* update, float* gains, bool host);
 int session_reset_state(TsneSession* s);
 // Unpadded CSR P in the caller's point order, columns ascending.
 int session_get_p(TsneSession* s, int* row_ptr, int* col, float* val);
+
+// ---- sharding (tsne_shard.cu) ----
+// Joins an nranks-way NCCL communicator (unique_id: ncclUniqueId bytes from
+// rank 0) and makes this session rank `rank` of a sharded run.  Every rank
+// must hold an identical session (same P, layout and state) and make the same
+// calls in the same order from then on.
+int session_shard(TsneSession* s, const void* unique_id, int nranks, int rank);
+// In-place all-gather of the per-rank row blocks of a point array.
+int shard_gather_rows(TsneSession* s, float2* rows);
+// Sum of the charge grids of all ranks, in place.
+int shard_sum_charges(TsneSession* s);
+void shard_release(TsneSession* s);
 
 // ---- ordering and the internal copy of P (tsne_reorder.cu) ----
 // Chooses the internal point order -- Morton order of the current layout when
@@ -261,6 +307,8 @@ int session_get_p(TsneSession* s, int* row_ptr, int* col, float* val);
 int session_reorder(TsneSession* s, bool by_layout);
 // CUB temporary storage the reorder needs for n points.
 int reorder_temp_bytes(int n, size_t* bytes);
+// Orders this rank's 32-row groups by estimated cost, most expensive first.
+int build_group_order(TsneSession* s);
 // Drops every captured iteration chunk.
 void drop_graphs(TsneSession* s);
 // out[perm[r]] = in[r] (internal -> caller order) and out[r] = in[perm[r]].
@@ -270,6 +318,8 @@ int launch_permute_in(TsneSession* s, const float2* in, float2* out);
 // ---- kernels (tsne_kernels.cu) ----
 // Raises per-kernel dynamic shared-memory limits for this session's FFT size.
 int configure_kernels(TsneSession* s);
+// Grid and block size of the fused gradient/update kernel for `rows` rows.
+void grad_update_launch_shape(int rows, int* blocks, int* threads);
 int launch_stats(TsneSession* s, int center);
 int launch_iteration(TsneSession* s, GradMode mode, float exaggeration, float momentum,
                      float learning_rate, float min_gain, float max_step_norm);

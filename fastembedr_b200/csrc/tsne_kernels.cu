@@ -27,6 +27,7 @@
 #include "tsne.cuh"
 
 #include <cfloat>
+#include <climits>
 
 namespace fe {
 namespace {
@@ -218,33 +219,55 @@ __device__ void stats_block_finish(StatsAcc a, double* __restrict__ partials,
   }
 }
 
-__global__ void layout_stats_kernel(const float2* __restrict__ y, int n, double* partials,
-                                    LayoutStats* stats, int center) {
+// Two points per 16-byte load; a fixed grid and fixed reduction order, so the
+// result depends only on the layout.
+__global__ void __launch_bounds__(512) layout_stats_kernel(const float2* __restrict__ y, int n,
+                                                           double* partials, LayoutStats* stats, int center) {
   StatsAcc a;
   stats_init(a);
-  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
-    stats_add(a, y[i]);
+  const int pairs = n >> 1;
+  const float4* y2 = reinterpret_cast<const float4*>(y);
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < pairs; i += gridDim.x * blockDim.x) {
+    const float4 v = y2[i];
+    stats_add(a, make_float2(v.x, v.y));
+    stats_add(a, make_float2(v.z, v.w));
   }
+  if ((n & 1) && blockIdx.x == 0 && threadIdx.x == 0) stats_add(a, y[n - 1]);
   stats_block_finish(a, partials, stats, &stats->stats_counter, center);
 }
 
 // ------------------------------------------------------------------ splat
 
-__device__ __forceinline__ void add_fixed(unsigned long long* dst, float v, double scale) {
-  const long long q = __double2ll_rn(static_cast<double>(v) * scale);
-  if (q != 0) atomicAdd(dst, static_cast<unsigned long long>(q));
+__device__ __forceinline__ long long to_fixed(float v, double scale) {
+  return __double2ll_rn(static_cast<double>(v) * scale);
 }
 
-// One thread per point.  Lanes of a warp whose points share a grid cell
-// (common: the layout is compact early on, and points are stored in Morton
-// order later) first sum their 12 contributions in lane order, then the
-// lowest such lane adds the sums with 64-bit integer atomics.
-__global__ void splat_kernel(float2* __restrict__ y, const LayoutStats* __restrict__ stats, int n,
-                             int g, ChargeCell* __restrict__ charges) {
+constexpr int kSplatThreads = 256;
+constexpr int kSplatTileNodes = 1024;  // 3 x 8 KB of 64-bit charges in shared memory
+
+// One thread per point, blocks of 256 consecutive (Morton-ordered) points.
+//  1. Lanes of a warp whose points share a grid cell sum their 12
+//     contributions (4 corner nodes x {1, x, y}) in lane order; the lowest
+//     such lane converts the sums to 64-bit fixed point.
+//  2. When the block's cells fit in a tile of at most 1024 grid nodes (the
+//     usual case: consecutive points are spatially close), those lanes add
+//     into the tile with shared-memory atomics and the block then adds each
+//     non-zero tile node to the grid once; otherwise they add to the grid
+//     directly.  Integer sums are exact, so both routes give the same charges.
+// Every point is centred; only points in [own_begin, own_end) are spread (a
+// shard spreads its own rows, the charge grids of all shards are then summed).
+__global__ void __launch_bounds__(kSplatThreads) splat_kernel(float2* __restrict__ y,
+                                                              LayoutStats* __restrict__ stats, int n, int g,
+                                                              ChargeCell* __restrict__ charges, int own_begin,
+                                                              int own_end) {
+  __shared__ unsigned long long tile[3][kSplatTileNodes];
+  __shared__ int s_box[4][kSplatThreads / 32];
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
-  const int lane = threadIdx.x & 31;
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
   const GridGeom q = grid_geometry(*stats, n, g);
+  if (i == 0) stats->row_groups_taken = 0u;  // work counter of this iteration's grad_update_kernel
   int key = -1;
+  Cell c{0, 0, 0.f, 0.f};
   float v[12];
 #pragma unroll
   for (int t = 0; t < 12; ++t) v[t] = 0.0f;
@@ -255,7 +278,10 @@ __global__ void splat_kernel(float2* __restrict__ y, const LayoutStats* __restri
       p.y -= q.mean_y;
       y[i] = p;
     }
-    const Cell c = grid_cell(p.x, p.y, q, g);
+  }
+  if (i >= own_begin && i < own_end) {
+    const float2 p = y[i];
+    c = grid_cell(p.x, p.y, q, g);
     key = c.y0 * g + c.x0;
     const float w[4] = {(1.0f - c.tx) * (1.0f - c.ty), c.tx * (1.0f - c.ty), (1.0f - c.tx) * c.ty,
                         c.tx * c.ty};
@@ -266,29 +292,100 @@ __global__ void splat_kernel(float2* __restrict__ y, const LayoutStats* __restri
       v[3 * k + 2] = w[k] * p.y;
     }
   }
+  const ChargeScales sc = charge_scales(q, n, g);
   const unsigned int peers = __match_any_sync(0xffffffffu, key);
   const int leader = __ffs(peers) - 1;
   if (__popc(peers) > 1) {
-    float s[12];
+    float sum[12];
 #pragma unroll
-    for (int t = 0; t < 12; ++t) s[t] = 0.0f;
+    for (int t = 0; t < 12; ++t) sum[t] = 0.0f;
     for (unsigned int m = peers; m; m &= m - 1) {
       const int src = __ffs(m) - 1;
 #pragma unroll
-      for (int t = 0; t < 12; ++t) s[t] += __shfl_sync(peers, v[t], src);
+      for (int t = 0; t < 12; ++t) sum[t] += __shfl_sync(peers, v[t], src);
     }
 #pragma unroll
-    for (int t = 0; t < 12; ++t) v[t] = s[t];
+    for (int t = 0; t < 12; ++t) v[t] = sum[t];
   }
-  if (key < 0 || lane != leader) return;
-  const ChargeScales sc = charge_scales(q, n, g);
-  const int corner[4] = {key, key + 1, key + g, key + g + 1};
+  const bool active = key >= 0 && lane == leader;
+  long long f[12];
+  if (active) {
 #pragma unroll
-  for (int k = 0; k < 4; ++k) {
-    ChargeCell* cell = charges + corner[k];
-    add_fixed(&cell->m, v[3 * k], sc.m);
-    add_fixed(&cell->mx, v[3 * k + 1], sc.xy);
-    add_fixed(&cell->my, v[3 * k + 2], sc.xy);
+    for (int k = 0; k < 4; ++k) {
+      f[3 * k] = to_fixed(v[3 * k], sc.m);
+      f[3 * k + 1] = to_fixed(v[3 * k + 1], sc.xy);
+      f[3 * k + 2] = to_fixed(v[3 * k + 2], sc.xy);
+    }
+  }
+
+  // Node box of the block's points (cells plus their +1 corners).
+  const bool own = key >= 0;
+  int x_lo = own ? c.x0 : INT_MAX, y_lo = own ? c.y0 : INT_MAX;
+  int x_hi = own ? c.x0 + 1 : INT_MIN, y_hi = own ? c.y0 + 1 : INT_MIN;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    x_lo = min(x_lo, __shfl_xor_sync(0xffffffffu, x_lo, o));
+    y_lo = min(y_lo, __shfl_xor_sync(0xffffffffu, y_lo, o));
+    x_hi = max(x_hi, __shfl_xor_sync(0xffffffffu, x_hi, o));
+    y_hi = max(y_hi, __shfl_xor_sync(0xffffffffu, y_hi, o));
+  }
+  if (lane == 0) {
+    s_box[0][wid] = x_lo;
+    s_box[1][wid] = y_lo;
+    s_box[2][wid] = x_hi;
+    s_box[3][wid] = y_hi;
+  }
+  __syncthreads();
+  x_lo = INT_MAX, y_lo = INT_MAX, x_hi = INT_MIN, y_hi = INT_MIN;
+  for (int w = 0; w < kSplatThreads / 32; ++w) {
+    x_lo = min(x_lo, s_box[0][w]);
+    y_lo = min(y_lo, s_box[1][w]);
+    x_hi = max(x_hi, s_box[2][w]);
+    y_hi = max(y_hi, s_box[3][w]);
+  }
+  if (x_hi < x_lo) return;  // no point of this block is spread (block-uniform)
+  const int box_w = x_hi - x_lo + 1, box_h = y_hi - y_lo + 1;
+  const bool tiled = box_w * box_h <= kSplatTileNodes;  // block-uniform
+
+  if (!tiled) {
+    if (!active) return;
+    const int corner[4] = {key, key + 1, key + g, key + g + 1};
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      ChargeCell* cell = charges + corner[k];
+      const long long a = f[3 * k], b = f[3 * k + 1], d = f[3 * k + 2];
+      if (a != 0) atomicAdd(&cell->m, static_cast<unsigned long long>(a));
+      if (b != 0) atomicAdd(&cell->mx, static_cast<unsigned long long>(b));
+      if (d != 0) atomicAdd(&cell->my, static_cast<unsigned long long>(d));
+    }
+    return;
+  }
+  const int nodes = box_w * box_h;
+  for (int t = threadIdx.x; t < nodes; t += kSplatThreads) {
+    tile[0][t] = 0ull;
+    tile[1][t] = 0ull;
+    tile[2][t] = 0ull;
+  }
+  __syncthreads();
+  if (active) {
+    const int base = (c.y0 - y_lo) * box_w + (c.x0 - x_lo);
+    const int corner[4] = {base, base + 1, base + box_w, base + box_w + 1};
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const long long a = f[3 * k], b = f[3 * k + 1], d = f[3 * k + 2];
+      if (a != 0) atomicAdd(&tile[0][corner[k]], static_cast<unsigned long long>(a));
+      if (b != 0) atomicAdd(&tile[1][corner[k]], static_cast<unsigned long long>(b));
+      if (d != 0) atomicAdd(&tile[2][corner[k]], static_cast<unsigned long long>(d));
+    }
+  }
+  __syncthreads();
+  for (int t = threadIdx.x; t < nodes; t += kSplatThreads) {
+    const int ty = t / box_w, tx = t - ty * box_w;
+    ChargeCell* cell = charges + static_cast<size_t>(y_lo + ty) * g + (x_lo + tx);
+    const unsigned long long a = tile[0][t], b = tile[1][t], d = tile[2][t];
+    if (a != 0ull) atomicAdd(&cell->m, a);
+    if (b != 0ull) atomicAdd(&cell->mx, b);
+    if (d != 0ull) atomicAdd(&cell->my, d);
   }
 }
 
@@ -489,6 +586,8 @@ __global__ void fft_rows_inv_kernel(const float2* __restrict__ colspec, ChargeCe
 
 struct UpdateParams {
   int n;
+  int row_begin;   // rows [row_begin, row_end) are attracted and updated
+  int row_end;
   int g;
   float exaggeration;
   float momentum;
@@ -546,30 +645,34 @@ __device__ __forceinline__ void attract4(float yix, float yiy, int4 c, float4 v,
   }
 }
 
-// 64 registers (4 blocks of 256 per SM): measured faster than the unbounded
-// 78-register build despite a few spilled bytes.
+// 64 registers: four blocks of 256 threads per SM, and the grid is exactly
+// the resident capacity (one wave).  Warps take 32-row groups from a global
+// counter (reset by the splat of the same iteration) in group_order, most
+// expensive group first, so no warp idles while another still holds a long
+// row and the heaviest groups do not form a tail; there is no block barrier.
 __global__ void __launch_bounds__(256, 4) grad_update_kernel(
     const int* __restrict__ row_ptr4, const int4* __restrict__ col4, const float4* __restrict__ val4,
     const float2* __restrict__ y, float2* __restrict__ y_next, float2* __restrict__ update,
     float2* __restrict__ gains, float2* __restrict__ grad_out, const float4* __restrict__ pot,
-    LayoutStats* __restrict__ stats, double* __restrict__ partials, UpdateParams prm) {
+    LayoutStats* __restrict__ stats, const int* __restrict__ group_order, UpdateParams prm) {
   const int lane = threadIdx.x & 31;
   const int sub = lane >> 3;  // which of the 4 rows of a round
   const int sl = lane & 7;    // lane within the row
-  const int warps_per_block = blockDim.x >> 5;
-  const int warp_global = blockIdx.x * warps_per_block + (threadIdx.x >> 5);
-  const int n_warps = gridDim.x * warps_per_block;
   const float ex = prm.exaggeration;
   const int4 zero_c = make_int4(0, 0, 0, 0);
   const float4 zero_v = make_float4(0.f, 0.f, 0.f, 0.f);
-  StatsAcc acc;
-  stats_init(acc);
-  for (int row0 = warp_global * 32; row0 < prm.n; row0 += n_warps * 32) {
+  const int groups = (prm.row_end - prm.row_begin + 31) >> 5;
+  for (;;) {
+    int ticket = 0;
+    if (lane == 0) ticket = static_cast<int>(atomicAdd(&stats->row_groups_taken, 1u));
+    ticket = __shfl_sync(0xffffffffu, ticket, 0);
+    if (ticket >= groups) break;
+    const int row0 = prm.row_begin + __ldg(group_order + ticket) * 32;
     float my_ax = 0.f, my_ay = 0.f;
 #pragma unroll 1
     for (int it = 0; it < 8; ++it) {
       const int row = row0 + 4 * it + sub;
-      const bool rv = row < prm.n;
+      const bool rv = row < prm.row_end;
       const int beg = rv ? __ldg(row_ptr4 + row) : 0;
       const int end = rv ? __ldg(row_ptr4 + row + 1) : 0;
       const float2 yi = rv ? y[row] : make_float2(0.f, 0.f);
@@ -619,7 +722,7 @@ __global__ void __launch_bounds__(256, 4) grad_update_kernel(
     }
     // Epilogue: lane L finishes row row0 + 4 (L % 8) + L / 8.
     const int row = row0 + 4 * sl + sub;
-    if (row >= prm.n) continue;
+    if (row >= prm.row_end) continue;
     const float2 yi = y[row];
     const GridGeom q = grid_geometry(*stats, prm.n, prm.g);
     const Cell c = grid_cell(yi.x, yi.y, q, prm.g);
@@ -665,10 +768,6 @@ __global__ void __launch_bounds__(256, 4) grad_update_kernel(
     update[row] = u;
     gains[row] = gn;
     y_next[row] = yn;
-    stats_add(acc, yn);
-  }
-  if (prm.mode == kGradUpdate) {
-    stats_block_finish(acc, partials, stats, &stats->update_counter, 1);
   }
 }
 
@@ -695,8 +794,16 @@ const char* kernel_kind_name(int kind) {
     case kKindFftCols: return "fft_cols_kernel";
     case kKindFftRowsInv: return "fft_rows_inv_kernel";
     case kKindGradUpdate: return "grad_update_kernel";
+    case kKindChargeSum: return "charge_allreduce";
+    case kKindLayoutGather: return "layout_allgather";
+    case kKindLayoutStats: return "layout_stats_kernel";
     default: return "?";
   }
+}
+
+void grad_update_launch_shape(int rows, int* blocks, int* threads) {
+  *threads = 256;  // 8 warps, each taking 32-row groups
+  *blocks = std::max(1, std::min(sm_count() * 4, (rows + 255) / 256));
 }
 
 int configure_kernels(TsneSession* s) {
@@ -711,8 +818,8 @@ int configure_kernels(TsneSession* s) {
 }
 
 int launch_stats(TsneSession* s, int center) {
-  const int blocks = std::min(1024, (s->n + 255) / 256);
-  layout_stats_kernel<<<blocks, 256, 0, s->stream>>>(s->y[s->cur], s->n, s->update_partials, s->stats, center);
+  const int blocks = std::max(1, std::min(2 * sm_count(), (s->n / 2 + 511) / 512));
+  layout_stats_kernel<<<blocks, 512, 0, s->stream>>>(s->y[s->cur], s->n, s->update_partials, s->stats, center);
   FE_LAUNCH("layout_stats_kernel");
   return 0;
 }
@@ -747,8 +854,13 @@ int launch_iteration(TsneSession* s, GradMode mode, float exaggeration, float mo
   const int row_len = g + 1;
   {
     ProfileScope ps(s, kKindSplat);
-    splat_kernel<<<(s->n + 255) / 256, 256, 0, s->stream>>>(s->y[s->cur], s->stats, s->n, g, s->charges);
+    splat_kernel<<<(s->n + kSplatThreads - 1) / kSplatThreads, kSplatThreads, 0, s->stream>>>(
+        s->y[s->cur], s->stats, s->n, g, s->charges, s->row_begin, s->row_end);
     FE_LAUNCH("splat_kernel");
+  }
+  if (s->sharded) {
+    ProfileScope ps(s, kKindChargeSum);
+    FE_TRY(shard_sum_charges(s));
   }
   {
     ProfileScope ps(s, kKindFftRows);
@@ -772,14 +884,24 @@ int launch_iteration(TsneSession* s, GradMode mode, float exaggeration, float mo
   }
   {
     ProfileScope ps(s, kKindGradUpdate);
-    UpdateParams prm{s->n, g, exaggeration, momentum, learning_rate, min_gain, max_step_norm,
-                     static_cast<int>(mode)};
+    UpdateParams prm{s->n, s->row_begin, s->row_end, g, exaggeration, momentum,
+                     learning_rate, min_gain, max_step_norm, static_cast<int>(mode)};
     grad_update_kernel<<<s->update_blocks, s->update_threads, 0, s->stream>>>(
         s->row_ptr4, s->csr4_col, s->csr4_val, s->y[s->cur], s->y[s->cur ^ 1], s->update,
-        s->gains, s->grad_out, s->pot, s->stats, s->update_partials, prm);
+        s->gains, s->grad_out, s->pot, s->stats, s->group_order, prm);
     FE_LAUNCH("grad_update_kernel");
   }
-  if (mode == kGradUpdate) s->cur ^= 1;
+  if (mode != kGradUpdate) return 0;
+  s->cur ^= 1;
+  if (s->sharded) {
+    // Every rank now holds its own updated rows: gather the others'.
+    ProfileScope ps(s, kKindLayoutGather);
+    FE_TRY(shard_gather_rows(s, s->y[s->cur]));
+  }
+  // Statistics of the whole new layout for the next iteration's grid, in one
+  // fixed reduction order (so identical on every rank of a sharded run).
+  ProfileScope ps(s, kKindLayoutStats);
+  FE_TRY(launch_stats(s, 1));
   return 0;
 }
 

@@ -80,12 +80,13 @@ __global__ void permute_points_kernel(const int* __restrict__ order, int n, cons
 // columns, padded with (own row, 0) to a whole group.
 __global__ void fill_rows_kernel(const int* __restrict__ perm, const int* __restrict__ rank,
                                  const int* __restrict__ row_ptr, const int* __restrict__ col,
-                                 const float* __restrict__ val, int n, const int* __restrict__ row_ptr4,
-                                 int* __restrict__ out_col, float* __restrict__ out_val) {
+                                 const float* __restrict__ val, int row_begin, int row_end,
+                                 const int* __restrict__ row_ptr4, int* __restrict__ out_col,
+                                 float* __restrict__ out_val) {
   const long long gid = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
-  const int r = static_cast<int>(gid >> 5);
+  const int r = row_begin + static_cast<int>(gid >> 5);
   const int lane = static_cast<int>(gid & 31);
-  if (r >= n) return;
+  if (r >= row_end) return;
   const int caller = perm[r];
   const int beg = row_ptr[caller];
   const int len = row_ptr[caller + 1] - beg;
@@ -114,10 +115,48 @@ __global__ void permute_in_kernel(const float2* __restrict__ in, const int* __re
   if (r < n) out[r] = in[perm[r]];
 }
 
+// Cost of a 32-row group for the attraction kernel: per round of four rows,
+// the passes of the longest row (a pass covers 16 groups of four entries),
+// plus one for the round's epilogue.
+__global__ void group_cost_kernel(const int* __restrict__ row_ptr4, int row_begin, int row_end, int groups,
+                                  unsigned int* __restrict__ cost, int* __restrict__ ids) {
+  const int grp = blockIdx.x * blockDim.x + threadIdx.x;
+  if (grp >= groups) return;
+  const int row0 = row_begin + grp * 32;
+  unsigned int total = 0;
+  for (int round = 0; round < 8; ++round) {
+    int passes = 0;
+    for (int sub = 0; sub < 4; ++sub) {
+      const int row = row0 + 4 * round + sub;
+      if (row < row_end) passes = max(passes, (row_ptr4[row + 1] - row_ptr4[row] + 15) >> 4);
+    }
+    total += static_cast<unsigned int>(passes) + 1u;
+  }
+  cost[grp] = total;
+  ids[grp] = grp;
+}
+
 }  // namespace
 
+int build_group_order(TsneSession* s) {
+  const int groups = (s->row_end - s->row_begin + 31) / 32;
+  if (groups <= 0) return 0;
+  group_cost_kernel<<<(groups + 255) / 256, 256, 0, s->stream>>>(s->row_ptr4, s->row_begin, s->row_end, groups,
+                                                                 s->group_cost, s->group_ids);
+  FE_LAUNCH("group_cost_kernel");
+  size_t tb = s->ro_temp_bytes;
+  FE_CUDA(cub::DeviceRadixSort::SortPairsDescending(s->ro_temp, tb, s->group_cost, s->group_cost_sorted,
+                                                    s->group_ids, s->group_order, groups, 0, 32, s->stream),
+          "cub::DeviceRadixSort(group cost)");
+  return 0;
+}
+
 int reorder_temp_bytes(int n, size_t* bytes) {
-  size_t sort_bytes = 0, scan_bytes = 0;
+  size_t sort_bytes = 0, scan_bytes = 0, desc_bytes = 0;
+  FE_CUDA(cub::DeviceRadixSort::SortPairsDescending(nullptr, desc_bytes, static_cast<unsigned int*>(nullptr),
+                                                    static_cast<unsigned int*>(nullptr), static_cast<int*>(nullptr),
+                                                    static_cast<int*>(nullptr), n / 32 + 1, 0, 32),
+          "cub::DeviceRadixSort(sizing)");
   FE_CUDA(cub::DeviceRadixSort::SortPairs(nullptr, sort_bytes, static_cast<unsigned int*>(nullptr),
                                           static_cast<unsigned int*>(nullptr), static_cast<int*>(nullptr),
                                           static_cast<int*>(nullptr), n, 0, 30),
@@ -125,7 +164,7 @@ int reorder_temp_bytes(int n, size_t* bytes) {
   FE_CUDA(cub::DeviceScan::ExclusiveSum(nullptr, scan_bytes, static_cast<int*>(nullptr),
                                         static_cast<int*>(nullptr), n + 1),
           "cub::DeviceScan(sizing)");
-  *bytes = std::max(sort_bytes, scan_bytes);
+  *bytes = std::max(std::max(sort_bytes, scan_bytes), desc_bytes);
   return 0;
 }
 
@@ -134,6 +173,12 @@ int session_reorder(TsneSession* s, bool by_layout) {
   const unsigned blocks = static_cast<unsigned>((n + 255) / 256);
   cudaStream_t st = s->stream;
   const int cur = s->cur;
+  if (s->sharded) {
+    // Each rank's optimizer state is current on its own rows only; rows
+    // change owners with the new order.
+    FE_TRY(shard_gather_rows(s, s->update));
+    FE_TRY(shard_gather_rows(s, s->gains));
+  }
 
   morton_keys_kernel<<<blocks, 256, 0, st>>>(s->y[cur], s->stats, n, s->grid, by_layout ? 1 : 0, s->ro_keys,
                                              s->ro_idx);
@@ -178,13 +223,18 @@ int session_reorder(TsneSession* s, bool by_layout) {
     s->csr4_groups = total;
     drop_graphs(s);
   }
-  const unsigned warp_blocks = static_cast<unsigned>((static_cast<long long>(n) * 32 + 255) / 256);
-  fill_rows_kernel<<<warp_blocks, 256, 0, st>>>(s->perm, s->rank, s->row_ptr, s->col, s->val, n, s->row_ptr4,
-                                                reinterpret_cast<int*>(s->csr4_col),
-                                                reinterpret_cast<float*>(s->csr4_val));
+  // Only this rank's rows are streamed by its attraction kernel; each row
+  // keeps its place in the whole-P layout of the copy.
+  const int rows = s->row_end - s->row_begin;
+  if (rows > 0) {
+    const unsigned warp_blocks = static_cast<unsigned>((static_cast<long long>(rows) * 32 + 255) / 256);
+    fill_rows_kernel<<<warp_blocks, 256, 0, st>>>(s->perm, s->rank, s->row_ptr, s->col, s->val, s->row_begin,
+                                                  s->row_end, s->row_ptr4, reinterpret_cast<int*>(s->csr4_col),
+                                                  reinterpret_cast<float*>(s->csr4_val));
+  }
   FE_LAUNCH("fill_rows_kernel");
   s->identity_perm = false;
-  return 0;
+  return build_group_order(s);
 }
 
 int launch_unpermute(TsneSession* s, const float2* in, float2* out) {

@@ -98,6 +98,9 @@ int session_create(TsneSession** out, int n, int grid, int* d_row_ptr, int* d_co
   s->reorder_every = env_int_nonneg("FASTEMBEDR_B200_REORDER_EVERY", n >= 4096 ? 50 : 0);
   if (!env_flag("FASTEMBEDR_B200_REORDER", true)) s->reorder_every = 0;
   s->next_reorder = s->reorder_every;
+  s->row_begin = 0;
+  s->row_end = n;
+  s->rows_per_rank = n;
   if (stream == nullptr) {
     if (check_cuda(cudaStreamCreateWithFlags(&s->stream, cudaStreamNonBlocking), "cudaStreamCreate")) {
       delete s;
@@ -110,11 +113,12 @@ int session_create(TsneSession** out, int n, int grid, int* d_row_ptr, int* d_co
 
   // Fused gradient/update kernel: a warp per block of 32 rows, persistent
   // blocks of 8 warps, 8 blocks per SM.
-  s->update_threads = 256;
-  s->update_blocks = sm_count() * 8;
-  s->update_blocks = std::max(1, std::min(s->update_blocks, (n + 255) / 256));
+  grad_update_launch_shape(n, &s->update_blocks, &s->update_threads);
   const int m = s->fft;
-  s->cols_per_block = std::max(1, std::min(16, 2048 / m));
+  // One spectrum column per block of the column FFT pass once the transform
+  // is long enough to occupy a block (G >= 128: G + 1 blocks, measured 1.9x
+  // faster than 4 columns per block at G = 256); several for short ones.
+  s->cols_per_block = m >= 256 ? 1 : std::max(1, std::min(16, 2048 / m));
   if (configure_kernels(s)) {
     if (s->own_stream) cudaStreamDestroy(s->stream);
     delete s;
@@ -134,11 +138,12 @@ int session_create(TsneSession** out, int n, int grid, int* d_row_ptr, int* d_co
   for (int pass = 0; pass < 2; ++pass) {
     if (pass == 0) a.begin_plan();
     else a.rewind();
-    s->y[0] = a.take<float2>(n);
-    s->y[1] = a.take<float2>(n);
-    s->update = a.take<float2>(n);
-    s->gains = a.take<float2>(n);
-    s->grad_out = a.take<float2>(n);
+    const size_t rows = static_cast<size_t>(n) + TsneSession::kPadRows;  // room for shard padding
+    s->y[0] = a.take<float2>(rows);
+    s->y[1] = a.take<float2>(rows);
+    s->update = a.take<float2>(rows);
+    s->gains = a.take<float2>(rows);
+    s->grad_out = a.take<float2>(rows);
     s->perm = a.take<int>(n);
     s->rank = a.take<int>(n);
     s->row_ptr4 = a.take<int>(static_cast<size_t>(n) + 1);
@@ -161,6 +166,11 @@ int session_create(TsneSession** out, int n, int grid, int* d_row_ptr, int* d_co
     s->ro_update = a.take<float2>(n);
     s->ro_gains = a.take<float2>(n);
     s->ro_temp = a.take<char>(s->ro_temp_bytes);
+    const size_t groups = static_cast<size_t>(n) / 32 + 2;
+    s->group_order = a.take<int>(groups);
+    s->group_cost = a.take<unsigned int>(groups);
+    s->group_cost_sorted = a.take<unsigned int>(groups);
+    s->group_ids = a.take<int>(groups);
     if (pass == 0) {
       if (memory_preflight(a.planned(), "t-SNE workspace preflight") || a.commit("t-SNE workspace")) {
         session_destroy(s);
@@ -198,6 +208,7 @@ void session_destroy(TsneSession* s) {
   if (s == nullptr) return;
   if (s->stream) cudaStreamSynchronize(s->stream);
   drop_graphs(s);
+  shard_release(s);
   for (cudaEvent_t e : s->events) cudaEventDestroy(e);
   if (s->row_ptr) cudaFree(s->row_ptr);
   if (s->col) cudaFree(s->col);
@@ -237,6 +248,10 @@ int session_set_state(TsneSession* s, const float* update, const float* gains, b
 }
 
 int session_get_state(TsneSession* s, float* update, float* gains, bool host) {
+  if (s->sharded) {
+    FE_TRY(shard_gather_rows(s, s->update));
+    FE_TRY(shard_gather_rows(s, s->gains));
+  }
   FE_TRY(store_caller_order(s, s->update, host, update, s->grad_out));
   FE_TRY(store_caller_order(s, s->gains, host, gains, s->grad_out));
   return 0;
@@ -266,6 +281,8 @@ int collect_profile(TsneSession* s) {
   s->event_kind.clear();
   return 0;
 }
+
+constexpr int kLongChunk = 24;
 
 // The captured chunk of `iters` iterations for this parameter set starting at
 // the current buffer parity; captured on first use.  Capturing only records
@@ -327,13 +344,16 @@ int iterate_block(TsneSession* s, int iters, float exaggeration, float momentum,
     }
     return collect_profile(s);
   }
-  // Captured chunks of up to 24 iterations (the reference captures chunks of
-  // 25, src/embedding_cuda_kernels.cpp:5902-5985).  Chunks have an even length,
-  // so a chunk returns the layout double buffer to the parity it started from.
+  // Captured chunks of 24 iterations (the reference captures chunks of 25,
+  // src/embedding_cuda_kernels.cpp:5902-5985) and of 2 for the rest.  Only
+  // these two lengths exist, so a parameter set needs at most two captures
+  // however the reorders cut the iterations, and both can be made ahead of
+  // time (session_prepare).  Even lengths return the layout double buffer to
+  // the parity a chunk started from.
   const float key[5] = {exaggeration, momentum, learning_rate, min_gain, max_step_norm};
   int done = 0;
   while (iters - done >= 2) {
-    const int chunk = std::min(iters - done, 24) & ~1;
+    const int chunk = iters - done >= kLongChunk ? kLongChunk : 2;
     cudaGraphExec_t exec = chunk_graph(s, chunk, key);
     if (exec == nullptr) return 1;
     FE_CUDA(cudaGraphLaunch(exec, s->stream), "cudaGraphLaunch(t-SNE chunk)");
@@ -364,10 +384,21 @@ int session_iterate(TsneSession* s, int iters, float exaggeration, float momentu
   return 0;
 }
 
+int session_prepare(TsneSession* s, float exaggeration, float momentum, float learning_rate, float min_gain,
+                    float max_step_norm) {
+  if (!s->use_graphs) return 0;
+  const float key[5] = {exaggeration, momentum, learning_rate, min_gain, max_step_norm};
+  for (int chunk : {kLongChunk, 2}) {
+    if (chunk_graph(s, chunk, key) == nullptr) return 1;
+  }
+  return 0;
+}
+
 int session_gradient(TsneSession* s, float exaggeration, float* grad_host, double* z_out) {
   // Evaluated at the stored layout exactly as given (no re-centring).
   FE_TRY(launch_stats(s, 0));
   FE_TRY(launch_iteration(s, kGradOnly, exaggeration, 0.f, 0.f, 0.f, 0.f));
+  if (s->sharded) FE_TRY(shard_gather_rows(s, s->grad_out));
   LayoutStats st;
   FE_CUDA(cudaMemcpyAsync(&st, s->stats, sizeof(st), cudaMemcpyDeviceToHost, s->stream), "D2H stats");
   FE_TRY(store_caller_order(s, s->grad_out, true, grad_host, s->y[s->cur ^ 1]));

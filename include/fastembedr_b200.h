@@ -204,6 +204,10 @@ int fe_b200_tsne_create_csr(const int* row_ptr, const int* col, const float* val
 /* Runs n_iter optimizer iterations with fixed phase parameters. */
 int fe_b200_tsne_iterate(fe_b200_tsne* s, int n_iter, float exaggeration, float momentum,
                          float learning_rate, float min_gain, float max_step_norm);
+/* Captures the CUDA graphs that fe_b200_tsne_iterate launches for this
+ * parameter set, ahead of the first iterate with it (no iteration is run). */
+int fe_b200_tsne_prepare(fe_b200_tsne* s, float exaggeration, float momentum, float learning_rate,
+                         float min_gain, float max_step_norm);
 /* Gradient at the current layout without updating it (grad: host float[n*2]). */
 int fe_b200_tsne_gradient(fe_b200_tsne* s, float exaggeration, float* grad, double* z);
 /* Current (centred) layout to host (on_device = 0) or device memory. */
@@ -220,11 +224,30 @@ int fe_b200_tsne_get_p(fe_b200_tsne* s, int* row_ptr, int* col, float* val);
 /* The cudaStream_t the session launches on. */
 void* fe_b200_tsne_stream(fe_b200_tsne* s);
 /* Per-kernel CUDA-event timing: enable, then read per-kind totals
- * (kinds: 0 splat, 1 fft rows, 2 fft cols, 3 fft rows inverse, 4 gradient+update). */
+ * (kinds: 0 splat, 1 fft rows, 2 fft cols, 3 fft rows inverse, 4 gradient+update,
+ * and for sharded sessions 5 charge all-reduce, 6 layout all-gather, 7 layout statistics). */
 int fe_b200_tsne_profile(fe_b200_tsne* s, int enable);
 int fe_b200_tsne_kernel_times(fe_b200_tsne* s, double* ms, long long* launches, int kinds);
 const char* fe_b200_tsne_kernel_name(int kind);
 void fe_b200_tsne_destroy(fe_b200_tsne* s);
+
+/* ---- sharding one t-SNE run across GPUs (one process per GPU) ----
+ * No counterpart in the reference's C ABI: the reference's multi-GPU build
+ * keeps one process and picks devices itself (src/embedding_cuda_impl.cpp:24-380
+ * declares no such call).  NCCL is loaded at run time ("libnccl.so.2", or the
+ * path in FASTEMBEDR_B200_NCCL_LIB).
+ *
+ * fe_b200_nccl_unique_id writes the id_bytes (>= 128) byte identifier of a new
+ * communicator; one rank makes it and the host hands the bytes to every rank.
+ * fe_b200_tsne_shard then joins the communicator (blocking until all nranks
+ * ranks have joined) and makes the session rank `rank` of the run: each rank
+ * spreads, attracts and updates its own block of points, the charge grid is
+ * all-reduced and the updated points all-gathered every iteration.  Every
+ * rank must create an identical session (same P, layout, grid) on its own
+ * GPU, and from then on make the same session calls with the same arguments
+ * in the same order.  Results are bit-identical for any number of ranks. */
+int fe_b200_nccl_unique_id(unsigned char* id, int id_bytes);
+int fe_b200_tsne_shard(fe_b200_tsne* s, const unsigned char* id, int id_bytes, int nranks, int rank);
 
 /* ---- UMAP parity hook ---- */
 /* Runs epochs [epoch_begin, epoch_end) of the COO optimizer on layout

@@ -1,0 +1,121 @@
+"""Sharded t-SNE on B200s, one process per GPU, through the C ABI.
+
+Each rank spreads, attracts and updates its own block of points; the charge
+grid is summed with an NCCL all-reduce and the updated points are all-gathered
+every iteration.  Charges are 64-bit fixed point and every rank reduces the
+layout statistics of the gathered layout in one fixed order, so a run on any
+number of ranks must give the same bits as a one-rank sharded run; a one-rank
+sharded run must give the unsharded session's gradient exactly and its layout
+to within the rounding of the (differently ordered) layout-mean sums.
+
+The two-rank test needs two GPUs and is skipped on a one-GPU box.
+"""
+import os
+import subprocess
+import sys
+
+if __name__ == "__main__":  # a rank process of the two-GPU test
+    sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+
+import numpy as np
+import pytest
+
+from fastembedr_b200 import api
+from fastembedr_b200 import synthetic as S
+
+pytestmark = pytest.mark.gpu
+
+N, K, PERPLEXITY = 6000, 45, 15.0  # n >= 4096: the run crosses spatial reorders
+EARLY, LATE = 100, 60
+
+
+def _problem_arrays():
+    x, _ = S.gaussian_mixture(S.MixtureSpec(n=N, components=8, seed=3))
+    idx, dist = S.exact_knn(x, K)
+    return idx, dist, S.tsne_init(N, seed=1)
+
+
+def run_session(idx, dist, init, shard=None):
+    """Gradient at the init, then EARLY + LATE iterations: final layout and state."""
+    lr_e, lr_l = float(np.float32(N / 12.0)), float(np.float32(N / 1.0))
+    with api.TsneSession.from_knn(idx, dist, perplexity=PERPLEXITY, init=init) as s:
+        if shard is not None:
+            s.shard(*shard)
+        grad, z = s.gradient(12.0)
+        s.iterate(EARLY, 12.0, 0.8, lr_e)
+        s.iterate(LATE, 1.0, 0.8, lr_l)
+        y = s.layout()
+        upd, gains = s.state()
+    return {"grad": grad, "z": np.float64(z), "y": y, "update": upd, "gains": gains}
+
+
+@pytest.fixture(scope="module")
+def problem(tmp_path_factory):
+    idx, dist, init = _problem_arrays()
+    path = tmp_path_factory.mktemp("shard") / "problem.npz"
+    np.savez(path, idx=idx, dist=dist, init=init)
+    return str(path)
+
+
+def test_one_rank_shard_matches_unsharded(problem):
+    p = np.load(problem)
+    plain = run_session(p["idx"], p["dist"], p["init"])
+    one = run_session(p["idx"], p["dist"], p["init"], shard=(api.nccl_unique_id(), 1, 0))
+    assert np.array_equal(one["grad"], plain["grad"])
+    assert one["z"] == plain["z"]
+    assert np.isfinite(one["y"]).all()
+    rel = np.linalg.norm(one["y"] - plain["y"]) / np.linalg.norm(plain["y"])
+    assert rel < 1e-3, rel
+
+
+def test_shard_rejects_bad_ranks(problem):
+    p = np.load(problem)
+    with api.TsneSession.from_knn(p["idx"], p["dist"], perplexity=PERPLEXITY, init=p["init"]) as s:
+        with pytest.raises(api.CudaBackendError, match="nranks"):
+            s.shard(api.nccl_unique_id(), 2, 2)
+        with pytest.raises(api.CudaBackendError, match="nranks"):
+            s.shard(api.nccl_unique_id(), 0, 0)
+
+
+def _gpu_count():
+    import torch
+
+    return torch.cuda.device_count()
+
+
+@pytest.mark.skipif(_gpu_count() < 2, reason="needs two GPUs")
+def test_two_ranks_bit_identical_to_one_rank(problem, tmp_path):
+    uid = api.nccl_unique_id()
+    procs = []
+    for rank in range(2):
+        out = tmp_path / f"rank{rank}.npz"
+        env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+        procs.append((out, subprocess.Popen([sys.executable, __file__, problem, uid.hex(), "2", str(rank), str(out)],
+                                            env=env)))
+    try:
+        codes = [p.wait(timeout=300) for _, p in procs]
+    finally:
+        for _, p in procs:  # a rank left waiting for a failed peer is ended here
+            if p.poll() is None:
+                p.kill()
+                p.wait()
+    assert codes == [0, 0], codes
+    p = np.load(problem)
+    one = run_session(p["idx"], p["dist"], p["init"], shard=(api.nccl_unique_id(), 1, 0))
+    for out, _ in procs:
+        got = np.load(out)
+        for key in ("grad", "z", "y", "update", "gains"):
+            assert np.array_equal(got[key], one[key]), key
+
+
+def _rank_main(problem, uid_hex, nranks, rank, out):
+    import torch
+
+    torch.cuda.set_device(rank)
+    p = np.load(problem)
+    res = run_session(p["idx"], p["dist"], p["init"], shard=(bytes.fromhex(uid_hex), nranks, rank))
+    np.savez(out, **res)
+
+
+if __name__ == "__main__":
+    _rank_main(sys.argv[1], sys.argv[2], int(sys.argv[3]), int(sys.argv[4]), sys.argv[5])

@@ -41,7 +41,12 @@ WORKLOADS = {
     "tsne_70k": dict(spec="tsne_70k", k=90, perplexity=30.0),
     "tsne_10k": dict(spec="tsne_10k", k=90, perplexity=30.0),
     "tsne_200k": dict(spec="tsne_200k", k=90, perplexity=30.0),
+    # UMAP configurations 1 and 4: k = 15 fuzzy graph, negative_sample_rate 5,
+    # a/b for min_dist 0.1, learning rate 1, start U(-10, 10).
+    "umap_70k": dict(spec="umap_70k", k=15, kind="umap", n_epochs=500),
+    "umap_2m": dict(spec="umap_2m", k=15, kind="umap", n_epochs=200),
 }
+UMAP_NSR, UMAP_MIN_DIST, UMAP_LR = 5, 0.1, 1.0
 EE_ITER, N_ITER, EE, EX, MOM = 250, 500, 12.0, 1.0, 0.8
 MIN_GAIN, MAX_STEP = 0.01, 5.0
 FALLBACK_HBM_GBS = 6650.0
@@ -214,6 +219,33 @@ def bench_reference(args):
         "cpu_baseline": {k: base[k] for k in ("value", "unit", "cores", "kind", "sample")},
         "e2e": {"value": base["value"], "unit": "iterations/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def bench_reference_umap(args):
+    """The reference's CPU COO optimizer on the first epochs of the workload's
+    edge list (from this library's device graph build, which follows the
+    reference's device-KNN path)."""
+    rank, _, _ = dist_env()
+    if rank != 0:
+        return 0
+    from fastembedr_b200 import api
+
+    idx, dist, init = umap_inputs(args.workload, "cuda" if _cuda_ok() else None)
+    with api.UmapSession.from_knn(idx, dist) as s:
+        graph = s.graph()
+    base = cpu_baseline_umap(graph, init)
+    line = {
+        "impl": "reference", "metric": "umap_edge_updates_per_second", "value": base["value"],
+        "unit": "edge_updates/s", "n_gpus": 0, "steps": 1, "warmup": 0,
+        "ms_per_step": None, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "f32", "data": "synthetic",
+        "config": {"workload": args.workload, "n": int(idx.shape[0]), "k": int(idx.shape[1]),
+                   "n_edges": int(graph["heads"].size)},
+        "cpu_baseline": {k: base[k] for k in ("value", "unit", "cores", "kind", "sample")},
+        "e2e": {"value": base["value"], "unit": "edge_updates/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
     return 0
@@ -427,6 +459,167 @@ def bench_ours(args):
     return 0
 
 
+def umap_inputs(workload: str, device):
+    from fastembedr_b200 import synthetic as S
+
+    w = WORKLOADS[workload]
+    spec = S.CONFIGS[w["spec"]]
+    t0 = time.time()
+    x, _ = S.gaussian_mixture(spec)
+    idx, dist = S.exact_knn(x, w["k"], device=device)
+    log(f"[bench] {workload}: n={spec.n} k={w['k']} inputs in {time.time() - t0:.1f}s")
+    return idx, dist, S.umap_random_init(spec.n, seed=0)
+
+
+def cpu_baseline_umap(graph, init, epochs: int = 0):
+    """The reference's own CPU COO optimizer (fast_knn_umap_coo_replay_cpp) on
+    the same edge list, epochs 0 .. epochs-1 of a schedule, all host threads.
+    Early epochs apply fewer positive samples than the schedule's average (an
+    edge of period p first fires at epoch p), so the sample runs long enough
+    for most edges to have fired: 100 epochs up to 5M edges, else 20."""
+    import oracle as O
+
+    threads = os.cpu_count() or 1
+    h, t, p = graph["heads"], graph["tails"], graph["epochs_per_sample"].astype(np.float32)
+    if epochs <= 0:
+        epochs = 100 if h.size <= 5_000_000 else 20
+    pos = int(np.floor(np.float32(epochs - 1) / p).astype(np.int64).sum())
+    if O.ref_available():
+        t0 = time.time()
+        O.ref_umap_coo_replay(h, t, (1.0 / p).astype(np.float32), p, init, epochs, min_dist=UMAP_MIN_DIST,
+                              negative_sample_rate=UMAP_NSR, learning_rate=UMAP_LR, threads=threads)
+        secs, kind, cores = time.time() - t0, "reference", threads
+    else:
+        t0 = time.time()
+        y = init.copy()
+        for e in range(epochs):
+            y = O.umap_epoch_delta(h, t, p, y, e, epochs)
+        secs, kind, cores = time.time() - t0, "port", 1
+    return {"value": pos / secs, "unit": "edge_updates/s", "cores": cores, "kind": kind,
+            "sample": f"epochs 0-{epochs - 1} of the full edge list ({h.size} edges, {pos} positive samples), "
+                      f"{cores} threads"}
+
+
+def bench_umap(args):
+    """A step is one UMAP epoch over the whole edge list; the metric counts
+    positive edge samples applied per second (negative samples alongside)."""
+    import torch
+
+    from fastembedr_b200 import _lib, api
+
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    w = WORKLOADS[args.workload]
+    n_epochs = w["n_epochs"]
+    idx, dist, init = umap_inputs(args.workload, f"cuda:{local}")
+    n, k = idx.shape
+    a, b = api.find_ab_params(1.0, UMAP_MIN_DIST)
+    d_idx, d_dist = torch.from_numpy(idx).cuda(), torch.from_numpy(dist).cuda()
+    t0 = time.time()
+    sess = api.UmapSession.from_knn(d_idx, d_dist)
+    info = sess.info()
+    log(f"[bench] umap: n={n} edges={info['n_edges']} (set-up {time.time() - t0:.2f}s)")
+    del d_idx, d_dist
+    init_dev = torch.from_numpy(init).cuda()
+    stream = torch.cuda.ExternalStream(sess.stream)
+
+    def spans(e0, count):
+        """(cyc_begin, cyc_end) pieces of epochs e0 .. e0+count of back-to-back runs of the schedule."""
+        e = e0
+        while e < e0 + count:
+            cyc = e % n_epochs
+            step = min(n_epochs - cyc, e0 + count - e)
+            yield cyc, cyc + step
+            e += step
+
+    def run(e0, count):
+        for c0, c1 in spans(e0, count):
+            if c0 == 0:
+                sess.set_layout(init_dev)  # a new run of the schedule starts from the init
+            sess.run(c0, c1, n_epochs, UMAP_NSR, UMAP_LR, UMAP_MIN_DIST, seed=42, optimizer_mode=0)
+
+    run(0, args.warmup)
+    torch.cuda.synchronize()
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        start.record(stream)
+        run(0, args.steps)
+        stop.record(stream)
+        torch.cuda.synchronize()
+    elapsed_ms = start.elapsed_time(stop)
+    pos = neg = 0
+    for c0, c1 in spans(0, args.steps):
+        p_, n_ = sess.count_samples(c0, c1, UMAP_NSR)
+        pos, neg = pos + p_, neg + n_
+    value = pos / (elapsed_ms / 1000.0)
+
+    # Device time per epoch of single-epoch launches (epoch kernel + sanitize);
+    # algorithmic bytes 12 E + 16 N (head, tail, period per edge; layout read + write).
+    sess.set_layout(init_dev)
+    probe = list(range(1, min(n_epochs, 41)))
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+    ev[0].record(stream)
+    for e in probe:
+        sess.run(e, e + 1, n_epochs, UMAP_NSR, UMAP_LR, UMAP_MIN_DIST, seed=42, optimizer_mode=0)
+    ev[1].record(stream)
+    torch.cuda.synchronize()
+    epoch_s = ev[0].elapsed_time(ev[1]) / 1000.0 / len(probe)
+    alg_bytes = 12 * info["n_edges"] + 16 * n
+    hbm, peak_kind = peaks()
+    achieved = alg_bytes / epoch_s / 1e9
+
+    graph = sess.graph()
+    e2e = None
+    if not args.skip_e2e:
+        idx_cm = torch.from_numpy(np.ascontiguousarray(idx.T)).pin_memory()
+        dist_cm = torch.from_numpy(np.ascontiguousarray(dist.T)).pin_memory()
+        out_h = torch.empty((n, 2), dtype=torch.float32).pin_memory()
+        import ctypes
+
+        L = _lib.load()
+        sni = api.umap_config(n, k)["spectral_n_iter"]
+
+        def call():
+            rc = L.fastembedr_cuda_umap_from_knn_spectral_float(
+                ctypes.c_void_p(idx_cm.data_ptr()), ctypes.c_void_p(dist_cm.data_ptr()), n, k, n_epochs,
+                UMAP_NSR, UMAP_LR, a, b, 1.0, sni, 42, 0, 0,
+                ctypes.cast(out_h.data_ptr(), ctypes.POINTER(ctypes.c_float)))
+            _lib.check(rc, "fastembedr_cuda_umap_from_knn_spectral_float")
+
+        call()
+        t0 = time.perf_counter()
+        call()
+        e2e_s = time.perf_counter() - t0
+        total_pos, _ = sess.count_samples(0, n_epochs, UMAP_NSR)
+        e2e = {"value": total_pos / e2e_s, "unit": "edge_updates/s",
+               "h2d_bytes_per_step": int(idx_cm.numel() * 4 + dist_cm.numel() * 4),
+               "d2h_bytes_per_step": int(out_h.numel() * 4), "seconds_per_call": e2e_s,
+               "call": f"fastembedr_cuda_umap_from_knn_spectral_float ({n_epochs} epochs, host KNN: graph, "
+                       f"diffusion start, epochs)"}
+    cpu = None if args.skip_cpu else cpu_baseline_umap(graph, init)
+    sess.close()
+    line = {
+        "metric": "umap_edge_updates_per_second", "value": value, "unit": "edge_updates/s",
+        "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": elapsed_ms / args.steps,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic",
+        "config": {"workload": args.workload, "n": int(n), "k": int(k), "n_edges": int(info["n_edges"]),
+                   "n_epochs": n_epochs, "negative_sample_rate": UMAP_NSR, "min_dist": UMAP_MIN_DIST,
+                   "optimizer": "Hogwild per sample (device-KNN path)", "init": "U(-10, 10)",
+                   "l2": "edge list %.2f GB" % (12 * info["n_edges"] / 1e9)},
+        "negative_samples_per_second": neg / (elapsed_ms / 1000.0),
+        "epochs_per_second": args.steps / (elapsed_ms / 1000.0),
+        "roofline": {"kernel": "umap_epoch_kernel (+ sanitize)", "bound": "hbm", "achieved": achieved,
+                     "peak": hbm, "peak_kind": peak_kind, "unit": "GB/s", "frac": achieved / hbm,
+                     "algorithmic_bytes_per_launch": alg_bytes, "avg_launch_ms": epoch_s * 1000.0,
+                     "traffic": profile_traffic("umap_epoch_kernel", args.workload)},
+        "gpu_launches": 2 * args.steps,
+        "clocks": clocks.summary(), "e2e": e2e, "cpu_baseline": cpu,
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -440,8 +633,13 @@ def main():
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be at least 3")
+    umap = WORKLOADS[args.workload].get("kind") == "umap"
     if args.impl == "reference":
-        return bench_reference(args)
+        return bench_reference_umap(args) if umap else bench_reference(args)
+    if umap:
+        if dist_env()[1] > 1:
+            ap.error("the UMAP workloads run on one GPU")
+        return bench_umap(args)
     return bench_ours(args)
 
 

@@ -61,6 +61,15 @@ _SIGNATURES = {
     "fe_b200_tsne_kernel_name": (ctypes.c_char_p, [I]),
     "fe_b200_tsne_destroy": (None, [c_void_p]),
     "fe_b200_nccl_unique_id": (I, [c_void_p, I]),
+    "fe_b200_umap_create": (I, [c_void_p, c_void_p, I, I, I, I, I, I, U, ctypes.POINTER(c_void_p)]),
+    "fe_b200_umap_run": (I, [c_void_p, I, I, I, I, F, F, F, F, U, I]),
+    "fe_b200_umap_count_samples": (I, [c_void_p, I, I, I, c_ll_p, c_ll_p]),
+    "fe_b200_umap_get_layout": (I, [c_void_p, c_void_p, I]),
+    "fe_b200_umap_set_layout": (I, [c_void_p, c_void_p, I]),
+    "fe_b200_umap_info": (I, [c_void_p, c_int_p, c_ll_p]),
+    "fe_b200_umap_get_graph": (I, [c_void_p, c_void_p, c_void_p, c_void_p]),
+    "fe_b200_umap_stream": (c_void_p, [c_void_p]),
+    "fe_b200_umap_destroy": (None, [c_void_p]),
     "fe_b200_tsne_shard": (I, [c_void_p, c_void_p, I, I, I]),
 }
 

@@ -475,6 +475,111 @@ def umap_knn(indices, distances, n_epochs: Optional[int] = None, negative_sample
     })
 
 
+class UmapSession:
+    """The device-KNN UMAP path with its graph, edge list and layout resident
+    on the device (fe_b200_umap_*): set-up once, then epoch ranges."""
+
+    def __init__(self, handle: int, n: int):
+        self._h = ctypes.c_void_p(handle)
+        self.n = n
+
+    @classmethod
+    def from_knn(cls, indices, distances, index_offset: Optional[int] = None, graph_mode: str = "fuzzy",
+                 spectral_n_iter: Optional[int] = None, seed: int = 42) -> "UmapSession":
+        if graph_mode not in ("fuzzy", "binary"):
+            raise ValueError("graph_mode must be 'fuzzy' or 'binary'")
+        on_device = hasattr(indices, "is_cuda") and indices.is_cuda
+        n, k = int(indices.shape[0]), int(indices.shape[1])
+        sni = umap_config(n, k)["spectral_n_iter"] if spectral_n_iter is None else int(spectral_n_iter)
+        h = ctypes.c_void_p()
+        if on_device:
+            import torch
+
+            idx_cm = indices.to(torch.int32).t().contiguous()
+            dist_cm = distances.to(torch.float32).t().contiguous()
+            off = index_offset if index_offset is not None else int(
+                bool((idx_cm.min() >= 1).item() and (idx_cm.max() <= n).item()))
+            ip, dp = ctypes.c_void_p(idx_cm.data_ptr()), ctypes.c_void_p(dist_cm.data_ptr())
+        else:
+            idx = np.asarray(indices)
+            off = index_offset if index_offset is not None else resolve_index_offset(idx)
+            idx_cm = column_major(idx, np.int32)
+            dist_cm = column_major(distances, np.float32)
+            ip, dp = ctypes.c_void_p(idx_cm.ctypes.data), ctypes.c_void_p(dist_cm.ctypes.data)
+        check(_lib.load().fe_b200_umap_create(ip, dp, n, k, off, int(on_device), int(graph_mode == "binary"), sni,
+                                              seed & 0xFFFFFFFF, ctypes.byref(h)), "fe_b200_umap_create")
+        return cls(h.value, n)
+
+    def run(self, epoch_begin: int, epoch_end: int, n_epochs: int, negative_sample_rate: int = 5,
+            learning_rate: float = 1.0, min_dist: float = 0.1, repulsion_strength: float = 1.0, seed: int = 42,
+            optimizer_mode: int = 0) -> None:
+        """Epochs [epoch_begin, epoch_end) of an n_epochs schedule (0: Hogwild per sample, 1: Jacobi)."""
+        a, b = find_ab_params(1.0, min_dist)
+        check(_lib.load().fe_b200_umap_run(self._h, epoch_begin, epoch_end, n_epochs, negative_sample_rate,
+                                           learning_rate, a, b, repulsion_strength, seed & 0xFFFFFFFF,
+                                           optimizer_mode), "fe_b200_umap_run")
+
+    def count_samples(self, epoch_begin: int, epoch_end: int, negative_sample_rate: int = 5) -> Tuple[int, int]:
+        """(positive, negative) edge samples that epochs [epoch_begin, epoch_end) apply."""
+        pos, neg = ctypes.c_longlong(), ctypes.c_longlong()
+        check(_lib.load().fe_b200_umap_count_samples(self._h, epoch_begin, epoch_end, negative_sample_rate,
+                                                     ctypes.byref(pos), ctypes.byref(neg)),
+              "fe_b200_umap_count_samples")
+        return pos.value, neg.value
+
+    def layout(self) -> np.ndarray:
+        y = np.zeros((self.n, 2), np.float32)
+        check(_lib.load().fe_b200_umap_get_layout(self._h, ctypes.c_void_p(y.ctypes.data), 0),
+              "fe_b200_umap_get_layout")
+        return y
+
+    def set_layout(self, y) -> None:
+        if hasattr(y, "is_cuda") and y.is_cuda:
+            import torch
+
+            y = y.to(torch.float32).contiguous()
+            check(_lib.load().fe_b200_umap_set_layout(self._h, ctypes.c_void_p(y.data_ptr()), 1),
+                  "fe_b200_umap_set_layout")
+            return
+        y = _f32(y)
+        check(_lib.load().fe_b200_umap_set_layout(self._h, ctypes.c_void_p(y.ctypes.data), 0),
+              "fe_b200_umap_set_layout")
+
+    def info(self) -> Dict[str, int]:
+        n, e = ctypes.c_int(), ctypes.c_longlong()
+        check(_lib.load().fe_b200_umap_info(self._h, ctypes.byref(n), ctypes.byref(e)), "fe_b200_umap_info")
+        return {"n": n.value, "n_edges": e.value}
+
+    def graph(self) -> Dict[str, np.ndarray]:
+        e = self.info()["n_edges"]
+        h, t, p = np.zeros(e, np.int32), np.zeros(e, np.int32), np.zeros(e, np.float32)
+        check(_lib.load().fe_b200_umap_get_graph(self._h, ctypes.c_void_p(h.ctypes.data),
+                                                 ctypes.c_void_p(t.ctypes.data), ctypes.c_void_p(p.ctypes.data)),
+              "fe_b200_umap_get_graph")
+        return {"heads": h, "tails": t, "epochs_per_sample": p}
+
+    @property
+    def stream(self) -> int:
+        return int(_lib.load().fe_b200_umap_stream(self._h) or 0)
+
+    def close(self) -> None:
+        if self._h is not None and self._h.value:
+            _lib.load().fe_b200_umap_destroy(self._h)
+        self._h = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
 def umap_graph_dump(indices, distances, index_offset: Optional[int] = None) -> Dict[str, Any]:
     """The device-KNN fuzzy graph as a rank-major COO list
     (fastembedr_cuda_umap_graph_dump_from_knn; umap_cuda_graph_dump_impl,

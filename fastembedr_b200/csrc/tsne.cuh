@@ -31,6 +31,22 @@ struct ChargeCell {
   unsigned long long m, mx, my, pad;
 };
 
+struct GridGeom {
+  float mean_x, mean_y;
+  float lower_x, lower_y;
+  float spacing, inv_spacing;
+};
+
+// Charges are accumulated in signed 64-bit fixed point, so the splat's
+// atomics are associative and the result does not depend on their order
+// (runs are bit-reproducible, and sharded runs sum exactly).  Scales are
+// powers of two chosen so that the largest possible node total stays below
+// 2^62: sum of weights <= n, and |x|, |y| <= the grid box half extent.
+struct ChargeScales {
+  double m;   // weight scale
+  double xy;  // coordinate-weighted scale
+};
+
 struct LayoutStats {
   double sum_x, sum_y;        // sums of the raw (uncentred) layout
   float min_x, max_x;         // bounds of the raw layout
@@ -42,12 +58,11 @@ struct LayoutStats {
   unsigned int row_groups_taken;  // grad_update_kernel work counter
   unsigned int fft_counter;       // last-block tickets
   unsigned int stats_counter;
-};
-
-struct GridGeom {
-  float mean_x, mean_y;
-  float lower_x, lower_y;
-  float spacing, inv_spacing;
+  // Derived once per layout by the statistics kernel (grid_geometry and
+  // charge_scales below) and read by every later kernel of the iteration,
+  // instead of every thread re-deriving them with double divisions.
+  GridGeom geom;
+  ChargeScales scales;
 };
 
 #ifdef __CUDACC__
@@ -77,15 +92,6 @@ __device__ __forceinline__ GridGeom grid_geometry(const LayoutStats& s, int n, i
   return q;
 }
 
-// Charges are accumulated in signed 64-bit fixed point, so the splat's
-// atomics are associative and the result does not depend on their order
-// (runs are bit-reproducible).  Scales are powers of two chosen so that the
-// largest possible node total stays below 2^62: sum of weights <= n, and
-// |x|, |y| <= the grid box half extent.
-struct ChargeScales {
-  double m;   // weight scale
-  double xy;  // coordinate-weighted scale
-};
 __device__ __forceinline__ double pow2_scale_for(double max_total) {
   int e = 0;
   frexp(fmax(max_total, 1.0), &e);  // max_total < 2^e

@@ -121,7 +121,7 @@ __device__ __forceinline__ void stats_add(StatsAcc& a, float2 p) {
 // finish fold all partials into *stats.  No block waits on another.
 __device__ void stats_block_finish(StatsAcc a, double* __restrict__ partials,
                                    LayoutStats* __restrict__ stats, unsigned int* counter,
-                                   int center) {
+                                   int center, int n, int g) {
   __shared__ double s_d[2][32];
   __shared__ float s_f[4][32];
   __shared__ bool s_last;
@@ -215,13 +215,16 @@ __device__ void stats_block_finish(StatsAcc a, double* __restrict__ partials,
     stats->min_y = r.mny;
     stats->max_y = r.mxy;
     stats->center = center;
+    const GridGeom q = grid_geometry(*stats, n, g);
+    stats->geom = q;
+    stats->scales = charge_scales(q, n, g);
     *counter = 0u;
   }
 }
 
 // Two points per 16-byte load; a fixed grid and fixed reduction order, so the
 // result depends only on the layout.
-__global__ void __launch_bounds__(512) layout_stats_kernel(const float2* __restrict__ y, int n,
+__global__ void __launch_bounds__(512) layout_stats_kernel(const float2* __restrict__ y, int n, int g,
                                                            double* partials, LayoutStats* stats, int center) {
   StatsAcc a;
   stats_init(a);
@@ -233,7 +236,7 @@ __global__ void __launch_bounds__(512) layout_stats_kernel(const float2* __restr
     stats_add(a, make_float2(v.z, v.w));
   }
   if ((n & 1) && blockIdx.x == 0 && threadIdx.x == 0) stats_add(a, y[n - 1]);
-  stats_block_finish(a, partials, stats, &stats->stats_counter, center);
+  stats_block_finish(a, partials, stats, &stats->stats_counter, center, n, g);
 }
 
 // ------------------------------------------------------------------ splat
@@ -247,8 +250,10 @@ constexpr int kSplatTileNodes = 1024;  // 3 x 8 KB of 64-bit charges in shared m
 
 // One thread per point, blocks of 256 consecutive (Morton-ordered) points.
 //  1. Lanes of a warp whose points share a grid cell sum their 12
-//     contributions (4 corner nodes x {1, x, y}) in lane order; the lowest
-//     such lane converts the sums to 64-bit fixed point.
+//     contributions (4 corner nodes x {1, x, y}) -- a butterfly when the whole
+//     warp shares the cell, else in lane order -- and the lowest such lane
+//     converts the sums to 64-bit fixed point.  Sharded runs cut the points
+//     at multiples of 32, so every warp sums the same lanes on any rank count.
 //  2. When the block's cells fit in a tile of at most 1024 grid nodes (the
 //     usual case: consecutive points are spatially close), those lanes add
 //     into the tile with shared-memory atomics and the block then adds each
@@ -264,7 +269,8 @@ __global__ void __launch_bounds__(kSplatThreads) splat_kernel(float2* __restrict
   __shared__ int s_box[4][kSplatThreads / 32];
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-  const GridGeom q = grid_geometry(*stats, n, g);
+  const GridGeom q = stats->geom;
+  const ChargeScales sc = stats->scales;
   if (i == 0) stats->row_groups_taken = 0u;  // work counter of this iteration's grad_update_kernel
   int key = -1;
   Cell c{0, 0, 0.f, 0.f};
@@ -292,10 +298,20 @@ __global__ void __launch_bounds__(kSplatThreads) splat_kernel(float2* __restrict
       v[3 * k + 2] = w[k] * p.y;
     }
   }
-  const ChargeScales sc = charge_scales(q, n, g);
   const unsigned int peers = __match_any_sync(0xffffffffu, key);
   const int leader = __ffs(peers) - 1;
-  if (__popc(peers) > 1) {
+  if (peers == 0xffffffffu) {
+    // The whole warp shares one cell (dense regions, compact early layouts):
+    // a five-step butterfly.  Non-spreading warps (key -1) skip it.
+    if (key >= 0) {
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+#pragma unroll
+        for (int t = 0; t < 12; ++t) v[t] += __shfl_xor_sync(0xffffffffu, v[t], o);
+      }
+    }
+  } else if (key >= 0 && __popc(peers) > 1) {
+    // Small groups: all groups of the warp step through their members in lock step.
     float sum[12];
 #pragma unroll
     for (int t = 0; t < 12; ++t) sum[t] = 0.0f;
@@ -408,8 +424,8 @@ __global__ void fft_rows_fwd_kernel(const ChargeCell* __restrict__ charges,
   float2* z1 = smem + m;
   float2* z2 = smem + 2 * m;
   const int r = blockIdx.x;
-  const GridGeom q = grid_geometry(*stats, n, g);
-  const ChargeScales sc = charge_scales(q, n, g);
+  const GridGeom q = stats->geom;
+  const ChargeScales sc = stats->scales;
   for (int x = threadIdx.x; x < m; x += blockDim.x) {
     float3 c = make_float3(0.f, 0.f, 0.f);
     if (x < g) c = read_charge(charges[static_cast<size_t>(r) * g + x], sc);
@@ -519,7 +535,7 @@ __global__ void fft_rows_inv_kernel(const float2* __restrict__ colspec, ChargeCe
   float2* z1 = smem + m;
   const int r = blockIdx.x;
   const int row_len = g + 1;
-  const double inv_scale_m = 1.0 / charge_scales(grid_geometry(*stats, n, g), n, g).m;
+  const double inv_scale_m = 1.0 / stats->scales.m;
   for (int k = threadIdx.x; k < m; k += blockDim.x) {
     const bool mirror = k > g;
     const int kk = mirror ? m - k : k;
@@ -724,7 +740,7 @@ __global__ void __launch_bounds__(256, 4) grad_update_kernel(
     const int row = row0 + 4 * sl + sub;
     if (row >= prm.row_end) continue;
     const float2 yi = y[row];
-    const GridGeom q = grid_geometry(*stats, prm.n, prm.g);
+    const GridGeom q = stats->geom;
     const Cell c = grid_cell(yi.x, yi.y, q, prm.g);
     const float3 ph = gather_potentials(pot, c, prm.g);
     const float inv_z = stats->inv_z;
@@ -819,7 +835,8 @@ int configure_kernels(TsneSession* s) {
 
 int launch_stats(TsneSession* s, int center) {
   const int blocks = std::max(1, std::min(2 * sm_count(), (s->n / 2 + 511) / 512));
-  layout_stats_kernel<<<blocks, 512, 0, s->stream>>>(s->y[s->cur], s->n, s->update_partials, s->stats, center);
+  layout_stats_kernel<<<blocks, 512, 0, s->stream>>>(s->y[s->cur], s->n, s->grid, s->update_partials, s->stats,
+                                                     center);
   FE_LAUNCH("layout_stats_kernel");
   return 0;
 }

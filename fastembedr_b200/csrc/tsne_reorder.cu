@@ -44,7 +44,7 @@ __global__ void morton_keys_kernel(const float2* __restrict__ y, const LayoutSta
     keys[i] = 0u;  // a stable sort keeps the current order
     return;
   }
-  const GridGeom q = grid_geometry(*stats, n, g);
+  const GridGeom q = stats->geom;
   float2 p = y[i];
   p.x -= q.mean_x;
   p.y -= q.mean_y;

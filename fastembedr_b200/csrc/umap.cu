@@ -272,7 +272,32 @@ __global__ void umap_sanitize_kernel(float2* layout, float2* delta, int n, float
   layout[i] = v;
 }
 
+// Samples an edge applies over epochs [epoch_begin, epoch_end), with the
+// epoch kernel's own schedules.
+__global__ void count_samples_kernel(const float* __restrict__ periods, long long n_edges, int epoch_begin,
+                                     int epoch_end, int nsr, long long* __restrict__ pos,
+                                     long long* __restrict__ neg) {
+  const long long e = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (e >= n_edges) return;
+  const float p = periods[e];
+  long long sp = 0, sn = 0;
+  for (int epoch = epoch_begin; epoch < epoch_end; ++epoch) {
+    sp += positive_samples(p, epoch);
+    sn += negative_samples(p, nsr, epoch);
+  }
+  pos[e] = sp;
+  neg[e] = sn;
+}
+
 }  // namespace
+
+int umap_count_samples(const float* periods, long long n_edges, int epoch_begin, int epoch_end, int nsr,
+                       long long* pos, long long* neg, cudaStream_t stream) {
+  const unsigned blocks = static_cast<unsigned>((n_edges + 255) / 256);
+  count_samples_kernel<<<blocks, 256, 0, stream>>>(periods, n_edges, epoch_begin, epoch_end, nsr, pos, neg);
+  FE_LAUNCH("count_samples_kernel");
+  return 0;
+}
 
 int umap_launch_epoch(UmapRun* r, int epoch) {
   const UmapParams& p = r->params;

@@ -45,6 +45,10 @@ struct UmapRun {
 int umap_launch_epoch(UmapRun* r, int epoch);
 int umap_run_epochs(UmapRun* r, int epoch_begin, int epoch_end);
 int umap_edge_blocks(long long n_edges);
+// Per edge: positive and negative samples the epoch kernel applies over
+// epochs [epoch_begin, epoch_end).
+int umap_count_samples(const float* periods, long long n_edges, int epoch_begin, int epoch_end, int nsr,
+                       long long* pos, long long* neg, cudaStream_t stream);
 
 // ---------------------------------------------------------------- graph from KNN
 

@@ -231,6 +231,34 @@ int fe_b200_tsne_kernel_times(fe_b200_tsne* s, double* ms, long long* launches, 
 const char* fe_b200_tsne_kernel_name(int kind);
 void fe_b200_tsne_destroy(fe_b200_tsne* s);
 
+/* ---- UMAP sessions (no counterpart in the reference) ----
+ * The device-KNN UMAP path of fastembedr_cuda_umap_from_device_knn_spectral_float
+ * split into set-up and epoch ranges.  fe_b200_umap_create builds the fuzzy
+ * graph from column-major KNN (host or device pointers, float32 distances),
+ * the diffusion start (spectral_n_iter rounds) and the rank-major COO edge
+ * list, all resident on the device.  fe_b200_umap_run applies epochs
+ * [epoch_begin, epoch_end) of an n_epochs schedule (optimizer_mode 0: Hogwild
+ * per sample, 1: Jacobi), negatives keyed on the tail vertex as in the
+ * reference's COO kernels.  fe_b200_umap_count_samples returns the positive
+ * and negative edge samples that an epoch range applies. */
+typedef struct fe_b200_umap fe_b200_umap;
+int fe_b200_umap_create(const int* indices, const float* distances, int n, int k, int index_offset,
+                        int inputs_on_device, int binary_graph, int spectral_n_iter, unsigned int seed,
+                        fe_b200_umap** out);
+int fe_b200_umap_run(fe_b200_umap* s, int epoch_begin, int epoch_end, int n_epochs, int negative_sample_rate,
+                     float learning_rate, float a, float b, float repulsion_strength, unsigned int seed,
+                     int optimizer_mode);
+int fe_b200_umap_count_samples(fe_b200_umap* s, int epoch_begin, int epoch_end, int negative_sample_rate,
+                               long long* positive, long long* negative);
+/* Layout (row-major float[n*2]) to/from host (on_device = 0) or device memory. */
+int fe_b200_umap_get_layout(fe_b200_umap* s, float* out, int on_device);
+int fe_b200_umap_set_layout(fe_b200_umap* s, const float* y, int on_device);
+int fe_b200_umap_info(fe_b200_umap* s, int* n, long long* n_edges);
+/* The COO edge list (host arrays of n_edges entries; any may be NULL). */
+int fe_b200_umap_get_graph(fe_b200_umap* s, int* heads, int* tails, float* epochs_per_sample);
+void* fe_b200_umap_stream(fe_b200_umap* s);
+void fe_b200_umap_destroy(fe_b200_umap* s);
+
 /* ---- sharding one t-SNE run across GPUs (one process per GPU) ----
  * No counterpart in the reference's C ABI: the reference's multi-GPU build
  * keeps one process and picks devices itself (src/embedding_cuda_impl.cpp:24-380

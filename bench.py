@@ -504,19 +504,40 @@ def bench_umap(args):
     """A step is one UMAP epoch over the whole edge list; the metric counts
     positive edge samples applied per second (negative samples alongside)."""
     import torch
+    import torch.distributed as tdist
 
     from fastembedr_b200 import _lib, api
 
     rank, world, local = dist_env()
     torch.cuda.set_device(local)
+    if world > 1:
+        tdist.init_process_group("nccl", init_method="env://", timeout=__import__("datetime").timedelta(seconds=300),
+                                 device_id=torch.device("cuda", local))
     w = WORKLOADS[args.workload]
     n_epochs = w["n_epochs"]
-    idx, dist, init = umap_inputs(args.workload, f"cuda:{local}")
+    if world == 1 or rank == 0:
+        idx, dist, init = umap_inputs(args.workload, f"cuda:{local}")
+    if world > 1:
+        # Rank 0's inputs on every rank.
+        from fastembedr_b200 import synthetic as S
+
+        nn = S.CONFIGS[w["spec"]].n
+        t = ([torch.from_numpy(idx).cuda(), torch.from_numpy(dist).cuda(), torch.from_numpy(init).cuda()]
+             if rank == 0 else
+             [torch.empty((nn, w["k"]), dtype=torch.int32, device="cuda"),
+              torch.empty((nn, w["k"]), dtype=torch.float32, device="cuda"),
+              torch.empty((nn, 2), dtype=torch.float32, device="cuda")])
+        for x in t:
+            tdist.broadcast(x, 0)
+        idx, dist, init = (x.cpu().numpy() for x in t)
     n, k = idx.shape
     a, b = api.find_ab_params(1.0, UMAP_MIN_DIST)
     d_idx, d_dist = torch.from_numpy(idx).cuda(), torch.from_numpy(dist).cuda()
     t0 = time.time()
     sess = api.UmapSession.from_knn(d_idx, d_dist)
+    if world > 1:
+        # Rank r owns the r-th block of vertices; layout all-gathered per epoch.
+        sess.shard_over()
     info = sess.info()
     log(f"[bench] umap: n={n} edges={info['n_edges']} (set-up {time.time() - t0:.2f}s)")
     del d_idx, d_dist
@@ -540,6 +561,8 @@ def bench_umap(args):
 
     run(0, args.warmup)
     torch.cuda.synchronize()
+    if world > 1:
+        tdist.barrier()
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clocks:
         start.record(stream)
@@ -547,6 +570,10 @@ def bench_umap(args):
         stop.record(stream)
         torch.cuda.synchronize()
     elapsed_ms = start.elapsed_time(stop)
+    if world > 1:
+        tt = torch.tensor([elapsed_ms], device="cuda")
+        tdist.all_reduce(tt, op=tdist.ReduceOp.MAX)
+        elapsed_ms = float(tt.item())
     pos = neg = 0
     for c0, c1 in spans(0, args.steps):
         p_, n_ = sess.count_samples(c0, c1, UMAP_NSR)
@@ -570,7 +597,7 @@ def bench_umap(args):
 
     graph = sess.graph()
     e2e = None
-    if not args.skip_e2e:
+    if not args.skip_e2e and world == 1:
         idx_cm = torch.from_numpy(np.ascontiguousarray(idx.T)).pin_memory()
         dist_cm = torch.from_numpy(np.ascontiguousarray(dist.T)).pin_memory()
         out_h = torch.empty((n, 2), dtype=torch.float32).pin_memory()
@@ -596,16 +623,23 @@ def bench_umap(args):
                "d2h_bytes_per_step": int(out_h.numel() * 4), "seconds_per_call": e2e_s,
                "call": f"fastembedr_cuda_umap_from_knn_spectral_float ({n_epochs} epochs, host KNN: graph, "
                        f"diffusion start, epochs)"}
-    cpu = None if args.skip_cpu else cpu_baseline_umap(graph, init)
+    cpu = None if (args.skip_cpu or world > 1) else cpu_baseline_umap(graph, init)
     sess.close()
+    if world > 1:
+        tdist.barrier()
+        tdist.destroy_process_group()
+        if rank != 0:
+            return 0
     line = {
         "metric": "umap_edge_updates_per_second", "value": value, "unit": "edge_updates/s",
-        "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": elapsed_ms / args.steps,
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": elapsed_ms / args.steps,
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic",
         "config": {"workload": args.workload, "n": int(n), "k": int(k), "n_edges": int(info["n_edges"]),
                    "n_epochs": n_epochs, "negative_sample_rate": UMAP_NSR, "min_dist": UMAP_MIN_DIST,
                    "optimizer": "Hogwild per sample (device-KNN path)", "init": "U(-10, 10)",
+                   "parallelism": (f"vertices sharded over {world} GPUs (per-epoch NCCL all-gather of the "
+                                   f"layout)" if world > 1 else "single"),
                    "l2": "edge list %.2f GB" % (12 * info["n_edges"] / 1e9)},
         "negative_samples_per_second": neg / (elapsed_ms / 1000.0),
         "epochs_per_second": args.steps / (elapsed_ms / 1000.0),
@@ -637,8 +671,6 @@ def main():
     if args.impl == "reference":
         return bench_reference_umap(args) if umap else bench_reference(args)
     if umap:
-        if dist_env()[1] > 1:
-            ap.error("the UMAP workloads run on one GPU")
         return bench_umap(args)
     return bench_ours(args)
 

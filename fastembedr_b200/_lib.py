@@ -70,6 +70,7 @@ _SIGNATURES = {
     "fe_b200_umap_get_graph": (I, [c_void_p, c_void_p, c_void_p, c_void_p]),
     "fe_b200_umap_stream": (c_void_p, [c_void_p]),
     "fe_b200_umap_destroy": (None, [c_void_p]),
+    "fe_b200_umap_shard": (I, [c_void_p, c_void_p, I, I, I]),
     "fe_b200_tsne_shard": (I, [c_void_p, c_void_p, I, I, I]),
 }
 

@@ -397,6 +397,15 @@ def shard_rows(n: int, nranks: int, rank: int) -> Tuple[int, int]:
     return begin, min(n, begin + per)
 
 
+def umap_shard_vertices(n: int, nranks: int, rank: int) -> Tuple[int, int]:
+    """Vertices [begin, end) that `rank` owns in an nranks-way sharded UMAP
+    session: blocks of ceil(n / nranks), the last one short (mirrors
+    fe_b200_umap_shard)."""
+    per = -(-n // nranks)
+    begin = min(n, rank * per)
+    return begin, min(n, begin + per)
+
+
 # ------------------------------------------------------------------ UMAP
 
 
@@ -526,6 +535,21 @@ class UmapSession:
                                                      ctypes.byref(pos), ctypes.byref(neg)),
               "fe_b200_umap_count_samples")
         return pos.value, neg.value
+
+    def shard(self, unique_id: bytes, nranks: int, rank: int) -> None:
+        """Makes this session rank `rank` of an nranks-way run (one process per
+        GPU); see fe_b200_umap_shard."""
+        uid = (ctypes.c_ubyte * len(unique_id)).from_buffer_copy(unique_id)
+        check(_lib.load().fe_b200_umap_shard(self._h, uid, len(unique_id), nranks, rank), "fe_b200_umap_shard")
+
+    def shard_over(self, group=None) -> None:
+        """Shards over a torch.distributed process group (any backend)."""
+        import torch.distributed as dist
+
+        box = [nccl_unique_id() if dist.get_rank(group) == 0 else None]
+        dist.broadcast_object_list(box, src=dist.get_global_rank(group, 0) if group is not None else 0,
+                                   group=group)
+        self.shard(box[0], dist.get_world_size(group), dist.get_rank(group))
 
     def layout(self) -> np.ndarray:
         y = np.zeros((self.n, 2), np.float32)

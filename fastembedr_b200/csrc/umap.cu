@@ -35,6 +35,8 @@
 //     together with the sanitize step; head moves are combined as above.
 #include "umap.cuh"
 
+#include "nccl_loader.cuh"
+
 #include <cfloat>
 #include <cmath>
 
@@ -120,6 +122,7 @@ __global__ void __launch_bounds__(256) umap_epoch_kernel(const int* __restrict__
   const float alpha = p.learning_rate * (1.0f - static_cast<float>(epoch) / fmaxf(1.0f, static_cast<float>(p.n_epochs)));
   const float2* src = Mode == kUmapDelta ? frozen : layout;
   float2* dst = Mode == kUmapDelta ? delta : layout;
+  auto owned = [&](int v) { return v >= p.own_begin && v < p.own_end; };
   const int lane = threadIdx.x & 31;
   long long local_pos = 0;
   const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
@@ -157,7 +160,7 @@ __global__ void __launch_bounds__(256) umap_epoch_kernel(const int* __restrict__
             dt.x -= gx;
             dt.y -= gy;
           }
-          for (int s = 0; s < neg; ++s) {
+          for (int s = 0; s < (owned(h) ? neg : 0); ++s) {
             const int k = negative_vertex(static_cast<unsigned int>(p.n), p.seed, epoch, h, key, s);
             if (k == h || k == t) continue;
             const float2 yk = src[k];
@@ -171,7 +174,7 @@ __global__ void __launch_bounds__(256) umap_epoch_kernel(const int* __restrict__
           }
           gx_h = dh.x;
           gy_h = dh.y;
-          atomicAdd(dst + t, dt);
+          if (owned(t)) atomicAdd(dst + t, dt);
         } else if (Mode == kUmapInplace) {
           // The edge's samples in the CPU replay's order on running copies.
           float2 yh = yh0, yt = yt0;
@@ -188,7 +191,7 @@ __global__ void __launch_bounds__(256) umap_epoch_kernel(const int* __restrict__
             yt.x += -gx;
             yt.y += -gy;
           }
-          for (int s = 0; s < neg; ++s) {
+          for (int s = 0; s < (owned(h) ? neg : 0); ++s) {
             const int k = negative_vertex(static_cast<unsigned int>(p.n), p.seed, epoch, h, key, s);
             if (k == h || k == t) continue;
             const float2 yk = src[k];
@@ -202,7 +205,7 @@ __global__ void __launch_bounds__(256) umap_epoch_kernel(const int* __restrict__
           }
           gx_h = yh.x - yh0.x;
           gy_h = yh.y - yh0.y;
-          atomicAdd(dst + t, make_float2(yt.x - yt0.x, yt.y - yt0.y));
+          if (owned(t)) atomicAdd(dst + t, make_float2(yt.x - yt0.x, yt.y - yt0.y));
         } else {
           // Each sample reads fresh positions and applies its move at once.
           float2 yh, yt;
@@ -216,10 +219,10 @@ __global__ void __launch_bounds__(256) umap_epoch_kernel(const int* __restrict__
             const float c = -2.0f * p.a * p.b * (d2b / d2) / (p.a * d2b + 1.0f);
             const float gx = clip4(c * dx) * alpha;
             const float gy = clip4(c * dy) * alpha;
-            atomicAdd(layout + h, make_float2(gx, gy));
-            atomicAdd(layout + t, make_float2(-gx, -gy));
+            if (owned(h)) atomicAdd(layout + h, make_float2(gx, gy));
+            if (owned(t)) atomicAdd(layout + t, make_float2(-gx, -gy));
           }
-          for (int s = 0; s < neg; ++s) {
+          for (int s = 0; s < (owned(h) ? neg : 0); ++s) {
             const int k = negative_vertex(static_cast<unsigned int>(p.n), p.seed, epoch, h, key, s);
             if (k == h || k == t) continue;
             yh = __ldcg(layout + h);
@@ -246,7 +249,7 @@ __global__ void __launch_bounds__(256) umap_epoch_kernel(const int* __restrict__
       sx += __shfl_sync(peers, gx_h, l);
       sy += __shfl_sync(peers, gy_h, l);
     }
-    if (lane == leader && h >= 0) atomicAdd(dst + h, make_float2(sx, sy));
+    if (lane == leader && h >= 0 && owned(h)) atomicAdd(dst + h, make_float2(sx, sy));
   }
   if (positive_count != nullptr) {
     local_pos = warp_sum(static_cast<double>(local_pos));
@@ -321,6 +324,17 @@ int umap_launch_epoch(UmapRun* r, int epoch) {
   umap_sanitize_kernel<<<(p.n + 255) / 256, 256, 0, r->stream>>>(
       r->layout, r->mode == kUmapDelta ? r->delta : nullptr, p.n, 16.0f);
   FE_LAUNCH("umap_sanitize_kernel");
+  if (r->comm != nullptr) {
+    // Every rank's copy of the layout becomes the next epoch's start: the
+    // owned rows of each rank, gathered in place.
+    const NcclApi* api = nccl_api();
+    if (api == nullptr) return 1;
+    const size_t count = 2 * static_cast<size_t>(r->rows_per_rank);
+    float* base = reinterpret_cast<float*>(r->layout);
+    FE_TRY(check_nccl(api->AllGather(base + count * r->shard_rank, base, count, ncclFloat32,
+                                     static_cast<ncclComm_t>(r->comm), r->stream),
+                      "ncclAllGather(UMAP layout rows)"));
+  }
   return 0;
 }
 

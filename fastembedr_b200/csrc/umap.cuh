@@ -25,6 +25,11 @@ struct UmapParams {
   float a;
   float b;
   float repulsion_strength;
+  // Vertices whose moves this launch applies: [own_begin, own_end).  A shard
+  // of a multi-GPU run owns a block of vertices and reads the others from the
+  // epoch-start copy every rank holds; unsharded runs own every vertex.
+  int own_begin = 0;
+  int own_end = 0x7fffffff;
 };
 
 struct UmapRun {
@@ -40,6 +45,12 @@ struct UmapRun {
   cudaStream_t stream = nullptr;
   int edge_blocks = 1;
   bool use_graphs = true;
+  // Sharded runs: after each epoch the owned rows (blocks of rows_per_rank,
+  // layout padded to shard_ranks * rows_per_rank rows) are all-gathered.
+  void* comm = nullptr;  // ncclComm_t
+  int shard_ranks = 1;
+  int shard_rank = 0;
+  int rows_per_rank = 0;
 };
 
 int umap_launch_epoch(UmapRun* r, int epoch);

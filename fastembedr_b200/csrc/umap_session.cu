@@ -10,9 +10,14 @@
 #include "fastembedr_b200.h"
 #pragma GCC visibility pop
 
+#include "nccl_loader.cuh"
 #include "umap.cuh"
 
 #include <cub/cub.cuh>
+
+#include <algorithm>
+#include <cstring>
+#include <string>
 
 struct fe_b200_umap {
   int n = 0;
@@ -28,8 +33,26 @@ struct fe_b200_umap {
   long long* counts = nullptr;  // [0] positive, [1] negative totals, then per-edge counts
   void* temp = nullptr;         // CUB reduction storage
   size_t temp_bytes = 0;
+  // Sharded sessions (fe_b200_umap_shard): this rank's vertex block, the
+  // edges that touch it, the layout padded for the in-place all-gather.
+  void* comm = nullptr;  // ncclComm_t
+  int shard_ranks = 1;
+  int shard_rank = 0;
+  int rows_per_rank = 0;
+  int own_begin = 0;
+  int own_end = 0x7fffffff;
+  long long own_edges = 0;
+  void* shard_mem = nullptr;  // own heads, tails, periods and the padded layout
+  int* own_heads = nullptr;
+  int* own_tails = nullptr;
+  float* own_periods = nullptr;
   ~fe_b200_umap() {
     if (stream) cudaStreamSynchronize(stream);
+    if (comm) {
+      const fe::NcclApi* api = fe::nccl_api();
+      if (api) api->CommDestroy(static_cast<ncclComm_t>(comm));
+    }
+    if (shard_mem) cudaFree(shard_mem);
     arena.release();
     if (stream) cudaStreamDestroy(stream);
   }
@@ -45,6 +68,14 @@ int check_session(const fe_b200_umap* s) {
     return 1;
   }
   return 0;
+}
+
+__global__ void touches_kernel(const int* __restrict__ heads, const int* __restrict__ tails, long long n_edges,
+                               int own_begin, int own_end, char* __restrict__ flags) {
+  const long long e = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (e >= n_edges) return;
+  const int h = heads[e], t = tails[e];
+  flags[e] = static_cast<char>((h >= own_begin && h < own_end) || (t >= own_begin && t < own_end));
 }
 
 }  // namespace
@@ -142,19 +173,126 @@ int fe_b200_umap_run(fe_b200_umap* s, int epoch_begin, int epoch_end, int n_epoc
     return 1;
   }
   fe::UmapRun r;
-  // Negatives keyed on the tail vertex, as the reference's COO kernels key them.
+  // Negatives keyed on the tail vertex, as the reference's COO kernels key
+  // them (and as a shard needs: the edge's position differs between shards).
   r.params = fe::UmapParams{s->n, n_epochs, negative_sample_rate, 1, seed, learning_rate, a, b, repulsion_strength};
   r.mode = optimizer_mode == 1 ? fe::kUmapDelta : fe::kUmapInplaceSample;
-  r.heads = s->heads;
-  r.tails = s->tails;
-  r.periods = s->periods;
-  r.n_edges = s->n_edges;
+  const bool sharded = s->comm != nullptr;
+  r.heads = sharded ? s->own_heads : s->heads;
+  r.tails = sharded ? s->own_tails : s->tails;
+  r.periods = sharded ? s->own_periods : s->periods;
+  r.n_edges = sharded ? s->own_edges : s->n_edges;
+  r.params.own_begin = s->own_begin;
+  r.params.own_end = s->own_end;
+  r.comm = s->comm;
+  r.shard_ranks = s->shard_ranks;
+  r.shard_rank = s->shard_rank;
+  r.rows_per_rank = s->rows_per_rank;
   r.layout = s->layout;
   r.delta = r.mode == fe::kUmapDelta ? s->delta : nullptr;
   r.stream = s->stream;
-  r.edge_blocks = fe::umap_edge_blocks(s->n_edges);
+  r.edge_blocks = fe::umap_edge_blocks(std::max(1ll, r.n_edges));
   r.use_graphs = fe::env_flag("FASTEMBEDR_CUDA_GRAPH_CAPTURE", true);
   return fe::umap_run_epochs(&r, epoch_begin, epoch_end);
+}
+
+int fe_b200_umap_shard(fe_b200_umap* s, const unsigned char* id, int id_bytes, int nranks, int rank) {
+  fe::clear_error();
+  FE_TRY(check_session(s));
+  if (id == nullptr || id_bytes < static_cast<int>(sizeof(ncclUniqueId))) {
+    set_error("invalid UMAP shard call");
+    return 1;
+  }
+  if (s->comm != nullptr) {
+    set_error("UMAP session is already sharded");
+    return 1;
+  }
+  if (nranks < 1 || nranks > 256 || rank < 0 || rank >= nranks) {
+    set_error("UMAP shard: need 1 <= nranks <= 256 and 0 <= rank < nranks");
+    return 1;
+  }
+  const fe::NcclApi* api = fe::nccl_api();
+  if (api == nullptr) return 1;
+  const int n = s->n;
+  const int per = (n + nranks - 1) / nranks;
+  const size_t padded_rows = static_cast<size_t>(per) * nranks;
+  const size_t e = static_cast<size_t>(s->n_edges);
+  // This rank's edges: those with an endpoint in its block (edges across
+  // blocks are kept by both ranks; each applies the moves of its own end).
+  size_t select_bytes = 0;
+  FE_CUDA(cub::DeviceSelect::Flagged(nullptr, select_bytes, static_cast<const int*>(nullptr),
+                                     static_cast<const char*>(nullptr), static_cast<int*>(nullptr),
+                                     static_cast<long long*>(nullptr), static_cast<int>(e)),
+          "cub::DeviceSelect(sizing)");
+  fe::Arena plan;
+  plan.begin_plan();
+  plan.take<int>(e);
+  plan.take<int>(e);
+  plan.take<float>(e);
+  plan.take<float2>(padded_rows);
+  plan.take<char>(e);
+  plan.take<long long>(1);
+  plan.take<char>(select_bytes);
+  FE_TRY(fe::memory_preflight(plan.planned(), "UMAP shard preflight"));
+  char* mem = nullptr;
+  FE_CUDA(cudaMalloc(&mem, plan.planned()), "cudaMalloc(UMAP shard)");
+  struct Free {
+    char** p;
+    ~Free() {
+      if (*p) cudaFree(*p);
+    }
+  } release{&mem};
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    char* q = mem + off;
+    off += fe::align_up(bytes);
+    return q;
+  };
+  int* own_heads = reinterpret_cast<int*>(take(e * sizeof(int)));
+  int* own_tails = reinterpret_cast<int*>(take(e * sizeof(int)));
+  float* own_periods = reinterpret_cast<float*>(take(e * sizeof(float)));
+  float2* layout = reinterpret_cast<float2*>(take(padded_rows * sizeof(float2)));
+  char* flags = take(e);
+  long long* selected = reinterpret_cast<long long*>(take(sizeof(long long)));
+  void* select_temp = take(select_bytes);
+  const int own_begin = std::min(n, rank * per);
+  const int own_end = std::min(n, own_begin + per);
+  touches_kernel<<<static_cast<unsigned>((e + 255) / 256), 256, 0, s->stream>>>(s->heads, s->tails, s->n_edges,
+                                                                               own_begin, own_end, flags);
+  FE_LAUNCH("touches_kernel");
+  size_t tb = select_bytes;
+  FE_CUDA(cub::DeviceSelect::Flagged(select_temp, tb, s->heads, flags, own_heads, selected, static_cast<int>(e),
+                                     s->stream), "cub::DeviceSelect(heads)");
+  tb = select_bytes;
+  FE_CUDA(cub::DeviceSelect::Flagged(select_temp, tb, s->tails, flags, own_tails, selected, static_cast<int>(e),
+                                     s->stream), "cub::DeviceSelect(tails)");
+  tb = select_bytes;
+  FE_CUDA(cub::DeviceSelect::Flagged(select_temp, tb, s->periods, flags, own_periods, selected,
+                                     static_cast<int>(e), s->stream), "cub::DeviceSelect(periods)");
+  FE_CUDA(cudaMemsetAsync(layout, 0, padded_rows * sizeof(float2), s->stream), "memset layout");
+  FE_CUDA(cudaMemcpyAsync(layout, s->layout, sizeof(float2) * n, cudaMemcpyDeviceToDevice, s->stream),
+          "copy layout");
+  long long own_edges = 0;
+  FE_CUDA(cudaMemcpyAsync(&own_edges, selected, sizeof(long long), cudaMemcpyDeviceToHost, s->stream), "D2H");
+  FE_CUDA(cudaStreamSynchronize(s->stream), "cudaStreamSynchronize(UMAP shard)");
+  ncclUniqueId uid;
+  std::memcpy(&uid, id, sizeof(uid));
+  ncclComm_t comm = nullptr;
+  FE_TRY(fe::check_nccl(api->CommInitRank(&comm, nranks, uid, rank), "ncclCommInitRank"));
+  s->comm = comm;
+  s->shard_ranks = nranks;
+  s->shard_rank = rank;
+  s->rows_per_rank = per;
+  s->own_begin = own_begin;
+  s->own_end = own_end;
+  s->own_edges = own_edges;
+  s->own_heads = own_heads;
+  s->own_tails = own_tails;
+  s->own_periods = own_periods;
+  s->layout = layout;  // the arena's copy stays allocated, unused
+  s->shard_mem = mem;
+  mem = nullptr;
+  return 0;
 }
 
 int fe_b200_umap_count_samples(fe_b200_umap* s, int epoch_begin, int epoch_end, int negative_sample_rate,

@@ -258,6 +258,16 @@ int fe_b200_umap_info(fe_b200_umap* s, int* n, long long* n_edges);
 int fe_b200_umap_get_graph(fe_b200_umap* s, int* heads, int* tails, float* epochs_per_sample);
 void* fe_b200_umap_stream(fe_b200_umap* s);
 void fe_b200_umap_destroy(fe_b200_umap* s);
+/* Makes the session rank `rank` of an nranks-way run, one process per GPU
+ * (id: bytes from fe_b200_nccl_unique_id made on one rank; blocks until every
+ * rank has joined).  Rank r owns the r-th block of ceil(n / nranks) vertices
+ * and keeps the edges that touch it; every epoch it applies the moves of its
+ * own vertices against the epoch-start positions of the others, and the
+ * blocks are then all-gathered.  Every rank must hold an identical session and
+ * make the same calls in the same order.  In Jacobi mode the sharded epoch is
+ * the unsharded one (up to float summation order); in Hogwild mode a rank
+ * sees other ranks' moves from the next epoch on. */
+int fe_b200_umap_shard(fe_b200_umap* s, const unsigned char* id, int id_bytes, int nranks, int rank);
 
 /* ---- sharding one t-SNE run across GPUs (one process per GPU) ----
  * No counterpart in the reference's C ABI: the reference's multi-GPU build

@@ -59,6 +59,7 @@ int session_shard(TsneSession* s, const void* unique_id, int nranks, int rank) {
 }
 
 int shard_gather_rows(TsneSession* s, float2* rows) {
+  if (s->shard_ranks == 1) return 0;  // one rank holds every row already
   const NcclApi* api = nccl_api();
   if (api == nullptr) return 1;
   const size_t count = 2 * static_cast<size_t>(s->rows_per_rank);  // floats per rank
@@ -69,6 +70,7 @@ int shard_gather_rows(TsneSession* s, float2* rows) {
 }
 
 int shard_sum_charges(TsneSession* s) {
+  if (s->shard_ranks == 1) return 0;  // the local grid is the sum
   const NcclApi* api = nccl_api();
   if (api == nullptr) return 1;
   const size_t words = 4 * static_cast<size_t>(s->grid) * s->grid;  // ChargeCell = 4 x u64

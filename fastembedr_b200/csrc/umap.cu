@@ -302,40 +302,55 @@ int umap_count_samples(const float* periods, long long n_edges, int epoch_begin,
   return 0;
 }
 
+namespace {
+
+int gather_layout(UmapRun* r) {
+  // Every rank's copy of the layout takes the owned rows of each rank,
+  // gathered in place.  One rank has nothing to gather.
+  if (r->comm == nullptr || r->shard_ranks <= 1) return 0;
+  const NcclApi* api = nccl_api();
+  if (api == nullptr) return 1;
+  const size_t count = 2 * static_cast<size_t>(r->rows_per_rank);
+  float* base = reinterpret_cast<float*>(r->layout);
+  return check_nccl(api->AllGather(base + count * r->shard_rank, base, count, ncclFloat32,
+                                   static_cast<ncclComm_t>(r->comm), r->stream),
+                    "ncclAllGather(UMAP layout rows)");
+}
+
+template <int Mode>
+int launch_edges(UmapRun* r, int epoch, long long e0, long long e1) {
+  umap_epoch_kernel<Mode><<<r->edge_blocks, 256, 0, r->stream>>>(
+      r->heads, r->tails, r->periods, e0, e1, r->layout, r->layout, Mode == kUmapDelta ? r->delta : nullptr,
+      r->params, epoch, r->positive_count);
+  FE_LAUNCH("umap_epoch_kernel");
+  return 0;
+}
+
+}  // namespace
+
 int umap_launch_epoch(UmapRun* r, int epoch) {
   const UmapParams& p = r->params;
+  const bool sharded = r->comm != nullptr && r->shard_ranks > 1;
   if (r->mode == kUmapDelta) {
-    umap_epoch_kernel<kUmapDelta><<<r->edge_blocks, 256, 0, r->stream>>>(
-        r->heads, r->tails, r->periods, 0, r->n_edges, r->layout, r->layout, r->delta, p, epoch,
-        r->positive_count);
-    FE_LAUNCH("umap_epoch_kernel");
+    // Jacobi: every force at the epoch-start layout, one gather per epoch.
+    FE_TRY(launch_edges<kUmapDelta>(r, epoch, 0, r->n_edges));
   } else {
-    if (r->mode == kUmapInplaceSample) {
-      umap_epoch_kernel<kUmapInplaceSample><<<r->edge_blocks, 256, 0, r->stream>>>(
-          r->heads, r->tails, r->periods, 0, r->n_edges, r->layout, r->layout, nullptr, p, epoch,
-          r->positive_count);
-    } else {
-      umap_epoch_kernel<kUmapInplace><<<r->edge_blocks, 256, 0, r->stream>>>(
-          r->heads, r->tails, r->periods, 0, r->n_edges, r->layout, r->layout, nullptr, p, epoch,
-          r->positive_count);
+    // Hogwild: a shard sees the other shards' moves only through the gathers,
+    // so its edges run in kShardGatherParts parts with a gather after each,
+    // which keeps remote positions at most a part of an epoch old.
+    const int parts = sharded ? kShardGatherParts : 1;
+    for (int part = 0; part < parts; ++part) {
+      const long long e0 = r->n_edges * part / parts;
+      const long long e1 = r->n_edges * (part + 1) / parts;
+      if (r->mode == kUmapInplaceSample) FE_TRY(launch_edges<kUmapInplaceSample>(r, epoch, e0, e1));
+      else FE_TRY(launch_edges<kUmapInplace>(r, epoch, e0, e1));
+      if (part + 1 < parts) FE_TRY(gather_layout(r));
     }
-    FE_LAUNCH("umap_epoch_kernel");
   }
   umap_sanitize_kernel<<<(p.n + 255) / 256, 256, 0, r->stream>>>(
       r->layout, r->mode == kUmapDelta ? r->delta : nullptr, p.n, 16.0f);
   FE_LAUNCH("umap_sanitize_kernel");
-  if (r->comm != nullptr) {
-    // Every rank's copy of the layout becomes the next epoch's start: the
-    // owned rows of each rank, gathered in place.
-    const NcclApi* api = nccl_api();
-    if (api == nullptr) return 1;
-    const size_t count = 2 * static_cast<size_t>(r->rows_per_rank);
-    float* base = reinterpret_cast<float*>(r->layout);
-    FE_TRY(check_nccl(api->AllGather(base + count * r->shard_rank, base, count, ncclFloat32,
-                                     static_cast<ncclComm_t>(r->comm), r->stream),
-                      "ncclAllGather(UMAP layout rows)"));
-  }
-  return 0;
+  return gather_layout(r);
 }
 
 int umap_run_epochs(UmapRun* r, int epoch_begin, int epoch_end) {

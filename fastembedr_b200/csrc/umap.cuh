@@ -53,6 +53,10 @@ struct UmapRun {
   int rows_per_rank = 0;
 };
 
+// Gathers per Hogwild epoch in a sharded run (the last one after the epoch's
+// sanitize step).
+constexpr int kShardGatherParts = 4;
+
 int umap_launch_epoch(UmapRun* r, int epoch);
 int umap_run_epochs(UmapRun* r, int epoch_begin, int epoch_end);
 int umap_edge_blocks(long long n_edges);

@@ -425,7 +425,7 @@ def bench_ours(args):
 
     sess.close()
     if rank == 0:
-        per_iter = 5 if world == 1 else 6  # sharded: + layout statistics (NCCL kernels not counted)
+        per_iter = 6  # splat, 3 FFT passes, gradient/update, layout statistics (NCCL kernels not counted)
         line = {
             "metric": "tsne_iterations_per_second", "value": value, "unit": "iterations/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
@@ -443,11 +443,12 @@ def bench_ours(args):
                          "traffic": profile_traffic("grad_update_kernel", args.workload) if world == 1 else None},
             "kernel_share": kernel_share,
             "kernel_ms": {kname: v[0] / max(v[1], 1) for kname, v in times.items()},
-            # per iteration: splat, 3 FFT passes, gradient/update (+ statistics when
-            # sharded); 5 per spatial reorder (every 50 iterations at n >= 4096;
-            # CUB sort/scan kernels not counted); 2 per run restart.
-            "gpu_launches": per_iter * args.steps + (5 * (args.steps // 50) if n >= 4096 else 0)
-                            + 2 * ((args.steps - 1) // (EE_ITER + N_ITER)),
+            # per iteration: splat, 3 FFT passes, gradient/update, statistics; 4 per
+            # spatial reorder (Morton keys, permutation, row fill, group cost, every
+            # 50 iterations at n >= 4096; CUB sort/scan kernels not counted); 3 per
+            # run restart (permute-in, statistics, gains fill).
+            "gpu_launches": per_iter * args.steps + (4 * (args.steps // 50) if n >= 4096 else 0)
+                            + 3 * ((args.steps - 1) // (EE_ITER + N_ITER)),
             "clocks": clocks.summary(),
             "e2e": e2e,
             "cpu_baseline": cpu,

@@ -132,7 +132,12 @@ __global__ void group_cost_kernel(const int* __restrict__ row_ptr4, int row_begi
     }
     total += static_cast<unsigned int>(passes) + 1u;
   }
-  cost[grp] = total;
+#ifndef FE_LPT_THRESHOLD
+#define FE_LPT_THRESHOLD 0
+#endif
+  // Groups at or below the threshold keep their (Morton) order behind the
+  // expensive ones: the descending sort is stable.
+  cost[grp] = total > FE_LPT_THRESHOLD ? total : 0u;
   ids[grp] = grp;
 }
 

@@ -128,6 +128,10 @@ __device__ __forceinline__ Cell grid_cell(float px, float py, const GridGeom& q,
 }
 #endif
 
+// A round of the attraction kernel (four rows, eight lanes each) whose longest
+// row needs more passes than this is run row by row with 32 lanes instead.
+constexpr int kLongRoundPasses = 6;
+
 // Exactly one of these modes is run by the fused gradient kernel.
 enum GradMode { kGradUpdate = 0, kGradOnly = 1 };
 

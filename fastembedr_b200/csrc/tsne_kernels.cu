@@ -661,6 +661,49 @@ __device__ __forceinline__ void attract4(float yix, float yiy, int4 c, float4 v,
   }
 }
 
+// Streams one row of the internal P (groups [beg, end) of four entries) with
+// S lanes: each lane takes groups lane, lane + S in a pass and the next pass
+// starts 2S groups on; the next pass's loads are issued before this pass's
+// gathers (FE_ATTRACT_PREFETCH).  `passes` may exceed the row's own need
+// (lanes then load nothing).
+template <int S>
+__device__ __forceinline__ void stream_row(int beg, int end, int l, int passes, float2 yi, float ex,
+                                           const int4* __restrict__ col4, const float4* __restrict__ val4,
+                                           const float2* __restrict__ y, float& ax, float& ay) {
+  const int4 zero_c = make_int4(0, 0, 0, 0);
+  const float4 zero_v = make_float4(0.f, 0.f, 0.f, 0.f);
+  int e = beg + l;
+#if FE_ATTRACT_PREFETCH
+  int4 c0 = e < end ? ld_stream(col4 + e) : zero_c;
+  float4 v0 = e < end ? ld_stream(val4 + e) : zero_v;
+  int4 c1 = e + S < end ? ld_stream(col4 + e + S) : zero_c;
+  float4 v1 = e + S < end ? ld_stream(val4 + e + S) : zero_v;
+  for (int p = 0; p < passes; ++p) {
+    const int en = e + 2 * S;
+    const int4 nc0 = en < end ? ld_stream(col4 + en) : zero_c;
+    const float4 nv0 = en < end ? ld_stream(val4 + en) : zero_v;
+    const int4 nc1 = en + S < end ? ld_stream(col4 + en + S) : zero_c;
+    const float4 nv1 = en + S < end ? ld_stream(val4 + en + S) : zero_v;
+    attract4(yi.x, yi.y, c0, v0, ex, y, ax, ay);
+    attract4(yi.x, yi.y, c1, v1, ex, y, ax, ay);
+    c0 = nc0;
+    v0 = nv0;
+    c1 = nc1;
+    v1 = nv1;
+    e = en;
+  }
+#else
+  for (int p = 0; p < passes; ++p, e += 2 * S) {
+    const int4 c0 = e < end ? ld_stream(col4 + e) : zero_c;
+    const float4 v0 = e < end ? ld_stream(val4 + e) : zero_v;
+    const int4 c1 = e + S < end ? ld_stream(col4 + e + S) : zero_c;
+    const float4 v1 = e + S < end ? ld_stream(val4 + e + S) : zero_v;
+    attract4(yi.x, yi.y, c0, v0, ex, y, ax, ay);
+    attract4(yi.x, yi.y, c1, v1, ex, y, ax, ay);
+  }
+#endif
+}
+
 // 64 registers: four blocks of 256 threads per SM, and the grid is exactly
 // the resident capacity (one wave).  Warps take 32-row groups from a global
 // counter (reset by the splat of the same iteration) in group_order, most
@@ -675,8 +718,6 @@ __global__ void __launch_bounds__(256, 4) grad_update_kernel(
   const int sub = lane >> 3;  // which of the 4 rows of a round
   const int sl = lane & 7;    // lane within the row
   const float ex = prm.exaggeration;
-  const int4 zero_c = make_int4(0, 0, 0, 0);
-  const float4 zero_v = make_float4(0.f, 0.f, 0.f, 0.f);
   const int groups = (prm.row_end - prm.row_begin + 31) >> 5;
   for (;;) {
     int ticket = 0;
@@ -695,45 +736,41 @@ __global__ void __launch_bounds__(256, 4) grad_update_kernel(
       int passes = (end - beg + 15) >> 4;
       passes = max(passes, __shfl_xor_sync(0xffffffffu, passes, 8));
       passes = max(passes, __shfl_xor_sync(0xffffffffu, passes, 16));
-      float ax = 0.f, ay = 0.f;
-      int e = beg + sl;
-#if FE_ATTRACT_PREFETCH
-      int4 c0 = e < end ? ld_stream(col4 + e) : zero_c;
-      float4 v0 = e < end ? ld_stream(val4 + e) : zero_v;
-      int4 c1 = e + 8 < end ? ld_stream(col4 + e + 8) : zero_c;
-      float4 v1 = e + 8 < end ? ld_stream(val4 + e + 8) : zero_v;
-      for (int p = 0; p < passes; ++p) {
-        const int en = e + 16;
-        const int4 nc0 = en < end ? ld_stream(col4 + en) : zero_c;
-        const float4 nv0 = en < end ? ld_stream(val4 + en) : zero_v;
-        const int4 nc1 = en + 8 < end ? ld_stream(col4 + en + 8) : zero_c;
-        const float4 nv1 = en + 8 < end ? ld_stream(val4 + en + 8) : zero_v;
-        attract4(yi.x, yi.y, c0, v0, ex, y, ax, ay);
-        attract4(yi.x, yi.y, c1, v1, ex, y, ax, ay);
-        c0 = nc0;
-        v0 = nv0;
-        c1 = nc1;
-        v1 = nv1;
-        e = en;
-      }
-#else
-      for (int p = 0; p < passes; ++p, e += 16) {
-        const int4 c0 = e < end ? ld_stream(col4 + e) : zero_c;
-        const float4 v0 = e < end ? ld_stream(val4 + e) : zero_v;
-        const int4 c1 = e + 8 < end ? ld_stream(col4 + e + 8) : zero_c;
-        const float4 v1 = e + 8 < end ? ld_stream(val4 + e + 8) : zero_v;
-        attract4(yi.x, yi.y, c0, v0, ex, y, ax, ay);
-        attract4(yi.x, yi.y, c1, v1, ex, y, ax, ay);
-      }
-#endif
+      if (passes <= kLongRoundPasses) {
+        // Four rows, eight lanes each.
+        float ax = 0.f, ay = 0.f;
+        stream_row<8>(beg, end, sl, passes, yi, ex, col4, val4, y, ax, ay);
 #pragma unroll
-      for (int o = 4; o > 0; o >>= 1) {
-        ax += __shfl_xor_sync(0xffffffffu, ax, o);
-        ay += __shfl_xor_sync(0xffffffffu, ay, o);
-      }
-      if (sl == it) {
-        my_ax = ax;
-        my_ay = ay;
+        for (int o = 4; o > 0; o >>= 1) {
+          ax += __shfl_xor_sync(0xffffffffu, ax, o);
+          ay += __shfl_xor_sync(0xffffffffu, ay, o);
+        }
+        if (sl == it) {
+          my_ax = ax;
+          my_ay = ay;
+        }
+      } else {
+        // A long (hub) row in the round: its four rows one after another, 32
+        // lanes each, so the round costs about a quarter of the longest row.
+#pragma unroll 1
+        for (int sr = 0; sr < 4; ++sr) {
+          const int row_s = row0 + 4 * it + sr;
+          const bool vs = row_s < prm.row_end;
+          const int beg_s = vs ? __ldg(row_ptr4 + row_s) : 0;
+          const int end_s = vs ? __ldg(row_ptr4 + row_s + 1) : 0;
+          const float2 yis = vs ? y[row_s] : make_float2(0.f, 0.f);
+          float ax = 0.f, ay = 0.f;
+          stream_row<32>(beg_s, end_s, lane, (end_s - beg_s + 63) >> 6, yis, ex, col4, val4, y, ax, ay);
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1) {
+            ax += __shfl_xor_sync(0xffffffffu, ax, o);
+            ay += __shfl_xor_sync(0xffffffffu, ay, o);
+          }
+          if (lane == 8 * sr + it) {
+            my_ax = ax;
+            my_ay = ay;
+          }
+        }
       }
     }
     // Epilogue: lane L finishes row row0 + 4 (L % 8) + L / 8.

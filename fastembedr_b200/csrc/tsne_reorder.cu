@@ -116,8 +116,9 @@ __global__ void permute_in_kernel(const float2* __restrict__ in, const int* __re
 }
 
 // Cost of a 32-row group for the attraction kernel: per round of four rows,
-// the passes of the longest row (a pass covers 16 groups of four entries),
-// plus one for the round's epilogue.
+// the passes of the longest row (a pass of eight lanes covers 16 groups of
+// four entries) plus one; a round past kLongRoundPasses runs its rows one by
+// one with 32 lanes (64 groups a pass), plus one per row.
 __global__ void group_cost_kernel(const int* __restrict__ row_ptr4, int row_begin, int row_end, int groups,
                                   unsigned int* __restrict__ cost, int* __restrict__ ids) {
   const int grp = blockIdx.x * blockDim.x + threadIdx.x;
@@ -125,12 +126,15 @@ __global__ void group_cost_kernel(const int* __restrict__ row_ptr4, int row_begi
   const int row0 = row_begin + grp * 32;
   unsigned int total = 0;
   for (int round = 0; round < 8; ++round) {
-    int passes = 0;
+    int passes = 0, wide = 0;
     for (int sub = 0; sub < 4; ++sub) {
       const int row = row0 + 4 * round + sub;
-      if (row < row_end) passes = max(passes, (row_ptr4[row + 1] - row_ptr4[row] + 15) >> 4);
+      if (row >= row_end) continue;
+      const int len = row_ptr4[row + 1] - row_ptr4[row];
+      passes = max(passes, (len + 15) >> 4);
+      wide += ((len + 63) >> 6) + 1;
     }
-    total += static_cast<unsigned int>(passes) + 1u;
+    total += passes <= kLongRoundPasses ? static_cast<unsigned int>(passes) + 1u : static_cast<unsigned int>(wide);
   }
 #ifndef FE_LPT_THRESHOLD
 #define FE_LPT_THRESHOLD 0

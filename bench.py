@@ -357,6 +357,12 @@ def bench_ours(args):
     alg_bytes = 4 * (rows + 1) + 8 * nnz / world + 8 * rows + 16 * rows + 24 * rows + 16 * grid * grid
     gu_ms, gu_cnt = times["grad_update_kernel"]
     gu_avg_s = gu_ms / max(gu_cnt, 1) / 1000.0
+    per_rank_gu = [gu_avg_s * 1000.0]
+    if world > 1:
+        # every rank's attraction time: the slowest rank paces the collectives
+        box = [None] * world
+        tdist.all_gather_object(box, gu_avg_s * 1000.0)
+        per_rank_gu = box
     hbm, peak_kind = peaks()
     achieved = alg_bytes / gu_avg_s / 1e9
     total_ms = sum(v[0] for v in times.values())
@@ -443,6 +449,7 @@ def bench_ours(args):
                          "traffic": profile_traffic("grad_update_kernel", args.workload) if world == 1 else None},
             "kernel_share": kernel_share,
             "kernel_ms": {kname: v[0] / max(v[1], 1) for kname, v in times.items()},
+            "grad_update_ms_per_rank": per_rank_gu,
             # per iteration: splat, 3 FFT passes, gradient/update, statistics; 4 per
             # spatial reorder (Morton keys, permutation, row fill, group cost, every
             # 50 iterations at n >= 4096; CUB sort/scan kernels not counted); 3 per

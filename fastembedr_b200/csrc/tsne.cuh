@@ -14,7 +14,9 @@
 //   pot      float4[G*G]   potentials {phi_q2, phi_xq2, phi_yq2, phi_q}
 //   stats    LayoutStats   bounds/sums of the layout and the normaliser Z
 //
-// Per iteration: splat -> fft_rows_fwd -> fft_cols -> fft_rows_inv -> gradient+update.
+// Per iteration: splat -> fft_rows_fwd -> fft_cols -> fft_rows_inv -> gradient+update
+// -> layout statistics (a sharded session adds an all-reduce of the charges
+// after the splat and an all-gather of the updated rows before the statistics).
 #pragma once
 
 #include "fe_common.cuh"

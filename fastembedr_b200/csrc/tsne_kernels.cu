@@ -11,19 +11,22 @@
 //
 // Kernels (all on the session stream):
 //   splat_kernel           centres the layout in place and spreads {1,x,y};
-//                          lanes sharing a cell combine first, then 64-bit
-//                          fixed-point atomics (order-independent, reproducible)
+//                          lanes sharing a cell combine first, then a block
+//                          tile and 64-bit fixed-point atomics
+//                          (order-independent, reproducible)
 //   fft_rows_fwd_kernel    x-direction real FFTs of the charge rows and of the
 //                          kernel rows (the kernels are even, so their
 //                          transforms are real)
 //   fft_cols_kernel        y-direction FFT, multiply by the real kernel
 //                          spectra, inverse y-FFT -- one column tile per block
 //   fft_rows_inv_kernel    inverse x-FFTs -> potentials, Z, and clears charges
-//   grad_update_kernel     attraction (8 lanes per row, 16-byte streaming
-//                          loads, next pass prefetched), repulsive gather,
-//                          gains / momentum / step clip,
-//                          layout write and layout statistics for the next
-//                          iteration (last-block reduction, no second launch)
+//   grad_update_kernel     attraction (8 lanes per row, 32 for rounds with a
+//                          hub row; 16-byte streaming loads, next pass
+//                          prefetched; 32-row groups taken most expensive
+//                          first), repulsive gather, gains / momentum / step
+//                          clip, layout write
+//   layout_stats_kernel    sums and bounds of the new layout in a fixed order;
+//                          the last block derives the next grid geometry
 #include "tsne.cuh"
 
 #include <cfloat>

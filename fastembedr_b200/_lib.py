@@ -71,6 +71,10 @@ _SIGNATURES = {
     "fe_b200_umap_stream": (c_void_p, [c_void_p]),
     "fe_b200_umap_destroy": (None, [c_void_p]),
     "fe_b200_umap_shard": (I, [c_void_p, c_void_p, I, I, I]),
+    "fe_b200_umap_shard_comm": (I, [c_void_p, c_void_p]),
+    "fe_b200_comm_create": (I, [c_void_p, I, I, I, ctypes.POINTER(c_void_p)]),
+    "fe_b200_comm_destroy": (None, [c_void_p]),
+    "fe_b200_tsne_shard_comm": (I, [c_void_p, c_void_p]),
     "fe_b200_tsne_shard": (I, [c_void_p, c_void_p, I, I, I]),
 }
 

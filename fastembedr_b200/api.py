@@ -352,6 +352,10 @@ class TsneSession:
         uid = (ctypes.c_ubyte * len(unique_id)).from_buffer_copy(unique_id)
         check(_lib.load().fe_b200_tsne_shard(self._h, uid, len(unique_id), nranks, rank), "fe_b200_tsne_shard")
 
+    def shard_comm(self, comm: "NcclComm") -> None:
+        """Shards this session on a communicator lent by the caller (kept open)."""
+        check(_lib.load().fe_b200_tsne_shard_comm(self._h, comm.handle), "fe_b200_tsne_shard_comm")
+
     def shard_over(self, group=None) -> None:
         """Shards over a torch.distributed process group (any backend): rank 0
         makes the communicator id and the group broadcasts it."""
@@ -385,6 +389,45 @@ def nccl_unique_id() -> bytes:
     buf = (ctypes.c_ubyte * 128)()
     check(_lib.load().fe_b200_nccl_unique_id(buf, 128), "fe_b200_nccl_unique_id")
     return bytes(buf)
+
+
+class NcclComm:
+    """An NCCL communicator made once and lent to sessions in turn
+    (fe_b200_comm_create): repeated sharded runs then skip NCCL's set-up.
+    Sessions sharing it must not run concurrently and must close first."""
+
+    def __init__(self, unique_id: bytes, nranks: int, rank: int):
+        uid = (ctypes.c_ubyte * len(unique_id)).from_buffer_copy(unique_id)
+        h = ctypes.c_void_p()
+        check(_lib.load().fe_b200_comm_create(uid, len(unique_id), nranks, rank, ctypes.byref(h)),
+              "fe_b200_comm_create")
+        self._h = h
+        self.nranks, self.rank = nranks, rank
+
+    @classmethod
+    def over(cls, group=None) -> "NcclComm":
+        """Joins every rank of a torch.distributed group (any backend)."""
+        import torch.distributed as dist
+
+        box = [nccl_unique_id() if dist.get_rank(group) == 0 else None]
+        dist.broadcast_object_list(box, src=dist.get_global_rank(group, 0) if group is not None else 0,
+                                   group=group)
+        return cls(box[0], dist.get_world_size(group), dist.get_rank(group))
+
+    @property
+    def handle(self) -> ctypes.c_void_p:
+        return self._h
+
+    def close(self) -> None:
+        if self._h is not None and self._h.value:
+            _lib.load().fe_b200_comm_destroy(self._h)
+        self._h = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
 
 
 def shard_rows(n: int, nranks: int, rank: int) -> Tuple[int, int]:
@@ -541,6 +584,10 @@ class UmapSession:
         GPU); see fe_b200_umap_shard."""
         uid = (ctypes.c_ubyte * len(unique_id)).from_buffer_copy(unique_id)
         check(_lib.load().fe_b200_umap_shard(self._h, uid, len(unique_id), nranks, rank), "fe_b200_umap_shard")
+
+    def shard_comm(self, comm: "NcclComm") -> None:
+        """Shards this session on a communicator lent by the caller (kept open)."""
+        check(_lib.load().fe_b200_umap_shard_comm(self._h, comm.handle), "fe_b200_umap_shard_comm")
 
     def shard_over(self, group=None) -> None:
         """Shards over a torch.distributed process group (any backend)."""

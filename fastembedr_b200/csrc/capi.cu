@@ -677,7 +677,45 @@ int fe_b200_tsne_shard(fe_b200_tsne* h, const unsigned char* id, int id_bytes, i
     set_error("invalid t-SNE shard call");
     return 1;
   }
-  return fe::session_shard(h->impl, id, nranks, rank);
+  return fe::session_shard(h->impl, id, nullptr, nranks, rank);
+}
+
+int fe_b200_comm_create(const unsigned char* id, int id_bytes, int nranks, int rank, fe_b200_comm** out) {
+  fe::clear_error();
+  if (out == nullptr || id == nullptr || id_bytes < static_cast<int>(sizeof(ncclUniqueId))) {
+    set_error("invalid communicator call");
+    return 1;
+  }
+  *out = nullptr;
+  if (nranks < 1 || rank < 0 || rank >= nranks) {
+    set_error("communicator: need nranks >= 1 and 0 <= rank < nranks");
+    return 1;
+  }
+  fe_b200_comm* c = new fe_b200_comm();
+  if (fe::comm_init(id, nranks, rank, &c->comm)) {
+    delete c;
+    return 1;
+  }
+  c->nranks = nranks;
+  c->rank = rank;
+  *out = c;
+  return 0;
+}
+
+void fe_b200_comm_destroy(fe_b200_comm* c) {
+  if (c == nullptr) return;
+  const fe::NcclApi* api = fe::nccl_api();
+  if (api != nullptr && c->comm != nullptr) api->CommDestroy(c->comm);
+  delete c;
+}
+
+int fe_b200_tsne_shard_comm(fe_b200_tsne* h, fe_b200_comm* comm) {
+  fe::clear_error();
+  if (h == nullptr || comm == nullptr || comm->comm == nullptr) {
+    set_error("invalid t-SNE shard call");
+    return 1;
+  }
+  return fe::session_shard(h->impl, nullptr, comm->comm, comm->nranks, comm->rank);
 }
 
 // ---------------------------------------------------------------- UMAP from KNN (device graph)

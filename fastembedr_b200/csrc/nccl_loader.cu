@@ -6,6 +6,7 @@
 #include <dlfcn.h>
 
 #include <cstdlib>
+#include <cstring>
 #include <mutex>
 #include <string>
 
@@ -54,6 +55,14 @@ const NcclApi* nccl_api() {
     return nullptr;
   }
   return &g_api;
+}
+
+int comm_init(const void* unique_id, int nranks, int rank, ncclComm_t* out) {
+  const NcclApi* api = nccl_api();
+  if (api == nullptr) return 1;
+  ncclUniqueId id;
+  std::memcpy(&id, unique_id, sizeof(id));
+  return check_nccl(api->CommInitRank(out, nranks, id, rank), "ncclCommInitRank");
 }
 
 int check_nccl(ncclResult_t code, const char* where) {

@@ -30,4 +30,16 @@ const NcclApi* nccl_api();
 // 0 on ncclSuccess; otherwise sets "<where>: <NCCL message>" and returns 1.
 int check_nccl(ncclResult_t code, const char* where);
 
+// Joins the communicator `unique_id` (ncclUniqueId bytes) as rank `rank` of
+// `nranks`, on the current device; blocks until every rank has joined.
+int comm_init(const void* unique_id, int nranks, int rank, ncclComm_t* out);
+
 }  // namespace fe
+
+// A communicator made once and lent to any number of sessions in turn
+// (fe_b200_comm_create); sessions never destroy it.
+struct fe_b200_comm {
+  ncclComm_t comm = nullptr;
+  int nranks = 0;
+  int rank = 0;
+};

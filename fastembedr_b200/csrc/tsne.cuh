@@ -241,6 +241,7 @@ struct TsneSession {
   int row_begin = 0;
   int row_end = 0;
   void* comm = nullptr;  // ncclComm_t
+  bool own_comm = false;  // destroyed with the session (not when lent by the caller)
 
   // Spatial ordering: internal point r is the caller's point perm[r], and
   // caller point i is internal point rank[i].
@@ -299,11 +300,12 @@ int session_reset_state(TsneSession* s);
 int session_get_p(TsneSession* s, int* row_ptr, int* col, float* val);
 
 // ---- sharding (tsne_shard.cu) ----
-// Joins an nranks-way NCCL communicator (unique_id: ncclUniqueId bytes from
-// rank 0) and makes this session rank `rank` of a sharded run.  Every rank
-// must hold an identical session (same P, layout and state) and make the same
-// calls in the same order from then on.
-int session_shard(TsneSession* s, const void* unique_id, int nranks, int rank);
+// Makes this session rank `rank` of an nranks-way sharded run, on the
+// communicator `comm` (lent by the caller, kept) or, when comm is null, on a
+// new one joined with unique_id (ncclUniqueId bytes from rank 0; destroyed
+// with the session).  Every rank must hold an identical session (same P,
+// layout and state) and make the same calls in the same order from then on.
+int session_shard(TsneSession* s, const void* unique_id, void* comm, int nranks, int rank);
 // In-place all-gather of the per-rank row blocks of a point array.
 int shard_gather_rows(TsneSession* s, float2* rows);
 // Sum of the charge grids of all ranks, in place.

@@ -24,7 +24,7 @@
 
 namespace fe {
 
-int session_shard(TsneSession* s, const void* unique_id, int nranks, int rank) {
+int session_shard(TsneSession* s, const void* unique_id, void* lent_comm, int nranks, int rank) {
   if (s->sharded) {
     set_error("t-SNE session is already sharded");
     return 1;
@@ -34,14 +34,11 @@ int session_shard(TsneSession* s, const void* unique_id, int nranks, int rank) {
               " and 0 <= rank < nranks");
     return 1;
   }
-  const NcclApi* api = nccl_api();
-  if (api == nullptr) return 1;
-  ncclUniqueId id;
-  std::memcpy(&id, unique_id, sizeof(id));
   FE_CUDA(cudaStreamSynchronize(s->stream), "cudaStreamSynchronize(shard)");
-  ncclComm_t comm = nullptr;
-  FE_TRY(check_nccl(api->CommInitRank(&comm, nranks, id, rank), "ncclCommInitRank"));
+  ncclComm_t comm = static_cast<ncclComm_t>(lent_comm);
+  if (comm == nullptr) FE_TRY(comm_init(unique_id, nranks, rank, &comm));
   s->comm = comm;
+  s->own_comm = lent_comm == nullptr;
   s->sharded = true;
   s->shard_ranks = nranks;
   s->shard_rank = rank;
@@ -83,7 +80,7 @@ int shard_sum_charges(TsneSession* s) {
 void shard_release(TsneSession* s) {
   if (s->comm == nullptr) return;
   const NcclApi* api = nccl_api();
-  if (api != nullptr) api->CommDestroy(static_cast<ncclComm_t>(s->comm));
+  if (api != nullptr && s->own_comm) api->CommDestroy(static_cast<ncclComm_t>(s->comm));
   s->comm = nullptr;
   s->sharded = false;
 }

@@ -36,6 +36,7 @@ struct fe_b200_umap {
   // Sharded sessions (fe_b200_umap_shard): this rank's vertex block, the
   // edges that touch it, the layout padded for the in-place all-gather.
   void* comm = nullptr;  // ncclComm_t
+  bool own_comm = false;  // destroyed with the session (not when lent by the caller)
   int shard_ranks = 1;
   int shard_rank = 0;
   int rows_per_rank = 0;
@@ -48,7 +49,7 @@ struct fe_b200_umap {
   float* own_periods = nullptr;
   ~fe_b200_umap() {
     if (stream) cudaStreamSynchronize(stream);
-    if (comm) {
+    if (comm && own_comm) {
       const fe::NcclApi* api = fe::nccl_api();
       if (api) api->CommDestroy(static_cast<ncclComm_t>(comm));
     }
@@ -196,13 +197,13 @@ int fe_b200_umap_run(fe_b200_umap* s, int epoch_begin, int epoch_end, int n_epoc
   return fe::umap_run_epochs(&r, epoch_begin, epoch_end);
 }
 
-int fe_b200_umap_shard(fe_b200_umap* s, const unsigned char* id, int id_bytes, int nranks, int rank) {
-  fe::clear_error();
-  FE_TRY(check_session(s));
-  if (id == nullptr || id_bytes < static_cast<int>(sizeof(ncclUniqueId))) {
-    set_error("invalid UMAP shard call");
-    return 1;
-  }
+}  // extern "C"
+
+namespace {
+
+// Shards the session on `lent` (kept by the caller) or, when null, on a new
+// communicator joined with `id` (destroyed with the session).
+int umap_shard_impl(fe_b200_umap* s, const unsigned char* id, ncclComm_t lent, int nranks, int rank) {
   if (s->comm != nullptr) {
     set_error("UMAP session is already sharded");
     return 1;
@@ -211,8 +212,6 @@ int fe_b200_umap_shard(fe_b200_umap* s, const unsigned char* id, int id_bytes, i
     set_error("UMAP shard: need 1 <= nranks <= 256 and 0 <= rank < nranks");
     return 1;
   }
-  const fe::NcclApi* api = fe::nccl_api();
-  if (api == nullptr) return 1;
   const int n = s->n;
   const int per = (n + nranks - 1) / nranks;
   const size_t padded_rows = static_cast<size_t>(per) * nranks;
@@ -275,11 +274,10 @@ int fe_b200_umap_shard(fe_b200_umap* s, const unsigned char* id, int id_bytes, i
   long long own_edges = 0;
   FE_CUDA(cudaMemcpyAsync(&own_edges, selected, sizeof(long long), cudaMemcpyDeviceToHost, s->stream), "D2H");
   FE_CUDA(cudaStreamSynchronize(s->stream), "cudaStreamSynchronize(UMAP shard)");
-  ncclUniqueId uid;
-  std::memcpy(&uid, id, sizeof(uid));
-  ncclComm_t comm = nullptr;
-  FE_TRY(fe::check_nccl(api->CommInitRank(&comm, nranks, uid, rank), "ncclCommInitRank"));
+  ncclComm_t comm = lent;
+  if (comm == nullptr) FE_TRY(fe::comm_init(id, nranks, rank, &comm));
   s->comm = comm;
+  s->own_comm = lent == nullptr;
   s->shard_ranks = nranks;
   s->shard_rank = rank;
   s->rows_per_rank = per;
@@ -293,6 +291,30 @@ int fe_b200_umap_shard(fe_b200_umap* s, const unsigned char* id, int id_bytes, i
   s->shard_mem = mem;
   mem = nullptr;
   return 0;
+}
+
+}  // namespace
+
+extern "C" {
+
+int fe_b200_umap_shard(fe_b200_umap* s, const unsigned char* id, int id_bytes, int nranks, int rank) {
+  fe::clear_error();
+  FE_TRY(check_session(s));
+  if (id == nullptr || id_bytes < static_cast<int>(sizeof(ncclUniqueId))) {
+    set_error("invalid UMAP shard call");
+    return 1;
+  }
+  return umap_shard_impl(s, id, nullptr, nranks, rank);
+}
+
+int fe_b200_umap_shard_comm(fe_b200_umap* s, fe_b200_comm* comm) {
+  fe::clear_error();
+  FE_TRY(check_session(s));
+  if (comm == nullptr || comm->comm == nullptr) {
+    set_error("invalid UMAP shard call");
+    return 1;
+  }
+  return umap_shard_impl(s, nullptr, comm->comm, comm->nranks, comm->rank);
 }
 
 int fe_b200_umap_count_samples(fe_b200_umap* s, int epoch_begin, int epoch_end, int negative_sample_rate,

@@ -268,6 +268,9 @@ void fe_b200_umap_destroy(fe_b200_umap* s);
  * the unsharded one (up to float summation order); in Hogwild mode a rank
  * sees other ranks' moves from the next epoch on. */
 int fe_b200_umap_shard(fe_b200_umap* s, const unsigned char* id, int id_bytes, int nranks, int rank);
+/* The same on a communicator lent by fe_b200_comm_create (declared below). */
+struct fe_b200_comm;
+int fe_b200_umap_shard_comm(fe_b200_umap* s, struct fe_b200_comm* comm);
 
 /* ---- sharding one t-SNE run across GPUs (one process per GPU) ----
  * No counterpart in the reference's C ABI: the reference's multi-GPU build
@@ -286,6 +289,15 @@ int fe_b200_umap_shard(fe_b200_umap* s, const unsigned char* id, int id_bytes, i
  * in the same order.  Results are bit-identical for any number of ranks. */
 int fe_b200_nccl_unique_id(unsigned char* id, int id_bytes);
 int fe_b200_tsne_shard(fe_b200_tsne* s, const unsigned char* id, int id_bytes, int nranks, int rank);
+/* A communicator made once per process and lent to sessions in turn (a session
+ * sharded with fe_b200_*_shard_comm keeps using it and never destroys it), so
+ * that repeated runs do not pay NCCL's set-up each time.  Sessions that share
+ * one communicator must not run concurrently, and the communicator must
+ * outlive them.  fe_b200_comm_create blocks until every rank has joined. */
+typedef struct fe_b200_comm fe_b200_comm;
+int fe_b200_comm_create(const unsigned char* id, int id_bytes, int nranks, int rank, fe_b200_comm** out);
+void fe_b200_comm_destroy(fe_b200_comm* comm);
+int fe_b200_tsne_shard_comm(fe_b200_tsne* s, fe_b200_comm* comm);
 
 /* ---- UMAP parity hook ---- */
 /* Runs epochs [epoch_begin, epoch_end) of the COO optimizer on layout

@@ -35,12 +35,14 @@ def _problem_arrays():
     return idx, dist, S.tsne_init(N, seed=1)
 
 
-def run_session(idx, dist, init, shard=None):
+def run_session(idx, dist, init, shard=None, comm=None):
     """Gradient at the init, then EARLY + LATE iterations: final layout and state."""
     lr_e, lr_l = float(np.float32(N / 12.0)), float(np.float32(N / 1.0))
     with api.TsneSession.from_knn(idx, dist, perplexity=PERPLEXITY, init=init) as s:
         if shard is not None:
             s.shard(*shard)
+        if comm is not None:
+            s.shard_comm(comm)
         grad, z = s.gradient(12.0)
         s.iterate(EARLY, 12.0, 0.8, lr_e)
         s.iterate(LATE, 1.0, 0.8, lr_l)
@@ -66,6 +68,16 @@ def test_one_rank_shard_matches_unsharded(problem):
     assert np.isfinite(one["y"]).all()
     rel = np.linalg.norm(one["y"] - plain["y"]) / np.linalg.norm(plain["y"])
     assert rel < 1e-3, rel
+
+
+def test_lent_communicator_serves_sessions_in_turn(problem):
+    p = np.load(problem)
+    own = run_session(p["idx"], p["dist"], p["init"], shard=(api.nccl_unique_id(), 1, 0))
+    with api.NcclComm(api.nccl_unique_id(), 1, 0) as comm:
+        for _ in range(2):  # the session closes, the communicator stays usable
+            lent = run_session(p["idx"], p["dist"], p["init"], comm=comm)
+            for key in ("grad", "z", "y", "update", "gains"):
+                assert np.array_equal(lent[key], own[key]), key
 
 
 def test_shard_rejects_bad_ranks(problem):

@@ -18,7 +18,8 @@ Our arm (--impl ours) prints one JSON line with
   cpu_baseline  the reference's own CPU loop (oracle/_ref) on a few iterations of the
              same workload, all host threads
 The reference arm (--impl reference) times the reference's own CPU
-implementation of the same loop (rank 0 only).
+implementation of the same loop (rank 0 only); with --reference-backend cuda it
+times the reference's own CUDA backend through the e2e entry point instead.
 """
 from __future__ import annotations
 
@@ -246,6 +247,79 @@ def bench_reference_umap(args):
                    "n_edges": int(graph["heads"].size)},
         "cpu_baseline": {k: base[k] for k in ("value", "unit", "cores", "kind", "sample")},
         "e2e": {"value": base["value"], "unit": "edge_updates/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def bench_reference_cuda(args):
+    """The reference's own CUDA backend (oracle/_ref/libferef_cuda.so, its
+    src/embedding_cuda_kernels.cpp built for sm_100a), timed through the same
+    entry point as our arm's e2e leg: host KNN in, host layout out, whole call.
+    Opt-in (--reference-backend cuda): the GPU bar beside the CPU reference arm."""
+    rank, _, local = dist_env()
+    if rank != 0:
+        return 0
+    import torch
+
+    import oracle as O
+
+    if not O.ref_cuda_available():
+        print(json.dumps({"impl": "reference", "backend": "cuda",
+                          "unavailable": "oracle/_ref/libferef_cuda.so not built"}), flush=True)
+        return 0
+    torch.cuda.set_device(local)
+    w = WORKLOADS[args.workload]
+    umap = w.get("kind") == "umap"
+    reps = 2
+    if umap:
+        from fastembedr_b200 import api
+
+        idx, dist, _ = umap_inputs(args.workload, f"cuda:{local}")
+        n, k = idx.shape
+        a, b = api.find_ab_params(1.0, UMAP_MIN_DIST)
+        sni = api.umap_config(n, k)["spectral_n_iter"]
+        with api.UmapSession.from_knn(idx, dist) as s:
+            units, _ = s.count_samples(0, w["n_epochs"], UMAP_NSR)
+            n_edges = s.info()["n_edges"]
+
+        def call():
+            O.ref_cuda_umap_fused(idx, dist, w["n_epochs"], negative_sample_rate=UMAP_NSR, learning_rate=UMAP_LR,
+                                  a=a, b=b, spectral_n_iter=sni, seed=42)
+
+        metric, unit = "umap_edge_updates_per_second", "edge_updates/s"
+        entry = (f"fastembedr_cuda_umap_from_knn_spectral_float ({w['n_epochs']} epochs, host KNN: graph, "
+                 f"diffusion start, epochs)")
+        cfg = {"workload": args.workload, "n": int(n), "k": int(k), "n_edges": int(n_edges),
+               "units": "positive samples of this library's edge list for the schedule"}
+    else:
+        idx, dist, init = make_inputs(args.workload, f"cuda:{local}")
+        n, k = idx.shape
+        units = EE_ITER + N_ITER
+
+        def call():
+            O.ref_cuda_tsne(idx, dist, init, perplexity=w["perplexity"], early_exaggeration_iter=EE_ITER,
+                            n_iter=N_ITER, early_exaggeration=EE, exaggeration=EX, momentum=MOM,
+                            min_gain=MIN_GAIN, max_step_norm=MAX_STEP)
+
+        metric, unit = "tsne_iterations_per_second", "iterations/s"
+        entry = "fastembedr_cuda_opentsne_fft_from_knn_float (750 iterations, host KNN)"
+        cfg = {"workload": args.workload, "n": int(n), "k": int(k), "perplexity": w["perplexity"],
+               "grid": "reference CUDA policy"}
+    call()  # warm: module load, cuFFT plans
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        call()
+    secs = (time.perf_counter() - t0) / reps
+    value = units / secs
+    line = {
+        "impl": "reference", "backend": "cuda (the reference's src/embedding_cuda_kernels.cpp, sm_100a)",
+        "metric": metric, "value": value, "unit": unit, "n_gpus": 1, "steps": reps, "warmup": 1,
+        "ms_per_step": None, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "f32", "data": "synthetic", "config": cfg, "seconds_per_call": secs, "call": entry,
+        "e2e": {"value": value, "unit": unit, "h2d_bytes_per_step": int(idx.size * 8),
+                "d2h_bytes_per_step": int(n * 8)},
     }
     print(json.dumps(line), flush=True)
     return 0
@@ -676,10 +750,14 @@ def main():
     ap.add_argument("--cpu-iters", type=int, default=5)
     ap.add_argument("--skip-e2e", action="store_true")
     ap.add_argument("--skip-cpu", action="store_true")
+    ap.add_argument("--reference-backend", choices=["cpu", "cuda"], default="cpu",
+                    help="with --impl reference: the reference's CPU loop (default) or its own CUDA backend")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be at least 3")
     umap = WORKLOADS[args.workload].get("kind") == "umap"
+    if args.impl == "reference" and args.reference_backend == "cuda":
+        return bench_reference_cuda(args)
     if args.impl == "reference":
         return bench_reference_umap(args) if umap else bench_reference(args)
     if umap:

@@ -16,6 +16,8 @@ namespace fe {
 struct NcclApi {
   ncclResult_t (*GetUniqueId)(ncclUniqueId*);
   ncclResult_t (*CommInitRank)(ncclComm_t*, int, ncclUniqueId, int);
+  ncclResult_t (*CommInitRankConfig)(ncclComm_t*, int, ncclUniqueId, int, ncclConfig_t*);
+  ncclResult_t (*CommGetAsyncError)(ncclComm_t, ncclResult_t*);
   ncclResult_t (*CommDestroy)(ncclComm_t);
   ncclResult_t (*CommAbort)(ncclComm_t);
   ncclResult_t (*AllReduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
@@ -30,8 +32,21 @@ const NcclApi* nccl_api();
 // 0 on ncclSuccess; otherwise sets "<where>: <NCCL message>" and returns 1.
 int check_nccl(ncclResult_t code, const char* where);
 
+// check_nccl for a call on `comm`: a nonblocking communicator may answer
+// ncclInProgress while NCCL finishes the call on its own threads (connection
+// set-up at the first collective, for one); that is waited out, bounded by the
+// join limit below, before the outcome is checked.
+int check_nccl_call(ncclComm_t comm, ncclResult_t code, const char* where);
+
+// Seconds a rank waits for the others to join a communicator:
+// FASTEMBEDR_B200_NCCL_INIT_TIMEOUT_S, or 0 (unset) for as long as they take.
+double join_timeout_seconds();
+
 // Joins the communicator `unique_id` (ncclUniqueId bytes) as rank `rank` of
-// `nranks`, on the current device; blocks until every rank has joined.
+// `nranks`, on the current device, and returns once every rank has joined.
+// With a join limit set the communicator is made nonblocking and polled; a
+// rank whose peers have not all joined within the limit aborts it and returns
+// 1 ("... timed out ...") instead of waiting for good.
 int comm_init(const void* unique_id, int nranks, int rank, ncclComm_t* out);
 
 }  // namespace fe

@@ -61,9 +61,9 @@ int shard_gather_rows(TsneSession* s, float2* rows) {
   if (api == nullptr) return 1;
   const size_t count = 2 * static_cast<size_t>(s->rows_per_rank);  // floats per rank
   float* base = reinterpret_cast<float*>(rows);
-  return check_nccl(api->AllGather(base + count * s->shard_rank, base, count, ncclFloat32,
-                                   static_cast<ncclComm_t>(s->comm), s->stream),
-                    "ncclAllGather(layout rows)");
+  ncclComm_t comm = static_cast<ncclComm_t>(s->comm);
+  return check_nccl_call(comm, api->AllGather(base + count * s->shard_rank, base, count, ncclFloat32, comm, s->stream),
+                         "ncclAllGather(layout rows)");
 }
 
 int shard_sum_charges(TsneSession* s) {
@@ -72,9 +72,9 @@ int shard_sum_charges(TsneSession* s) {
   if (api == nullptr) return 1;
   const size_t words = 4 * static_cast<size_t>(s->grid) * s->grid;  // ChargeCell = 4 x u64
   // Two's-complement sums of the fixed-point words: exactly the unsharded atomics.
-  return check_nccl(api->AllReduce(s->charges, s->charges, words, ncclUint64, ncclSum,
-                                   static_cast<ncclComm_t>(s->comm), s->stream),
-                    "ncclAllReduce(charges)");
+  ncclComm_t comm = static_cast<ncclComm_t>(s->comm);
+  return check_nccl_call(comm, api->AllReduce(s->charges, s->charges, words, ncclUint64, ncclSum, comm, s->stream),
+                         "ncclAllReduce(charges)");
 }
 
 void shard_release(TsneSession* s) {

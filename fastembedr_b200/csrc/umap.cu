@@ -312,9 +312,9 @@ int gather_layout(UmapRun* r) {
   if (api == nullptr) return 1;
   const size_t count = 2 * static_cast<size_t>(r->rows_per_rank);
   float* base = reinterpret_cast<float*>(r->layout);
-  return check_nccl(api->AllGather(base + count * r->shard_rank, base, count, ncclFloat32,
-                                   static_cast<ncclComm_t>(r->comm), r->stream),
-                    "ncclAllGather(UMAP layout rows)");
+  ncclComm_t comm = static_cast<ncclComm_t>(r->comm);
+  return check_nccl_call(comm, api->AllGather(base + count * r->shard_rank, base, count, ncclFloat32, comm, r->stream),
+                         "ncclAllGather(UMAP layout rows)");
 }
 
 template <int Mode>

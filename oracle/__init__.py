@@ -667,3 +667,23 @@ def ref_cuda_umap_fused(idx: np.ndarray, dist: np.ndarray, n_epochs: int, negati
         optimizer_mode, _ptr(out, ctypes.c_float))
     _ref_cuda_check(rc, "fused UMAP")
     return out
+
+
+def ref_cuda_tsne(idx: np.ndarray, dist: np.ndarray, init: np.ndarray, perplexity: float = 30.0,
+                  early_exaggeration_iter: int = 250, n_iter: int = 500, early_exaggeration: float = 12.0,
+                  exaggeration: float = 1.0, momentum: float = 0.8, min_gain: float = 0.01,
+                  max_step_norm: float = 5.0, seed: int = 42, index_offset: int = 0) -> np.ndarray:
+    """fastembedr_cuda_opentsne_fft_from_knn_float of the reference
+    (src/embedding_cuda_kernels.cpp:5453-6008 behind the prototype at
+    src/embedding_cuda_impl.cpp:100-120): host KNN to host layout, learning
+    rate "auto", the grid from the reference's own CUDA policy."""
+    n, k = idx.shape
+    idx_cm, dist_cm = _cm(idx, np.int32), _cm(dist, np.float32)
+    init = np.ascontiguousarray(init, np.float32)
+    out = np.zeros((n, 2), np.float32)
+    rc = ref_cuda().fastembedr_cuda_opentsne_fft_from_knn_float(
+        _ptr(idx_cm, ctypes.c_int), _ptr(dist_cm, ctypes.c_float), _ptr(init, ctypes.c_float), 1, n, k, 2,
+        perplexity, early_exaggeration_iter, n_iter, early_exaggeration, exaggeration, 0.0, 1, momentum,
+        momentum, min_gain, max_step_norm, seed & 0xFFFFFFFF, index_offset, _ptr(out, ctypes.c_float))
+    _ref_cuda_check(rc, "openTSNE FFT")
+    return out

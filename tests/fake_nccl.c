@@ -1,18 +1,39 @@
 /* A stand-in NCCL for failure-path tests (built by tests/test_nccl_faults_cpu.py).
  *
- * Every entry point the library resolves exists and fails: ncclGetUniqueId
- * returns ncclSystemError (2), as a host without a usable network interface
- * would, and the communicator calls return ncclRemoteError (6), as when a peer
- * has gone away.  Built with -DFAKE_NCCL_MISSING_ALLGATHER it lacks
- * ncclAllGather, like an incompatible library.  No GPU is touched. */
+ * Default build: every entry point the library resolves exists and fails:
+ * ncclGetUniqueId returns ncclSystemError (2), as a host without a usable
+ * network interface would, and the communicator calls return ncclRemoteError
+ * (6), as when a peer has gone away.  Built with -DFAKE_NCCL_MISSING_ALLGATHER
+ * it lacks ncclAllGather, like an incompatible library.
+ *
+ * Built with -DFAKE_NCCL_JOIN_POLLS=n it models the join of a communicator
+ * instead: ncclGetUniqueId succeeds, ncclCommInitRankConfig answers
+ * ncclInProgress (7), and ncclCommGetAsyncError reports ncclInProgress for the
+ * first n polls and ncclSuccess after them; n < 0 is a peer that never joins.
+ * The blocking ncclCommInitRank succeeds at once when n >= 0 and returns
+ * ncclInvalidUsage (5) when n < 0 (the real call would wait for good).
+ * fake_nccl_aborts / _polls / _last_blocking count what the caller did.
+ * No GPU is touched. */
+#include <stddef.h>
 #include <string.h>
 
 typedef struct { char internal[128]; } fake_unique_id;
 typedef void* fake_comm;
+/* The leading fields of ncclConfig_t (NCCL's stable C ABI). */
+typedef struct { size_t size; unsigned int magic; unsigned int version; int blocking; } fake_config_prefix;
 
 static const char* const kMessages[] = {"no error", "unhandled cuda error", "fake: no usable network interface",
                                         "internal error", "invalid argument", "invalid usage",
                                         "fake: remote process exited", "operation in progress"};
+
+static int g_aborts = 0;
+static int g_polls = 0;
+static int g_last_blocking = -1;
+static int g_comm_storage = 0;
+
+int fake_nccl_aborts(void) { return g_aborts; }
+int fake_nccl_polls(void) { return g_polls; }
+int fake_nccl_last_blocking(void) { return g_last_blocking; }
 
 const char* ncclGetErrorString(int code) {
   return code >= 0 && code < 8 ? kMessages[code] : "unknown";
@@ -20,15 +41,50 @@ const char* ncclGetErrorString(int code) {
 
 int ncclGetUniqueId(fake_unique_id* id) {
   memset(id, 0, sizeof(*id));
+#ifdef FAKE_NCCL_JOIN_POLLS
+  return 0;
+#else
   return 2;
+#endif
 }
 
 int ncclCommInitRank(fake_comm* comm, int nranks, fake_unique_id id, int rank) {
   (void)nranks;
   (void)id;
   (void)rank;
+#ifdef FAKE_NCCL_JOIN_POLLS
+  *comm = FAKE_NCCL_JOIN_POLLS >= 0 ? (fake_comm)&g_comm_storage : 0;
+  return FAKE_NCCL_JOIN_POLLS >= 0 ? 0 : 5;
+#else
   *comm = 0;
   return 6;
+#endif
+}
+
+int ncclCommInitRankConfig(fake_comm* comm, int nranks, fake_unique_id id, int rank, fake_config_prefix* config) {
+  (void)nranks;
+  (void)id;
+  (void)rank;
+  g_last_blocking = config ? config->blocking : -1;
+#ifdef FAKE_NCCL_JOIN_POLLS
+  *comm = (fake_comm)&g_comm_storage;
+  g_polls = 0;
+  return 7;
+#else
+  *comm = 0;
+  return 6;
+#endif
+}
+
+int ncclCommGetAsyncError(fake_comm comm, int* state) {
+  (void)comm;
+  ++g_polls;
+#ifdef FAKE_NCCL_JOIN_POLLS
+  *state = (FAKE_NCCL_JOIN_POLLS < 0 || g_polls <= FAKE_NCCL_JOIN_POLLS) ? 7 : 0;
+#else
+  *state = 6;
+#endif
+  return 0;
 }
 
 int ncclCommDestroy(fake_comm comm) {
@@ -38,6 +94,7 @@ int ncclCommDestroy(fake_comm comm) {
 
 int ncclCommAbort(fake_comm comm) {
   (void)comm;
+  ++g_aborts;
   return 0;
 }
 

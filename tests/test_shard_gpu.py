@@ -89,6 +89,44 @@ def test_shard_rejects_bad_ranks(problem):
             s.shard(api.nccl_unique_id(), 0, 0)
 
 
+JOIN_PROBE = r"""
+import sys
+sys.path.insert(0, {root!r})
+import numpy as np
+from fastembedr_b200 import api
+try:
+    api.NcclComm(api.nccl_unique_id(), 2, 0)  # rank 1 is never started
+except api.CudaBackendError as e:
+    print("ERROR:", e)
+else:
+    print("JOINED")
+x = np.random.default_rng(0).normal(size=(600, 10)).astype(np.float32)
+d = ((x[:, None] - x[None]) ** 2).sum(-1)
+np.fill_diagonal(d, np.inf)
+idx = np.argsort(d, 1)[:, :20].astype(np.int32)
+dist = np.sqrt(np.take_along_axis(d, idx, 1)).astype(np.float32)
+with api.NcclComm(api.nccl_unique_id(), 1, 0) as comm:  # the same bounded join, one rank
+    with api.TsneSession.from_knn(idx, dist, perplexity=10.0) as s:
+        s.shard_comm(comm)
+        s.iterate(5, 12.0, 0.8, 50.0)
+        print("AFTER", bool(np.isfinite(s.layout()).all()))
+"""
+
+
+def test_peer_that_never_joins_times_out():
+    """A rank whose peer never starts gives up after the join limit, aborts the
+    communicator and returns status 1; the process and its device stay usable.
+    Host side only: no kernel or collective is in flight while it waits."""
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    env = dict(os.environ, FASTEMBEDR_B200_NCCL_INIT_TIMEOUT_S="3", NCCL_NVLS_ENABLE="0")
+    r = subprocess.run([sys.executable, "-c", JOIN_PROBE.format(root=root)], env=env, capture_output=True,
+                       text=True, timeout=180)
+    assert r.returncode == 0, r.stderr[-2000:]
+    lines = r.stdout.strip().splitlines()
+    assert lines[0].startswith("ERROR:") and "timed out after 3 s" in lines[0], lines
+    assert lines[-1] == "AFTER True", lines
+
+
 def _gpu_count():
     import torch
 

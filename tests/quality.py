@@ -9,31 +9,35 @@ share the point's label.  Evaluated over every point, in row blocks.
 import numpy as np
 
 
-def layout_knn(y, k, block=4096):
+def layout_knn(y, k, block=4096, rows=None):
+    """The k nearest layout neighbours (self excluded) of every point, or of
+    the points `rows` (a fixed sample at large n), among all points."""
     import torch
 
     Y = torch.from_numpy(np.ascontiguousarray(y, np.float32)).cuda()
-    n = Y.shape[0]
-    out = np.empty((n, k), np.int64)
-    for s in range(0, n, block):
-        e = min(n, s + block)
-        d = torch.cdist(Y[s:e], Y)
-        d[torch.arange(e - s, device=Y.device), torch.arange(s, e, device=Y.device)] = float("inf")
+    rows = np.arange(Y.shape[0]) if rows is None else np.asarray(rows, np.int64)
+    out = np.empty((rows.size, k), np.int64)
+    for s in range(0, rows.size, block):
+        e = min(rows.size, s + block)
+        r = torch.from_numpy(rows[s:e]).cuda()
+        d = torch.cdist(Y[r], Y)
+        d[torch.arange(e - s, device=Y.device), r] = float("inf")
         out[s:e] = torch.topk(d, k, largest=False).indices.cpu().numpy()
     return out
 
 
-def knn_preservation(y, idx, k=15):
-    nn = layout_knn(y, k)
-    hi = np.asarray(idx)[:, :k]
+def knn_preservation(y, idx, k=15, rows=None):
+    nn = layout_knn(y, k, rows=rows)
+    hi = np.asarray(idx)[:, :k] if rows is None else np.asarray(idx)[rows, :k]
     hits = (nn[:, :, None] == hi[:, None, :]).any(-1).sum(1)
     return float(hits.mean() / k)
 
 
-def label_accuracy(y, labels, k=15):
-    nn = layout_knn(y, k)
+def label_accuracy(y, labels, k=15, rows=None):
+    nn = layout_knn(y, k, rows=rows)
     lab = np.asarray(labels)
-    return float((lab[nn] == lab[:, None]).mean())
+    own = lab if rows is None else lab[rows]
+    return float((lab[nn] == own[:, None]).mean())
 
 
 def within_reference(ours, ref, rel=0.02, z=2.0):

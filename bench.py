@@ -15,8 +15,8 @@ Our arm (--impl ours) prints one JSON line with
              from pinned host KNN to host layout: H2D, P build, 750 iterations, D2H
   roofline   the fused gradient/update kernel: algorithmic bytes per launch over its
              CUDA-event duration, against MEASURED_PEAKS.json's HBM copy bandwidth
-  cpu_baseline  the reference's own CPU loop (oracle/_ref) on a few iterations of the
-             same workload, all host threads
+  cpu_baseline  the reference's own CPU loop (oracle/_ref) on the first iterations of the
+             same workload (about 10 s of loop, --cpu-seconds), all host threads
 The reference arm (--impl reference) times the reference's own CPU
 implementation of the same loop (rank 0 only); with --reference-backend cuda it
 times the reference's own CUDA backend through the e2e entry point instead.
@@ -183,32 +183,40 @@ def profile_traffic(kernel: str, workload: str):
     return float(m.group(1)) if m else None
 
 
-def cpu_baseline_tsne(idx, dist, perplexity, init, iters: int):
-    """The reference's own CPU loop on `iters` iterations of the workload."""
+def cpu_baseline_tsne(idx, dist, perplexity, init, chunk: int, seconds: float,
+                      max_iters: int = EE_ITER + N_ITER):
+    """The reference's own CPU loop on the first iterations of the standard
+    schedule: chunks of at most `chunk` iterations (none crossing the phase
+    boundary), continuing the optimizer state, until the loop has run
+    `seconds` or `max_iters` iterations (at most one run); P build excluded."""
     import oracle as O
 
     threads = os.cpu_count() or 1
     n = idx.shape[0]
-    ex, mom, lr = phase_params(0, n)
+    max_iters = min(max_iters, EE_ITER + N_ITER)
     upd = np.zeros_like(init)
     gains = np.ones_like(init)
-    if O.ref_available():
-        t0 = time.time()
-        P = O.ref_tsne_build_p(idx, dist, perplexity, threads=threads)
-        setup = time.time() - t0
-        _, _, _, secs = O.ref_tsne_iterate(P, O.tsne_zero_mean(init), upd, gains, iters, ex, mom, lr,
-                                           MIN_GAIN, MAX_STEP, threads=threads)
-        kind, cores = "reference", threads
-    else:
-        t0 = time.time()
-        P = O.tsne_build_p(idx, dist, perplexity)
-        setup = time.time() - t0
-        t0 = time.time()
-        O.tsne_iterate(P, O.tsne_zero_mean(init), upd, gains, iters, ex, mom, lr, MIN_GAIN, MAX_STEP)
-        secs = time.time() - t0
-        kind, cores = "port", 1
-    return {"value": iters / secs, "unit": "iterations/s", "cores": cores, "kind": kind,
-            "sample": f"{iters} optimizer iterations of the full n={n} workload "
+    y = O.tsne_zero_mean(init)
+    iters, secs = 0, 0.0
+    use_ref = O.ref_available()
+    t0 = time.time()
+    P = O.ref_tsne_build_p(idx, dist, perplexity, threads=threads) if use_ref else O.tsne_build_p(idx, dist, perplexity)
+    setup = time.time() - t0
+    while secs < seconds and iters < max_iters:
+        ex, mom, lr = phase_params(iters, n)
+        step = min(chunk, (EE_ITER if iters < EE_ITER else EE_ITER + N_ITER) - iters, max_iters - iters)
+        if use_ref:
+            y, upd, gains, s = O.ref_tsne_iterate(P, y, upd, gains, step, ex, mom, lr, MIN_GAIN, MAX_STEP,
+                                                  threads=threads)
+        else:
+            t1 = time.time()
+            y, upd, gains = O.tsne_iterate(P, y, upd, gains, step, ex, mom, lr, MIN_GAIN, MAX_STEP)
+            s = time.time() - t1
+        iters, secs = iters + step, secs + s
+    kind, cores = ("reference", threads) if use_ref else ("port", 1)
+    return {"value": iters / secs, "unit": "iterations/s", "cores": cores, "kind": kind, "iterations": iters,
+            "seconds": secs,
+            "sample": f"the first {iters} optimizer iterations of the full n={n} workload, {secs:.1f}s of loop "
                       f"(P build {setup:.1f}s excluded), {cores} threads"}
 
 
@@ -219,12 +227,13 @@ def bench_reference(args):
     w = WORKLOADS[args.workload]
     device = "cuda" if _cuda_ok() else None
     idx, dist, init = make_inputs(args.workload, device)
-    iters = max(1, min(args.steps, 40))
-    base = cpu_baseline_tsne(idx, dist, w["perplexity"], init, iters)
+    base = cpu_baseline_tsne(idx, dist, w["perplexity"], init, args.cpu_iters, args.cpu_seconds,
+                             max_iters=max(args.cpu_iters, args.steps))
+    iters = base["iterations"]
     line = {
         "impl": "reference", "metric": "tsne_iterations_per_second", "value": base["value"],
         "unit": "iterations/s", "n_gpus": 0, "steps": iters, "warmup": 0,
-        "ms_per_step": 1000.0 / base["value"], "higher_is_better": True, "scaling": "weak",
+        "ms_per_step": 1000.0 / base["value"], "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": {"workload": args.workload, "n": int(idx.shape[0]), "k": w["k"],
                    "perplexity": w["perplexity"], "grid": "reference CPU policy"},
@@ -516,7 +525,7 @@ def bench_ours(args):
 
     cpu = None
     if rank == 0 and world == 1 and not args.skip_cpu:
-        cpu = cpu_baseline_tsne(idx, dist, w["perplexity"], init, args.cpu_iters)
+        cpu = cpu_baseline_tsne(idx, dist, w["perplexity"], init, args.cpu_iters, args.cpu_seconds)
 
     sess.close()
     if rank == 0:
@@ -758,7 +767,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=30)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="tsne_1m")
-    ap.add_argument("--cpu-iters", type=int, default=5)
+    ap.add_argument("--cpu-iters", type=int, default=5, help="iterations per chunk of the CPU sample")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0, help="loop time of the CPU sample")
     ap.add_argument("--skip-e2e", action="store_true")
     ap.add_argument("--skip-cpu", action="store_true")
     ap.add_argument("--reference-backend", choices=["cpu", "cuda"], default="cpu",

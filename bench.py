@@ -246,17 +246,19 @@ def bench_reference(args):
 
 
 def bench_reference_umap(args):
-    """The reference's CPU COO optimizer on the first epochs of the workload's
-    edge list (from this library's device graph build, which follows the
-    reference's device-KNN path)."""
+    """The reference's CPU path end to end on the host: its own fuzzy graph
+    (build_graph_csr_native_direct_values, src/fast_knn_umap.cpp:1553-1771) as
+    COO, then its COO optimizer on the first epochs; only the optimizer is timed."""
     rank, _, _ = dist_env()
     if rank != 0:
         return 0
-    from fastembedr_b200 import api
+    import oracle as O
 
     idx, dist, init = umap_inputs(args.workload, "cuda" if _cuda_ok() else None)
-    with api.UmapSession.from_knn(idx, dist) as s:
-        graph = s.graph()
+    t0 = time.time()
+    g = O.ref_umap_graph(idx, dist, threads=os.cpu_count() or 1) if O.ref_available() else O.umap_graph(idx, dist)
+    graph = {"heads": g.heads(), "tails": g.neighbors, "epochs_per_sample": g.epochs_per_sample}
+    log(f"[bench] reference CPU graph: {graph['heads'].size} edges in {time.time() - t0:.1f}s")
     base = cpu_baseline_umap(graph, init)
     line = {
         "impl": "reference", "metric": "umap_edge_updates_per_second", "value": base["value"],
@@ -577,18 +579,41 @@ def umap_inputs(workload: str, device):
     return idx, dist, S.umap_random_init(spec.n, seed=0)
 
 
+CPU_UMAP_SAMPLES = 4e7  # positive samples in the CPU sample: ~10-15 s of the reference loop on 16 threads
+
+
+def cpu_sample_epochs(p, budget: float = CPU_UMAP_SAMPLES, lo: int = 3, hi: int = 100) -> int:
+    """The most epochs (lo..hi) whose positive samples, sum of floor((E-1)/p),
+    stay within `budget`: a CPU sample of bounded length that still runs past
+    the first epochs (an edge of period p first fires at epoch p)."""
+    stride = max(1, p.size // 1_000_000)  # sizing only: an every-stride-th edge estimate
+    sub = p[::stride]
+
+    def pos(e):
+        return int(np.floor(np.float32(e - 1) / sub).astype(np.int64).sum()) * stride
+
+    if pos(lo) > budget:
+        return lo
+    while lo < hi:  # largest e with pos(e) <= budget
+        mid = (lo + hi + 1) // 2
+        if pos(mid) <= budget:
+            lo = mid
+        else:
+            hi = mid - 1
+    return lo
+
+
 def cpu_baseline_umap(graph, init, epochs: int = 0):
     """The reference's own CPU COO optimizer (fast_knn_umap_coo_replay_cpp) on
-    the same edge list, epochs 0 .. epochs-1 of a schedule, all host threads.
-    Early epochs apply fewer positive samples than the schedule's average (an
-    edge of period p first fires at epoch p), so the sample runs long enough
-    for most edges to have fired: 100 epochs up to 5M edges, else 20."""
+    the same edge list, epochs 0 .. epochs-1 of a schedule, all host threads;
+    by default as many epochs (3-100) as keep the sample near
+    CPU_UMAP_SAMPLES positive samples."""
     import oracle as O
 
     threads = os.cpu_count() or 1
     h, t, p = graph["heads"], graph["tails"], graph["epochs_per_sample"].astype(np.float32)
     if epochs <= 0:
-        epochs = 100 if h.size <= 5_000_000 else 20
+        epochs = cpu_sample_epochs(p)
     pos = int(np.floor(np.float32(epochs - 1) / p).astype(np.int64).sum())
     if O.ref_available():
         t0 = time.time()

@@ -194,30 +194,39 @@ def cpu_baseline_tsne(idx, dist, perplexity, init, chunk: int, seconds: float,
     threads = os.cpu_count() or 1
     n = idx.shape[0]
     max_iters = min(max_iters, EE_ITER + N_ITER)
-    upd = np.zeros_like(init)
-    gains = np.ones_like(init)
-    y = O.tsne_zero_mean(init)
-    iters, secs = 0, 0.0
     use_ref = O.ref_available()
     t0 = time.time()
     P = O.ref_tsne_build_p(idx, dist, perplexity, threads=threads) if use_ref else O.tsne_build_p(idx, dist, perplexity)
     setup = time.time() - t0
-    while secs < seconds and iters < max_iters:
-        ex, mom, lr = phase_params(iters, n)
-        step = min(chunk, (EE_ITER if iters < EE_ITER else EE_ITER + N_ITER) - iters, max_iters - iters)
-        if use_ref:
-            y, upd, gains, s = O.ref_tsne_iterate(P, y, upd, gains, step, ex, mom, lr, MIN_GAIN, MAX_STEP,
-                                                  threads=threads)
-        else:
-            t1 = time.time()
-            y, upd, gains = O.tsne_iterate(P, y, upd, gains, step, ex, mom, lr, MIN_GAIN, MAX_STEP)
-            s = time.time() - t1
-        iters, secs = iters + step, secs + s
+
+    def sample(variant, limit_s, limit_iters):
+        upd = np.zeros_like(init)
+        gains = np.ones_like(init)
+        y = O.tsne_zero_mean(init)
+        iters, secs = 0, 0.0
+        while secs < limit_s and iters < limit_iters:
+            ex, mom, lr = phase_params(iters, n)
+            step = min(chunk, (EE_ITER if iters < EE_ITER else EE_ITER + N_ITER) - iters, limit_iters - iters)
+            if use_ref:
+                y, upd, gains, s = O.ref_tsne_iterate(P, y, upd, gains, step, ex, mom, lr, MIN_GAIN, MAX_STEP,
+                                                      threads=threads, variant=variant)
+            else:
+                t1 = time.time()
+                y, upd, gains = O.tsne_iterate(P, y, upd, gains, step, ex, mom, lr, MIN_GAIN, MAX_STEP)
+                s = time.time() - t1
+            iters, secs = iters + step, secs + s
+        return iters, secs
+
+    iters, secs = sample("O2", seconds, max_iters)
     kind, cores = ("reference", threads) if use_ref else ("port", 1)
-    return {"value": iters / secs, "unit": "iterations/s", "cores": cores, "kind": kind, "iterations": iters,
-            "seconds": secs,
-            "sample": f"the first {iters} optimizer iterations of the full n={n} workload, {secs:.1f}s of loop "
-                      f"(P build {setup:.1f}s excluded), {cores} threads"}
+    out = {"value": iters / secs, "unit": "iterations/s", "cores": cores, "kind": kind, "iterations": iters,
+           "seconds": secs, "flags": "-O2 (R's default package build)" if use_ref else "-O2",
+           "sample": f"the first {iters} optimizer iterations of the full n={n} workload, {secs:.1f}s of loop "
+                     f"(P build {setup:.1f}s excluded), {cores} threads"}
+    if use_ref and O.ref_available("O3"):
+        it3, s3 = sample("O3", float("inf"), iters)  # the same iterations
+        out["O3"] = {"value": it3 / s3, "seconds": s3, "flags": "-O3 -march=x86-64-v3"}
+    return out
 
 
 def bench_reference(args):
@@ -237,7 +246,8 @@ def bench_reference(args):
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": {"workload": args.workload, "n": int(idx.shape[0]), "k": w["k"],
                    "perplexity": w["perplexity"], "grid": "reference CPU policy"},
-        "cpu_baseline": {k: base[k] for k in ("value", "unit", "cores", "kind", "sample")},
+        "cpu_baseline": {k: base[k] for k in ("value", "unit", "cores", "kind", "sample", "flags", "O3")
+                         if k in base},
         "e2e": {"value": base["value"], "unit": "iterations/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
@@ -267,7 +277,8 @@ def bench_reference_umap(args):
         "dtype": "f32", "data": "synthetic",
         "config": {"workload": args.workload, "n": int(idx.shape[0]), "k": int(idx.shape[1]),
                    "n_edges": int(graph["heads"].size)},
-        "cpu_baseline": {k: base[k] for k in ("value", "unit", "cores", "kind", "sample")},
+        "cpu_baseline": {k: base[k] for k in ("value", "unit", "cores", "kind", "sample", "flags", "O3")
+                         if k in base},
         "e2e": {"value": base["value"], "unit": "edge_updates/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -626,9 +637,17 @@ def cpu_baseline_umap(graph, init, epochs: int = 0):
         for e in range(epochs):
             y = O.umap_epoch_delta(h, t, p, y, e, epochs)
         secs, kind, cores = time.time() - t0, "port", 1
-    return {"value": pos / secs, "unit": "edge_updates/s", "cores": cores, "kind": kind,
-            "sample": f"epochs 0-{epochs - 1} of the full edge list ({h.size} edges, {pos} positive samples), "
-                      f"{cores} threads"}
+    out = {"value": pos / secs, "unit": "edge_updates/s", "cores": cores, "kind": kind,
+           "flags": "-O2 (R's default package build)" if kind == "reference" else "-O2",
+           "sample": f"epochs 0-{epochs - 1} of the full edge list ({h.size} edges, {pos} positive samples), "
+                     f"{cores} threads"}
+    if kind == "reference" and O.ref_available("O3"):
+        t0 = time.time()
+        O.ref_umap_coo_replay(h, t, (1.0 / p).astype(np.float32), p, init, epochs, min_dist=UMAP_MIN_DIST,
+                              negative_sample_rate=UMAP_NSR, learning_rate=UMAP_LR, threads=threads, variant="O3")
+        s3 = time.time() - t0
+        out["O3"] = {"value": pos / s3, "seconds": s3, "flags": "-O3 -march=x86-64-v3"}
+    return out
 
 
 def bench_umap(args):

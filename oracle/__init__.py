@@ -29,6 +29,10 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 ORACLE_SO = os.path.join(HERE, "liboracle.so")
 REF_SO = os.path.join(HERE, "_ref", "libferef.so")
+# The same reference sources built at -O3 for x86-64-v3 hosts (a second CPU
+# baseline beside R's default -O2; see Makefile).
+REF_O3_SO = os.path.join(HERE, "_ref", "libferef_o3.so")
+REF_VARIANTS = {"O2": REF_SO, "O3": REF_O3_SO}
 
 _c_int_p = ctypes.POINTER(ctypes.c_int)
 _c_float_p = ctypes.POINTER(ctypes.c_float)
@@ -36,6 +40,7 @@ _c_double_p = ctypes.POINTER(ctypes.c_double)
 
 _lib = None
 _ref = None
+_ref_variants = {}
 
 
 def build(ref_src: Optional[str] = None) -> None:
@@ -71,79 +76,88 @@ def lib() -> ctypes.CDLL:
     return _lib
 
 
-def ref_available() -> bool:
-    return os.path.exists(REF_SO)
+def ref_available(variant: str = "O2") -> bool:
+    return os.path.exists(REF_VARIANTS[variant])
 
 
-def ref() -> ctypes.CDLL:
-    """The reference's own CPU code (raises if it was never built)."""
+def ref(variant: str = "O2") -> ctypes.CDLL:
+    """The reference's own CPU code (raises if it was never built); `variant`
+    "O3" is the same code built at -O3 for x86-64-v3 hosts."""
     global _ref
+    if variant != "O2":
+        if variant not in _ref_variants:
+            _ref_variants[variant] = _load_ref(REF_VARIANTS[variant])
+        return _ref_variants[variant]
     if _ref is None:
-        if not os.path.exists(REF_SO):
-            raise FileNotFoundError(f"{REF_SO} missing: build it where the reference sources exist")
-        R = ctypes.CDLL(REF_SO)
-        R.feref_tsne_last_error.restype = ctypes.c_char_p
-        R.feref_umap_last_error.restype = ctypes.c_char_p
-        R.feref_tsne_p_build.restype = ctypes.c_void_p
-        R.feref_tsne_p_build.argtypes = [_c_int_p, _c_float_p, ctypes.c_int, ctypes.c_int,
-                                         ctypes.c_double, ctypes.c_int]
-        R.feref_tsne_p_nnz.restype = ctypes.c_longlong
-        R.feref_tsne_p_nnz.argtypes = [ctypes.c_void_p]
-        R.feref_tsne_p_copy.argtypes = [ctypes.c_void_p, _c_int_p, _c_int_p, _c_float_p]
-        R.feref_tsne_p_free.argtypes = [ctypes.c_void_p]
-        R.feref_tsne_gradient_fft.argtypes = [_c_int_p, _c_int_p, _c_float_p, ctypes.c_int,
-                                              _c_float_p, ctypes.c_float, ctypes.c_int,
-                                              ctypes.c_int, _c_float_p]
-        R.feref_tsne_gradient_exact.argtypes = [_c_int_p, _c_int_p, _c_float_p, ctypes.c_int,
-                                                _c_float_p, ctypes.c_float, ctypes.c_int,
-                                                _c_float_p]
-        R.feref_tsne_attractive.argtypes = R.feref_tsne_gradient_exact.argtypes
-        R.feref_tsne_update.argtypes = [_c_float_p, _c_float_p, _c_float_p, _c_float_p,
-                                        ctypes.c_int, ctypes.c_float, ctypes.c_float,
-                                        ctypes.c_float, ctypes.c_float, ctypes.c_int]
-        R.feref_tsne_zero_mean.argtypes = [_c_float_p, ctypes.c_int]
-        R.feref_tsne_iterate.argtypes = [_c_int_p, _c_int_p, _c_float_p, ctypes.c_int, _c_float_p,
-                                         _c_float_p, _c_float_p, ctypes.c_int, ctypes.c_float,
-                                         ctypes.c_float, ctypes.c_float, ctypes.c_float,
-                                         ctypes.c_float, ctypes.c_int, ctypes.c_int, _c_double_p]
-        R.feref_tsne_kl.argtypes = [_c_int_p, _c_int_p, _c_float_p, ctypes.c_int, _c_float_p,
-                                    ctypes.c_int, _c_double_p]
-        R.feref_tsne_run.argtypes = [_c_int_p, _c_float_p, ctypes.c_int, ctypes.c_int, _c_float_p,
-                                     ctypes.c_double, ctypes.c_int, ctypes.c_int, ctypes.c_double,
-                                     ctypes.c_double, ctypes.c_double, ctypes.c_int,
-                                     ctypes.c_double, ctypes.c_double, ctypes.c_double,
-                                     ctypes.c_double, ctypes.c_int, ctypes.c_int, ctypes.c_int,
-                                     _c_float_p]
-        R.feref_tsne_grid_size.argtypes = [ctypes.c_int, ctypes.c_int]
-        R.feref_tsne_auto_parameters.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.c_double,
-                                                 ctypes.c_int, _c_double_p]
-        R.feref_umap_graph.restype = ctypes.c_void_p
-        R.feref_umap_graph.argtypes = [_c_int_p, _c_float_p, ctypes.c_int, ctypes.c_int,
-                                       ctypes.c_int]
-        R.feref_umap_graph_nnz.restype = ctypes.c_longlong
-        R.feref_umap_graph_nnz.argtypes = [ctypes.c_void_p]
-        R.feref_umap_graph_copy.argtypes = [ctypes.c_void_p, _c_int_p, _c_int_p, _c_float_p,
-                                            _c_float_p, _c_float_p]
-        R.feref_umap_graph_free.argtypes = [ctypes.c_void_p]
-        R.feref_umap_coo_replay.argtypes = [_c_int_p, _c_int_p, _c_float_p, _c_float_p,
-                                            _c_float_p, ctypes.c_int, ctypes.c_int, ctypes.c_int,
-                                            ctypes.c_double, ctypes.c_int, ctypes.c_double,
-                                            ctypes.c_double, ctypes.c_int, ctypes.c_int,
-                                            ctypes.c_int, _c_float_p]
-        R.feref_umap_csr_optimize.argtypes = [_c_int_p, _c_int_p, _c_float_p, _c_float_p,
-                                              ctypes.c_int, ctypes.c_int, ctypes.c_int,
-                                              ctypes.c_double, ctypes.c_int, ctypes.c_double,
-                                              ctypes.c_double, ctypes.c_int, ctypes.c_int,
-                                              _c_float_p]
-        R.feref_umap_powf.restype = ctypes.c_float
-        R.feref_umap_powf.argtypes = [ctypes.c_float, ctypes.c_float]
-        R.feref_umap_positive_samples.argtypes = [ctypes.c_float, ctypes.c_int]
-        R.feref_umap_negative_samples.argtypes = [ctypes.c_float, ctypes.c_int, ctypes.c_int]
-        R.feref_umap_negative_vertex.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.c_int,
-                                                 ctypes.c_int, ctypes.c_longlong, ctypes.c_int]
-        R.feref_find_ab.argtypes = [ctypes.c_double, ctypes.c_double, _c_double_p, _c_double_p]
-        _ref = R
+        _ref = _load_ref(REF_SO)
     return _ref
+
+
+def _load_ref(path: str) -> ctypes.CDLL:
+    if not os.path.exists(path):
+        raise FileNotFoundError(f"{path} missing: build it where the reference sources exist")
+    R = ctypes.CDLL(path)
+    R.feref_tsne_last_error.restype = ctypes.c_char_p
+    R.feref_umap_last_error.restype = ctypes.c_char_p
+    R.feref_tsne_p_build.restype = ctypes.c_void_p
+    R.feref_tsne_p_build.argtypes = [_c_int_p, _c_float_p, ctypes.c_int, ctypes.c_int,
+                                     ctypes.c_double, ctypes.c_int]
+    R.feref_tsne_p_nnz.restype = ctypes.c_longlong
+    R.feref_tsne_p_nnz.argtypes = [ctypes.c_void_p]
+    R.feref_tsne_p_copy.argtypes = [ctypes.c_void_p, _c_int_p, _c_int_p, _c_float_p]
+    R.feref_tsne_p_free.argtypes = [ctypes.c_void_p]
+    R.feref_tsne_gradient_fft.argtypes = [_c_int_p, _c_int_p, _c_float_p, ctypes.c_int,
+                                          _c_float_p, ctypes.c_float, ctypes.c_int,
+                                          ctypes.c_int, _c_float_p]
+    R.feref_tsne_gradient_exact.argtypes = [_c_int_p, _c_int_p, _c_float_p, ctypes.c_int,
+                                            _c_float_p, ctypes.c_float, ctypes.c_int,
+                                            _c_float_p]
+    R.feref_tsne_attractive.argtypes = R.feref_tsne_gradient_exact.argtypes
+    R.feref_tsne_update.argtypes = [_c_float_p, _c_float_p, _c_float_p, _c_float_p,
+                                    ctypes.c_int, ctypes.c_float, ctypes.c_float,
+                                    ctypes.c_float, ctypes.c_float, ctypes.c_int]
+    R.feref_tsne_zero_mean.argtypes = [_c_float_p, ctypes.c_int]
+    R.feref_tsne_iterate.argtypes = [_c_int_p, _c_int_p, _c_float_p, ctypes.c_int, _c_float_p,
+                                     _c_float_p, _c_float_p, ctypes.c_int, ctypes.c_float,
+                                     ctypes.c_float, ctypes.c_float, ctypes.c_float,
+                                     ctypes.c_float, ctypes.c_int, ctypes.c_int, _c_double_p]
+    R.feref_tsne_kl.argtypes = [_c_int_p, _c_int_p, _c_float_p, ctypes.c_int, _c_float_p,
+                                ctypes.c_int, _c_double_p]
+    R.feref_tsne_run.argtypes = [_c_int_p, _c_float_p, ctypes.c_int, ctypes.c_int, _c_float_p,
+                                 ctypes.c_double, ctypes.c_int, ctypes.c_int, ctypes.c_double,
+                                 ctypes.c_double, ctypes.c_double, ctypes.c_int,
+                                 ctypes.c_double, ctypes.c_double, ctypes.c_double,
+                                 ctypes.c_double, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                 _c_float_p]
+    R.feref_tsne_grid_size.argtypes = [ctypes.c_int, ctypes.c_int]
+    R.feref_tsne_auto_parameters.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.c_double,
+                                             ctypes.c_int, _c_double_p]
+    R.feref_umap_graph.restype = ctypes.c_void_p
+    R.feref_umap_graph.argtypes = [_c_int_p, _c_float_p, ctypes.c_int, ctypes.c_int,
+                                   ctypes.c_int]
+    R.feref_umap_graph_nnz.restype = ctypes.c_longlong
+    R.feref_umap_graph_nnz.argtypes = [ctypes.c_void_p]
+    R.feref_umap_graph_copy.argtypes = [ctypes.c_void_p, _c_int_p, _c_int_p, _c_float_p,
+                                        _c_float_p, _c_float_p]
+    R.feref_umap_graph_free.argtypes = [ctypes.c_void_p]
+    R.feref_umap_coo_replay.argtypes = [_c_int_p, _c_int_p, _c_float_p, _c_float_p,
+                                        _c_float_p, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                        ctypes.c_double, ctypes.c_int, ctypes.c_double,
+                                        ctypes.c_double, ctypes.c_int, ctypes.c_int,
+                                        ctypes.c_int, _c_float_p]
+    R.feref_umap_csr_optimize.argtypes = [_c_int_p, _c_int_p, _c_float_p, _c_float_p,
+                                          ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                          ctypes.c_double, ctypes.c_int, ctypes.c_double,
+                                          ctypes.c_double, ctypes.c_int, ctypes.c_int,
+                                          _c_float_p]
+    R.feref_umap_powf.restype = ctypes.c_float
+    R.feref_umap_powf.argtypes = [ctypes.c_float, ctypes.c_float]
+    R.feref_umap_positive_samples.argtypes = [ctypes.c_float, ctypes.c_int]
+    R.feref_umap_negative_samples.argtypes = [ctypes.c_float, ctypes.c_int, ctypes.c_int]
+    R.feref_umap_negative_vertex.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                             ctypes.c_int, ctypes.c_longlong, ctypes.c_int]
+    R.feref_find_ab.argtypes = [ctypes.c_double, ctypes.c_double, _c_double_p, _c_double_p]
+    return R
 
 
 def _cm(a: np.ndarray, dtype) -> np.ndarray:
@@ -422,9 +436,9 @@ def umap_replay_serial(heads, tails, epochs_per_sample, layout, epoch_begin, epo
 # ------------------------------------------------------------ the reference
 
 
-def _ref_check(rc: int, which: str = "tsne") -> None:
+def _ref_check(rc: int, which: str = "tsne", variant: str = "O2") -> None:
     if rc != 0:
-        R = ref()
+        R = ref(variant)
         msg = (R.feref_tsne_last_error() if which == "tsne" else R.feref_umap_last_error())
         raise RuntimeError(f"reference {which} call failed: {msg.decode()}")
 
@@ -479,15 +493,15 @@ def ref_tsne_update(y, update, gains, grad, learning_rate, momentum, min_gain=0.
 
 
 def ref_tsne_iterate(P: Csr, y, update, gains, iters, exaggeration, momentum, learning_rate,
-                     min_gain=0.01, max_step_norm=5.0, threads=1, grid_override=0):
+                     min_gain=0.01, max_step_norm=5.0, threads=1, grid_override=0, variant="O2"):
     """The reference's own iteration loop; returns (y, update, gains, loop_seconds)."""
     y, update, gains = (_f32(a).copy() for a in (y, update, gains))
     secs = ctypes.c_double(0.0)
-    _ref_check(ref().feref_tsne_iterate(
+    _ref_check(ref(variant).feref_tsne_iterate(
         _ptr(P.row_ptr, ctypes.c_int), _ptr(P.col, ctypes.c_int), _ptr(P.val, ctypes.c_float), P.n,
         _ptr(y, ctypes.c_float), _ptr(update, ctypes.c_float), _ptr(gains, ctypes.c_float), iters,
         exaggeration, momentum, learning_rate, min_gain, max_step_norm, threads, grid_override,
-        ctypes.byref(secs)))
+        ctypes.byref(secs)), "tsne", variant)
     return y, update, gains, secs.value
 
 
@@ -551,14 +565,14 @@ def ref_umap_graph(idx, dist, threads=1) -> UmapGraph:
 
 def ref_umap_coo_replay(heads, tails, weights, epochs_per_sample, init, n_epochs, min_dist=0.1,
                         negative_sample_rate=5, learning_rate=1.0, repulsion_strength=1.0,
-                        threads=1, seed=42, sanitize_each_epoch=True) -> np.ndarray:
+                        threads=1, seed=42, sanitize_each_epoch=True, variant="O2") -> np.ndarray:
     heads, tails, w, eps, init = _i32(heads), _i32(tails), _f32(weights), _f32(epochs_per_sample), _f32(init)
     out = np.zeros_like(init)
-    _ref_check(ref().feref_umap_coo_replay(
+    _ref_check(ref(variant).feref_umap_coo_replay(
         _ptr(heads, ctypes.c_int), _ptr(tails, ctypes.c_int), _ptr(w, ctypes.c_float),
         _ptr(eps, ctypes.c_float), _ptr(init, ctypes.c_float), init.shape[0], heads.size,
         n_epochs, min_dist, negative_sample_rate, learning_rate, repulsion_strength, threads,
-        seed, int(sanitize_each_epoch), _ptr(out, ctypes.c_float)), "umap")
+        seed, int(sanitize_each_epoch), _ptr(out, ctypes.c_float)), "umap", variant)
     return out
 
 

@@ -14,6 +14,7 @@ import pytest
 
 import oracle as O
 from fastembedr_b200 import _lib, api
+from fastembedr_b200.api import _ptr
 
 REFERENCE_WRAPPER_SYMBOLS = [
     # every prototype of the extern "C" block in src/embedding_cuda_impl.cpp:24-380
@@ -214,3 +215,62 @@ def test_synthetic_configs_shapes():
     d = np.linalg.norm(x[:, None, :].astype(np.float64) - x[None, :, :], axis=-1)
     np.fill_diagonal(d, np.inf)
     np.testing.assert_allclose(np.sort(d, axis=1)[:, :10], dist, rtol=1e-5)
+
+
+def test_extension_entry_points_validate_before_device_work():
+    """The library's own entry points (sessions, epoch ranges, no-allocation
+    epochs, NCCL id and communicator) reject bad arguments with status 1 and a
+    message before any CUDA or NCCL call."""
+    L = _lib.load()
+    h = ctypes.c_void_p()
+    idx = np.zeros((10, 3), np.int32)
+    dist = np.ones((10, 3), np.float32)
+    ip, dp = ctypes.c_void_p(idx.ctypes.data), ctypes.c_void_p(dist.ctypes.data)
+
+    def rejects(rc, msg):
+        assert rc == 1
+        assert msg in _lib.last_error(), _lib.last_error()
+
+    # t-SNE sessions
+    rejects(L.fe_b200_tsne_create(None, dp, 10, 3, 0, 5.0, None, 1, 0, 0, ctypes.byref(h)),
+            "null CUDA openTSNE input pointer")
+    for n, k, perp in ((1, 3, 5.0), (10, 0, 5.0), (10, 300, 5.0), (10, 3, 0.0)):
+        rejects(L.fe_b200_tsne_create(ip, dp, n, k, 0, perp, None, 1, 0, 0, ctypes.byref(h)),
+                "invalid CUDA openTSNE FFT-grid dimensions or parameters")
+    rp = np.array([0, 1, 2], np.int32)
+    col = np.array([1, 0], np.int32)
+    val = np.full(2, 0.5, np.float32)
+    y = np.zeros((2, 2), np.float32)
+    rejects(L.fe_b200_tsne_create_csr(_ptr(rp, ctypes.c_int), _ptr(col, ctypes.c_int), _ptr(val, ctypes.c_float), 1,
+                                      _ptr(y, ctypes.c_float), 0, ctypes.byref(h)), "invalid CSR session arguments")
+    rejects(L.fe_b200_tsne_iterate(None, 1, 1.0, 0.8, 1.0, 0.01, 5.0), "invalid t-SNE session call")
+    # UMAP sessions and epoch ranges
+    rejects(L.fe_b200_umap_create(None, dp, 10, 3, 0, 0, 0, 30, 1, ctypes.byref(h)), "null pointer")
+    rejects(L.fe_b200_umap_create(ip, dp, 1, 3, 0, 0, 0, 30, 1, ctypes.byref(h)),
+            "invalid UMAP session dimensions or parameters")
+    heads = np.array([0, 1], np.int32)
+    tails = np.array([1, 0], np.int32)
+    eps = np.ones(2, np.float32)
+    lay = np.zeros((2, 2), np.float32)
+    args = [_ptr(heads, ctypes.c_int), _ptr(tails, ctypes.c_int), _ptr(eps, ctypes.c_float), 2,
+            _ptr(lay, ctypes.c_float), 2]
+    tail = [5, 1.0, 1.5769434601962196, 0.8950608781227859, 1.0, 42, 0, 0, None]
+    for b, e in ((-1, 2), (3, 2), (0, 11)):
+        rejects(L.fe_b200_umap_epochs(*args, b, e, 10, *tail), "invalid epoch range")
+    # no-allocation epochs: the vertex cap and the range
+    na = [ctypes.c_void_p(1), ctypes.c_void_p(1), ctypes.c_void_p(1), 2, ctypes.c_void_p(1)]
+    rejects(L.fe_b200_umap_epochs_noalloc(*na, 2_000_000, 0, 1, 10, 5, 1.0, 1.5, 0.9, 1.0, 42, 1, None),
+            "exceeds the fixed scratch capacity")
+    rejects(L.fe_b200_umap_epochs_noalloc(*na, 2, 5, 1, 10, 5, 1.0, 1.5, 0.9, 1.0, 42, 1, None),
+            "invalid epoch range")
+    rejects(L.fe_b200_umap_epochs_noalloc(None, *na[1:], 2, 0, 1, 10, 5, 1.0, 1.5, 0.9, 1.0, 42, 1, None),
+            "null device pointer")
+    # NCCL id and communicator
+    small = (ctypes.c_ubyte * 16)()
+    rejects(L.fe_b200_nccl_unique_id(small, 16), "at least 128 bytes")
+    uid = (ctypes.c_ubyte * 128)()
+    rejects(L.fe_b200_comm_create(uid, 16, 2, 0, ctypes.byref(h)), "invalid communicator call")
+    for nranks, rank in ((0, 0), (2, 2), (2, -1)):
+        rejects(L.fe_b200_comm_create(uid, 128, nranks, rank, ctypes.byref(h)), "need nranks >= 1")
+    rejects(L.fe_b200_tsne_shard_comm(None, None), "invalid t-SNE shard call")
+    L.fe_b200_comm_destroy(None)  # a null communicator is ignored

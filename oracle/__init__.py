@@ -76,7 +76,20 @@ def lib() -> ctypes.CDLL:
     return _lib
 
 
+def host_supports_x86_64_v3() -> bool:
+    """Whether this host's CPU runs x86-64-v3 code (AVX2, BMI1/2, F16C, FMA,
+    LZCNT, MOVBE), so that the -O3 build cannot stop on an illegal instruction."""
+    try:
+        with open("/proc/cpuinfo") as f:
+            flags = next((line.split(":", 1)[1].split() for line in f if line.startswith("flags")), [])
+    except OSError:
+        return False
+    return {"avx2", "bmi1", "bmi2", "f16c", "fma", "abm", "movbe"} <= set(flags)
+
+
 def ref_available(variant: str = "O2") -> bool:
+    if variant == "O3" and not host_supports_x86_64_v3():
+        return False
     return os.path.exists(REF_VARIANTS[variant])
 
 

@@ -86,6 +86,43 @@ int opentsne_impl(const int* indices, const void* distances, bool dist_double, c
     set_error("invalid CUDA openTSNE FFT-grid dimensions or parameters");
     return 1;
   }
+  // Learning rate per phase: n / exaggeration when automatic (src/tsne_neighbors.cpp:1734-1737).
+  const float lr_early = learning_rate_auto
+      ? static_cast<float>(static_cast<double>(n) / std::max(static_cast<double>(early_exaggeration), DBL_MIN))
+      : learning_rate;
+  const float lr_normal = learning_rate_auto
+      ? static_cast<float>(static_cast<double>(n) / std::max(static_cast<double>(exaggeration), DBL_MIN))
+      : learning_rate;
+  const float clip = std::isfinite(max_step_norm) ? max_step_norm : NAN;
+  std::vector<int> devices;
+  FE_TRY(fe::multi_device_list(&devices));
+  if (devices.size() >= 2) {
+    fe::MultiDeviceTsne job;
+    job.devices = devices;
+    job.indices = indices;
+    job.distances = distances;
+    job.dist_double = dist_double;
+    job.on_device = on_device;
+    job.init = has_init ? init : nullptr;
+    job.seed = seed;
+    job.n = n;
+    job.k = k;
+    job.index_offset = index_offset;
+    job.perplexity = perplexity;
+    job.grid = resolve_grid(n, 0);
+    job.early_iter = early_exaggeration_iter;
+    job.early_exaggeration = early_exaggeration;
+    job.initial_momentum = initial_momentum;
+    job.lr_early = lr_early;
+    job.n_iter = n_iter;
+    job.exaggeration = exaggeration;
+    job.final_momentum = final_momentum;
+    job.lr_normal = lr_normal;
+    job.min_gain = min_gain;
+    job.max_step_norm = clip;
+    job.out = out;
+    return fe::opentsne_multi_device(job);
+  }
   cudaStream_t stream = nullptr;
   FE_CUDA(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking), "cudaStreamCreate(openTSNE)");
   struct StreamGuard {
@@ -131,14 +168,6 @@ int opentsne_impl(const int* indices, const void* distances, bool dist_double, c
   } else {
     FE_TRY(fe::session_random_layout(s, seed));
   }
-  // Learning rate per phase: n / exaggeration when automatic (src/tsne_neighbors.cpp:1734-1737).
-  const float lr_early = learning_rate_auto
-      ? static_cast<float>(static_cast<double>(n) / std::max(static_cast<double>(early_exaggeration), DBL_MIN))
-      : learning_rate;
-  const float lr_normal = learning_rate_auto
-      ? static_cast<float>(static_cast<double>(n) / std::max(static_cast<double>(exaggeration), DBL_MIN))
-      : learning_rate;
-  const float clip = std::isfinite(max_step_norm) ? max_step_norm : NAN;
   FE_TRY(fe::session_iterate(s, early_exaggeration_iter, early_exaggeration, initial_momentum, lr_early,
                              min_gain, clip));
   FE_TRY(fe::session_iterate(s, n_iter, exaggeration, final_momentum, lr_normal, min_gain, clip));

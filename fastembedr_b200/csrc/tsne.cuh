@@ -312,6 +312,42 @@ int shard_gather_rows(TsneSession* s, float2* rows);
 int shard_sum_charges(TsneSession* s);
 void shard_release(TsneSession* s);
 
+// ---- one process, several GPUs (multi_device.cu) ----
+// One openTSNE run from KNN as one sharded session per device, one host
+// thread each, in this process; what the one-shot entry points run when
+// FASTEMBEDR_B200_DEVICES lists two or more devices.
+struct MultiDeviceTsne {
+  std::vector<int> devices;
+  const int* indices = nullptr;    // column-major n x k, host or (on_device) the caller's device
+  const void* distances = nullptr;
+  bool dist_double = false;
+  bool on_device = false;
+  int caller_device = 0;
+  const float* init = nullptr;     // host, or null for the hashed random start
+  unsigned int seed = 0;
+  int n = 0;
+  int k = 0;
+  int index_offset = 0;
+  float perplexity = 0.0f;
+  int grid = 0;
+  int early_iter = 0;
+  float early_exaggeration = 0.0f;
+  float initial_momentum = 0.0f;
+  float lr_early = 0.0f;
+  int n_iter = 0;
+  float exaggeration = 0.0f;
+  float final_momentum = 0.0f;
+  float lr_normal = 0.0f;
+  float min_gain = 0.0f;
+  float max_step_norm = 0.0f;
+  float* out = nullptr;            // host, row-major n x 2
+  const void* unique_id = nullptr;  // set by opentsne_multi_device
+};
+// The devices FASTEMBEDR_B200_DEVICES lists ("0,1,..."; empty when unset);
+// status 1 for a malformed list, an ordinal out of range or a repeat.
+int multi_device_list(std::vector<int>* devices);
+int opentsne_multi_device(MultiDeviceTsne job);
+
 // ---- ordering and the internal copy of P (tsne_reorder.cu) ----
 // Chooses the internal point order -- Morton order of the current layout when
 // by_layout, else the caller's order -- permutes the point arrays, and

@@ -274,3 +274,25 @@ def test_extension_entry_points_validate_before_device_work():
         rejects(L.fe_b200_comm_create(uid, 128, nranks, rank, ctypes.byref(h)), "need nranks >= 1")
     rejects(L.fe_b200_tsne_shard_comm(None, None), "invalid t-SNE shard call")
     L.fe_b200_comm_destroy(None)  # a null communicator is ignored
+
+
+def test_multi_device_list_is_checked_before_device_work(monkeypatch):
+    """FASTEMBEDR_B200_DEVICES (one process, several GPUs behind the one-shot
+    entry points): a malformed or repeated list is rejected with status 1
+    before any device call; a list of two or more devices needs the devices
+    (on this GPU-less host the device query itself fails cleanly)."""
+    L = _lib.load()
+    out = np.zeros((10, 2), np.float32)
+    fout = out.ctypes.data_as(ctypes.POINTER(ctypes.c_float))
+    idx = np.zeros(30, np.int32)
+    dist = np.ones(30, np.float32)
+    args = [ctypes.c_void_p(idx.ctypes.data), ctypes.c_void_p(dist.ctypes.data), None, 0, 10, 3, 2, 1.0,
+            10, 10, 12.0, 1.0, 0.0, 1, 0.8, 0.8, 0.01, 5.0, 1, 0, fout]
+    for value, msg in (("x", "is not a device ordinal"), ("0,", "is not a device ordinal"),
+                       ("1,1", "lists device 1 twice"), ("0,1", "cudaGetDeviceCount(FASTEMBEDR_B200_DEVICES)")):
+        monkeypatch.setenv("FASTEMBEDR_B200_DEVICES", value)
+        assert L.fastembedr_cuda_opentsne_fft_from_knn_float(*args) == 1
+        assert msg in _lib.last_error(), (value, _lib.last_error())
+    monkeypatch.setenv("FASTEMBEDR_B200_DEVICES", "0")  # one device: the ordinary path
+    assert L.fastembedr_cuda_opentsne_fft_from_knn_float(*args) == 1
+    assert "FASTEMBEDR_B200_DEVICES" not in _lib.last_error()

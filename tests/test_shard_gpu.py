@@ -159,6 +159,32 @@ def test_two_ranks_bit_identical_to_one_rank(problem, tmp_path):
             assert np.array_equal(got[key], one[key]), key
 
 
+@pytest.mark.skipif(_gpu_count() < 2 or os.environ.get("FASTEMBEDR_B200_MULTI_DEVICE_TESTS") != "1",
+                    reason="needs two GPUs; the single-process multi-device mode is enabled for testing with "
+                           "FASTEMBEDR_B200_MULTI_DEVICE_TESTS=1")
+def test_single_process_two_devices_match_one_rank(problem, tmp_path):
+    """FASTEMBEDR_B200_DEVICES=0,1: the unchanged one-shot entry point runs one
+    sharded session per device in this process; the layout must be the bits
+    of a one-rank sharded session (the decomposition does not change them)."""
+    p = np.load(problem)
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0", FASTEMBEDR_B200_DEVICES="0,1")
+    script = (
+        "import sys, numpy as np\n"
+        f"sys.path.insert(0, {os.path.dirname(os.path.dirname(os.path.abspath(__file__)))!r})\n"
+        "from fastembedr_b200 import api\n"
+        f"p = np.load({problem!r})\n"
+        f"res = api.opentsne_knn(p['idx'], p['dist'], perplexity={PERPLEXITY}, init=p['init'],\n"
+        f"                       early_exaggeration_iter={EARLY}, n_iter={LATE})\n"
+        f"np.save({str(tmp_path / 'multi.npy')!r}, res.Y)\n")
+    r = subprocess.run([sys.executable, "-c", script], env=env, capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stderr[-2000:]
+    got = np.load(tmp_path / "multi.npy")
+    with api.TsneSession.from_knn(p["idx"], p["dist"], perplexity=PERPLEXITY, init=p["init"]) as s:
+        s.shard(api.nccl_unique_id(), 1, 0)
+        want = s.run(EARLY, LATE)
+    assert np.array_equal(got, want)
+
+
 def _rank_main(problem, uid_hex, nranks, rank, out):
     import torch
 

@@ -10,7 +10,9 @@
 // GPU (tsne_shard.cu).  Failure handling never leaves a rank waiting on a peer:
 //   * every rank builds its inputs, P and session first; a host barrier checks
 //     them all before any rank joins the communicator;
-//   * a second barrier checks that every rank joined; ranks whose peers failed
+//   * the join is bounded (the environment's limit, else kJoinLimitSeconds), so
+//     a rank whose peer failed inside the join gives up instead of waiting;
+//     a second barrier checks that every rank joined; ranks whose peers failed
 //     to join abort their communicator instead of destroying it;
 //   * during the run the calling thread watches a failure flag and aborts
 //     every communicator if a rank fails, which ends the others' collectives;
@@ -81,9 +83,14 @@ struct Shared {
   }
 };
 
+// Join limit of this mode when the environment sets none: a rank whose join
+// fails must not leave the others inside a blocking ncclCommInitRank.
+constexpr double kJoinLimitSeconds = 600.0;
+
 void rank_main(const MultiDeviceTsne& job, int rank, Shared* sh) {
   const int nranks = static_cast<int>(job.devices.size());
   const int dev = job.devices[rank];
+  const JoinLimit join_limit(kJoinLimitSeconds);
   auto fail = [&](const std::string& why) {
     sh->ok[rank] = 0;
     sh->msg[rank] = "device " + std::to_string(dev) + ": " + why;

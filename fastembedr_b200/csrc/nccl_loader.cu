@@ -62,12 +62,19 @@ const NcclApi* nccl_api() {
   return &g_api;
 }
 
+namespace {
+thread_local double t_join_limit = 0.0;
+}  // namespace
+
 double join_timeout_seconds() {
   const char* v = std::getenv("FASTEMBEDR_B200_NCCL_INIT_TIMEOUT_S");
-  if (v == nullptr || *v == '\0') return 0.0;
+  if (v == nullptr || *v == '\0') return t_join_limit;
   const double s = std::strtod(v, nullptr);
   return s > 0.0 ? s : 0.0;
 }
+
+JoinLimit::JoinLimit(double seconds) : prev_(t_join_limit) { t_join_limit = seconds; }
+JoinLimit::~JoinLimit() { t_join_limit = prev_; }
 
 namespace {
 

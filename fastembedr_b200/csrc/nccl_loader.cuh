@@ -39,8 +39,22 @@ int check_nccl(ncclResult_t code, const char* where);
 int check_nccl_call(ncclComm_t comm, ncclResult_t code, const char* where);
 
 // Seconds a rank waits for the others to join a communicator:
-// FASTEMBEDR_B200_NCCL_INIT_TIMEOUT_S, or 0 (unset) for as long as they take.
+// FASTEMBEDR_B200_NCCL_INIT_TIMEOUT_S, else the calling thread's JoinLimit,
+// else 0 (as long as they take).
 double join_timeout_seconds();
+
+// A join limit for the calling thread while in scope (used where a library
+// component joins several ranks itself and must never wait for good).
+class JoinLimit {
+ public:
+  explicit JoinLimit(double seconds);
+  ~JoinLimit();
+  JoinLimit(const JoinLimit&) = delete;
+  JoinLimit& operator=(const JoinLimit&) = delete;
+
+ private:
+  double prev_;
+};
 
 // Joins the communicator `unique_id` (ncclUniqueId bytes) as rank `rank` of
 // `nranks`, on the current device, and returns once every rank has joined.

@@ -161,8 +161,11 @@ void rank_main(const MultiDeviceTsne& job, int rank, Shared* sh) {
   sh->barrier.wait();
   const bool run = sh->all_ok();
   if (run) {
-    rc = session_iterate(s, job.early_iter, job.early_exaggeration, job.initial_momentum, job.lr_early,
-                         job.min_gain, job.max_step_norm);
+    rc = shard_warm_up(s);
+    if (rc == 0) {
+      rc = session_iterate(s, job.early_iter, job.early_exaggeration, job.initial_momentum, job.lr_early,
+                           job.min_gain, job.max_step_norm);
+    }
     if (rc == 0) {
       rc = session_iterate(s, job.n_iter, job.exaggeration, job.final_momentum, job.lr_normal, job.min_gain,
                            job.max_step_norm);

@@ -310,6 +310,9 @@ int session_shard(TsneSession* s, const void* unique_id, void* comm, int nranks,
 int shard_gather_rows(TsneSession* s, float2* rows);
 // Sum of the charge grids of all ranks, in place.
 int shard_sum_charges(TsneSession* s);
+// One uncaptured round of both collectives on buffers they leave unchanged
+// (fresh sessions only: zero charges and zero steps).
+int shard_warm_up(TsneSession* s);
 void shard_release(TsneSession* s);
 
 // ---- one process, several GPUs (multi_device.cu) ----

@@ -77,6 +77,17 @@ int shard_sum_charges(TsneSession* s) {
                          "ncclAllReduce(charges)");
 }
 
+int shard_warm_up(TsneSession* s) {
+  // Both collectives of an iteration, outside any graph capture, on buffers
+  // they leave unchanged: the charge grid is all zeros between iterations and
+  // the step buffer of a fresh session is zero on every rank.  NCCL sets up
+  // its connections here rather than inside the first captured iteration.
+  FE_TRY(shard_sum_charges(s));
+  FE_TRY(shard_gather_rows(s, s->update));
+  FE_CUDA(cudaStreamSynchronize(s->stream), "cudaStreamSynchronize(shard warm-up)");
+  return 0;
+}
+
 void shard_release(TsneSession* s) {
   if (s->comm == nullptr) return;
   const NcclApi* api = nccl_api();

@@ -64,6 +64,17 @@ def l2_note(stream_bytes: int, what: str) -> str:
     return f"inputs fit in L2 ({what} is {stream_bytes / 1e9:.3f} GB): an in-L2 figure, not an HBM one"
 
 
+def median_call_seconds(call, reps: int = 3) -> float:
+    """Median wall time of `reps` calls of a synchronous call, after one warm call."""
+    call()
+    times = []
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        call()
+        times.append(time.perf_counter() - t0)
+    return float(np.median(times))
+
+
 def log(*a):
     print(*a, file=sys.stderr, flush=True)
 
@@ -304,7 +315,7 @@ def bench_reference_cuda(args):
     torch.cuda.set_device(local)
     w = WORKLOADS[args.workload]
     umap = w.get("kind") == "umap"
-    reps = 2
+    reps = 3
     if umap:
         from fastembedr_b200 import api
 
@@ -339,16 +350,12 @@ def bench_reference_cuda(args):
         entry = "fastembedr_cuda_opentsne_fft_from_knn_float (750 iterations, host KNN)"
         cfg = {"workload": args.workload, "n": int(n), "k": int(k), "perplexity": w["perplexity"],
                "grid": "reference CUDA policy"}
-    call()  # warm: module load, cuFFT plans
-    torch.cuda.synchronize()
-    t0 = time.perf_counter()
-    for _ in range(reps):
-        call()
-    secs = (time.perf_counter() - t0) / reps
+    secs = median_call_seconds(call, reps)  # the warm call loads modules and makes cuFFT plans
     value = units / secs
     line = {
         "impl": "reference", "backend": "cuda (the reference's src/embedding_cuda_kernels.cpp, sm_100a)",
         "metric": metric, "value": value, "unit": unit, "n_gpus": 1, "steps": reps, "warmup": 1,
+        "timing": f"median of {reps} calls after a warm one",
         "ms_per_step": None, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
         "dtype": "f32", "data": "synthetic", "config": cfg, "seconds_per_call": secs, "call": entry,
         "e2e": {"value": value, "unit": unit, "h2d_bytes_per_step": int(idx.size * 8),
@@ -494,15 +501,11 @@ def bench_ours(args):
                 ctypes.cast(out_h.data_ptr(), ctypes.POINTER(ctypes.c_float)))
             _lib.check(rc, "fastembedr_cuda_opentsne_fft_from_knn_float")
 
-        call()  # warm (first-call module load)
-        reps = 2
-        t0 = time.perf_counter()
-        for _ in range(reps):
-            call()
-        e2e_s = (time.perf_counter() - t0) / reps
+        e2e_s = median_call_seconds(call)  # the warm call loads the module
         e2e = {"value": (EE_ITER + N_ITER) / e2e_s, "unit": "iterations/s",
                "h2d_bytes_per_step": int(idx_cm.numel() * 4 + dist_cm.numel() * 4 + init_h.numel() * 4),
                "d2h_bytes_per_step": int(out_h.numel() * 4), "seconds_per_call": e2e_s,
+               "timing": "median of 3 calls after a warm one",
                "call": "fastembedr_cuda_opentsne_fft_from_knn_float (750 iterations, host KNN)"}
     elif not args.skip_e2e:
         # Every rank: pinned host KNN -> device, P build, shard, 750 iterations,
@@ -763,14 +766,12 @@ def bench_umap(args):
                 ctypes.cast(out_h.data_ptr(), ctypes.POINTER(ctypes.c_float)))
             _lib.check(rc, "fastembedr_cuda_umap_from_knn_spectral_float")
 
-        call()
-        t0 = time.perf_counter()
-        call()
-        e2e_s = time.perf_counter() - t0
+        e2e_s = median_call_seconds(call)
         total_pos, _ = sess.count_samples(0, n_epochs, UMAP_NSR)
         e2e = {"value": total_pos / e2e_s, "unit": "edge_updates/s",
                "h2d_bytes_per_step": int(idx_cm.numel() * 4 + dist_cm.numel() * 4),
                "d2h_bytes_per_step": int(out_h.numel() * 4), "seconds_per_call": e2e_s,
+               "timing": "median of 3 calls after a warm one",
                "call": f"fastembedr_cuda_umap_from_knn_spectral_float ({n_epochs} epochs, host KNN: graph, "
                        f"diffusion start, epochs)"}
     cpu = None if (args.skip_cpu or world > 1) else cpu_baseline_umap(graph, init)

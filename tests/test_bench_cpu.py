@@ -29,3 +29,21 @@ def test_reference_arm_prints_one_contract_line():
     assert cb["kind"] in ("reference", "port") and cb["cores"] >= 1 and "iterations" in cb["sample"]
     assert d["e2e"] == {"value": d["value"], "unit": d["unit"], "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
     assert 1 <= d["steps"] <= 750
+
+
+def test_median_call_seconds_warms_once_then_takes_the_median():
+    sys.path.insert(0, ROOT)
+    import time
+
+    import bench
+
+    calls = []
+    durations = iter([0.0, 0.03, 0.01, 0.02])  # the first (warm) call is not timed
+
+    def call():
+        calls.append(1)
+        time.sleep(next(durations))
+
+    secs = bench.median_call_seconds(call)
+    assert len(calls) == 4
+    assert 0.015 < secs < 0.05

@@ -26,7 +26,7 @@ NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 
 SOURCES = ["common.cu", "nccl_loader.cu", "tsne_affinity.cu", "tsne_kernels.cu", "tsne_session.cu",
            "tsne_reorder.cu", "tsne_shard.cu", "multi_device.cu", "umap.cu", "umap_graph.cu", "umap_noalloc.cu", "umap_session.cu", "capi.cu"]
-HEADERS = ["fe_common.cuh", "nccl_loader.cuh", "tsne.cuh", "umap.cuh"]
+HEADERS = ["fe_common.cuh", "nccl_loader.cuh", "rank_group.h", "tsne.cuh", "umap.cuh"]
 
 NVCC_FLAGS = [
     "-std=c++17", "-O3", "-lineinfo", "--fmad=false",

@@ -92,6 +92,15 @@ int env_int_nonneg(const char* name, int fallback) {
   return static_cast<int>(v);
 }
 
+double env_double(const char* name, double fallback) {
+  const char* raw = std::getenv(name);
+  if (raw == nullptr || raw[0] == '\0') return fallback;
+  char* end = nullptr;
+  const double v = std::strtod(raw, &end);
+  if (end == raw || !(v > 0.0) || v > 1e9) return fallback;
+  return v;
+}
+
 bool env_flag(const char* name, bool fallback) {
   const char* raw = std::getenv(name);
   if (raw == nullptr || raw[0] == '\0') return fallback;

@@ -97,6 +97,7 @@ int sm_count();
 int env_int(const char* name, int fallback);         // positive values only
 int env_int_nonneg(const char* name, int fallback);  // zero allowed
 bool env_flag(const char* name, bool fallback);
+double env_double(const char* name, double fallback);  // positive values only
 
 }  // namespace fe
 

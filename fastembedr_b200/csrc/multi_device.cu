@@ -14,10 +14,22 @@
 //     a rank whose peer failed inside the join gives up instead of waiting;
 //     a second barrier checks that every rank joined; ranks whose peers failed
 //     to join abort their communicator instead of destroying it;
-//   * during the run the calling thread watches a failure flag and aborts
-//     every communicator if a rank fails, which ends the others' collectives;
-//   * communicators are destroyed only after every rank has finished.
+//   * during the run every collective goes through a RankGroup (rank_group.h):
+//     the ranks agree on the host before each one, so a rank that fails on the
+//     host stops its peers before they enqueue a collective it will not join;
+//     each rank has at most one collective in flight, and a collective that
+//     does not complete within the stall limit fails the group;
+//   * only a rank whose own enqueue failed after its peers had enqueued theirs,
+//     or a stalled collective, makes the calling thread abort the communicators
+//     (each under its rank's lock, so no NCCL call follows an abort); that
+//     ends the one collective each rank may have in flight;
+//   * communicators are released only after every rank has finished.
+// FASTEMBEDR_B200_INJECT_HOST_FAILURE="<rank>:<collective>" makes that rank
+// fail on the host just before its collective number <collective> (counted
+// from 0, warm-up included), with none of its collectives in flight: the
+// failure path is exercised without faulting or stalling a GPU.
 #include "nccl_loader.cuh"
+#include "rank_group.h"
 #include "tsne.cuh"
 
 #include <atomic>
@@ -64,16 +76,12 @@ struct RankBuf {
 };
 
 struct Shared {
-  explicit Shared(int n) : barrier(n), ok(n, 0), msg(n), comm(n) {
-    for (auto& c : comm) c = nullptr;
-  }
-  HostBarrier barrier;
+  explicit Shared(int n) : barrier(n), group(n), ok(n, 0) {}
+  HostBarrier barrier;  // set-up and tear-down points, which every rank reaches
+  RankGroup group;      // collectives of the run, and the communicators
   std::vector<int> ok;
-  std::vector<std::string> msg;
-  // A joined rank's communicator until whoever aborts or destroys it takes it
-  // (exchange with nullptr), so that it is released exactly once.
-  std::vector<std::atomic<void*>> comm;
-  std::atomic<bool> failed{false};
+  std::mutex msg_lock;
+  std::string first_msg;  // the first failure reported (its cause, not its echoes)
   std::atomic<int> finished{0};
   bool all_ok() const {
     for (int v : ok) {
@@ -86,6 +94,20 @@ struct Shared {
 // Join limit of this mode when the environment sets none: a rank whose join
 // fails must not leave the others inside a blocking ncclCommInitRank.
 constexpr double kJoinLimitSeconds = 600.0;
+// A collective of this mode that has not completed after this long is treated
+// as a failed peer (FASTEMBEDR_B200_COLLECTIVE_TIMEOUT_S overrides).
+constexpr double kStallLimitSeconds = 300.0;
+
+// FASTEMBEDR_B200_INJECT_HOST_FAILURE="<rank>:<collective>" for `rank`, else -1.
+long long injected_failure(int rank) {
+  const char* v = std::getenv("FASTEMBEDR_B200_INJECT_HOST_FAILURE");
+  if (v == nullptr || *v == '\0') return -1;
+  char* end = nullptr;
+  const long r = std::strtol(v, &end, 10);
+  if (end == nullptr || *end != ':' || r != rank) return -1;
+  const long long at = std::strtoll(end + 1, nullptr, 10);
+  return at >= 0 ? at : -1;
+}
 
 void rank_main(const MultiDeviceTsne& job, int rank, Shared* sh) {
   const int nranks = static_cast<int>(job.devices.size());
@@ -93,8 +115,11 @@ void rank_main(const MultiDeviceTsne& job, int rank, Shared* sh) {
   const JoinLimit join_limit(kJoinLimitSeconds);
   auto fail = [&](const std::string& why) {
     sh->ok[rank] = 0;
-    sh->msg[rank] = "device " + std::to_string(dev) + ": " + why;
-    sh->failed = true;
+    {
+      std::lock_guard<std::mutex> l(sh->msg_lock);
+      if (sh->first_msg.empty()) sh->first_msg = "device " + std::to_string(dev) + ": " + why;
+    }
+    sh->group.fail();
   };
   TsneSession* s = nullptr;
   cudaStream_t stream = nullptr;
@@ -142,6 +167,10 @@ void rank_main(const MultiDeviceTsne& job, int rank, Shared* sh) {
   if (rc == 0) {
     rc = job.init != nullptr ? session_set_layout(s, job.init, true, true) : session_random_layout(s, job.seed);
   }
+  if (rc == 0) {
+    rc = check_cuda(cudaEventCreateWithFlags(&s->collective_done, cudaEventDisableTiming),
+                    "cudaEventCreate(collective)");
+  }
   if (rc == 0) rc = check_cuda(cudaStreamSynchronize(stream), "cudaStreamSynchronize(set-up)");
   if (rc == 0) sh->ok[rank] = 1;
   else fail(last_error());
@@ -153,7 +182,7 @@ void rank_main(const MultiDeviceTsne& job, int rank, Shared* sh) {
     rc = session_shard(s, job.unique_id, nullptr, nranks, rank);
     if (rc == 0) {
       joined = true;
-      sh->comm[rank] = s->comm;
+      sh->group.set_comm(rank, s->comm);
     } else {
       fail(last_error());
     }
@@ -161,6 +190,9 @@ void rank_main(const MultiDeviceTsne& job, int rank, Shared* sh) {
   sh->barrier.wait();
   const bool run = sh->all_ok();
   if (run) {
+    s->group = &sh->group;
+    s->stall_limit_s = env_double("FASTEMBEDR_B200_COLLECTIVE_TIMEOUT_S", kStallLimitSeconds);
+    s->inject_failure_at = injected_failure(rank);
     rc = shard_warm_up(s);
     if (rc == 0) {
       rc = session_iterate(s, job.early_iter, job.early_exaggeration, job.initial_momentum, job.lr_early,
@@ -170,27 +202,37 @@ void rank_main(const MultiDeviceTsne& job, int rank, Shared* sh) {
       rc = session_iterate(s, job.n_iter, job.exaggeration, job.final_momentum, job.lr_normal, job.min_gain,
                            job.max_step_norm);
     }
+    // The newest collective completes (bounded) before any blocking wait on
+    // the stream, so no rank blocks on a collective a failed peer left alone.
+    if (rc == 0) rc = shard_quiesce(s);
     if (rc == 0) {
       rc = rank == 0 ? session_get_layout(s, job.out, true)
                      : check_cuda(cudaStreamSynchronize(stream), "cudaStreamSynchronize(run)");
     }
     if (rc != 0) fail(last_error());
+    if (shard_quiesce(s) != 0 && rc == 0) fail(last_error());
   }
   ++sh->finished;
   // No communicator is destroyed while a peer may still use it.
   sh->barrier.wait();
   if (s != nullptr && joined) {
-    void* mine = sh->comm[rank].exchange(nullptr);
-    if (mine == nullptr || !run || sh->failed) {
+    void* mine = sh->group.take_comm(rank);
+    if (mine == nullptr || !run || sh->group.failed()) {
       // Aborted by the calling thread, or peers never ran or failed (a
       // destroy could wait on them): abort it here unless already done.
+      // Nothing of this rank is in flight on it any more (quiesced above).
       const NcclApi* api = nccl_api();
       if (mine != nullptr && api != nullptr) api->CommAbort(static_cast<ncclComm_t>(mine));
       s->comm = nullptr;
       s->own_comm = false;
     }
   }
-  if (s != nullptr) session_destroy(s);
+  if (s != nullptr) {
+    s->group = nullptr;
+    if (s->collective_done != nullptr) cudaEventDestroy(s->collective_done);
+    s->collective_done = nullptr;
+    session_destroy(s);
+  }
   if (stream != nullptr) {
     cudaStreamSynchronize(stream);
     cudaStreamDestroy(stream);
@@ -256,23 +298,19 @@ int opentsne_multi_device(MultiDeviceTsne job) {
   std::vector<std::thread> threads;
   threads.reserve(nranks);
   for (int r = 0; r < nranks; ++r) threads.emplace_back(rank_main, std::cref(job), r, &sh);
-  // A failed rank stops issuing collectives, which would leave its peers'
-  // collectives waiting on the device: abort every joined communicator then.
+  // A collective a rank enqueued without a peer (the peer's enqueue failed
+  // after both arrived), or one that stalled, waits on the device for good:
+  // abort every communicator then, which ends it.  Host-side failures need no
+  // abort: the group stops the other ranks before their next collective.
+  auto abort_comm = [&](void* c) { api->CommAbort(static_cast<ncclComm_t>(c)); };
   while (sh.finished.load() < nranks) {
-    if (sh.failed) {
-      for (auto& slot : sh.comm) {
-        void* c = slot.exchange(nullptr);
-        if (c != nullptr) api->CommAbort(static_cast<ncclComm_t>(c));
-      }
-    }
+    if (sh.group.abort_needed()) sh.group.abort_all(abort_comm);
     std::this_thread::sleep_for(std::chrono::milliseconds(1));
   }
   for (std::thread& t : threads) t.join();
-  for (int r = 0; r < nranks; ++r) {
-    if (!sh.ok[r] && !sh.msg[r].empty()) {
-      set_error("multi-device openTSNE: " + sh.msg[r]);
-      return 1;
-    }
+  if (!sh.first_msg.empty()) {
+    set_error("multi-device openTSNE: " + sh.first_msg);
+    return 1;
   }
   if (!sh.all_ok()) {
     set_error("multi-device openTSNE: a rank stopped because a peer failed");

@@ -27,6 +27,8 @@
 
 namespace fe {
 
+class RankGroup;
+
 // Layout statistics carried between kernels (device resident).
 // One grid node's charges {sum w, sum w x, sum w y} in fixed point (+ pad to 32 B).
 struct ChargeCell {
@@ -242,6 +244,17 @@ struct TsneSession {
   int row_end = 0;
   void* comm = nullptr;  // ncclComm_t
   bool own_comm = false;  // destroyed with the session (not when lent by the caller)
+  // Single-process multi-device mode (multi_device.cu): the host-side group of
+  // the ranks this process runs.  Collectives then go through the group (every
+  // rank agrees on the host before each one; see rank_group.h), at most one
+  // collective of this rank is in flight at a time, and iterations launch
+  // without graphs, so that an abort can only ever end the newest collective.
+  RankGroup* group = nullptr;
+  cudaEvent_t collective_done = nullptr;  // completion of the newest collective
+  bool collective_pending = false;
+  long long collectives_issued = 0;
+  double stall_limit_s = 0.0;  // a collective taking longer is treated as a failed peer
+  long long inject_failure_at = -1;  // FASTEMBEDR_B200_INJECT_HOST_FAILURE for this rank
 
   // Spatial ordering: internal point r is the caller's point perm[r], and
   // caller point i is internal point rank[i].
@@ -313,6 +326,10 @@ int shard_sum_charges(TsneSession* s);
 // One uncaptured round of both collectives on buffers they leave unchanged
 // (fresh sessions only: zero charges and zero steps).
 int shard_warm_up(TsneSession* s);
+// Grouped sessions: waits until this rank's newest collective has completed,
+// bounded by stall_limit_s (then the group is failed, which aborts every
+// communicator, and the wait resumes, bounded again).  No-op otherwise.
+int shard_quiesce(TsneSession* s);
 void shard_release(TsneSession* s);
 
 // ---- one process, several GPUs (multi_device.cu) ----

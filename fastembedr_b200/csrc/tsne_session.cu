@@ -335,7 +335,9 @@ cudaGraphExec_t chunk_graph(TsneSession* s, int iters, const float key[5]) {
 int iterate_block(TsneSession* s, int iters, float exaggeration, float momentum, float learning_rate,
                   float min_gain, float max_step_norm) {
   if (iters <= 0) return 0;
-  const bool graphs = s->use_graphs && !s->profile && iters > 1;
+  // Grouped (single-process multi-device) sessions launch without graphs: a
+  // graph would queue many collectives at once (see rank_group.h).
+  const bool graphs = s->use_graphs && !s->profile && iters > 1 && s->group == nullptr;
   if (!graphs) {
     for (int it = 0; it < iters; ++it) {
       FE_TRY(launch_iteration(s, kGradUpdate, exaggeration, momentum, learning_rate, min_gain,

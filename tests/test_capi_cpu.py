@@ -7,7 +7,9 @@
 * the host-side parameter policies match the reference.
 """
 import ctypes
+import os
 import re
+import subprocess
 
 import numpy as np
 import pytest
@@ -15,6 +17,8 @@ import pytest
 import oracle as O
 from fastembedr_b200 import _lib, api
 from fastembedr_b200.api import _ptr
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
 REFERENCE_WRAPPER_SYMBOLS = [
     # every prototype of the extern "C" block in src/embedding_cuda_impl.cpp:24-380
@@ -296,3 +300,49 @@ def test_multi_device_list_is_checked_before_device_work(monkeypatch):
     monkeypatch.setenv("FASTEMBEDR_B200_DEVICES", "0")  # one device: the ordinary path
     assert L.fastembedr_cuda_opentsne_fft_from_knn_float(*args) == 1
     assert "FASTEMBEDR_B200_DEVICES" not in _lib.last_error()
+
+
+def _reference_prototype_block():
+    """The reference wrapper's own extern "C" prototype block
+    (src/embedding_cuda_impl.cpp:24-380), read from the reference sources at
+    test time; None where they are absent."""
+    src = os.environ.get("FASTEMBEDR_REFERENCE_SRC") or os.path.join(os.path.dirname(ROOT), "reference", "src")
+    path = os.path.join(src, "embedding_cuda_impl.cpp")
+    if not os.path.exists(path):
+        return None
+    lines = open(path).read().splitlines()
+    start = lines.index('extern "C" {')
+    end = lines.index("}", start)
+    return "\n".join(lines[start:end + 1]) + "\n"
+
+
+def _compile_against(header_text, block, tmp_path):
+    inc = tmp_path / "inc"
+    inc.mkdir(exist_ok=True)
+    (inc / "fastembedr_b200.h").write_text(header_text)
+    tu = tmp_path / "boundary.cpp"
+    # R's opaque object handle, for the two helpers the wrapper declares in
+    # the block and defines itself (src/embedding_cuda_impl.cpp:230-231).
+    tu.write_text('#include "fastembedr_b200.h"\ntypedef struct SEXPREC* SEXP;\n' + block)
+    return subprocess.run(["g++", "-std=c++17", "-fsyntax-only", "-I", str(inc), str(tu)],
+                          capture_output=True, text=True)
+
+
+def test_header_compiles_against_reference_prototypes(tmp_path):
+    """Every prototype the reference wrapper declares for the backend library,
+    compiled in one translation unit with include/fastembedr_b200.h: a C-linkage
+    function declared twice with different parameter or return types does not
+    compile, so the signatures agree type for type, not only by name.  A copy
+    of the header with one argument type changed must then fail."""
+    block = _reference_prototype_block()
+    if block is None:
+        pytest.skip("reference sources not present on this host")
+    header = open(os.path.join(ROOT, "include", "fastembedr_b200.h")).read()
+    ok = _compile_against(header, block, tmp_path)
+    assert ok.returncode == 0, ok.stderr[-3000:]
+    # Negative control: the last argument kind of the UMAP COO optimizer.
+    bad = header.replace("int optimizer_mode, float* out);", "float optimizer_mode, float* out);", 1)
+    assert bad != header
+    broken = _compile_against(bad, block, tmp_path)
+    assert broken.returncode != 0
+    assert "fastembedr_cuda_umap_optimize_coo" in broken.stderr

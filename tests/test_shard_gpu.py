@@ -159,9 +159,7 @@ def test_two_ranks_bit_identical_to_one_rank(problem, tmp_path):
             assert np.array_equal(got[key], one[key]), key
 
 
-@pytest.mark.skipif(_gpu_count() < 2 or os.environ.get("FASTEMBEDR_B200_MULTI_DEVICE_TESTS") != "1",
-                    reason="needs two GPUs; the single-process multi-device mode is enabled for testing with "
-                           "FASTEMBEDR_B200_MULTI_DEVICE_TESTS=1")
+@pytest.mark.skipif(_gpu_count() < 2, reason="needs two GPUs")
 def test_single_process_two_devices_match_one_rank(problem, tmp_path):
     """FASTEMBEDR_B200_DEVICES=0,1: the unchanged one-shot entry point runs one
     sharded session per device in this process; the layout must be the bits
@@ -183,6 +181,50 @@ def test_single_process_two_devices_match_one_rank(problem, tmp_path):
         s.shard(api.nccl_unique_id(), 1, 0)
         want = s.run(EARLY, LATE)
     assert np.array_equal(got, want)
+
+
+INJECT_PROBE = r"""
+import os, sys, numpy as np
+sys.path.insert(0, {root!r})
+from fastembedr_b200 import api
+p = np.load({problem!r})
+kw = dict(perplexity={perp}, init=p['init'], early_exaggeration_iter={early}, n_iter={late})
+try:
+    api.opentsne_knn(p['idx'], p['dist'], **kw)
+except api.CudaBackendError as e:
+    print("ERROR:", e)
+else:
+    print("RAN")
+del os.environ["FASTEMBEDR_B200_INJECT_HOST_FAILURE"]
+res = api.opentsne_knn(p['idx'], p['dist'], **kw)  # the same process runs again
+np.save({out!r}, res.Y)
+print("AFTER")
+"""
+
+
+@pytest.mark.skipif(_gpu_count() < 2, reason="needs two GPUs")
+def test_single_process_host_failure_stops_every_rank(problem, tmp_path):
+    """FASTEMBEDR_B200_DEVICES=0,1 with rank 1 failing on the host before its
+    41st collective (mid-run, none of its collectives in flight): rank 0 learns
+    of it on the host before enqueuing that collective, both ranks stop, the
+    call returns status 1 naming the cause, and the same process then runs the
+    call again to the bits of a one-rank sharded session.  No collective is left
+    waiting on a GPU, so no communicator is aborted with work in flight."""
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    out = str(tmp_path / "after.npy")
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0", FASTEMBEDR_B200_DEVICES="0,1",
+               FASTEMBEDR_B200_INJECT_HOST_FAILURE="1:40", FASTEMBEDR_B200_COLLECTIVE_TIMEOUT_S="60")
+    script = INJECT_PROBE.format(root=root, problem=problem, perp=PERPLEXITY, early=EARLY, late=LATE, out=out)
+    r = subprocess.run([sys.executable, "-c", script], env=env, capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stderr[-2000:]
+    lines = [ln for ln in r.stdout.splitlines() if ln.startswith(("ERROR:", "RAN", "AFTER"))]
+    assert len(lines) == 2 and lines[0].startswith("ERROR:") and lines[1] == "AFTER", r.stdout[-2000:]
+    assert "injected host failure of rank 1 before collective 40" in lines[0], lines[0]
+    p = np.load(problem)
+    with api.TsneSession.from_knn(p["idx"], p["dist"], perplexity=PERPLEXITY, init=p["init"]) as s:
+        s.shard(api.nccl_unique_id(), 1, 0)
+        want = s.run(EARLY, LATE)
+    assert np.array_equal(np.load(out), want)
 
 
 def _rank_main(problem, uid_hex, nranks, rank, out):

@@ -42,6 +42,8 @@ WORKLOADS = {
     "tsne_70k": dict(spec="tsne_70k", k=90, perplexity=30.0),
     "tsne_10k": dict(spec="tsne_10k", k=90, perplexity=30.0),
     "tsne_200k": dict(spec="tsne_200k", k=90, perplexity=30.0),
+    # N = 2M, generated like configuration 3: the size the scaling target names
+    "tsne_2m": dict(spec="tsne_2m", k=90, perplexity=30.0),
     # UMAP configurations 1 and 4: k = 15 fuzzy graph, negative_sample_rate 5,
     # a/b for min_dist 0.1, learning rate 1, start U(-10, 10).
     "umap_70k": dict(spec="umap_70k", k=15, kind="umap", n_epochs=500),
@@ -296,6 +298,54 @@ def bench_reference_umap(args):
     return 0
 
 
+def reference_cuda_tsne(idx, dist, init, perplexity, reps: int = 1):
+    """The reference's own CUDA backend (oracle/_ref/libferef_cuda.so, its
+    src/embedding_cuda_kernels.cpp built for sm_100a) on the same host KNN,
+    through the same entry point as our e2e leg: the GPU bar, reported beside
+    the CPU baseline and never part of our timed region.  None when not built."""
+    import oracle as O
+
+    if not O.ref_cuda_available():
+        return None
+    n, k = idx.shape
+
+    def call():
+        O.ref_cuda_tsne(idx, dist, init, perplexity=perplexity, early_exaggeration_iter=EE_ITER, n_iter=N_ITER,
+                        early_exaggeration=EE, exaggeration=EX, momentum=MOM, min_gain=MIN_GAIN,
+                        max_step_norm=MAX_STEP)
+
+    secs = median_call_seconds(call, reps)  # the warm call loads modules and makes cuFFT plans
+    return {"value": (EE_ITER + N_ITER) / secs, "unit": "iterations/s", "seconds_per_call": secs,
+            "timing": f"median of {reps} call(s) after a warm one",
+            "grid": "reference CUDA policy (G = 1024 at n >= 100k)",
+            "call": "fastembedr_cuda_opentsne_fft_from_knn_float of the reference (750 iterations, pageable host "
+                    "KNN), src/embedding_cuda_kernels.cpp built for sm_100a"}
+
+
+def reference_cuda_umap(idx, dist, n_epochs, graph_edges, units, reps: int = 3):
+    """The reference's own CUDA fused UMAP path (graph, diffusion start,
+    epochs) on the same host KNN; edge updates counted as this library's
+    positive samples of a whole run (the same schedule).  None when not built."""
+    import oracle as O
+    from fastembedr_b200 import api
+
+    if not O.ref_cuda_available():
+        return None
+    n, k = idx.shape
+    a, b = api.find_ab_params(1.0, UMAP_MIN_DIST)
+    sni = api.umap_config(n, k)["spectral_n_iter"]
+
+    def call():
+        O.ref_cuda_umap_fused(idx, dist, n_epochs, negative_sample_rate=UMAP_NSR, learning_rate=UMAP_LR,
+                              a=a, b=b, spectral_n_iter=sni, seed=42)
+
+    secs = median_call_seconds(call, reps)
+    return {"value": units / secs, "unit": "edge_updates/s", "seconds_per_call": secs,
+            "timing": f"median of {reps} calls after a warm one", "n_edges": int(graph_edges),
+            "call": f"fastembedr_cuda_umap_from_knn_spectral_float of the reference ({n_epochs} epochs, host KNN: "
+                    f"graph, diffusion start, epochs), src/embedding_cuda_kernels.cpp built for sm_100a"}
+
+
 def bench_reference_cuda(args):
     """The reference's own CUDA backend (oracle/_ref/libferef_cuda.so, its
     src/embedding_cuda_kernels.cpp built for sm_100a), timed through the same
@@ -405,10 +455,6 @@ def bench_ours(args):
     from fastembedr_b200 import _lib, api
 
     rank, world, local = dist_env()
-    torch.cuda.set_device(local)
-    if world > 1:
-        tdist.init_process_group("nccl", init_method="env://", timeout=__import__("datetime").timedelta(seconds=300),
-                                 device_id=torch.device("cuda", local))
     w = WORKLOADS[args.workload]
     idx, dist, init = shared_inputs(args, rank, world, local)
     n, k = idx.shape
@@ -454,6 +500,26 @@ def bench_ours(args):
     # The whole job advances one iteration per step on every rank together.
     value = args.steps / (elapsed_ms / 1000.0)
 
+    # --- one complete standard run (250 + 500 iterations, spatial reorders
+    # included) in a single CUDA-event interval, beside the K timed steps ---
+    full_iters = EE_ITER + N_ITER
+    sess.set_layout(init_dev, reset_state=True)
+    torch.cuda.synchronize()
+    if world > 1:
+        tdist.barrier()
+    start.record(stream)
+    run_schedule(sess, 0, full_iters, n)
+    stop.record(stream)
+    torch.cuda.synchronize()
+    full_ms = start.elapsed_time(stop)
+    if world > 1:
+        t = torch.tensor([full_ms], device="cuda")
+        tdist.all_reduce(t, op=tdist.ReduceOp.MAX)
+        full_ms = float(t.item())
+    full_run = {"iterations": full_iters, "ms": full_ms, "value": full_iters / (full_ms / 1000.0),
+                "unit": "iterations/s", "timing": "one CUDA-event interval around a whole standard run from the "
+                                                  "init (P and state resident)"}
+
     # --- per-kernel CUDA-event timing of one full standard run (roofline) ---
     sess.set_layout(init_dev, reset_state=True)
     sess.profile(True)
@@ -482,31 +548,47 @@ def bench_ours(args):
     total_ms = sum(v[0] for v in times.values())
     kernel_share = {kname: round(v[0] / total_ms, 4) for kname, v in times.items()}
 
-    # --- end to end through the public API with pinned host buffers ---
+    # --- end to end through the public API from host buffers ---
+    # The reference's R wrapper hands the library pageable std::vector copies
+    # (src/embedding_cuda_impl.cpp:776-784, 817), so the headline e2e passes
+    # plain (pageable) host arrays; the same call from pinned buffers is
+    # reported beside it.
     e2e = None
     if not args.skip_e2e and world == 1:
-        idx_cm = torch.from_numpy(np.ascontiguousarray(idx.T)).pin_memory()
-        dist_cm = torch.from_numpy(np.ascontiguousarray(dist.T)).pin_memory()
-        init_h = torch.from_numpy(init).pin_memory()
-        out_h = torch.empty((n, 2), dtype=torch.float32).pin_memory()
         import ctypes
 
         L = _lib.load()
+        idx_cm = np.ascontiguousarray(idx.T)
+        dist_cm = np.ascontiguousarray(dist.T)
+        init_h = np.ascontiguousarray(init, dtype=np.float32)
+        out_h = np.empty((n, 2), np.float32)
 
-        def call():
-            rc = L.fastembedr_cuda_opentsne_fft_from_knn_float(
-                ctypes.c_void_p(idx_cm.data_ptr()), ctypes.c_void_p(dist_cm.data_ptr()),
-                ctypes.cast(init_h.data_ptr(), ctypes.POINTER(ctypes.c_float)), 1, n, k, 2,
-                w["perplexity"], EE_ITER, N_ITER, EE, EX, 0.0, 1, MOM, MOM, MIN_GAIN, MAX_STEP, 42, 0,
-                ctypes.cast(out_h.data_ptr(), ctypes.POINTER(ctypes.c_float)))
-            _lib.check(rc, "fastembedr_cuda_opentsne_fft_from_knn_float")
+        def e2e_call(i_ptr, d_ptr, init_ptr, out_ptr):
+            def call():
+                rc = L.fastembedr_cuda_opentsne_fft_from_knn_float(
+                    ctypes.c_void_p(i_ptr), ctypes.c_void_p(d_ptr),
+                    ctypes.cast(init_ptr, ctypes.POINTER(ctypes.c_float)), 1, n, k, 2,
+                    w["perplexity"], EE_ITER, N_ITER, EE, EX, 0.0, 1, MOM, MOM, MIN_GAIN, MAX_STEP, 42, 0,
+                    ctypes.cast(out_ptr, ctypes.POINTER(ctypes.c_float)))
+                _lib.check(rc, "fastembedr_cuda_opentsne_fft_from_knn_float")
+            return call
 
-        e2e_s = median_call_seconds(call)  # the warm call loads the module
+        e2e_s = median_call_seconds(e2e_call(idx_cm.ctypes.data, dist_cm.ctypes.data, init_h.ctypes.data,
+                                             out_h.ctypes.data))  # the warm call loads the module
+        p_idx = torch.from_numpy(idx_cm).pin_memory()
+        p_dist = torch.from_numpy(dist_cm).pin_memory()
+        p_init = torch.from_numpy(init_h).pin_memory()
+        p_out = torch.empty((n, 2), dtype=torch.float32).pin_memory()
+        pinned_s = median_call_seconds(e2e_call(p_idx.data_ptr(), p_dist.data_ptr(), p_init.data_ptr(),
+                                                p_out.data_ptr()))
+        del p_idx, p_dist, p_init, p_out
         e2e = {"value": (EE_ITER + N_ITER) / e2e_s, "unit": "iterations/s",
-               "h2d_bytes_per_step": int(idx_cm.numel() * 4 + dist_cm.numel() * 4 + init_h.numel() * 4),
-               "d2h_bytes_per_step": int(out_h.numel() * 4), "seconds_per_call": e2e_s,
+               "h2d_bytes_per_step": int(idx_cm.nbytes + dist_cm.nbytes + init_h.nbytes),
+               "d2h_bytes_per_step": int(out_h.nbytes), "seconds_per_call": e2e_s,
+               "host_buffers": "pageable (numpy), as the reference's R wrapper passes them",
                "timing": "median of 3 calls after a warm one",
-               "call": "fastembedr_cuda_opentsne_fft_from_knn_float (750 iterations, host KNN)"}
+               "call": "fastembedr_cuda_opentsne_fft_from_knn_float (750 iterations, host KNN)",
+               "pinned": {"value": (EE_ITER + N_ITER) / pinned_s, "seconds_per_call": pinned_s}}
     elif not args.skip_e2e:
         # Every rank: pinned host KNN -> device, P build, shard, 750 iterations,
         # layout back to the host; max over ranks.  The NCCL communicator is made
@@ -539,11 +621,21 @@ def bench_ours(args):
                        "communicator made once per process"}
         comm.close()
 
-    cpu = None
+    sess.close()
+    # Baselines, outside every timed region: the reference's own CPU loop
+    # (cpu_baseline) and its own CUDA backend (reference_cuda, the GPU bar).
+    cpu = ref_gpu = None
     if rank == 0 and world == 1 and not args.skip_cpu:
         cpu = cpu_baseline_tsne(idx, dist, w["perplexity"], init, args.cpu_iters, args.cpu_seconds)
-
-    sess.close()
+        if not args.skip_reference_cuda:
+            ref_gpu = reference_cuda_tsne(idx, dist, init, w["perplexity"])
+    del idx, dist
+    # UMAP edge updates/s, the metric's second half, on configuration 4
+    # (N = 2M), in the same line.
+    umap = None
+    if args.workload == "tsne_1m" and not args.skip_umap:
+        umap = umap_measure("umap_2m", WORKLOADS["umap_2m"]["n_epochs"], 3, args.skip_e2e, args.skip_cpu,
+                            ref_cuda=not args.skip_reference_cuda)
     if rank == 0:
         per_iter = 6  # splat, 3 FFT passes, gradient/update, layout statistics (NCCL kernels not counted)
         line = {
@@ -572,12 +664,14 @@ def bench_ours(args):
                             + 3 * ((args.steps - 1) // (EE_ITER + N_ITER)),
             "clocks": clocks.summary(),
             "e2e": e2e,
+            "full_run": full_run,
             "cpu_baseline": cpu,
         }
+        if ref_gpu is not None:
+            line["reference_cuda"] = ref_gpu
+        if umap is not None:
+            line["umap"] = umap
         print(json.dumps(line), flush=True)
-    if world > 1:
-        tdist.barrier()
-        tdist.destroy_process_group()
     return 0
 
 
@@ -653,23 +747,20 @@ def cpu_baseline_umap(graph, init, epochs: int = 0):
     return out
 
 
-def bench_umap(args):
+def umap_measure(workload: str, steps: int, warmup: int, skip_e2e: bool, skip_cpu: bool, ref_cuda: bool):
     """A step is one UMAP epoch over the whole edge list; the metric counts
-    positive edge samples applied per second (negative samples alongside)."""
+    positive edge samples applied per second (negative samples alongside).
+    Returns the JSON line (rank 0; None on other ranks)."""
     import torch
     import torch.distributed as tdist
 
     from fastembedr_b200 import _lib, api
 
     rank, world, local = dist_env()
-    torch.cuda.set_device(local)
-    if world > 1:
-        tdist.init_process_group("nccl", init_method="env://", timeout=__import__("datetime").timedelta(seconds=300),
-                                 device_id=torch.device("cuda", local))
-    w = WORKLOADS[args.workload]
+    w = WORKLOADS[workload]
     n_epochs = w["n_epochs"]
     if world == 1 or rank == 0:
-        idx, dist, init = umap_inputs(args.workload, f"cuda:{local}")
+        idx, dist, init = umap_inputs(workload, f"cuda:{local}")
     if world > 1:
         # Rank 0's inputs on every rank.
         from fastembedr_b200 import synthetic as S
@@ -712,14 +803,14 @@ def bench_umap(args):
                 sess.set_layout(init_dev)  # a new run of the schedule starts from the init
             sess.run(c0, c1, n_epochs, UMAP_NSR, UMAP_LR, UMAP_MIN_DIST, seed=42, optimizer_mode=0)
 
-    run(0, args.warmup)
+    run(0, warmup)
     torch.cuda.synchronize()
     if world > 1:
         tdist.barrier()
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clocks:
         start.record(stream)
-        run(0, args.steps)
+        run(0, steps)
         stop.record(stream)
         torch.cuda.synchronize()
     elapsed_ms = start.elapsed_time(stop)
@@ -728,7 +819,7 @@ def bench_umap(args):
         tdist.all_reduce(tt, op=tdist.ReduceOp.MAX)
         elapsed_ms = float(tt.item())
     pos = neg = 0
-    for c0, c1 in spans(0, args.steps):
+    for c0, c1 in spans(0, steps):
         p_, n_ = sess.count_samples(c0, c1, UMAP_NSR)
         pos, neg = pos + p_, neg + n_
     value = pos / (elapsed_ms / 1000.0)
@@ -749,11 +840,13 @@ def bench_umap(args):
     achieved = alg_bytes / epoch_s / 1e9
 
     graph = sess.graph()
+    sess_total_pos, _ = sess.count_samples(0, n_epochs, UMAP_NSR)
     e2e = None
-    if not args.skip_e2e and world == 1:
-        idx_cm = torch.from_numpy(np.ascontiguousarray(idx.T)).pin_memory()
-        dist_cm = torch.from_numpy(np.ascontiguousarray(dist.T)).pin_memory()
-        out_h = torch.empty((n, 2), dtype=torch.float32).pin_memory()
+    if not skip_e2e and world == 1:
+        # Pageable host arrays, as the reference's R wrapper passes them.
+        idx_cm = np.ascontiguousarray(idx.T)
+        dist_cm = np.ascontiguousarray(dist.T)
+        out_h = np.empty((n, 2), np.float32)
         import ctypes
 
         L = _lib.load()
@@ -761,47 +854,62 @@ def bench_umap(args):
 
         def call():
             rc = L.fastembedr_cuda_umap_from_knn_spectral_float(
-                ctypes.c_void_p(idx_cm.data_ptr()), ctypes.c_void_p(dist_cm.data_ptr()), n, k, n_epochs,
+                ctypes.c_void_p(idx_cm.ctypes.data), ctypes.c_void_p(dist_cm.ctypes.data), n, k, n_epochs,
                 UMAP_NSR, UMAP_LR, a, b, 1.0, sni, 42, 0, 0,
-                ctypes.cast(out_h.data_ptr(), ctypes.POINTER(ctypes.c_float)))
+                ctypes.cast(out_h.ctypes.data, ctypes.POINTER(ctypes.c_float)))
             _lib.check(rc, "fastembedr_cuda_umap_from_knn_spectral_float")
 
         e2e_s = median_call_seconds(call)
         total_pos, _ = sess.count_samples(0, n_epochs, UMAP_NSR)
         e2e = {"value": total_pos / e2e_s, "unit": "edge_updates/s",
-               "h2d_bytes_per_step": int(idx_cm.numel() * 4 + dist_cm.numel() * 4),
-               "d2h_bytes_per_step": int(out_h.numel() * 4), "seconds_per_call": e2e_s,
+               "h2d_bytes_per_step": int(idx_cm.nbytes + dist_cm.nbytes),
+               "d2h_bytes_per_step": int(out_h.nbytes), "seconds_per_call": e2e_s,
+               "host_buffers": "pageable (numpy), as the reference's R wrapper passes them",
                "timing": "median of 3 calls after a warm one",
                "call": f"fastembedr_cuda_umap_from_knn_spectral_float ({n_epochs} epochs, host KNN: graph, "
                        f"diffusion start, epochs)"}
-    cpu = None if (args.skip_cpu or world > 1) else cpu_baseline_umap(graph, init)
     sess.close()
+    cpu = ref_gpu = None
+    if rank == 0 and world == 1 and not skip_cpu:
+        cpu = cpu_baseline_umap(graph, init)
+        if ref_cuda:
+            ref_gpu = reference_cuda_umap(idx, dist, n_epochs, graph_edges=info["n_edges"],
+                                          units=int(sess_total_pos))
     if world > 1:
         tdist.barrier()
-        tdist.destroy_process_group()
         if rank != 0:
-            return 0
+            return None
     line = {
         "metric": "umap_edge_updates_per_second", "value": value, "unit": "edge_updates/s",
-        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": elapsed_ms / args.steps,
+        "n_gpus": world, "steps": steps, "warmup": warmup, "ms_per_step": elapsed_ms / steps,
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic",
-        "config": {"workload": args.workload, "n": int(n), "k": int(k), "n_edges": int(info["n_edges"]),
+        "config": {"workload": workload, "n": int(n), "k": int(k), "n_edges": int(info["n_edges"]),
                    "n_epochs": n_epochs, "negative_sample_rate": UMAP_NSR, "min_dist": UMAP_MIN_DIST,
                    "optimizer": "Hogwild per sample (device-KNN path)", "init": "U(-10, 10)",
                    "parallelism": (f"vertices sharded over {world} GPUs (per-epoch NCCL all-gather of the "
                                    f"layout)" if world > 1 else "single"),
                    "l2": l2_note(12 * info["n_edges"], "the edge list")},
         "negative_samples_per_second": neg / (elapsed_ms / 1000.0),
-        "epochs_per_second": args.steps / (elapsed_ms / 1000.0),
+        "epochs_per_second": steps / (elapsed_ms / 1000.0),
+        "edges_scanned_per_second": info["n_edges"] * steps / (elapsed_ms / 1000.0),
         "roofline": {"kernel": "umap_epoch_kernel (+ sanitize)", "bound": "hbm", "achieved": achieved,
                      "peak": hbm, "peak_kind": peak_kind, "unit": "GB/s", "frac": achieved / hbm,
                      "algorithmic_bytes_per_launch": alg_bytes, "avg_launch_ms": epoch_s * 1000.0,
-                     "traffic": profile_traffic("umap_epoch_kernel", args.workload)},
-        "gpu_launches": 2 * args.steps,
+                     "traffic": profile_traffic("umap_epoch_kernel", workload)},
+        "gpu_launches": 2 * steps,
         "clocks": clocks.summary(), "e2e": e2e, "cpu_baseline": cpu,
     }
-    print(json.dumps(line), flush=True)
+    if ref_gpu is not None:
+        line["reference_cuda"] = ref_gpu
+    return line
+
+
+def bench_umap(args):
+    line = umap_measure(args.workload, args.steps, args.warmup, args.skip_e2e, args.skip_cpu,
+                        ref_cuda=not args.skip_reference_cuda)
+    if line is not None:
+        print(json.dumps(line), flush=True)
     return 0
 
 
@@ -816,6 +924,9 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="loop time of the CPU sample")
     ap.add_argument("--skip-e2e", action="store_true")
     ap.add_argument("--skip-cpu", action="store_true")
+    ap.add_argument("--skip-umap", action="store_true", help="leave the UMAP block out of the t-SNE line")
+    ap.add_argument("--skip-reference-cuda", action="store_true",
+                    help="leave out the reference CUDA backend's time (reference_cuda)")
     ap.add_argument("--reference-backend", choices=["cpu", "cuda"], default="cpu",
                     help="with --impl reference: the reference's CPU loop (default) or its own CUDA backend")
     args = ap.parse_args()
@@ -826,9 +937,22 @@ def main():
         return bench_reference_cuda(args)
     if args.impl == "reference":
         return bench_reference_umap(args) if umap else bench_reference(args)
-    if umap:
-        return bench_umap(args)
-    return bench_ours(args)
+    import torch
+    import torch.distributed as tdist
+
+    _, world, local = dist_env()
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+
+        tdist.init_process_group("nccl", init_method="env://", timeout=datetime.timedelta(seconds=300),
+                                 device_id=torch.device("cuda", local))
+    try:
+        return bench_umap(args) if umap else bench_ours(args)
+    finally:
+        if world > 1:
+            tdist.barrier()
+            tdist.destroy_process_group()
 
 
 if __name__ == "__main__":

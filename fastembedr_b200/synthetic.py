@@ -35,6 +35,8 @@ CONFIGS = {
     "tsne_70k": MixtureSpec(n=70_000, components=10, anisotropic=True),
     "tsne_1m": MixtureSpec(n=1_000_000, components=20, anisotropic=True, dirichlet_weights=True),
     "umap_2m": MixtureSpec(n=2_000_000, components=20),
+    # the north star's scaling size for t-SNE (N >= 2M), generated as tsne_1m
+    "tsne_2m": MixtureSpec(n=2_000_000, components=20, anisotropic=True, dirichlet_weights=True),
     # profiling stand-in for tsne_1m: same generator, P (~0.25 GB) still larger than L2
     "tsne_200k": MixtureSpec(n=200_000, components=20, anisotropic=True, dirichlet_weights=True),
 }

@@ -59,19 +59,29 @@ def test_sample_counts_match_the_schedule(mixture):
 
 
 def test_split_jacobi_run_matches_one_shot_quality(mixture):
-    from quality import knn_preservation, label_accuracy
+    """A run split into epoch ranges reaches the one-shot call's quality.  Jacobi
+    epochs sum per-vertex moves with float atomics, so single runs at n = 5000
+    differ by a few percent in kNN preservation; the bar is on means over
+    seeds (3% plus two standard errors of the difference)."""
+    from quality import knn_preservation, label_accuracy, within_reference
 
     idx, dist, labels = mixture
-    one = api.umap_knn(idx, dist, n_epochs=200, min_dist=0.1, seed=42, optimizer_mode=1).Y
-    with api.UmapSession.from_knn(idx, dist, seed=42) as s:
-        for b, e in ((0, 60), (60, 61), (61, 200)):
-            s.run(b, e, 200, min_dist=0.1, seed=42, optimizer_mode=1)
-        y = s.layout()
-    assert np.isfinite(y).all() and np.abs(y).max() <= 16.0
-    q1, q2 = knn_preservation(one, idx), knn_preservation(y, idx)
-    l1, l2 = label_accuracy(one, labels), label_accuracy(y, labels)
-    assert q2 >= 0.97 * q1, (q2, q1)
-    assert l2 >= 0.97 * l1, (l2, l1)
+    q1, q2, l1, l2 = [], [], [], []
+    for seed in (42, 43, 44, 45):
+        one = api.umap_knn(idx, dist, n_epochs=200, min_dist=0.1, seed=seed, optimizer_mode=1).Y
+        with api.UmapSession.from_knn(idx, dist, seed=seed) as s:
+            for b, e in ((0, 60), (60, 61), (61, 200)):
+                s.run(b, e, 200, min_dist=0.1, seed=seed, optimizer_mode=1)
+            y = s.layout()
+        assert np.isfinite(y).all() and np.abs(y).max() <= 16.0
+        q1.append(knn_preservation(one, idx))
+        q2.append(knn_preservation(y, idx))
+        l1.append(label_accuracy(one, labels))
+        l2.append(label_accuracy(y, labels))
+    ok_q, msg_q = within_reference(q2, q1, rel=0.03)
+    ok_l, msg_l = within_reference(l2, l1, rel=0.03)
+    assert ok_q, msg_q
+    assert ok_l, msg_l
 
 
 def test_session_rejects_bad_ranges(mixture):

@@ -30,6 +30,9 @@ _SIGNATURES = {
     "fastembedr_cuda_opentsne_fft_from_knn": (I, _TSNE_KNN_ARGS),
     "fastembedr_cuda_opentsne_fft_from_knn_float": (I, _TSNE_KNN_ARGS),
     "fastembedr_cuda_opentsne_fft_from_device_knn_float": (I, _TSNE_KNN_ARGS),
+    "fastembedr_cuda_landmark_tsne_from_device_knn": (I, [c_void_p, c_void_p, I, c_float_p, c_float_p, c_float_p,
+                                                          I, I, I, I, F, I, I, F, F, F, F, F, F, F, I, I, U, I,
+                                                          F, F, c_float_p]),
     "fastembedr_cuda_umap_optimize_coo": (I, [c_int_p, c_int_p, c_float_p, c_float_p, c_float_p, I, I, I, I,
                                               F, F, F, F, U, I, c_float_p]),
     "fastembedr_cuda_umap_from_knn_spectral": (I, [c_void_p, c_void_p, I, I, I, I, F, F, F, F, I, U, I, I,
@@ -54,6 +57,14 @@ _SIGNATURES = {
     "fe_b200_tsne_get_state": (I, [c_void_p, c_float_p, c_float_p]),
     "fe_b200_tsne_set_state": (I, [c_void_p, c_float_p, c_float_p]),
     "fe_b200_tsne_info": (I, [c_void_p, c_int_p, c_int_p, c_ll_p, c_ll_p]),
+    "fe_b200_tsne_staged_blocks": (I, [c_void_p, c_int_p, c_int_p]),
+    "fe_b200_pca_start": (I, [c_void_p, I, I, I, c_float_p]),
+    "fastembedr_cuda_opentsne_fft_from_device_knn_float_pca_double": (I, [c_void_p, c_void_p, c_void_p, I, I, I,
+                                                                         I, F, I, I, F, F, F, I, F, F, F, F, U, I,
+                                                                         c_float_p]),
+    "fastembedr_cuda_opentsne_fft_from_device_knn_float_pca_float": (I, [c_void_p, c_void_p, c_void_p, I, I, I,
+                                                                        I, F, I, I, F, F, F, I, F, F, F, F, U, I,
+                                                                        c_float_p]),
     "fe_b200_tsne_get_p": (I, [c_void_p, c_int_p, c_int_p, c_float_p]),
     "fe_b200_tsne_stream": (c_void_p, [c_void_p]),
     "fe_b200_tsne_profile": (I, [c_void_p, I]),

@@ -198,6 +198,47 @@ def opentsne_knn(indices, distances, n_components: int = 2, perplexity: Optional
     })
 
 
+def landmark_tsne_transform(indices, distances, reference_data, query_data, reference_layout,
+                            perplexity: float = 30.0, n_iter: int = 250, early_exaggeration_iter: int = 50,
+                            learning_rate: float = 0.1, early_exaggeration: float = 4.0,
+                            exaggeration: float = 1.5, initial_momentum: float = 0.8,
+                            final_momentum: float = 0.8, max_grad_norm: float = 0.25,
+                            max_step_norm: float = float("inf"), n_negatives: Optional[int] = None,
+                            exact_repulsion_threshold: int = 4096, seed: int = 1009, affine_neighbors: int = 12,
+                            affine_ridge: float = 1e-3, max_extrapolation: float = 2.5,
+                            index_offset: int = 0) -> np.ndarray:
+    """Places query points in a fixed reference layout (the openTSNE transform
+    behind landmark_tsne_transform_cuda_gpu_cpp, src/embedding_cuda_impl.cpp:2486-2580,
+    and fastembedr_cuda_landmark_tsne_from_device_knn): `indices` / `distances`
+    are the queries' KNN into the reference, (n_query, k), on the device (torch
+    CUDA tensors) or on the host (copied to the device here); the data and the
+    reference layout are (n, d) host arrays.  Defaults follow the R wrapper
+    (R/landmark_model.R:442-477): n_negatives = n_reference up to the exact
+    threshold, else min(256, n_reference)."""
+    import torch
+
+    n_ref, dim = np.asarray(reference_data).shape
+    n_q, k = tuple(indices.shape)
+    if n_negatives is None:
+        n_negatives = n_ref if n_ref <= exact_repulsion_threshold else min(256, n_ref)
+    # column-major (R) device KNN
+    ti = torch.as_tensor(indices).to(device="cuda", dtype=torch.int32).t().contiguous()
+    td = torch.as_tensor(distances).to(device="cuda", dtype=torch.float32).t().contiguous()
+    rd = np.ascontiguousarray(np.asarray(reference_data, np.float32).T).reshape(-1)
+    qd = np.ascontiguousarray(np.asarray(query_data, np.float32).T).reshape(-1)
+    rl = np.ascontiguousarray(np.asarray(reference_layout, np.float32).T).reshape(-1)
+    out = np.zeros((n_q, 2), np.float32)
+    torch.cuda.synchronize()
+    rc = _lib.load().fastembedr_cuda_landmark_tsne_from_device_knn(
+        ctypes.c_void_p(ti.data_ptr()), ctypes.c_void_p(td.data_ptr()), index_offset, _ptr(rd, ctypes.c_float),
+        _ptr(qd, ctypes.c_float), _ptr(rl, ctypes.c_float), n_ref, n_q, dim, k, perplexity, n_iter,
+        early_exaggeration_iter, learning_rate, early_exaggeration, exaggeration, initial_momentum,
+        final_momentum, max_grad_norm, max_step_norm, n_negatives, exact_repulsion_threshold,
+        seed & 0xFFFFFFFF, affine_neighbors, affine_ridge, max_extrapolation, _ptr(out, ctypes.c_float))
+    check(rc, "fastembedr_cuda_landmark_tsne_from_device_knn")
+    return out
+
+
 class TsneSession:
     """Device-resident t-SNE state (P, layout, gains, update) across calls."""
 
@@ -316,6 +357,14 @@ class TsneSession:
                                             ctypes.byref(nnzp)), "fe_b200_tsne_info")
         return {"n": n.value, "grid": g.value, "nnz": nnz.value, "nnz_padded": nnzp.value}
 
+    def staged_blocks(self) -> Tuple[int, int]:
+        """(staged, total) 128-row blocks of this session's rows at the last
+        spatial reorder; staged blocks gather y from shared memory."""
+        st, tot = ctypes.c_int(), ctypes.c_int()
+        check(_lib.load().fe_b200_tsne_staged_blocks(self._h, ctypes.byref(st), ctypes.byref(tot)),
+              "fe_b200_tsne_staged_blocks")
+        return st.value, tot.value
+
     def p(self):
         inf = self.info()
         rp = np.zeros(inf["n"] + 1, np.int32)
@@ -336,7 +385,7 @@ class TsneSession:
     def kernel_times(self) -> Dict[str, Tuple[float, int]]:
         """Per-kind CUDA-event totals (ms, launches) since profiling was enabled;
         the collective kinds appear only for sharded sessions."""
-        kinds = 8
+        kinds = 9
         ms = np.zeros(kinds, np.float64)
         cnt = np.zeros(kinds, np.int64)
         L = _lib.load()

@@ -72,7 +72,7 @@ int opentsne_impl(const int* indices, const void* distances, bool dist_double, c
                   float exaggeration, float learning_rate, int learning_rate_auto,
                   float initial_momentum, float final_momentum, float min_gain,
                   float max_step_norm, unsigned int seed, int index_offset, float* out,
-                  bool on_device) {
+                  bool on_device, const void* pca_values = nullptr, bool pca_double = false, int pca_p = 0) {
   fe::clear_error();
   if (indices == nullptr || distances == nullptr || out == nullptr || (has_init && init == nullptr)) {
     set_error("null CUDA openTSNE input pointer");
@@ -94,8 +94,33 @@ int opentsne_impl(const int* indices, const void* distances, bool dist_double, c
       ? static_cast<float>(static_cast<double>(n) / std::max(static_cast<double>(exaggeration), DBL_MIN))
       : learning_rate;
   const float clip = std::isfinite(max_step_norm) ? max_step_norm : NAN;
+  const bool pca = !has_init && pca_values != nullptr;
+  if (pca && (pca_p < 2 || pca_p < n_components)) {
+    set_error("invalid dimensions in device PCA initialization");
+    return 1;
+  }
   std::vector<int> devices;
   FE_TRY(fe::multi_device_list(&devices));
+  std::vector<float> pca_host;
+  if (devices.size() >= 2 && pca) {
+    // The PCA start is made once, on the calling device, and handed to every
+    // rank as a host init.
+    cudaStream_t ps = nullptr;
+    FE_CUDA(cudaStreamCreateWithFlags(&ps, cudaStreamNonBlocking), "cudaStreamCreate(PCA)");
+    float2* d_start = nullptr;
+    int rc = fe::check_cuda(cudaMalloc(&d_start, sizeof(float2) * static_cast<size_t>(n)), "cudaMalloc(PCA start)");
+    if (rc == 0) rc = fe::pca_start_layout(pca_values, pca_double, n, pca_p, ps, d_start);
+    if (rc == 0) {
+      pca_host.resize(2 * static_cast<size_t>(n));
+      rc = fe::check_cuda(cudaMemcpy(pca_host.data(), d_start, sizeof(float2) * static_cast<size_t>(n),
+                                     cudaMemcpyDeviceToHost), "D2H PCA start");
+    }
+    if (d_start != nullptr) cudaFree(d_start);
+    cudaStreamDestroy(ps);
+    if (rc != 0) return 1;
+    init = pca_host.data();
+    has_init = 1;
+  }
   if (devices.size() >= 2) {
     fe::MultiDeviceTsne job;
     job.devices = devices;
@@ -165,6 +190,11 @@ int opentsne_impl(const int* indices, const void* distances, bool dist_double, c
   } sguard{s};
   if (has_init) {
     FE_TRY(fe::session_set_layout(s, init, true, true));
+  } else if (pca) {
+    // The reference's PCA start (RAFT TSVD scores, scaled to sd 1e-4), made on
+    // the device into a free session buffer.
+    FE_TRY(fe::pca_start_layout(pca_values, pca_double, n, pca_p, s->stream, s->grad_out));
+    FE_TRY(fe::session_set_layout(s, reinterpret_cast<const float*>(s->grad_out), false, true));
   } else {
     FE_TRY(fe::session_random_layout(s, seed));
   }
@@ -431,17 +461,33 @@ int fastembedr_cuda_opentsne_fft_from_device_knn_float(
 }
 
 int fastembedr_cuda_opentsne_fft_from_device_knn_float_pca_double(
-    const int*, const float*, const double*, int, int, int, int, float, int, int, float, float,
-    float, int, float, float, float, float, unsigned int, int, float*) {
-  set_error("CUDA device-resident PCA initialization requires RAPIDS RAFT/cuML TSVD support.");
-  return 1;
+    const int* indices, const float* distances, const double* pca_init_values, int pca_init_p, int n, int k,
+    int n_components, float perplexity, int early_exaggeration_iter, int n_iter, float early_exaggeration,
+    float exaggeration, float learning_rate, int learning_rate_auto, float initial_momentum, float final_momentum,
+    float min_gain, float max_step_norm, unsigned int seed, int index_offset, float* out) {
+  if (pca_init_values == nullptr) {
+    set_error("null pointer in device PCA initialization");
+    return 1;
+  }
+  return opentsne_impl(indices, distances, false, nullptr, 0, n, k, n_components, perplexity,
+                       early_exaggeration_iter, n_iter, early_exaggeration, exaggeration, learning_rate,
+                       learning_rate_auto, initial_momentum, final_momentum, min_gain, max_step_norm, seed,
+                       index_offset, out, true, pca_init_values, true, pca_init_p);
 }
 
 int fastembedr_cuda_opentsne_fft_from_device_knn_float_pca_float(
-    const int*, const float*, const float*, int, int, int, int, float, int, int, float, float,
-    float, int, float, float, float, float, unsigned int, int, float*) {
-  set_error("CUDA device-resident PCA initialization requires RAPIDS RAFT/cuML TSVD support.");
-  return 1;
+    const int* indices, const float* distances, const float* pca_init_values, int pca_init_p, int n, int k,
+    int n_components, float perplexity, int early_exaggeration_iter, int n_iter, float early_exaggeration,
+    float exaggeration, float learning_rate, int learning_rate_auto, float initial_momentum, float final_momentum,
+    float min_gain, float max_step_norm, unsigned int seed, int index_offset, float* out) {
+  if (pca_init_values == nullptr) {
+    set_error("null pointer in device PCA initialization");
+    return 1;
+  }
+  return opentsne_impl(indices, distances, false, nullptr, 0, n, k, n_components, perplexity,
+                       early_exaggeration_iter, n_iter, early_exaggeration, exaggeration, learning_rate,
+                       learning_rate_auto, initial_momentum, final_momentum, min_gain, max_step_norm, seed,
+                       index_offset, out, true, pca_init_values, false, pca_init_p);
 }
 
 int fastembedr_cuda_umap_optimize_coo(const int* heads, const int* tails, const float* weights,
@@ -657,12 +703,53 @@ int fe_b200_tsne_get_p(fe_b200_tsne* h, int* row_ptr, int* col, float* val) {
   return fe::session_get_p(h->impl, row_ptr, col, val);
 }
 
+int fe_b200_tsne_staged_blocks(fe_b200_tsne* h, int* staged, int* blocks) {
+  fe::clear_error();
+  if (h == nullptr || staged == nullptr || blocks == nullptr) {
+    set_error("invalid t-SNE session call");
+    return 1;
+  }
+  fe::TsneSession* s = h->impl;
+  const int rows = std::max(0, s->row_end - s->row_begin);
+  *blocks = (rows + fe::kStageRows - 1) / fe::kStageRows;
+  unsigned int count = 0;
+  if (s->stage_enabled) {
+    FE_CUDA(cudaMemcpyAsync(&count, &s->stats->stage_count, sizeof(count), cudaMemcpyDeviceToHost, s->stream),
+            "D2H staged blocks");
+    FE_CUDA(cudaStreamSynchronize(s->stream), "cudaStreamSynchronize(staged blocks)");
+  }
+  *staged = static_cast<int>(count);
+  return 0;
+}
+
+int fe_b200_pca_start(const void* values, int values_double, int n, int p, float* out) {
+  fe::clear_error();
+  if (values == nullptr || out == nullptr || n < 2 || p < 2) {
+    set_error("invalid dimensions in device PCA initialization");
+    return 1;
+  }
+  cudaStream_t st = nullptr;
+  FE_CUDA(cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking), "cudaStreamCreate(PCA)");
+  float2* d = nullptr;
+  int rc = fe::check_cuda(cudaMalloc(&d, sizeof(float2) * static_cast<size_t>(n)), "cudaMalloc(PCA start)");
+  if (rc == 0) rc = fe::pca_start_layout(values, values_double != 0, n, p, st, d);
+  if (rc == 0) {
+    rc = fe::check_cuda(cudaMemcpyAsync(out, d, sizeof(float2) * static_cast<size_t>(n), cudaMemcpyDeviceToHost, st),
+                        "D2H PCA start");
+  }
+  if (rc == 0) rc = fe::check_cuda(cudaStreamSynchronize(st), "cudaStreamSynchronize(PCA start)");
+  cudaStreamSynchronize(st);
+  if (d != nullptr) cudaFree(d);
+  cudaStreamDestroy(st);
+  return rc;
+}
+
 void* fe_b200_tsne_stream(fe_b200_tsne* h) { return h == nullptr ? nullptr : h->impl->stream; }
 
 int fe_b200_tsne_profile(fe_b200_tsne* h, int enable) {
   if (h == nullptr) return 1;
   h->impl->profile = enable != 0;
-  for (int k = 0; k < 8; ++k) {
+  for (int k = 0; k < fe::kKindCount; ++k) {
     h->impl->kernel_ms[k] = 0.0;
     h->impl->kernel_launches[k] = 0;
   }
@@ -878,12 +965,18 @@ int fastembedr_cuda_exact_tsne_from_knn(const int*, const double*, const float*,
                                         int, float*) {
   return out_of_scope("fastembedr_cuda_exact_tsne_from_knn");
 }
-int fastembedr_cuda_landmark_tsne_from_device_knn(const int*, const float*, int, const float*,
-                                                  const float*, const float*, int, int, int, int,
-                                                  float, int, int, float, float, float, float, float,
-                                                  float, float, int, int, unsigned int, int, float,
-                                                  float, float*) {
-  return out_of_scope("fastembedr_cuda_landmark_tsne_from_device_knn");
+int fastembedr_cuda_landmark_tsne_from_device_knn(
+    const int* device_indices, const float* device_distances, int index_offset, const float* reference_data,
+    const float* query_data, const float* reference_layout, int n_reference, int n_query, int n_features, int k,
+    float perplexity, int n_iter, int early_exaggeration_iter, float learning_rate, float early_exaggeration,
+    float exaggeration, float initial_momentum, float final_momentum, float max_grad_norm, float max_step_norm,
+    int n_negatives, int exact_repulsion_threshold, unsigned int seed, int affine_neighbors, float affine_ridge,
+    float max_extrapolation, float* out) {
+  return fe::landmark_tsne(device_indices, device_distances, index_offset, reference_data, query_data,
+                           reference_layout, n_reference, n_query, n_features, k, perplexity, n_iter,
+                           early_exaggeration_iter, learning_rate, early_exaggeration, exaggeration,
+                           initial_momentum, final_momentum, max_grad_norm, max_step_norm, n_negatives,
+                           exact_repulsion_threshold, seed, affine_neighbors, affine_ridge, max_extrapolation, out);
 }
 int fastembedr_cuda_landmark_umap_from_device_knn(const int*, const float*, int, const float*,
                                                   const float*, const float*, const int*, const int*,

@@ -134,6 +134,7 @@ __device__ __forceinline__ float warp_max(float v) {
 // Streaming (evict-first) 16-byte loads for data read once per pass.
 __device__ __forceinline__ int4 ld_stream(const int4* p) { return __ldcs(p); }
 __device__ __forceinline__ float4 ld_stream(const float4* p) { return __ldcs(p); }
+__device__ __forceinline__ uint2 ld_stream(const uint2* p) { return __ldcs(p); }
 
 // The reference's counter-based uniform in [-1, 1] for coordinate `col` of
 // point `row` (deterministic_unit, src/embedding_cuda_kernels.cpp:266-274):

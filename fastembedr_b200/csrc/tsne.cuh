@@ -62,6 +62,9 @@ struct LayoutStats {
   unsigned int row_groups_taken;  // grad_update_kernel work counter
   unsigned int fft_counter;       // last-block tickets
   unsigned int stats_counter;
+  unsigned int stage_taken;       // staged_grad_kernel work counter
+  unsigned int stage_count;       // staged row blocks (set at each reorder)
+  unsigned int group_count;       // 32-row groups left to grad_update_kernel (set at each reorder)
   // Derived once per layout by the statistics kernel (grid_geometry and
   // charge_scales below) and read by every later kernel of the iteration,
   // instead of every thread re-deriving them with double divisions.
@@ -136,8 +139,27 @@ __device__ __forceinline__ Cell grid_cell(float px, float py, const GridGeom& q,
 // row needs more passes than this is run row by row with 32 lanes instead.
 constexpr int kLongRoundPasses = 6;
 
+// Staged row blocks (staged_grad_kernel; opt-in, FASTEMBEDR_B200_STAGED_ATTRACTION=1).
+// Internal rows are cut into blocks of kStageRows; a block whose entries
+// reference at most kStageCap distinct points (its column union) and span at
+// most kStageSpan internal indices gets its union list and 16-bit union-local
+// column indices at each reorder, and its attraction gathers y_j from the
+// union staged in shared memory instead of from L2.  Other blocks stay with
+// grad_update_kernel.  Results are bit-identical either way.  On the
+// benchmark's mixtures a union holds each point only 1.2-1.6 times, and a
+// block waits for its longest round, so the staged kernel measured slower
+// (0.80 ms against 0.60 ms per iteration at N = 1M); it stays off by default.
+constexpr int kStageRows = 128;
+constexpr int kStageRounds = kStageRows / 4;
+constexpr int kStageThreads = 1024;
+constexpr int kStageCap = 24576;        // 192 KB of float2 in shared memory
+constexpr int kStageSpan = 1 << 20;     // bitmap of the build: 128 KB
+constexpr int kStageBuildThreads = 512;
+
 // Exactly one of these modes is run by the fused gradient kernel.
 enum GradMode { kGradUpdate = 0, kGradOnly = 1 };
+
+constexpr int kKindCountMax = 9;
 
 struct TsneSession {
   int device = 0;
@@ -161,6 +183,20 @@ struct TsneSession {
   int* row_ptr4 = nullptr;         // n + 1 offsets, in 16-byte groups
   int4* csr4_col = nullptr;
   float4* csr4_val = nullptr;
+  // Staged row blocks: per entry (csr4 positions) the index of its column in
+  // the block's union; per block the union list (sorted internal indices, at
+  // the block's first entry position, since a union is never longer than its
+  // block's entries), {union offset, union size, staged?, entries} and the
+  // order of its 32 four-row rounds (most expensive first).
+  uint2* stage_col16 = nullptr;    // four 16-bit indices per csr4 group
+  int* stage_union = nullptr;
+  int4* stage_meta = nullptr;
+  unsigned char* stage_rounds = nullptr;
+  unsigned int* stage_cost = nullptr;
+  unsigned int* stage_cost_sorted = nullptr;
+  int* stage_ids = nullptr;
+  int* stage_order = nullptr;      // staged blocks, most expensive first
+  bool stage_enabled = true;       // FASTEMBEDR_B200_STAGED_ATTRACTION
   long long csr4_groups = 0;       // groups in use
   long long csr4_capacity = 0;     // groups allocated
   float2* y[2] = {nullptr, nullptr};
@@ -168,6 +204,7 @@ struct TsneSession {
   float2* update = nullptr;
   float2* gains = nullptr;
   float2* grad_out = nullptr;  // kGradOnly target
+  float2* attraction = nullptr;  // staged rows' attraction sums, for staged_finish_kernel
   LayoutStats* stats = nullptr;
   double* update_partials = nullptr;  // 6 per block
   double* z_partials = nullptr;       // one per grid row
@@ -186,8 +223,8 @@ struct TsneSession {
   bool profile = false;
   std::vector<cudaEvent_t> events;
   std::vector<int> event_kind;
-  double kernel_ms[8] = {0};
-  long long kernel_launches[8] = {0};
+  double kernel_ms[kKindCountMax] = {0};
+  long long kernel_launches[kKindCountMax] = {0};
   long long iterations_run = 0;
 
   // Captured iteration chunks, keyed by chunk length, parameter set and the
@@ -231,11 +268,11 @@ struct TsneSession {
   // block of rows_per_rank rows: it splats, attracts and updates only those,
   // the charge grid is summed with one all-reduce and the updated rows are
   // all-gathered, in place, once per iteration.  Blocks are whole multiples
-  // of 32 rows, so a warp never straddles two ranks and the splat combines the
-  // same lanes as an unsharded run; point arrays have room for the padding of
-  // the last block (kPadRows).
+  // of kStageRows (128) rows, so neither a warp nor a staged row block
+  // straddles two ranks and the splat combines the same lanes as an unsharded
+  // run; point arrays have room for the padding of the last block (kPadRows).
   static constexpr int kMaxRanks = 256;
-  static constexpr int kPadRows = 32 * kMaxRanks;
+  static constexpr int kPadRows = kStageRows * kMaxRanks;
   bool sharded = false;
   int shard_ranks = 1;
   int shard_rank = 0;
@@ -274,7 +311,8 @@ enum KernelKind {
   kKindChargeSum = 5,     // sharded: all-reduce of the charge grid
   kKindLayoutGather = 6,  // sharded: all-gather of the updated rows
   kKindLayoutStats = 7,   // statistics of the new layout
-  kKindCount = 8
+  kKindStagedGrad = 8,    // attraction + update of the staged row blocks
+  kKindCount = 9
 };
 const char* kernel_kind_name(int kind);
 
@@ -397,5 +435,22 @@ int launch_center_output(TsneSession* s, float2* out);
 
 // CPU grid-size policy (tsne_fft_grid_size, src/tsne_neighbors.cpp:392-398).
 int default_grid_size(int n);
+
+// ---- PCA start of the PCA-initialised entry points (pca.cu) ----
+// values: host, n x p column-major (double or float).  Writes the scaled
+// two-component scores, row-major, to d_out (n float2) on stream st.
+int pca_start_layout(const void* values, bool values_double, int n, int p, cudaStream_t st, float2* d_out);
+
+// ---- openTSNE transform against a fixed reference layout (landmark.cu) ----
+// fastembedr_cuda_landmark_tsne_from_device_knn: device KNN of the queries
+// into the reference (column-major n_query x k), host data and layout in R's
+// column-major order, host output row-major n_query x 2.
+int landmark_tsne(const int* device_indices, const float* device_distances, int index_offset,
+                  const float* reference_data, const float* query_data, const float* reference_layout,
+                  int n_reference, int n_query, int n_features, int k, float perplexity, int n_iter,
+                  int early_exaggeration_iter, float learning_rate, float early_exaggeration, float exaggeration,
+                  float initial_momentum, float final_momentum, float max_grad_norm, float max_step_norm,
+                  int n_negatives, int exact_repulsion_threshold, unsigned int seed, int affine_neighbors,
+                  float affine_ridge, float max_extrapolation, float* out);
 
 }  // namespace fe

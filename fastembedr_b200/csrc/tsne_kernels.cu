@@ -274,7 +274,11 @@ __global__ void __launch_bounds__(kSplatThreads) splat_kernel(float2* __restrict
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
   const GridGeom q = stats->geom;
   const ChargeScales sc = stats->scales;
-  if (i == 0) stats->row_groups_taken = 0u;  // work counter of this iteration's grad_update_kernel
+  if (i == 0) {
+    // work counters of this iteration's attraction kernels
+    stats->row_groups_taken = 0u;
+    stats->stage_taken = 0u;
+  }
   int key = -1;
   Cell c{0, 0, 0.f, 0.f};
   float v[12];
@@ -633,6 +637,60 @@ __device__ __forceinline__ float3 gather_potentials(const float4* __restrict__ p
   return r;
 }
 
+// The fused epilogue of one row: repulsive gather, gains / momentum / step
+// clip (apply_open_tsne_update_f, src/tsne_neighbors.cpp:1213-1244), layout
+// write; or the gradient alone (kGradOnly).  (ax, ay) is the row's attraction.
+__device__ __forceinline__ void finish_row(int row, float ax, float ay, const float2* __restrict__ y,
+                                           float2* __restrict__ y_next, float2* __restrict__ update,
+                                           float2* __restrict__ gains, float2* __restrict__ grad_out,
+                                           const float4* __restrict__ pot, const LayoutStats* __restrict__ stats,
+                                           const UpdateParams& prm) {
+  const float2 yi = y[row];
+  const GridGeom q = stats->geom;
+  const Cell c = grid_cell(yi.x, yi.y, q, prm.g);
+  const float3 ph = gather_potentials(pot, c, prm.g);
+  const float inv_z = stats->inv_z;
+  const float gx = -(yi.x * ph.x - ph.y) * inv_z + ax;
+  const float gy = -(yi.y * ph.x - ph.z) * inv_z + ay;
+  if (prm.mode == kGradOnly) {
+    grad_out[row] = make_float2(gx, gy);
+    return;
+  }
+  float2 u = update[row];
+  float2 gn = gains[row];
+  if (sign_f(u.x) != sign_f(gx)) gn.x += 0.2f;
+  else gn.x = gn.x * 0.8f + prm.min_gain;
+  if (gn.x < prm.min_gain) gn.x = prm.min_gain;
+  u.x = prm.momentum * u.x - prm.learning_rate * gn.x * gx;
+  if (sign_f(u.y) != sign_f(gy)) gn.y += 0.2f;
+  else gn.y = gn.y * 0.8f + prm.min_gain;
+  if (gn.y < prm.min_gain) gn.y = prm.min_gain;
+  u.y = prm.momentum * u.y - prm.learning_rate * gn.y * gy;
+  float norm_sq = 0.0f;
+  norm_sq += u.x * u.x;
+  norm_sq += u.y * u.y;
+  if (isfinite(prm.max_step_norm) && prm.max_step_norm > 0.0f &&
+      norm_sq > prm.max_step_norm * prm.max_step_norm) {
+    if (isfinite(norm_sq)) {
+      const float scale = prm.max_step_norm / sqrtf(fmaxf(norm_sq, FLT_MIN));
+      u.x *= scale;
+      u.y *= scale;
+    } else {
+      // An infinite step (Z collapsed to FLT_MIN): the reference's clip would
+      // form inf * 0; keep the step's direction at the maximum length instead.
+      const float sx = isinf(u.x) ? copysignf(1.0f, u.x) : 0.0f;
+      const float sy = isinf(u.y) ? copysignf(1.0f, u.y) : 0.0f;
+      const float len = sqrtf(sx * sx + sy * sy);
+      u.x = len > 0.0f ? sx / len * prm.max_step_norm : 0.0f;
+      u.y = len > 0.0f ? sy / len * prm.max_step_norm : 0.0f;
+    }
+  }
+  const float2 yn = make_float2(yi.x + u.x, yi.y + u.y);
+  update[row] = u;
+  gains[row] = gn;
+  y_next[row] = yn;
+}
+
 // Attraction over the internal-order P, eight lanes per row: a warp takes a
 // block of 32 rows in 8 rounds of 4 rows.  Each pass a lane streams two
 // 16-byte groups of columns and two of values (stride 8 groups within its
@@ -721,7 +779,8 @@ __global__ void __launch_bounds__(256, 4) grad_update_kernel(
   const int sub = lane >> 3;  // which of the 4 rows of a round
   const int sl = lane & 7;    // lane within the row
   const float ex = prm.exaggeration;
-  const int groups = (prm.row_end - prm.row_begin + 31) >> 5;
+  // 32-row groups not taken by staged_grad_kernel (set at each reorder).
+  const int groups = static_cast<int>(stats->group_count);
   for (;;) {
     int ticket = 0;
     if (lane == 0) ticket = static_cast<int>(atomicAdd(&stats->row_groups_taken, 1u));
@@ -779,52 +838,204 @@ __global__ void __launch_bounds__(256, 4) grad_update_kernel(
     // Epilogue: lane L finishes row row0 + 4 (L % 8) + L / 8.
     const int row = row0 + 4 * sl + sub;
     if (row >= prm.row_end) continue;
-    const float2 yi = y[row];
-    const GridGeom q = stats->geom;
-    const Cell c = grid_cell(yi.x, yi.y, q, prm.g);
-    const float3 ph = gather_potentials(pot, c, prm.g);
-    const float inv_z = stats->inv_z;
-    const float gx = -(yi.x * ph.x - ph.y) * inv_z + my_ax;
-    const float gy = -(yi.y * ph.x - ph.z) * inv_z + my_ay;
-    if (prm.mode == kGradOnly) {
-      grad_out[row] = make_float2(gx, gy);
-      continue;
+    finish_row(row, my_ax, my_ay, y, y_next, update, gains, grad_out, pot, stats, prm);
+  }
+}
+
+
+// ---- staged row blocks ------------------------------------------------------
+
+constexpr int kStagePerThread = kStageCap / kStageThreads;
+static_assert(kStagePerThread * kStageThreads == kStageCap, "union capacity is a whole number of passes");
+constexpr int kStageBatch = 8;  // union points whose indices a thread holds at once
+static_assert(kStagePerThread % kStageBatch == 0, "whole batches");
+
+// 8-byte asynchronous copy global -> shared (through L1), and the wait for all
+// of this thread's outstanding copies.
+__device__ __forceinline__ void cp_async8(float2* dst_smem, const float2* src) {
+  const unsigned int d = static_cast<unsigned int>(__cvta_generic_to_shared(dst_smem));
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 8;\n" ::"r"(d), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.commit_group;\ncp.async.wait_group 0;\n" ::: "memory");
+}
+
+// attract4 with y_j from the staged union: four 16-bit union indices.  The
+// per-entry arithmetic and its order are attract4's, so a row's sum is the
+// same bits whichever kernel computes it.
+__device__ __forceinline__ void attract4_staged(float yix, float yiy, uint2 c, float4 v, float ex,
+                                                const float2* __restrict__ ys, float& ax, float& ay) {
+  // Union indices are below the block's union size by construction; the
+  // clamp keeps every shared-memory read inside the staged array regardless.
+  const float2 g[4] = {ys[min(c.x & 0xffffu, kStageCap - 1u)], ys[min(c.x >> 16, kStageCap - 1u)],
+                       ys[min(c.y & 0xffffu, kStageCap - 1u)], ys[min(c.y >> 16, kStageCap - 1u)]};
+  const float pv[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const float dx = yix - g[q].x;
+    const float dy = yiy - g[q].y;
+    float d2 = 0.0f;
+    d2 += dx * dx;
+    d2 += dy * dy;
+    const float qq = 1.0f / (1.0f + d2);
+    const float w = ex * pv[q] * qq;
+    ax += w * dx;
+    ay += w * dy;
+  }
+}
+
+// stream_row over the union-local column indices (same lane/group assignment
+// and prefetch as stream_row, hence the same summation order).
+template <int S>
+__device__ __forceinline__ void stream_row_staged(int beg, int end, int l, int passes, float2 yi, float ex,
+                                                  const uint2* __restrict__ col16, const float4* __restrict__ val4,
+                                                  const float2* __restrict__ ys, float& ax, float& ay) {
+  const uint2 zero_c = make_uint2(0u, 0u);
+  const float4 zero_v = make_float4(0.f, 0.f, 0.f, 0.f);
+  int e = beg + l;
+  uint2 c0 = e < end ? ld_stream(col16 + e) : zero_c;
+  float4 v0 = e < end ? ld_stream(val4 + e) : zero_v;
+  uint2 c1 = e + S < end ? ld_stream(col16 + e + S) : zero_c;
+  float4 v1 = e + S < end ? ld_stream(val4 + e + S) : zero_v;
+  for (int p = 0; p < passes; ++p) {
+    const int en = e + 2 * S;
+    const uint2 nc0 = en < end ? ld_stream(col16 + en) : zero_c;
+    const float4 nv0 = en < end ? ld_stream(val4 + en) : zero_v;
+    const uint2 nc1 = en + S < end ? ld_stream(col16 + en + S) : zero_c;
+    const float4 nv1 = en + S < end ? ld_stream(val4 + en + S) : zero_v;
+    attract4_staged(yi.x, yi.y, c0, v0, ex, ys, ax, ay);
+    attract4_staged(yi.x, yi.y, c1, v1, ex, ys, ax, ay);
+    c0 = nc0;
+    v0 = nv0;
+    c1 = nc1;
+    v1 = nv1;
+    e = en;
+  }
+}
+
+// One block per SM, persistent.  A block takes staged row blocks (kStageRows
+// rows each, most expensive first) from a global counter; per row block it
+//   1. stages y of the block's column union in shared memory -- one union
+//      point per thread, the union list sorted, so a warp's 32 loads touch a
+//      few lines of L2 instead of 32 (the union of a 128-row block holds its
+//      entries' columns at 0.2-0.27 lines per entry);
+//   2. runs the block's 32 four-row rounds (eight lanes per row, a hub round
+//      row by row with 32 lanes), taken by the warps from a shared counter in
+//      the order stored at the reorder, gathering y_j from shared memory;
+//   3. writes each row's attraction sum; staged_finish_kernel then finishes
+//      the rows (repulsive gather and update) with one thread per row.
+__global__ void __launch_bounds__(kStageThreads, 1) staged_grad_kernel(
+    const int* __restrict__ row_ptr4, const uint2* __restrict__ col16, const float4* __restrict__ val4,
+    const int* __restrict__ stage_union, const int4* __restrict__ stage_meta, const int* __restrict__ stage_order,
+    const unsigned char* __restrict__ stage_rounds, const float2* __restrict__ y,
+    float2* __restrict__ attraction, LayoutStats* __restrict__ stats, UpdateParams prm) {
+  extern __shared__ float2 ys[];  // kStageCap points
+  __shared__ float2 acc[kStageRows];
+  __shared__ int s_ticket;
+  __shared__ int s_round;
+  const int lane = threadIdx.x & 31;
+  const int sub = lane >> 3;
+  const int sl = lane & 7;
+  const float ex = prm.exaggeration;
+  const int count = static_cast<int>(stats->stage_count);
+  for (;;) {
+    if (threadIdx.x == 0) {
+      s_ticket = static_cast<int>(atomicAdd(&stats->stage_taken, 1u));
+      s_round = 0;
     }
-    // apply_open_tsne_update_f, src/tsne_neighbors.cpp:1213-1244.
-    float2 u = update[row];
-    float2 gn = gains[row];
-    if (sign_f(u.x) != sign_f(gx)) gn.x += 0.2f;
-    else gn.x = gn.x * 0.8f + prm.min_gain;
-    if (gn.x < prm.min_gain) gn.x = prm.min_gain;
-    u.x = prm.momentum * u.x - prm.learning_rate * gn.x * gx;
-    if (sign_f(u.y) != sign_f(gy)) gn.y += 0.2f;
-    else gn.y = gn.y * 0.8f + prm.min_gain;
-    if (gn.y < prm.min_gain) gn.y = prm.min_gain;
-    u.y = prm.momentum * u.y - prm.learning_rate * gn.y * gy;
-    float norm_sq = 0.0f;
-    norm_sq += u.x * u.x;
-    norm_sq += u.y * u.y;
-    if (isfinite(prm.max_step_norm) && prm.max_step_norm > 0.0f &&
-        norm_sq > prm.max_step_norm * prm.max_step_norm) {
-      if (isfinite(norm_sq)) {
-        const float scale = prm.max_step_norm / sqrtf(fmaxf(norm_sq, FLT_MIN));
-        u.x *= scale;
-        u.y *= scale;
+    __syncthreads();
+    const int ticket = s_ticket;
+    if (ticket >= count) break;  // block-uniform
+    const int b = __ldg(stage_order + ticket);
+    const int4 meta = __ldg(stage_meta + b);
+    const int row0 = prm.row_begin + b * kStageRows;
+    {
+      // All union indices of this thread first (independent coalesced loads),
+      // then the gathers as asynchronous global-to-shared copies: two memory
+      // latencies per block instead of one per union point.
+      const int* __restrict__ un = stage_union + meta.x;
+#pragma unroll 1
+      for (int j0 = 0; j0 < kStagePerThread; j0 += kStageBatch) {
+        if (static_cast<int>(threadIdx.x) + j0 * kStageThreads >= meta.y) break;
+        int idx[kStageBatch];
+#pragma unroll
+        for (int j = 0; j < kStageBatch; ++j) {
+          const int u = static_cast<int>(threadIdx.x) + (j0 + j) * kStageThreads;
+          idx[j] = u < meta.y ? __ldg(un + u) : 0;
+        }
+#pragma unroll
+        for (int j = 0; j < kStageBatch; ++j) {
+          const int u = static_cast<int>(threadIdx.x) + (j0 + j) * kStageThreads;
+          if (u < meta.y) cp_async8(ys + u, y + idx[j]);
+        }
+      }
+      cp_async_wait_all();
+    }
+    __syncthreads();
+    for (;;) {
+      int r = 0;
+      if (lane == 0) r = atomicAdd(&s_round, 1);
+      r = __shfl_sync(0xffffffffu, r, 0);
+      if (r >= kStageRounds) break;
+      const int round = __ldg(stage_rounds + static_cast<size_t>(b) * kStageRounds + r);
+      const int row = row0 + 4 * round + sub;
+      const bool rv = row < prm.row_end;
+      const int beg = rv ? __ldg(row_ptr4 + row) : 0;
+      const int end = rv ? __ldg(row_ptr4 + row + 1) : 0;
+      const float2 yi = rv ? y[row] : make_float2(0.f, 0.f);
+      int passes = (end - beg + 15) >> 4;
+      passes = max(passes, __shfl_xor_sync(0xffffffffu, passes, 8));
+      passes = max(passes, __shfl_xor_sync(0xffffffffu, passes, 16));
+      if (passes <= kLongRoundPasses) {
+        float ax = 0.f, ay = 0.f;
+        stream_row_staged<8>(beg, end, sl, passes, yi, ex, col16, val4, ys, ax, ay);
+#pragma unroll
+        for (int o = 4; o > 0; o >>= 1) {
+          ax += __shfl_xor_sync(0xffffffffu, ax, o);
+          ay += __shfl_xor_sync(0xffffffffu, ay, o);
+        }
+        if (sl == 0) acc[4 * round + sub] = make_float2(ax, ay);
       } else {
-        // An infinite step (Z collapsed to FLT_MIN): the reference's clip would
-        // form inf * 0; keep the step's direction at the maximum length instead.
-        const float sx = isinf(u.x) ? copysignf(1.0f, u.x) : 0.0f;
-        const float sy = isinf(u.y) ? copysignf(1.0f, u.y) : 0.0f;
-        const float len = sqrtf(sx * sx + sy * sy);
-        u.x = len > 0.0f ? sx / len * prm.max_step_norm : 0.0f;
-        u.y = len > 0.0f ? sy / len * prm.max_step_norm : 0.0f;
+#pragma unroll 1
+        for (int sr = 0; sr < 4; ++sr) {
+          const int row_s = row0 + 4 * round + sr;
+          const bool vs = row_s < prm.row_end;
+          const int beg_s = vs ? __ldg(row_ptr4 + row_s) : 0;
+          const int end_s = vs ? __ldg(row_ptr4 + row_s + 1) : 0;
+          const float2 yis = vs ? y[row_s] : make_float2(0.f, 0.f);
+          float ax = 0.f, ay = 0.f;
+          stream_row_staged<32>(beg_s, end_s, lane, (end_s - beg_s + 63) >> 6, yis, ex, col16, val4, ys, ax, ay);
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1) {
+            ax += __shfl_xor_sync(0xffffffffu, ax, o);
+            ay += __shfl_xor_sync(0xffffffffu, ay, o);
+          }
+          if (lane == 0) acc[4 * round + sr] = make_float2(ax, ay);
+        }
       }
     }
-    const float2 yn = make_float2(yi.x + u.x, yi.y + u.y);
-    update[row] = u;
-    gains[row] = gn;
-    y_next[row] = yn;
+    __syncthreads();
+    if (threadIdx.x < kStageRows) {
+      const int row = row0 + static_cast<int>(threadIdx.x);
+      if (row < prm.row_end) attraction[row] = acc[threadIdx.x];
+    }
   }
+}
+
+// The staged rows' epilogue (repulsive gather and update), one thread per row
+// of each staged block: a streaming pass kept out of staged_grad_kernel, whose
+// single block per SM would otherwise idle through its dependent loads.
+__global__ void __launch_bounds__(kStageRows) staged_finish_kernel(
+    const int* __restrict__ stage_order, const float2* __restrict__ attraction, const float2* __restrict__ y,
+    float2* __restrict__ y_next, float2* __restrict__ update, float2* __restrict__ gains,
+    float2* __restrict__ grad_out, const float4* __restrict__ pot, const LayoutStats* __restrict__ stats,
+    UpdateParams prm) {
+  if (static_cast<int>(blockIdx.x) >= static_cast<int>(stats->stage_count)) return;
+  const int b = stage_order[blockIdx.x];
+  const int row = prm.row_begin + b * kStageRows + static_cast<int>(threadIdx.x);
+  if (row >= prm.row_end) return;
+  const float2 a = attraction[row];
+  finish_row(row, a.x, a.y, y, y_next, update, gains, grad_out, pot, stats, prm);
 }
 
 __global__ void center_copy_kernel(const float2* __restrict__ y, const LayoutStats* __restrict__ stats,
@@ -853,6 +1064,7 @@ const char* kernel_kind_name(int kind) {
     case kKindChargeSum: return "charge_allreduce";
     case kKindLayoutGather: return "layout_allgather";
     case kKindLayoutStats: return "layout_stats_kernel";
+    case kKindStagedGrad: return "staged_grad_kernel";
     default: return "?";
   }
 }
@@ -870,6 +1082,9 @@ int configure_kernels(TsneSession* s) {
                                static_cast<int>(cols_smem)), "cudaFuncSetAttribute(fft_cols_kernel)");
   FE_CUDA(cudaFuncSetAttribute(fft_rows_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                static_cast<int>(rows_smem)), "cudaFuncSetAttribute(fft_rows_fwd_kernel)");
+  FE_CUDA(cudaFuncSetAttribute(staged_grad_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               static_cast<int>(kStageCap * sizeof(float2))),
+          "cudaFuncSetAttribute(staged_grad_kernel)");
   return 0;
 }
 
@@ -939,10 +1154,22 @@ int launch_iteration(TsneSession* s, GradMode mode, float exaggeration, float mo
         s->colspec, s->charges, s->n, g, m, lm, s->twiddle, s->pot, s->z_partials, s->stats);
     FE_LAUNCH("fft_rows_inv_kernel");
   }
+  const UpdateParams prm{s->n, s->row_begin, s->row_end, g, exaggeration, momentum,
+                         learning_rate, min_gain, max_step_norm, static_cast<int>(mode)};
+  if (s->stage_enabled) {
+    ProfileScope ps(s, kKindStagedGrad);
+    staged_grad_kernel<<<sm_count(), kStageThreads, kStageCap * sizeof(float2), s->stream>>>(
+        s->row_ptr4, s->stage_col16, s->csr4_val, s->stage_union, s->stage_meta, s->stage_order,
+        s->stage_rounds, s->y[s->cur], s->attraction, s->stats, prm);
+    FE_LAUNCH("staged_grad_kernel");
+    const int blocks = std::max(1, (s->row_end - s->row_begin + kStageRows - 1) / kStageRows);
+    staged_finish_kernel<<<blocks, kStageRows, 0, s->stream>>>(
+        s->stage_order, s->attraction, s->y[s->cur], s->y[s->cur ^ 1], s->update, s->gains, s->grad_out,
+        s->pot, s->stats, prm);
+    FE_LAUNCH("staged_finish_kernel");
+  }
   {
     ProfileScope ps(s, kKindGradUpdate);
-    UpdateParams prm{s->n, s->row_begin, s->row_end, g, exaggeration, momentum,
-                     learning_rate, min_gain, max_step_norm, static_cast<int>(mode)};
     grad_update_kernel<<<s->update_blocks, s->update_threads, 0, s->stream>>>(
         s->row_ptr4, s->csr4_col, s->csr4_val, s->y[s->cur], s->y[s->cur ^ 1], s->update,
         s->gains, s->grad_out, s->pot, s->stats, s->group_order, prm);

@@ -21,6 +21,7 @@
 #include <cub/cub.cuh>
 
 #include <algorithm>
+#include <climits>
 
 namespace fe {
 namespace {
@@ -120,9 +121,16 @@ __global__ void permute_in_kernel(const float2* __restrict__ in, const int* __re
 // four entries) plus one; a round past kLongRoundPasses runs its rows one by
 // one with 32 lanes (64 groups a pass), plus one per row.
 __global__ void group_cost_kernel(const int* __restrict__ row_ptr4, int row_begin, int row_end, int groups,
-                                  unsigned int* __restrict__ cost, int* __restrict__ ids) {
+                                  const int4* __restrict__ stage_meta, unsigned int* __restrict__ cost,
+                                  int* __restrict__ ids, unsigned int* __restrict__ group_count) {
   const int grp = blockIdx.x * blockDim.x + threadIdx.x;
   if (grp >= groups) return;
+  if (stage_meta != nullptr && stage_meta[(grp * 32) / kStageRows].z) {
+    // Staged row block: its rows belong to staged_grad_kernel; sorted last.
+    cost[grp] = 0u;
+    ids[grp] = grp;
+    return;
+  }
   const int row0 = row_begin + grp * 32;
   unsigned int total = 0;
   for (int round = 0; round < 8; ++round) {
@@ -140,18 +148,191 @@ __global__ void group_cost_kernel(const int* __restrict__ row_ptr4, int row_begi
 #define FE_LPT_THRESHOLD 0
 #endif
   // Groups at or below the threshold keep their (Morton) order behind the
-  // expensive ones: the descending sort is stable.
-  cost[grp] = total > FE_LPT_THRESHOLD ? total : 0u;
+  // expensive ones (the descending sort is stable), ahead of staged groups.
+  cost[grp] = total > FE_LPT_THRESHOLD ? total : 1u;
   ids[grp] = grp;
+  atomicAdd(group_count, 1u);
+}
+
+// Cost estimate of one four-row round (group_cost_kernel's per-round term).
+__device__ __forceinline__ unsigned int round_cost(const int* __restrict__ row_ptr4, int row0, int row_end) {
+  int passes = 0, wide = 0;
+  for (int sub = 0; sub < 4; ++sub) {
+    const int row = row0 + sub;
+    if (row >= row_end) continue;
+    const int len = row_ptr4[row + 1] - row_ptr4[row];
+    passes = max(passes, (len + 15) >> 4);
+    wide += ((len + 63) >> 6) + 1;
+  }
+  return passes <= kLongRoundPasses ? static_cast<unsigned int>(passes) + 1u : static_cast<unsigned int>(wide);
+}
+
+// One block per staged row block candidate (kStageRows internal rows, whose
+// entries are contiguous in the internal copy of P).
+//   1. bounds [lo, hi] of the block's column indices; a span above kStageSpan
+//      leaves the block to grad_update_kernel;
+//   2. a bitmap of the columns present, then the union size as the sum of
+//      popcounts (an exclusive scan gives each bitmap word its union prefix);
+//      a union above kStageCap, or one spread over more than 0.6 lines of y
+//      per entry, leaves the block to grad_update_kernel;
+//   3. the union list (sorted internal indices) at the block's first entry
+//      position, and each entry's union index: prefix of its word plus the
+//      set bits below its own;
+//   4. {union offset, union size, staged, entries}, a cost for the block order
+//      and the block's rounds sorted by cost, most expensive first.
+__global__ void __launch_bounds__(kStageBuildThreads, 1) stage_build_kernel(
+    const int* __restrict__ row_ptr4, const int* __restrict__ csr_col, int row_begin, int row_end,
+    unsigned short* __restrict__ col16, int* __restrict__ stage_union, int4* __restrict__ stage_meta,
+    unsigned char* __restrict__ stage_rounds, unsigned int* __restrict__ stage_cost, int* __restrict__ stage_ids,
+    unsigned int* __restrict__ stage_count) {
+  extern __shared__ unsigned int bits[];  // kStageSpan / 32 words, then the per-word prefixes
+  unsigned short* wpref = reinterpret_cast<unsigned short*>(bits + kStageSpan / 32);
+  __shared__ int s_lo[kStageBuildThreads / 32], s_hi[kStageBuildThreads / 32];
+  __shared__ int s_scan[kStageBuildThreads / 32];
+  __shared__ unsigned int s_rcost[kStageRounds];
+  const int b = blockIdx.x;
+  const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+  constexpr int nw = kStageBuildThreads / 32;
+  const int r0 = row_begin + b * kStageRows;
+  const int r1 = min(row_end, r0 + kStageRows);
+  const long long e0 = static_cast<long long>(row_ptr4[r0]) * 4;
+  const long long e1 = static_cast<long long>(row_ptr4[r1]) * 4;
+  if (tid < kStageRounds) s_rcost[tid] = round_cost(row_ptr4, r0 + 4 * tid, r1);
+
+  int lo = INT_MAX, hi = INT_MIN;
+  for (long long e = e0 + tid; e < e1; e += kStageBuildThreads) {
+    const int c = csr_col[e];
+    lo = min(lo, c);
+    hi = max(hi, c);
+  }
+  lo = __reduce_min_sync(0xffffffffu, lo);
+  hi = __reduce_max_sync(0xffffffffu, hi);
+  if (lane == 0) {
+    s_lo[wid] = lo;
+    s_hi[wid] = hi;
+  }
+  __syncthreads();
+  lo = INT_MAX;
+  hi = INT_MIN;
+  for (int w = 0; w < nw; ++w) {
+    lo = min(lo, s_lo[w]);
+    hi = max(hi, s_hi[w]);
+  }
+  const long long span = e1 > e0 ? static_cast<long long>(hi) - lo + 1 : 0;
+  bool staged = span <= kStageSpan;
+  int total = 0;
+  if (staged && span > 0) {  // block-uniform
+    const int words = static_cast<int>((span + 31) >> 5);
+    for (int w = tid; w < words; w += kStageBuildThreads) bits[w] = 0u;
+    __syncthreads();
+    for (long long e = e0 + tid; e < e1; e += kStageBuildThreads) {
+      const int c = csr_col[e] - lo;
+      atomicOr(&bits[c >> 5], 1u << (c & 31));
+    }
+    __syncthreads();
+    const int per = (words + kStageBuildThreads - 1) / kStageBuildThreads;
+    const int w0 = min(words, tid * per);
+    const int w1 = min(words, w0 + per);
+    int mine = 0, lines = 0;
+    for (int w = w0; w < w1; ++w) {
+      const unsigned int m = bits[w];
+      mine += __popc(m);
+      lines += ((m & 0xffffu) != 0u) + ((m >> 16) != 0u);  // 16 points of y per 128-byte line
+    }
+    lines = __reduce_add_sync(0xffffffffu, lines);
+    if (lane == 0) s_lo[wid] = lines;  // the bounds are no longer needed
+    int incl = mine;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int v = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += v;
+    }
+    if (lane == 31) s_scan[wid] = incl;
+    __syncthreads();
+    if (wid == 0) {
+      int v = lane < nw ? s_scan[lane] : 0;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int u = __shfl_up_sync(0xffffffffu, v, o);
+        if (lane >= o) v += u;
+      }
+      if (lane < nw) s_scan[lane] = v;
+    }
+    __syncthreads();
+    total = s_scan[nw - 1];
+    int all_lines = 0;
+    for (int w = 0; w < nw; ++w) all_lines += s_lo[w];
+    // Staging pays when the union's points share lines: at most 0.6 lines per
+    // entry (ordered layouts: 0.12-0.27; the caller's order before the first
+    // spatial reorder: about 1).
+    staged = total <= kStageCap && 5LL * all_lines <= 3LL * (e1 - e0);
+    if (staged) {
+      int run = incl - mine + (wid > 0 ? s_scan[wid - 1] : 0);
+      for (int w = w0; w < w1; ++w) {
+        wpref[w] = static_cast<unsigned short>(run);
+        for (unsigned int m = bits[w]; m; m &= m - 1u) {
+          stage_union[e0 + run] = lo + 32 * w + (__ffs(m) - 1);
+          ++run;
+        }
+      }
+    }
+    __syncthreads();
+    if (staged) {
+      for (long long e = e0 + tid; e < e1; e += kStageBuildThreads) {
+        const int c = csr_col[e] - lo;
+        const int w = c >> 5;
+        const unsigned int below = bits[w] & ((1u << (c & 31)) - 1u);
+        col16[e] = static_cast<unsigned short>(wpref[w] + __popc(below));
+      }
+    }
+  }
+  __syncthreads();
+  if (tid == 0) {
+    stage_meta[b] = make_int4(static_cast<int>(e0), total, staged ? 1 : 0, static_cast<int>(e1 - e0));
+    stage_cost[b] = staged ? static_cast<unsigned int>((e1 - e0) + total / 4 + 1) : 0u;
+    stage_ids[b] = b;
+    if (staged) atomicAdd(stage_count, 1u);
+    unsigned char order[kStageRounds];
+    for (int r = 0; r < kStageRounds; ++r) {
+      // insertion sort, most expensive first, ties in round order
+      int j = r;
+      while (j > 0 && s_rcost[order[j - 1]] < s_rcost[r]) {
+        order[j] = order[j - 1];
+        --j;
+      }
+      order[j] = static_cast<unsigned char>(r);
+    }
+    for (int r = 0; r < kStageRounds; ++r) stage_rounds[static_cast<size_t>(b) * kStageRounds + r] = order[r];
+  }
 }
 
 }  // namespace
 
 int build_group_order(TsneSession* s) {
-  const int groups = (s->row_end - s->row_begin + 31) / 32;
+  FE_CUDA(cudaMemsetAsync(&s->stats->stage_count, 0, sizeof(unsigned int), s->stream), "memset stage count");
+  FE_CUDA(cudaMemsetAsync(&s->stats->group_count, 0, sizeof(unsigned int), s->stream), "memset group count");
+  const int rows = s->row_end - s->row_begin;
+  const int groups = (rows + 31) / 32;
   if (groups <= 0) return 0;
-  group_cost_kernel<<<(groups + 255) / 256, 256, 0, s->stream>>>(s->row_ptr4, s->row_begin, s->row_end, groups,
-                                                                 s->group_cost, s->group_ids);
+  const bool staged = s->stage_enabled && s->stage_col16 != nullptr;
+  if (staged) {
+    const int blocks = (rows + kStageRows - 1) / kStageRows;
+    const int smem = kStageSpan / 32 * static_cast<int>(sizeof(unsigned int) + sizeof(unsigned short));
+    FE_CUDA(cudaFuncSetAttribute(stage_build_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
+            "cudaFuncSetAttribute(stage_build_kernel)");
+    stage_build_kernel<<<blocks, kStageBuildThreads, smem, s->stream>>>(
+        s->row_ptr4, reinterpret_cast<const int*>(s->csr4_col), s->row_begin, s->row_end,
+        reinterpret_cast<unsigned short*>(s->stage_col16), s->stage_union, s->stage_meta, s->stage_rounds,
+        s->stage_cost, s->stage_ids, &s->stats->stage_count);
+    FE_LAUNCH("stage_build_kernel");
+    size_t tb = s->ro_temp_bytes;
+    FE_CUDA(cub::DeviceRadixSort::SortPairsDescending(s->ro_temp, tb, s->stage_cost, s->stage_cost_sorted,
+                                                      s->stage_ids, s->stage_order, blocks, 0, 32, s->stream),
+            "cub::DeviceRadixSort(stage cost)");
+  }
+  group_cost_kernel<<<(groups + 255) / 256, 256, 0, s->stream>>>(
+      s->row_ptr4, s->row_begin, s->row_end, groups, staged ? s->stage_meta : nullptr, s->group_cost,
+      s->group_ids, &s->stats->group_count);
   FE_LAUNCH("group_cost_kernel");
   size_t tb = s->ro_temp_bytes;
   FE_CUDA(cub::DeviceRadixSort::SortPairsDescending(s->ro_temp, tb, s->group_cost, s->group_cost_sorted,
@@ -228,6 +409,15 @@ int session_reorder(TsneSession* s, bool by_layout) {
     const size_t groups = std::max<size_t>(1, static_cast<size_t>(total));
     FE_CUDA(cudaMalloc(&s->csr4_col, sizeof(int4) * groups), "cudaMalloc(P cols)");
     FE_CUDA(cudaMalloc(&s->csr4_val, sizeof(float4) * groups), "cudaMalloc(P vals)");
+    // Staged row blocks address entries and union lists with 32-bit offsets.
+    if (s->stage_enabled && static_cast<long long>(total) * 4 < INT_MAX &&
+        memory_preflight(static_cast<size_t>(total) * 24, "staged P preflight") == 0) {
+      FE_CUDA(cudaMalloc(&s->stage_col16, sizeof(uint2) * groups), "cudaMalloc(staged P cols)");
+      FE_CUDA(cudaMalloc(&s->stage_union, sizeof(int4) * groups), "cudaMalloc(staged unions)");
+    } else {
+      clear_error();
+      s->stage_enabled = false;
+    }
     s->csr4_capacity = total;
     s->csr4_groups = total;
     drop_graphs(s);

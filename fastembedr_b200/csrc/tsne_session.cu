@@ -94,6 +94,9 @@ int session_create(TsneSession** out, int n, int grid, int* d_row_ptr, int* d_co
   s->col = d_col;
   s->val = d_val;
   s->use_graphs = env_flag("FASTEMBEDR_CUDA_GRAPH_CAPTURE", true);
+  // Opt-in: measured slower than the L2 gathers on the benchmark mixtures
+  // (0.80 against 0.60 ms at N = 1M; unions hold each point only 1.2-1.6 times).
+  s->stage_enabled = env_flag("FASTEMBEDR_B200_STAGED_ATTRACTION", false);
   // Spatial reordering pays once gathers start missing the caches.
   s->reorder_every = env_int_nonneg("FASTEMBEDR_B200_REORDER_EVERY", n >= 4096 ? 50 : 0);
   if (!env_flag("FASTEMBEDR_B200_REORDER", true)) s->reorder_every = 0;
@@ -144,6 +147,7 @@ int session_create(TsneSession** out, int n, int grid, int* d_row_ptr, int* d_co
     s->update = a.take<float2>(rows);
     s->gains = a.take<float2>(rows);
     s->grad_out = a.take<float2>(rows);
+    s->attraction = a.take<float2>(rows);
     s->perm = a.take<int>(n);
     s->rank = a.take<int>(n);
     s->row_ptr4 = a.take<int>(static_cast<size_t>(n) + 1);
@@ -171,6 +175,13 @@ int session_create(TsneSession** out, int n, int grid, int* d_row_ptr, int* d_co
     s->group_cost = a.take<unsigned int>(groups);
     s->group_cost_sorted = a.take<unsigned int>(groups);
     s->group_ids = a.take<int>(groups);
+    const size_t sblocks = static_cast<size_t>(n) / kStageRows + 2;
+    s->stage_meta = a.take<int4>(sblocks);
+    s->stage_rounds = a.take<unsigned char>(sblocks * kStageRounds);
+    s->stage_cost = a.take<unsigned int>(sblocks);
+    s->stage_cost_sorted = a.take<unsigned int>(sblocks);
+    s->stage_ids = a.take<int>(sblocks);
+    s->stage_order = a.take<int>(sblocks);
     if (pass == 0) {
       if (memory_preflight(a.planned(), "t-SNE workspace preflight") || a.commit("t-SNE workspace")) {
         session_destroy(s);
@@ -215,6 +226,8 @@ void session_destroy(TsneSession* s) {
   if (s->val) cudaFree(s->val);
   if (s->csr4_col) cudaFree(s->csr4_col);
   if (s->csr4_val) cudaFree(s->csr4_val);
+  if (s->stage_col16) cudaFree(s->stage_col16);
+  if (s->stage_union) cudaFree(s->stage_union);
   s->arena.release();
   if (s->own_stream && s->stream) cudaStreamDestroy(s->stream);
   delete s;

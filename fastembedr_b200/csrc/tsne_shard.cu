@@ -125,8 +125,10 @@ int session_shard(TsneSession* s, const void* unique_id, void* lent_comm, int nr
   s->sharded = true;
   s->shard_ranks = nranks;
   s->shard_rank = rank;
+  // Whole staged row blocks (kStageRows, a multiple of 32) per rank, so every
+  // block and 32-row group is the same on any rank count.
   const int per = (s->n + nranks - 1) / nranks;
-  s->rows_per_rank = (per + 31) & ~31;
+  s->rows_per_rank = (per + kStageRows - 1) / kStageRows * kStageRows;
   s->row_begin = std::min(s->n, rank * s->rows_per_rank);
   s->row_end = std::min(s->n, s->row_begin + s->rows_per_rank);
   // The attraction grid covers this rank's rows only.

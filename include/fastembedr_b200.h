@@ -68,8 +68,12 @@ int fastembedr_cuda_opentsne_fft_from_device_knn_float(
     float early_exaggeration, float exaggeration, float learning_rate, int learning_rate_auto,
     float initial_momentum, float final_momentum, float min_gain, float max_step_norm,
     unsigned int seed, int index_offset, float* out);
-/* Device-KNN with device PCA init (RAFT TSVD in the reference; returns 1 here, as the
- * reference does without RAFT).  src/embedding_cuda_impl.cpp:142-183. */
+/* Device-KNN with a PCA init computed on the device from the host data matrix
+ * pca_init_values (n x pca_init_p, R column-major): the reference's RAFT TSVD start
+ * (src/embedding_cuda_kernels.cpp:3357-3495, used at :5692-5724), here a double
+ * covariance eigen-decomposition; the scores are signed so that each component's
+ * largest-magnitude score is positive, then centred and scaled to sd 1e-4.
+ * src/embedding_cuda_impl.cpp:142-183. */
 int fastembedr_cuda_opentsne_fft_from_device_knn_float_pca_double(
     const int* indices, const float* distances, const double* pca_init_values, int pca_init_p,
     int n, int k, int n_components, float perplexity, int early_exaggeration_iter, int n_iter,
@@ -221,11 +225,21 @@ int fe_b200_tsne_set_state(fe_b200_tsne* s, const float* update, const float* ga
 int fe_b200_tsne_info(fe_b200_tsne* s, int* n, int* grid, long long* nnz, long long* nnz_padded);
 /* Copies the (unpadded) CSR P to host arrays of size n+1 / nnz / nnz. */
 int fe_b200_tsne_get_p(fe_b200_tsne* s, int* row_ptr, int* col, float* val);
+/* Row blocks of this session's rows (128 internal rows each) and how many of
+ * them are staged: their attraction gathers y from the block's column union in
+ * shared memory (set at each spatial reorder; the rest gather from L2).
+ * Synchronises the session stream. */
+int fe_b200_tsne_staged_blocks(fe_b200_tsne* s, int* staged, int* blocks);
+/* The PCA start of the _pca_ entry points on its own: host data (n x p, R
+ * column-major, double when values_double else float) to a host layout
+ * out[2n] (row-major), on the current device. */
+int fe_b200_pca_start(const void* values, int values_double, int n, int p, float* out);
 /* The cudaStream_t the session launches on. */
 void* fe_b200_tsne_stream(fe_b200_tsne* s);
 /* Per-kernel CUDA-event timing: enable, then read per-kind totals
- * (kinds: 0 splat, 1 fft rows, 2 fft cols, 3 fft rows inverse, 4 gradient+update,
- * 7 layout statistics, and for sharded sessions 5 charge all-reduce, 6 layout all-gather). */
+ * (kinds: 0 splat, 1 fft rows, 2 fft cols, 3 fft rows inverse, 4 gradient+update (gather),
+ * 7 layout statistics, 8 gradient+update of staged row blocks, and for sharded
+ * sessions 5 charge all-reduce, 6 layout all-gather). */
 int fe_b200_tsne_profile(fe_b200_tsne* s, int enable);
 int fe_b200_tsne_kernel_times(fe_b200_tsne* s, double* ms, long long* launches, int kinds);
 const char* fe_b200_tsne_kernel_name(int kind);

@@ -651,6 +651,9 @@ def ref_cuda() -> ctypes.CDLL:
             _c_int_p, _c_int_p, _c_float_p, _c_float_p, _c_float_p, I, I, I, I, F, F, F, F, U, I, _c_float_p]
         C.fastembedr_cuda_opentsne_fft_from_knn_float.argtypes = [
             _c_int_p, _c_float_p, _c_float_p, I, I, I, I, F, I, I, F, F, F, I, F, F, F, F, U, I, _c_float_p]
+        C.fastembedr_cuda_landmark_tsne_from_device_knn.argtypes = [
+            ctypes.c_void_p, ctypes.c_void_p, I, _c_float_p, _c_float_p, _c_float_p, I, I, I, I, F, I, I, F, F, F,
+            F, F, F, F, I, I, U, I, F, F, _c_float_p]
         _ref_cuda = C
     return _ref_cuda
 
@@ -714,3 +717,60 @@ def ref_cuda_tsne(idx: np.ndarray, dist: np.ndarray, init: np.ndarray, perplexit
         momentum, min_gain, max_step_norm, seed & 0xFFFFFFFF, index_offset, _ptr(out, ctypes.c_float))
     _ref_cuda_check(rc, "openTSNE FFT")
     return out
+
+
+def ref_cuda_landmark_tsne(d_indices: int, d_distances: int, index_offset: int, reference_data: np.ndarray,
+                           query_data: np.ndarray, reference_layout: np.ndarray, k: int, perplexity: float = 30.0,
+                           n_iter: int = 250, early_exaggeration_iter: int = 50, learning_rate: float = 0.1,
+                           early_exaggeration: float = 4.0, exaggeration: float = 1.5,
+                           initial_momentum: float = 0.8, final_momentum: float = 0.8, max_grad_norm: float = 0.25,
+                           max_step_norm: float = float("inf"), n_negatives: int = 256,
+                           exact_repulsion_threshold: int = 4096, seed: int = 1009, affine_neighbors: int = 12,
+                           affine_ridge: float = 1e-3, max_extrapolation: float = 2.5) -> np.ndarray:
+    """fastembedr_cuda_landmark_tsne_from_device_knn of the reference
+    (src/embedding_cuda_kernels.cpp:3496-3610): device KNN pointers of the
+    queries into the reference (column-major n_query x k), host data and layout
+    as (n, d) arrays (passed in R's column-major order), host layout out.
+    Defaults are the R wrapper's (R/landmark_model.R:442-477)."""
+    n_ref, dim = reference_data.shape
+    n_q = query_data.shape[0]
+    rd = np.ascontiguousarray(np.asarray(reference_data, np.float32).T).reshape(-1)
+    qd = np.ascontiguousarray(np.asarray(query_data, np.float32).T).reshape(-1)
+    rl = np.ascontiguousarray(np.asarray(reference_layout, np.float32).T).reshape(-1)
+    out = np.zeros((n_q, 2), np.float32)
+    rc = ref_cuda().fastembedr_cuda_landmark_tsne_from_device_knn(
+        ctypes.c_void_p(d_indices), ctypes.c_void_p(d_distances), index_offset, _ptr(rd, ctypes.c_float),
+        _ptr(qd, ctypes.c_float), _ptr(rl, ctypes.c_float), n_ref, n_q, dim, k, perplexity, n_iter,
+        early_exaggeration_iter, learning_rate, early_exaggeration, exaggeration, initial_momentum, final_momentum,
+        max_grad_norm, max_step_norm, n_negatives, exact_repulsion_threshold, seed & 0xFFFFFFFF, affine_neighbors,
+        affine_ridge, max_extrapolation, _ptr(out, ctypes.c_float))
+    _ref_cuda_check(rc, "landmark t-SNE")
+    return out
+
+
+def pca_start(x: np.ndarray) -> np.ndarray:
+    """PCA start of the PCA-initialised openTSNE entry points, restated:
+    column means in double, the data centred in float (as the reference's
+    raft_tsvd_scores_to_device, src/embedding_cuda_kernels.cpp:3357-3390), the two
+    leading eigenvectors of the covariance (RAFT TSVD's COV_EIG_DQ solver),
+    scores signed so that each component's largest-magnitude score is positive
+    (the TSVD sign flip), then centred and scaled so the larger standard
+    deviation is 1e-4 (finalize_tsne_pca_init_stats_kernel /
+    scale_tsne_pca_init_kernel, :1336-1404).  x: (n, p)."""
+    x = np.asarray(x)
+    mean = x.astype(np.float64).mean(0)
+    xc = (x.astype(np.float32) - mean.astype(np.float32)).astype(np.float32)
+    xd = xc.astype(np.float64)
+    w, v = np.linalg.eigh(xd.T @ xd)
+    v = v[:, np.argsort(-w, kind="stable")[:2]]
+    s = xd @ v
+    for c in range(2):
+        if s[np.argmax(np.abs(s[:, c])), c] < 0:
+            s[:, c] = -s[:, c]
+    s = s.astype(np.float32).astype(np.float64)
+    n = s.shape[0]
+    mu = s.mean(0)
+    ss = np.maximum((s * s).sum(0) - s.sum(0) ** 2 / n, 0.0)
+    sd = np.sqrt(ss / max(n - 1, 1))
+    scale = 1e-4 / sd.max() if np.isfinite(sd.max()) and sd.max() > 0 else 1.0
+    return ((s - mu) * scale).astype(np.float32)

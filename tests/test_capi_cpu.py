@@ -96,11 +96,26 @@ def test_out_of_scope_symbols_fail_cleanly(name, nargs):
     assert "not provided by the B200 backend" in _lib.last_error()
 
 
-def test_pca_init_variant_reports_raft_requirement():
-    fn = _lib.load().fastembedr_cuda_opentsne_fft_from_device_knn_float_pca_float
-    fn.restype = ctypes.c_int
-    assert fn(*([ctypes.c_void_p(0)] * 21)) == 1
-    assert "RAFT" in _lib.last_error()
+def test_pca_init_variants_validate_before_device_work():
+    """The PCA-initialised entry points compute their start on the device
+    (no RAFT needed); a missing data matrix or too few features is rejected
+    before any device call."""
+    L = _lib.load()
+    out = np.zeros((10, 2), np.float32)
+    fout = out.ctypes.data_as(ctypes.POINTER(ctypes.c_float))
+    idx = np.zeros(30, np.int32)
+    dist = np.ones(30, np.float32)
+    x = np.zeros(10, np.float64)
+    for fn in (L.fastembedr_cuda_opentsne_fft_from_device_knn_float_pca_double,
+               L.fastembedr_cuda_opentsne_fft_from_device_knn_float_pca_float):
+        args = [ctypes.c_void_p(idx.ctypes.data), ctypes.c_void_p(dist.ctypes.data), None, 2, 10, 3, 2, 1.0, 10, 10,
+                12.0, 1.0, 0.0, 1, 0.8, 0.8, 0.01, 5.0, 1, 0, fout]
+        assert fn(*args) == 1
+        assert "PCA" in _lib.last_error()
+        args[2] = ctypes.c_void_p(x.ctypes.data)
+        args[3] = 1  # one feature
+        assert fn(*args) == 1
+        assert _lib.last_error() == "invalid dimensions in device PCA initialization"
 
 
 def test_parameter_validation_precedes_device_work():

@@ -319,3 +319,30 @@ def test_end_to_end_at_scale_vs_reference_cpu(cfg2):
     print(f"N=70k: KL {kl:.4f} vs reference {klr:.4f}; kNN preservation {q:.4f} vs {qr:.4f}")
     assert abs(kl - klr) / klr < 0.02
     assert q >= qr * 0.98
+
+
+def test_staged_attraction_is_bit_identical_to_gathers(monkeypatch):
+    """Row blocks whose column union fits in shared memory gather y_j from it
+    (staged_grad_kernel); the rest gather from L2 (grad_update_kernel).  Both
+    run a row with the same per-entry arithmetic in the same order, so a run
+    with staging must give the bits of a run without it, across reorders."""
+    x, _ = S.gaussian_mixture(S.MixtureSpec(n=30_000, components=6, seed=5))
+    idx, dist = S.exact_knn(x, 60, device="cuda")
+    n = idx.shape[0]
+    init = S.tsne_init(n, seed=2)
+    outs = {}
+    for flag in ("1", "0"):  # staging is opt-in
+        monkeypatch.setenv("FASTEMBEDR_B200_STAGED_ATTRACTION", flag)
+        with api.TsneSession.from_knn(idx, dist, perplexity=20.0, init=init) as s:
+            s.iterate(120, 12.0, 0.8, float(np.float32(n / 12.0)))  # crosses the reorders at 50 and 100
+            s.iterate(40, 1.0, 0.8, float(np.float32(n)))
+            staged, blocks = s.staged_blocks()
+            grad, z = s.gradient(1.0)
+            outs[flag] = (s.layout(), *s.state(), grad, staged, blocks)
+    staged, blocks = outs["1"][4], outs["1"][5]
+    print(f"staged row blocks: {staged} of {blocks}")
+    assert blocks == (n + 127) // 128
+    assert staged > blocks // 2  # after the Morton reorders most blocks stage
+    assert outs["0"][4] == 0
+    for a, b in zip(outs["1"][:4], outs["0"][:4]):
+        assert np.array_equal(a, b)

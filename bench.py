@@ -95,14 +95,17 @@ def peaks():
     return FALLBACK_HBM_GBS, "fallback"
 
 
-def make_inputs(workload: str, device: str):
+def make_inputs(workload: str, device: str, producer: str = "b200"):
+    """The workload's exact KNN and init.  The reference arm builds its inputs
+    with torch's brute force (producer="torch"), so it runs no code of this
+    library; both give the exact KNN."""
     from fastembedr_b200 import synthetic as S
 
     w = WORKLOADS[workload]
     spec = S.CONFIGS[w["spec"]]
     t0 = time.time()
     x, _ = S.gaussian_mixture(spec)
-    idx, dist = S.exact_knn(x, w["k"], device=device)
+    idx, dist = S.exact_knn(x, w["k"], device=device, producer=producer)
     log(f"[bench] {workload}: n={spec.n} k={w['k']} inputs in {time.time() - t0:.1f}s")
     return idx, dist, S.tsne_init(spec.n, seed=0)
 
@@ -248,7 +251,7 @@ def bench_reference(args):
         return 0
     w = WORKLOADS[args.workload]
     device = "cuda" if _cuda_ok() else None
-    idx, dist, init = make_inputs(args.workload, device)
+    idx, dist, init = make_inputs(args.workload, device, producer="torch")
     base = cpu_baseline_tsne(idx, dist, w["perplexity"], init, args.cpu_iters, args.cpu_seconds,
                              max_iters=max(args.cpu_iters, args.steps))
     iters = base["iterations"]
@@ -277,7 +280,7 @@ def bench_reference_umap(args):
         return 0
     import oracle as O
 
-    idx, dist, init = umap_inputs(args.workload, "cuda" if _cuda_ok() else None)
+    idx, dist, init = umap_inputs(args.workload, "cuda" if _cuda_ok() else None, producer="torch")
     t0 = time.time()
     g = O.ref_umap_graph(idx, dist, threads=os.cpu_count() or 1) if O.ref_available() else O.umap_graph(idx, dist)
     graph = {"heads": g.heads(), "tails": g.neighbors, "epochs_per_sample": g.epochs_per_sample}
@@ -369,7 +372,7 @@ def bench_reference_cuda(args):
     if umap:
         from fastembedr_b200 import api
 
-        idx, dist, _ = umap_inputs(args.workload, f"cuda:{local}")
+        idx, dist, _ = umap_inputs(args.workload, f"cuda:{local}", producer="torch")
         n, k = idx.shape
         a, b = api.find_ab_params(1.0, UMAP_MIN_DIST)
         sni = api.umap_config(n, k)["spectral_n_iter"]
@@ -387,7 +390,7 @@ def bench_reference_cuda(args):
         cfg = {"workload": args.workload, "n": int(n), "k": int(k), "n_edges": int(n_edges),
                "units": "positive samples of this library's edge list for the schedule"}
     else:
-        idx, dist, init = make_inputs(args.workload, f"cuda:{local}")
+        idx, dist, init = make_inputs(args.workload, f"cuda:{local}", producer="torch")
         n, k = idx.shape
         units = EE_ITER + N_ITER
 
@@ -681,14 +684,14 @@ def bench_ours(args):
     return 0
 
 
-def umap_inputs(workload: str, device):
+def umap_inputs(workload: str, device, producer: str = "b200"):
     from fastembedr_b200 import synthetic as S
 
     w = WORKLOADS[workload]
     spec = S.CONFIGS[w["spec"]]
     t0 = time.time()
     x, _ = S.gaussian_mixture(spec)
-    idx, dist = S.exact_knn(x, w["k"], device=device)
+    idx, dist = S.exact_knn(x, w["k"], device=device, producer=producer)
     log(f"[bench] {workload}: n={spec.n} k={w['k']} inputs in {time.time() - t0:.1f}s")
     return idx, dist, S.umap_random_init(spec.n, seed=0)
 

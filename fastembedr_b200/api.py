@@ -198,6 +198,39 @@ def opentsne_knn(indices, distances, n_components: int = 2, perplexity: Optional
     })
 
 
+def knn_exact(data, k: int, exclude_self: bool = True, device_output: bool = False):
+    """Exact Euclidean KNN on the device (fe_b200_knn_exact): the GPU-KNN
+    producer.  `data` is (n, p), a numpy array or a CUDA tensor (float32 or
+    float64).  Returns 0-based (n, k) int32 indices and float32 distances,
+    ascending -- numpy arrays, or with device_output the column-major CUDA
+    tensors (k, n) the device-KNN entry points take (1-based)."""
+    import torch
+
+    if isinstance(data, torch.Tensor) and data.is_cuda:
+        dt = data.to(torch.float64 if data.dtype == torch.float64 else torch.float32)
+        cm = dt.t().contiguous()
+        n, p = data.shape
+        ptr, on_dev, dbl = cm.data_ptr(), 1, int(dt.dtype == torch.float64)
+        keep = cm
+    else:
+        arr = np.asarray(data)
+        dbl = int(arr.dtype == np.float64)
+        arr = arr.astype(np.float64 if dbl else np.float32, copy=False)
+        keep = np.ascontiguousarray(arr.T)
+        n, p = arr.shape
+        ptr, on_dev = keep.ctypes.data, 0
+    d_idx = torch.empty((k, n), dtype=torch.int32, device="cuda")
+    d_dist = torch.empty((k, n), dtype=torch.float32, device="cuda")
+    torch.cuda.synchronize()
+    rc = _lib.load().fe_b200_knn_exact(ctypes.c_void_p(ptr), dbl, on_dev, n, p, k, int(exclude_self),
+                                       ctypes.c_void_p(d_idx.data_ptr()), ctypes.c_void_p(d_dist.data_ptr()))
+    del keep
+    check(rc, "fe_b200_knn_exact")
+    if device_output:
+        return d_idx, d_dist
+    return (d_idx.t().cpu().numpy() - 1).astype(np.int32), d_dist.t().cpu().numpy()
+
+
 def landmark_tsne_transform(indices, distances, reference_data, query_data, reference_layout,
                             perplexity: float = 30.0, n_iter: int = 250, early_exaggeration_iter: int = 50,
                             learning_rate: float = 0.1, early_exaggeration: float = 4.0,

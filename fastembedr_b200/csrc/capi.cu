@@ -722,6 +722,18 @@ int fe_b200_tsne_staged_blocks(fe_b200_tsne* h, int* staged, int* blocks) {
   return 0;
 }
 
+int fe_b200_knn_exact(const void* data, int data_double, int data_on_device, int n, int p, int k, int exclude_self,
+                      int* d_indices, float* d_distances) {
+  fe::clear_error();
+  cudaStream_t st = nullptr;
+  FE_CUDA(cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking), "cudaStreamCreate(KNN)");
+  const int rc = fe::knn_exact(data, data_double != 0, data_on_device != 0, true, n, p, k, exclude_self != 0,
+                               d_indices, d_distances, st);
+  cudaStreamSynchronize(st);
+  cudaStreamDestroy(st);
+  return rc;
+}
+
 int fe_b200_pca_start(const void* values, int values_double, int n, int p, float* out) {
   fe::clear_error();
   if (values == nullptr || out == nullptr || n < 2 || p < 2) {

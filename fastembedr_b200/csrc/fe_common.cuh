@@ -88,6 +88,14 @@ class Arena {
 // (the reference's preflight, src/embedding_cuda_kernels.cpp:224-241).
 int memory_preflight(std::size_t bytes, const char* where);
 
+// ---------------------------------------------------------------- exact KNN (knn.cu)
+
+// Exact Euclidean KNN of n points (n x p; column-major when col_major, else
+// row-major; double or float; host or device) into caller device arrays,
+// column-major n x k, indices 1-based.  Synchronises `st`.
+int knn_exact(const void* data, bool data_double, bool data_on_device, bool col_major, int n, int p, int k,
+              bool exclude_self, int* d_indices, float* d_distances, cudaStream_t st);
+
 // ---------------------------------------------------------------- launch shape
 
 // SM count of the current device (cached per device).

@@ -2,8 +2,9 @@
 
 The reference benchmarks on MNIST / flow18 / ImageNet embeddings, which are
 not available here; Gaussian mixtures with the configured sizes stand in for
-them.  Exact Euclidean non-self KNN is computed by blocked brute force
-(NumPy on the CPU for small n, torch on a GPU when one is given).
+them.  Exact Euclidean non-self KNN is computed by brute force: NumPy on the
+CPU for small n, this library's exact KNN on a GPU (torch's blocked brute
+force stays available as an independent producer).
 
 KNN results are ``(n, k)`` int32 indices (0-based, self excluded, sorted by
 distance) and float32 distances; ``column_major`` converts to the R layout the
@@ -107,8 +108,18 @@ def exact_knn_torch(x: np.ndarray, k: int, device: str = "cuda",
         return idx.cpu().numpy(), dist.cpu().numpy()
 
 
-def exact_knn(x: np.ndarray, k: int, device: Optional[str] = None) -> Tuple[np.ndarray, np.ndarray]:
+def exact_knn(x: np.ndarray, k: int, device: Optional[str] = None, producer: str = "b200") -> Tuple[np.ndarray, np.ndarray]:
+    """Exact non-self KNN: on a GPU with this library's producer
+    (fe_b200_knn_exact) by default, or torch's blocked brute force
+    (producer="torch", an independent implementation); NumPy without a device."""
     if device is not None and device.startswith("cuda"):
+        if producer == "b200":
+            import torch
+
+            from . import api
+
+            with torch.cuda.device(torch.device(device)):
+                return api.knn_exact(x, k)
         return exact_knn_torch(x, k, device)
     return exact_knn_numpy(x, k)
 

@@ -230,6 +230,17 @@ int fe_b200_tsne_get_p(fe_b200_tsne* s, int* row_ptr, int* col, float* val);
  * shared memory (set at each spatial reorder; the rest gather from L2).
  * Synchronises the session stream. */
 int fe_b200_tsne_staged_blocks(fe_b200_tsne* s, int* staged, int* blocks);
+/* Exact Euclidean KNN on the device: the producer of the GPU-KNN object the
+ * device-KNN entry points consume (the reference's native_cuda_knn_impl with its
+ * exact route and finalize step, src/native_knn_cuda_impl.cpp:511-700, 418-470;
+ * src/embedding_cuda_kernels.cpp:1412-1464).  data: n x p, R column-major,
+ * double when data_double, on the device when data_on_device else on the host.
+ * Writes the k nearest non-self points (exclude_self: the query's own index is
+ * skipped) into caller-allocated device arrays, column-major n x k: indices
+ * 1-based int32 (0 where fewer than k exist) and float32 Euclidean distances,
+ * ascending (ties by index).  1 <= k <= min(n - 1, 247). */
+int fe_b200_knn_exact(const void* data, int data_double, int data_on_device, int n, int p, int k,
+                      int exclude_self, int* d_indices, float* d_distances);
 /* The PCA start of the _pca_ entry points on its own: host data (n x p, R
  * column-major, double when values_double else float) to a host layout
  * out[2n] (row-major), on the current device. */

@@ -59,6 +59,7 @@ _SIGNATURES = {
     "fe_b200_tsne_info": (I, [c_void_p, c_int_p, c_int_p, c_ll_p, c_ll_p]),
     "fe_b200_tsne_staged_blocks": (I, [c_void_p, c_int_p, c_int_p]),
     "fe_b200_pca_start": (I, [c_void_p, I, I, I, c_float_p]),
+    "fe_b200_tsne_set_interpolation": (I, [c_void_p, I]),
     "fe_b200_knn_exact": (I, [c_void_p, I, I, I, I, I, I, c_void_p, c_void_p]),
     "fastembedr_cuda_opentsne_fft_from_device_knn_float_pca_double": (I, [c_void_p, c_void_p, c_void_p, I, I, I,
                                                                          I, F, I, I, F, F, F, I, F, F, F, F, U, I,

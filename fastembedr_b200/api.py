@@ -390,6 +390,12 @@ class TsneSession:
                                             ctypes.byref(nnzp)), "fe_b200_tsne_info")
         return {"n": n.value, "grid": g.value, "nnz": nnz.value, "nnz_padded": nnzp.value}
 
+    def set_interpolation(self, mode: str) -> None:
+        """"bilinear" (the reference's grid, the default) or "lagrange"
+        (FIt-SNE boxes with three Lagrange nodes per side)."""
+        code = {"bilinear": 0, "lagrange": 1}[mode]
+        check(_lib.load().fe_b200_tsne_set_interpolation(self._h, code), "fe_b200_tsne_set_interpolation")
+
     def staged_blocks(self) -> Tuple[int, int]:
         """(staged, total) 128-row blocks of this session's rows at the last
         spatial reorder; staged blocks gather y from shared memory."""

@@ -722,6 +722,15 @@ int fe_b200_tsne_staged_blocks(fe_b200_tsne* h, int* staged, int* blocks) {
   return 0;
 }
 
+int fe_b200_tsne_set_interpolation(fe_b200_tsne* h, int mode) {
+  fe::clear_error();
+  if (h == nullptr) {
+    set_error("invalid t-SNE session call");
+    return 1;
+  }
+  return fe::session_set_interpolation(h->impl, mode);
+}
+
 int fe_b200_knn_exact(const void* data, int data_double, int data_on_device, int n, int p, int k, int exclude_self,
                       int* d_indices, float* d_distances) {
   fe::clear_error();

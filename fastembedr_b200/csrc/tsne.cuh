@@ -38,7 +38,9 @@ struct ChargeCell {
 struct GridGeom {
   float mean_x, mean_y;
   float lower_x, lower_y;
-  float spacing, inv_spacing;
+  float spacing, inv_spacing;  // node spacing of the (uniform) FFT grid
+  int boxes;                   // Lagrange mode: boxes per side (0 in bilinear mode)
+  float inv_box;               // Lagrange mode: 1 / box width
 };
 
 // Charges are accumulated in signed 64-bit fixed point, so the splat's
@@ -56,7 +58,7 @@ struct LayoutStats {
   float min_x, max_x;         // bounds of the raw layout
   float min_y, max_y;
   int center;                 // 1: subtract the mean before use (iterations)
-  int pad0;
+  int lagrange;               // interpolation: 0 bilinear (the reference's), 1 Lagrange 3-node boxes
   double z;                   // sum_i interp(phi_q)(y_i) - n
   float inv_z;                // 1 / max(z, FLT_MIN)
   unsigned int row_groups_taken;  // grad_update_kernel work counter
@@ -87,6 +89,26 @@ __device__ __forceinline__ GridGeom grid_geometry(const LayoutStats& s, int n, i
   }
   const float min_x = s.min_x - q.mean_x, max_x = s.max_x - q.mean_x;
   const float min_y = s.min_y - q.mean_y, max_y = s.max_y - q.mean_y;
+  q.boxes = 0;
+  q.inv_box = 0.0f;
+  if (s.lagrange) {
+    // FIt-SNE's box grid: square boxes of about one unit of the embedding
+    // (intervals_per_integer = 1), at least 50 per side, covering the layout's
+    // bounding square from its lower corner; three interpolation nodes per box
+    // and side at (j + 1/2) / 3, so the nodes form a uniform grid of spacing
+    // box / 3 for the FFT convolution.  At most g / 3 boxes fit the grid.
+    float extent = fmaxf(max_x - min_x, max_y - min_y);
+    if (!isfinite(extent) || extent <= 0.0f) extent = 1.0f;
+    const int boxes = max(1, min(g / 3, max(50, static_cast<int>(ceilf(extent)))));
+    const float box = extent / static_cast<float>(boxes);
+    q.lower_x = min_x;
+    q.lower_y = min_y;
+    q.boxes = boxes;
+    q.inv_box = 1.0f / box;
+    q.spacing = box / 3.0f;
+    q.inv_spacing = 1.0f / q.spacing;
+    return q;
+  }
   const float cx = 0.5f * (min_x + max_x);
   const float cy = 0.5f * (min_y + max_y);
   float span = fmaxf(max_x - min_x, max_y - min_y);
@@ -108,9 +130,37 @@ __device__ __forceinline__ ChargeScales charge_scales(const GridGeom& q, int n, 
   const float extent = q.spacing * static_cast<float>(g - 1);
   const double xmax = fmax(fmax(fabs(static_cast<double>(q.lower_x)), fabs(static_cast<double>(q.lower_x) + extent)),
                            fmax(fabs(static_cast<double>(q.lower_y)), fabs(static_cast<double>(q.lower_y) + extent)));
+  // Lagrange weights reach 1.875 in magnitude per dimension (3.52 per node),
+  // so a node's total can exceed the bilinear bound by 4x: two more bits.
+  const double headroom = q.boxes > 0 ? 4.0 : 1.0;
   ChargeScales c;
-  c.m = pow2_scale_for(static_cast<double>(n));
-  c.xy = pow2_scale_for(static_cast<double>(n) * (xmax + 1.0));
+  c.m = pow2_scale_for(headroom * static_cast<double>(n));
+  c.xy = pow2_scale_for(headroom * static_cast<double>(n) * (xmax + 1.0));
+  return c;
+}
+
+// Lagrange mode: the box of a point and the quadratic Lagrange weights of its
+// position in the box at the three nodes t_j = (j + 1/2) / 3 of each side
+// (FIt-SNE's interpolation, p = 3).  Node (j, k) of box (bx, by) is grid node
+// (3 bx + j, 3 by + k).  Spread and gather use these same weights.
+struct LagrangeCell {
+  int bx, by;
+  float wx[3], wy[3];
+};
+__device__ __forceinline__ void lagrange_weights(float t, float* w) {
+  const float t0 = 1.0f / 6.0f, t1 = 0.5f, t2 = 5.0f / 6.0f;
+  w[0] = 4.5f * (t - t1) * (t - t2);
+  w[1] = -9.0f * (t - t0) * (t - t2);
+  w[2] = 4.5f * (t - t0) * (t - t1);
+}
+__device__ __forceinline__ LagrangeCell lagrange_cell(float px, float py, const GridGeom& q) {
+  LagrangeCell c;
+  const float ux = (px - q.lower_x) * q.inv_box;
+  const float uy = (py - q.lower_y) * q.inv_box;
+  c.bx = max(0, min(q.boxes - 1, static_cast<int>(floorf(ux))));
+  c.by = max(0, min(q.boxes - 1, static_cast<int>(floorf(uy))));
+  lagrange_weights(fminf(1.0f, fmaxf(0.0f, ux - static_cast<float>(c.bx))), c.wx);
+  lagrange_weights(fminf(1.0f, fmaxf(0.0f, uy - static_cast<float>(c.by))), c.wy);
   return c;
 }
 
@@ -215,6 +265,7 @@ struct TsneSession {
   float4* pot = nullptr;
   float2* twiddle = nullptr;  // exp(-2 pi i k / M), k < M/2
 
+  int interp = 0;  // 0 bilinear (the reference's), 1 Lagrange 3-node boxes (FIt-SNE)
   int update_blocks = 0;
   int update_threads = 256;
   int cols_per_block = 1;
@@ -433,8 +484,16 @@ int launch_iteration(TsneSession* s, GradMode mode, float exaggeration, float mo
                      float learning_rate, float min_gain, float max_step_norm);
 int launch_center_output(TsneSession* s, float2* out);
 
-// CPU grid-size policy (tsne_fft_grid_size, src/tsne_neighbors.cpp:392-398).
+// CPU grid-size policy (tsne_fft_grid_size, src/tsne_neighbors.cpp:392-398);
+// in Lagrange mode twice that (up to 1024), so unit boxes fit the layouts'
+// extents.
 int default_grid_size(int n);
+// The interpolation FASTEMBEDR_B200_INTERPOLATION selects: 1 for "lagrange",
+// else 0 (bilinear).
+int interpolation_from_env();
+// Switches a session's interpolation (0 bilinear, 1 Lagrange boxes); drops
+// its captured graphs and re-derives the grid geometry of its layout.
+int session_set_interpolation(TsneSession* s, int mode);
 
 // ---- PCA start of the PCA-initialised entry points (pca.cu) ----
 // values: host, n x p column-major (double or float).  Writes the scaled

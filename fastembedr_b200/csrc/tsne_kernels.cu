@@ -412,6 +412,156 @@ __global__ void __launch_bounds__(kSplatThreads) splat_kernel(float2* __restrict
   }
 }
 
+
+// Lagrange mode (FIt-SNE boxes, three nodes per box and side): as
+// splat_kernel with each point spreading {1, x, y} to the 3 x 3 nodes of its
+// box with quadratic Lagrange weights (which can be negative; the fixed-point
+// sums are two's complement).  Lanes sharing a box combine first; a block's
+// nodes go through the shared-memory tile when they fit.
+__global__ void __launch_bounds__(kSplatThreads) splat_lagrange_kernel(float2* __restrict__ y,
+                                                                       LayoutStats* __restrict__ stats, int n, int g,
+                                                                       ChargeCell* __restrict__ charges,
+                                                                       int own_begin, int own_end) {
+  __shared__ unsigned long long tile[3][kSplatTileNodes];
+  __shared__ int s_box[4][kSplatThreads / 32];
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  const GridGeom q = stats->geom;
+  const ChargeScales sc = stats->scales;
+  if (i == 0) {
+    stats->row_groups_taken = 0u;
+    stats->stage_taken = 0u;
+  }
+  int key = -1;
+  LagrangeCell c;
+  c.bx = 0;
+  c.by = 0;
+  float v[27];
+#pragma unroll
+  for (int t = 0; t < 27; ++t) v[t] = 0.0f;
+  if (i < n) {
+    float2 p = y[i];
+    if (stats->center) {
+      p.x -= q.mean_x;
+      p.y -= q.mean_y;
+      y[i] = p;
+    }
+  }
+  if (i >= own_begin && i < own_end) {
+    const float2 p = y[i];
+    c = lagrange_cell(p.x, p.y, q);
+    key = c.by * q.boxes + c.bx;
+#pragma unroll
+    for (int k = 0; k < 3; ++k) {
+#pragma unroll
+      for (int j = 0; j < 3; ++j) {
+        const float w = c.wx[j] * c.wy[k];
+        v[3 * (3 * k + j)] = w;
+        v[3 * (3 * k + j) + 1] = w * p.x;
+        v[3 * (3 * k + j) + 2] = w * p.y;
+      }
+    }
+  }
+  const unsigned int peers = __match_any_sync(0xffffffffu, key);
+  const int leader = __ffs(peers) - 1;
+  if (peers == 0xffffffffu) {
+    if (key >= 0) {
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+#pragma unroll
+        for (int t = 0; t < 27; ++t) v[t] += __shfl_xor_sync(0xffffffffu, v[t], o);
+      }
+    }
+  } else if (key >= 0 && __popc(peers) > 1) {
+    float sum[27];
+#pragma unroll
+    for (int t = 0; t < 27; ++t) sum[t] = 0.0f;
+    for (unsigned int m = peers; m; m &= m - 1) {
+      const int src = __ffs(m) - 1;
+#pragma unroll
+      for (int t = 0; t < 27; ++t) sum[t] += __shfl_sync(peers, v[t], src);
+    }
+#pragma unroll
+    for (int t = 0; t < 27; ++t) v[t] = sum[t];
+  }
+  const bool active = key >= 0 && lane == leader;
+
+  // Node box of the block's points (the 3 x 3 nodes of each box).
+  const bool own = key >= 0;
+  int x_lo = own ? 3 * c.bx : INT_MAX, y_lo = own ? 3 * c.by : INT_MAX;
+  int x_hi = own ? 3 * c.bx + 2 : INT_MIN, y_hi = own ? 3 * c.by + 2 : INT_MIN;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    x_lo = min(x_lo, __shfl_xor_sync(0xffffffffu, x_lo, o));
+    y_lo = min(y_lo, __shfl_xor_sync(0xffffffffu, y_lo, o));
+    x_hi = max(x_hi, __shfl_xor_sync(0xffffffffu, x_hi, o));
+    y_hi = max(y_hi, __shfl_xor_sync(0xffffffffu, y_hi, o));
+  }
+  if (lane == 0) {
+    s_box[0][wid] = x_lo;
+    s_box[1][wid] = y_lo;
+    s_box[2][wid] = x_hi;
+    s_box[3][wid] = y_hi;
+  }
+  __syncthreads();
+  x_lo = INT_MAX, y_lo = INT_MAX, x_hi = INT_MIN, y_hi = INT_MIN;
+  for (int w = 0; w < kSplatThreads / 32; ++w) {
+    x_lo = min(x_lo, s_box[0][w]);
+    y_lo = min(y_lo, s_box[1][w]);
+    x_hi = max(x_hi, s_box[2][w]);
+    y_hi = max(y_hi, s_box[3][w]);
+  }
+  if (x_hi < x_lo) return;  // no point of this block is spread (block-uniform)
+  const int box_w = x_hi - x_lo + 1, box_h = y_hi - y_lo + 1;
+  const bool tiled = box_w * box_h <= kSplatTileNodes;  // block-uniform
+  if (!tiled) {
+    if (!active) return;
+#pragma unroll
+    for (int k = 0; k < 3; ++k) {
+#pragma unroll
+      for (int j = 0; j < 3; ++j) {
+        ChargeCell* cell = charges + static_cast<size_t>(3 * c.by + k) * g + (3 * c.bx + j);
+        const int t = 3 * (3 * k + j);
+        const long long a = to_fixed(v[t], sc.m), b = to_fixed(v[t + 1], sc.xy), d = to_fixed(v[t + 2], sc.xy);
+        if (a != 0) atomicAdd(&cell->m, static_cast<unsigned long long>(a));
+        if (b != 0) atomicAdd(&cell->mx, static_cast<unsigned long long>(b));
+        if (d != 0) atomicAdd(&cell->my, static_cast<unsigned long long>(d));
+      }
+    }
+    return;
+  }
+  const int nodes = box_w * box_h;
+  for (int t = threadIdx.x; t < nodes; t += kSplatThreads) {
+    tile[0][t] = 0ull;
+    tile[1][t] = 0ull;
+    tile[2][t] = 0ull;
+  }
+  __syncthreads();
+  if (active) {
+#pragma unroll
+    for (int k = 0; k < 3; ++k) {
+#pragma unroll
+      for (int j = 0; j < 3; ++j) {
+        const int node = (3 * c.by + k - y_lo) * box_w + (3 * c.bx + j - x_lo);
+        const int t = 3 * (3 * k + j);
+        const long long a = to_fixed(v[t], sc.m), b = to_fixed(v[t + 1], sc.xy), d = to_fixed(v[t + 2], sc.xy);
+        if (a != 0) atomicAdd(&tile[0][node], static_cast<unsigned long long>(a));
+        if (b != 0) atomicAdd(&tile[1][node], static_cast<unsigned long long>(b));
+        if (d != 0) atomicAdd(&tile[2][node], static_cast<unsigned long long>(d));
+      }
+    }
+  }
+  __syncthreads();
+  for (int t = threadIdx.x; t < nodes; t += kSplatThreads) {
+    const int ty = t / box_w, tx = t - ty * box_w;
+    ChargeCell* cell = charges + static_cast<size_t>(y_lo + ty) * g + (x_lo + tx);
+    const unsigned long long a = tile[0][t], b = tile[1][t], d = tile[2][t];
+    if (a != 0ull) atomicAdd(&cell->m, a);
+    if (b != 0ull) atomicAdd(&cell->mx, b);
+    if (d != 0ull) atomicAdd(&cell->my, d);
+  }
+}
+
 __device__ __forceinline__ float3 read_charge(const ChargeCell& c, const ChargeScales& sc) {
   return make_float3(static_cast<float>(static_cast<double>(static_cast<long long>(c.m)) / sc.m),
                      static_cast<float>(static_cast<double>(static_cast<long long>(c.mx)) / sc.xy),
@@ -622,6 +772,25 @@ struct UpdateParams {
 
 __device__ __forceinline__ float sign_f(float x) { return x == 0.0f ? 0.0f : (x < 0.0f ? -1.0f : 1.0f); }
 
+// Lagrange mode: the 3 x 3 nodes of the point's box with its Lagrange weights.
+__device__ __forceinline__ float3 gather_potentials_lagrange(const float4* __restrict__ pot, const LagrangeCell& c,
+                                                             int g) {
+  float3 r = make_float3(0.0f, 0.0f, 0.0f);
+#pragma unroll
+  for (int k = 0; k < 3; ++k) {
+    const float4* rowp = pot + static_cast<size_t>(3 * c.by + k) * g + 3 * c.bx;
+#pragma unroll
+    for (int j = 0; j < 3; ++j) {
+      const float4 v = __ldg(rowp + j);
+      const float w = c.wx[j] * c.wy[k];
+      r.x += w * v.x;
+      r.y += w * v.y;
+      r.z += w * v.z;
+    }
+  }
+  return r;
+}
+
 // bilinear_grid_value_t (src/tsne_neighbors.cpp:760-781) on three planes at once.
 __device__ __forceinline__ float3 gather_potentials(const float4* __restrict__ pot, const Cell& c, int g) {
   const float4* base = pot + static_cast<size_t>(c.y0) * g + c.x0;
@@ -647,8 +816,12 @@ __device__ __forceinline__ void finish_row(int row, float ax, float ay, const fl
                                            const UpdateParams& prm) {
   const float2 yi = y[row];
   const GridGeom q = stats->geom;
-  const Cell c = grid_cell(yi.x, yi.y, q, prm.g);
-  const float3 ph = gather_potentials(pot, c, prm.g);
+  float3 ph;
+  if (q.boxes > 0) {
+    ph = gather_potentials_lagrange(pot, lagrange_cell(yi.x, yi.y, q), prm.g);
+  } else {
+    ph = gather_potentials(pot, grid_cell(yi.x, yi.y, q, prm.g), prm.g);
+  }
   const float inv_z = stats->inv_z;
   const float gx = -(yi.x * ph.x - ph.y) * inv_z + ax;
   const float gy = -(yi.y * ph.x - ph.z) * inv_z + ay;
@@ -1126,9 +1299,16 @@ int launch_iteration(TsneSession* s, GradMode mode, float exaggeration, float mo
   const int row_len = g + 1;
   {
     ProfileScope ps(s, kKindSplat);
-    splat_kernel<<<(s->n + kSplatThreads - 1) / kSplatThreads, kSplatThreads, 0, s->stream>>>(
-        s->y[s->cur], s->stats, s->n, g, s->charges, s->row_begin, s->row_end);
-    FE_LAUNCH("splat_kernel");
+    const unsigned blocks = static_cast<unsigned>((s->n + kSplatThreads - 1) / kSplatThreads);
+    if (s->interp == 1) {
+      splat_lagrange_kernel<<<blocks, kSplatThreads, 0, s->stream>>>(s->y[s->cur], s->stats, s->n, g, s->charges,
+                                                                     s->row_begin, s->row_end);
+      FE_LAUNCH("splat_lagrange_kernel");
+    } else {
+      splat_kernel<<<blocks, kSplatThreads, 0, s->stream>>>(s->y[s->cur], s->stats, s->n, g, s->charges,
+                                                            s->row_begin, s->row_end);
+      FE_LAUNCH("splat_kernel");
+    }
   }
   if (s->sharded) {
     ProfileScope ps(s, kKindChargeSum);

@@ -4,6 +4,7 @@
 #include "tsne.cuh"
 
 #include <algorithm>
+#include <cstdlib>
 #include <cmath>
 #include <cstring>
 #include <utility>
@@ -68,12 +69,39 @@ void drop_graphs(TsneSession* s) {
   s->graphs.clear();
 }
 
+int interpolation_from_env() {
+  const char* v = std::getenv("FASTEMBEDR_B200_INTERPOLATION");
+  return (v != nullptr && std::strcmp(v, "lagrange") == 0) ? 1 : 0;
+}
+
 int default_grid_size(int n) {
   const int fallback = n >= 50000 ? 256 : (n >= 10000 ? 128 : 64);
   const int requested = env_int("FASTEMBEDR_TSNE_FFT_GRID", fallback);
   int grid = 32;
   while (grid < requested && grid < 512) grid <<= 1;
-  return std::max(32, std::min(512, grid));
+  grid = std::max(32, std::min(512, grid));
+  if (interpolation_from_env() == 1 && env_int("FASTEMBEDR_TSNE_FFT_GRID", 0) == 0) {
+    grid = std::min(1024, std::max(256, 2 * grid));
+  }
+  return grid;
+}
+
+int session_set_interpolation(TsneSession* s, int mode) {
+  if (mode != 0 && mode != 1) {
+    set_error("t-SNE interpolation must be 0 (bilinear) or 1 (Lagrange boxes)");
+    return 1;
+  }
+  if (mode == 1 && s->grid < 192) {
+    set_error("Lagrange boxes need an FFT grid of at least 256 nodes per side");
+    return 1;
+  }
+  s->interp = mode;
+  drop_graphs(s);
+  FE_CUDA(cudaMemcpyAsync(&s->stats->lagrange, &s->interp, sizeof(int), cudaMemcpyHostToDevice, s->stream),
+          "H2D interpolation");
+  // Re-derive the geometry of the current layout in the new mode (uncentred
+  // statistics, as after a set_layout; the next splat centres).
+  return launch_stats(s, 1);
 }
 
 int session_create(TsneSession** out, int n, int grid, int* d_row_ptr, int* d_col, float* d_val,
@@ -94,6 +122,7 @@ int session_create(TsneSession** out, int n, int grid, int* d_row_ptr, int* d_co
   s->col = d_col;
   s->val = d_val;
   s->use_graphs = env_flag("FASTEMBEDR_CUDA_GRAPH_CAPTURE", true);
+  s->interp = interpolation_from_env();
   // Opt-in: measured slower than the L2 gathers on the benchmark mixtures
   // (0.80 against 0.60 ms at N = 1M; unions hold each point only 1.2-1.6 times).
   s->stage_enabled = env_flag("FASTEMBEDR_B200_STAGED_ATTRACTION", false);
@@ -197,6 +226,8 @@ int session_create(TsneSession** out, int n, int grid, int* d_row_ptr, int* d_co
   if (check_cuda(cudaMemcpyAsync(s->twiddle, tw.data(), sizeof(float2) * tw.size(),
                                  cudaMemcpyHostToDevice, s->stream), "H2D twiddles") ||
       check_cuda(cudaMemsetAsync(s->stats, 0, sizeof(LayoutStats), s->stream), "memset stats") ||
+      check_cuda(cudaMemcpyAsync(&s->stats->lagrange, &s->interp, sizeof(int), cudaMemcpyHostToDevice, s->stream),
+                 "H2D interpolation") ||
       check_cuda(cudaMemsetAsync(s->charges, 0, sizeof(ChargeCell) * cells, s->stream), "memset charges") ||
       check_cuda(cudaMemsetAsync(s->update, 0, sizeof(float2) * n, s->stream), "memset update")) {
     session_destroy(s);

@@ -230,6 +230,13 @@ int fe_b200_tsne_get_p(fe_b200_tsne* s, int* row_ptr, int* col, float* val);
  * shared memory (set at each spatial reorder; the rest gather from L2).
  * Synchronises the session stream. */
 int fe_b200_tsne_staged_blocks(fe_b200_tsne* s, int* staged, int* blocks);
+/* Repulsion interpolation of a session: 0 = bilinear on the reference's G x G grid
+ * (default; the reference's scheme, src/tsne_neighbors.cpp:1076-1182), 1 = FIt-SNE
+ * boxes: square boxes of about one layout unit (at least 50 per side, at most G/3),
+ * three nodes per box and side, quadratic Lagrange spread and gather.  No
+ * counterpart in the reference; FASTEMBEDR_B200_INTERPOLATION=lagrange selects 1
+ * for every session and one-shot call (and doubles the default G). */
+int fe_b200_tsne_set_interpolation(fe_b200_tsne* s, int mode);
 /* Exact Euclidean KNN on the device: the producer of the GPU-KNN object the
  * device-KNN entry points consume (the reference's native_cuda_knn_impl with its
  * exact route and finalize step, src/native_knn_cuda_impl.cpp:511-700, 418-470;

@@ -774,3 +774,81 @@ def pca_start(x: np.ndarray) -> np.ndarray:
     sd = np.sqrt(ss / max(n - 1, 1))
     scale = 1e-4 / sd.max() if np.isfinite(sd.max()) and sd.max() > 0 else 1.0
     return ((s - mu) * scale).astype(np.float32)
+
+
+def _lagrange3(t):
+    """Quadratic Lagrange basis at the nodes (j + 1/2) / 3, j = 0, 1, 2."""
+    t0, t1, t2 = 1.0 / 6.0, 0.5, 5.0 / 6.0
+    return np.stack([4.5 * (t - t1) * (t - t2), -9.0 * (t - t0) * (t - t2), 4.5 * (t - t0) * (t - t1)], -1)
+
+
+def tsne_gradient_lagrange(P: Csr, y: np.ndarray, exaggeration: float, grid_size: int, return_z: bool = False):
+    """The openTSNE gradient with FIt-SNE's box interpolation, restated in double
+    (Linderman et al., "Fast interpolation-based t-SNE", Nature Methods 2019):
+    square boxes of about one unit (intervals_per_integer = 1), at least 50 and at
+    most grid_size // 3 per side, over the layout's bounding square from its lower
+    corner; three nodes per box and side at (j + 1/2)/3 of the box, which form a
+    uniform grid of spacing box / 3; charges {1, y_x, y_y} spread with quadratic
+    Lagrange weights; linear convolution (zero-padded FFT) with 1/(1+d^2) and
+    its square; the potentials gathered with the same weights;
+    Z = sum_i phi_q(y_i) - n.  The attraction is the reference's
+    (add_sparse_attractive_gradient_f, src/tsne_neighbors.cpp:985-1012)."""
+    y = np.asarray(y, np.float32)
+    yd = y.astype(np.float64)
+    n = y.shape[0]
+    g = grid_size
+    lo = y.min(0).astype(np.float64)
+    ext = float((y.max(0) - y.min(0)).max())
+    if not np.isfinite(ext) or ext <= 0:
+        ext = 1.0
+    boxes = max(1, min(g // 3, max(50, int(np.ceil(np.float32(ext))))))
+    box = ext / boxes
+    h = box / 3.0
+    u = (yd - lo) / box
+    b = np.clip(np.floor(u), 0, boxes - 1).astype(np.int64)
+    t = np.clip(u - b, 0.0, 1.0)
+    wx, wy = _lagrange3(t[:, 0]), _lagrange3(t[:, 1])
+    charges = np.zeros((3, g, g))
+    nodes = []
+    for k in range(3):
+        for j in range(3):
+            w = wx[:, j] * wy[:, k]
+            ix, iy = 3 * b[:, 0] + j, 3 * b[:, 1] + k
+            nodes.append((w, iy, ix))
+            np.add.at(charges[0], (iy, ix), w)
+            np.add.at(charges[1], (iy, ix), w * yd[:, 0])
+            np.add.at(charges[2], (iy, ix), w * yd[:, 1])
+    m = 2 * g
+    off = np.arange(m)
+    off = np.where(off < g, off, off - m).astype(np.float64) * h
+    d2 = off[:, None] ** 2 + off[None, :] ** 2
+    kq = 1.0 / (1.0 + d2)
+    kq[g, :] = 0.0
+    kq[:, g] = 0.0
+    fq, fq2 = np.fft.rfft2(kq), np.fft.rfft2(kq * kq)
+
+    def conv(c, kf):
+        pad = np.zeros((m, m))
+        pad[:g, :g] = c
+        return np.fft.irfft2(np.fft.rfft2(pad) * kf, s=(m, m))[:g, :g]
+
+    phi_q, phi_q2 = conv(charges[0], fq), conv(charges[0], fq2)
+    phi_x, phi_y = conv(charges[1], fq2), conv(charges[2], fq2)
+    gq = np.zeros(n)
+    gq2 = np.zeros(n)
+    gx = np.zeros(n)
+    gy = np.zeros(n)
+    for w, iy, ix in nodes:
+        gq += w * phi_q[iy, ix]
+        gq2 += w * phi_q2[iy, ix]
+        gx += w * phi_x[iy, ix]
+        gy += w * phi_y[iy, ix]
+    z = float(gq.sum() - n)
+    rep = -np.stack([yd[:, 0] * gq2 - gx, yd[:, 1] * gq2 - gy], 1) / z
+    rows = np.repeat(np.arange(n), np.diff(P.row_ptr))
+    dd = yd[rows] - yd[P.col]
+    q = 1.0 / (1.0 + (dd * dd).sum(1))
+    att = np.zeros((n, 2))
+    np.add.at(att, rows, (exaggeration * P.val.astype(np.float64) * q)[:, None] * dd)
+    grad = (rep + att).astype(np.float32)
+    return (grad, z) if return_z else grad

@@ -263,7 +263,6 @@ struct TsneSession {
   float2* krow = nullptr;
   float2* colspec = nullptr;
   float4* pot = nullptr;
-  float2* twiddle = nullptr;  // exp(-2 pi i k / M), k < M/2
 
   int interp = 0;  // 0 bilinear (the reference's), 1 Lagrange 3-node boxes (FIt-SNE)
   int update_blocks = 0;

@@ -43,42 +43,79 @@ __device__ __forceinline__ float2 csub(float2 a, float2 b) { return make_float2(
 __device__ __forceinline__ float2 conjf2(float2 a) { return make_float2(a.x, -a.y); }
 __device__ __forceinline__ float2 cscale(float2 a, float s) { return make_float2(a.x * s, a.y * s); }
 
-// In-place radix-2 decimation-in-time FFT of `count` length-M sequences laid
-// out back to back in shared memory.  tw[k] = exp(-2 pi i k / M), k < M/2.
-// The inverse is unnormalised.
-__device__ void block_fft(float2* buf, int count, int m, int log_m, const float2* __restrict__ tw,
-                          bool inverse) {
-  const int total = count * m;
-  for (int t = threadIdx.x; t < total; t += blockDim.x) {
-    const int s = t >> log_m;
-    const int i = t & (m - 1);
-    const int j = static_cast<int>(__brev(static_cast<unsigned>(i)) >> (32 - log_m));
-    if (i < j) {
-      float2* base = buf + (s << log_m);
-      const float2 a = base[i];
-      base[i] = base[j];
-      base[j] = a;
+// In-place FFT of `count` length-m sequences laid out back to back in shared
+// memory (m a power of two, count * m <= 8192, blockDim.x = 256), Stockham
+// radix 4 with a final radix-2 pass when log2 m is odd: every pass reads each
+// element once into registers, waits at one barrier, applies the twiddles
+// exp(-+2 pi i q k / (4 ns)) and a 4-point DFT, and writes each element once
+// to its Stockham position, so the output is in natural order without a
+// bit-reversal pass.  Twiddles come from sincospif (the FP pipe) rather than a
+// table in memory.  The inverse is unnormalised.
+constexpr int kFftMaxBatch = 8;  // four-element groups per thread and pass
+
+__device__ __forceinline__ float2 twiddle_pi(float turns_times_two) {
+  float sn, cs;
+  sincospif(turns_times_two, &sn, &cs);
+  return make_float2(cs, sn);
+}
+
+__device__ void block_fft(float2* buf, int count, int m, int log_m, bool inverse) {
+  const int quarter = m >> 2;
+  const int lq = log_m - 2;
+  const int total4 = count * quarter;
+  const float sgn = inverse ? 2.0f : -2.0f;
+  int ns = 1;
+  for (int pass = 0; pass < (log_m >> 1); ++pass) {
+    float2 x[kFftMaxBatch][4];
+#pragma unroll
+    for (int b = 0; b < kFftMaxBatch; ++b) {
+      const int t = static_cast<int>(threadIdx.x) + b * static_cast<int>(blockDim.x);
+      if (t < total4) {
+        const float2* src = buf + ((t >> lq) << log_m) + (t & (quarter - 1));
+#pragma unroll
+        for (int q = 0; q < 4; ++q) x[b][q] = src[q * quarter];
+      }
     }
+    __syncthreads();
+#pragma unroll
+    for (int b = 0; b < kFftMaxBatch; ++b) {
+      const int t = static_cast<int>(threadIdx.x) + b * static_cast<int>(blockDim.x);
+      if (t < total4) {
+        const int j = t & (quarter - 1);
+        const int k = j & (ns - 1);
+        if (ns > 1) {
+          const float inv_span = 1.0f / static_cast<float>(4 * ns);
+#pragma unroll
+          for (int q = 1; q < 4; ++q) {
+            x[b][q] = cmul(x[b][q], twiddle_pi(sgn * static_cast<float>(q * k) * inv_span));
+          }
+        }
+        const float2 a0 = cadd(x[b][0], x[b][2]);
+        const float2 a1 = csub(x[b][0], x[b][2]);
+        const float2 a2 = cadd(x[b][1], x[b][3]);
+        const float2 d = csub(x[b][1], x[b][3]);
+        const float2 a3 = inverse ? make_float2(-d.y, d.x) : make_float2(d.y, -d.x);  // +-i d
+        float2* dst = buf + ((t >> lq) << log_m) + ((j - k) << 2) + k;
+        dst[0] = cadd(a0, a2);
+        dst[ns] = cadd(a1, a3);
+        dst[2 * ns] = csub(a0, a2);
+        dst[3 * ns] = csub(a1, a3);
+      }
+    }
+    __syncthreads();
+    ns <<= 2;
   }
-  __syncthreads();
-  const int half_total = count * (m >> 1);
-  for (int stage = 1; stage <= log_m; ++stage) {
-    const int half = 1 << (stage - 1);
-    const int tw_shift = log_m - stage;  // twiddle index = j * (M / len)
-    for (int t = threadIdx.x; t < half_total; t += blockDim.x) {
-      const int s = t >> (log_m - 1);
-      const int b = t & ((m >> 1) - 1);
-      const int grp = b >> (stage - 1);
-      const int j = b & (half - 1);
-      float2* base = buf + (s << log_m);
-      const int u = (grp << stage) + j;
-      const int v = u + half;
-      float2 w = __ldg(tw + (j << tw_shift));
-      if (inverse) w.y = -w.y;
-      const float2 x = cmul(base[v], w);
-      const float2 a = base[u];
-      base[v] = csub(a, x);
-      base[u] = cadd(a, x);
+  if (log_m & 1) {
+    // Last pass, radix 2 with span m / 2: each thread owns the pair (j, j + m/2).
+    const int half = m >> 1;
+    const float inv_m = 1.0f / static_cast<float>(m);
+    for (int t = threadIdx.x; t < count * half; t += blockDim.x) {
+      const int j = t & (half - 1);
+      float2* base = buf + ((t >> (log_m - 1)) << log_m);
+      const float2 a = base[j];
+      const float2 b = cmul(base[j + half], twiddle_pi(sgn * static_cast<float>(j) * inv_m));
+      base[j] = cadd(a, b);
+      base[j + half] = csub(a, b);
     }
     __syncthreads();
   }
@@ -574,8 +611,7 @@ __device__ __forceinline__ float3 read_charge(const ChargeCell& c, const ChargeS
 // (m + i mx), (my + i Kq), (Kq2) into three complex length-M FFTs.
 __global__ void fft_rows_fwd_kernel(const ChargeCell* __restrict__ charges,
                                     const LayoutStats* __restrict__ stats, int n, int g, int m,
-                                    int log_m, const float2* __restrict__ tw,
-                                    float2* __restrict__ rowspec, float2* __restrict__ krow) {
+                                    int log_m, float2* __restrict__ rowspec, float2* __restrict__ krow) {
   extern __shared__ float2 smem[];
   float2* z0 = smem;
   float2* z1 = smem + m;
@@ -597,7 +633,7 @@ __global__ void fft_rows_fwd_kernel(const ChargeCell* __restrict__ charges,
     z2[x] = make_float2(kq2, 0.f);
   }
   __syncthreads();
-  block_fft(smem, 3, m, log_m, tw, false);
+  block_fft(smem, 3, m, log_m, false);
   const int row_len = g + 1;
   for (int k = threadIdx.x; k <= g; k += blockDim.x) {
     const int km = (m - k) & (m - 1);
@@ -623,8 +659,7 @@ __global__ void fft_rows_fwd_kernel(const ChargeCell* __restrict__ charges,
 // of the real, even kernel columns (Kq + i Kq2 packs two real spectra), product,
 // inverse y-FFT, keep rows [0, G).
 __global__ void fft_cols_kernel(const float2* __restrict__ rowspec, const float2* __restrict__ krow,
-                                int g, int m, int log_m, int tk, const float2* __restrict__ tw,
-                                float2* __restrict__ colspec) {
+                                int g, int m, int log_m, int tk, float2* __restrict__ colspec) {
   extern __shared__ float2 smem[];
   const int row_len = g + 1;
   const int k0 = blockIdx.x * tk;
@@ -652,7 +687,7 @@ __global__ void fft_cols_kernel(const float2* __restrict__ rowspec, const float2
     b[3 * m + r] = kk;
   }
   __syncthreads();
-  block_fft(smem, cols * 4, m, log_m, tw, false);
+  block_fft(smem, cols * 4, m, log_m, false);
   for (int t = threadIdx.x; t < cols * m; t += blockDim.x) {
     const int c = t >> log_m;
     const int r = t & (m - 1);
@@ -666,7 +701,7 @@ __global__ void fft_cols_kernel(const float2* __restrict__ rowspec, const float2
     b[2 * m + r] = cscale(b[2 * m + r], kq2);  // phi_yq2
   }
   __syncthreads();
-  block_fft(smem, cols * 4, m, log_m, tw, true);
+  block_fft(smem, cols * 4, m, log_m, true);
   for (int t = threadIdx.x; t < cols * g; t += blockDim.x) {
     const int c = t / g;
     const int r = t - c * g;
@@ -684,8 +719,7 @@ __global__ void fft_cols_kernel(const float2* __restrict__ rowspec, const float2
 // from their half spectra, potentials, this row's share of Z, and clearing of
 // the charges for the next splat.  The last block folds Z.
 __global__ void fft_rows_inv_kernel(const float2* __restrict__ colspec, ChargeCell* __restrict__ charges,
-                                    int n, int g, int m, int log_m, const float2* __restrict__ tw,
-                                    float4* __restrict__ pot, double* __restrict__ z_partials,
+                                    int n, int g, int m, int log_m, float4* __restrict__ pot, double* __restrict__ z_partials,
                                     LayoutStats* __restrict__ stats) {
   extern __shared__ float2 smem[];
   float2* z0 = smem;
@@ -708,7 +742,7 @@ __global__ void fft_rows_inv_kernel(const float2* __restrict__ colspec, ChargeCe
     z1[k] = make_float2(c.x - d.y, c.y + d.x);
   }
   __syncthreads();
-  block_fft(smem, 2, m, log_m, tw, true);
+  block_fft(smem, 2, m, log_m, true);
   const float scale = 1.0f / (static_cast<float>(m) * static_cast<float>(m));
   double zpart = 0.0;
   for (int x = threadIdx.x; x < g; x += blockDim.x) {
@@ -1317,7 +1351,7 @@ int launch_iteration(TsneSession* s, GradMode mode, float exaggeration, float mo
   {
     ProfileScope ps(s, kKindFftRows);
     fft_rows_fwd_kernel<<<g, 256, 3 * m * sizeof(float2), s->stream>>>(
-        s->charges, s->stats, s->n, g, m, lm, s->twiddle, s->rowspec, s->krow);
+        s->charges, s->stats, s->n, g, m, lm, s->rowspec, s->krow);
     FE_LAUNCH("fft_rows_fwd_kernel");
   }
   {
@@ -1325,13 +1359,13 @@ int launch_iteration(TsneSession* s, GradMode mode, float exaggeration, float mo
     const int tk = s->cols_per_block;
     const int blocks = (row_len + tk - 1) / tk;
     fft_cols_kernel<<<blocks, 256, static_cast<size_t>(tk) * 4 * m * sizeof(float2), s->stream>>>(
-        s->rowspec, s->krow, g, m, lm, tk, s->twiddle, s->colspec);
+        s->rowspec, s->krow, g, m, lm, tk, s->colspec);
     FE_LAUNCH("fft_cols_kernel");
   }
   {
     ProfileScope ps(s, kKindFftRowsInv);
     fft_rows_inv_kernel<<<g, 256, 2 * m * sizeof(float2), s->stream>>>(
-        s->colspec, s->charges, s->n, g, m, lm, s->twiddle, s->pot, s->z_partials, s->stats);
+        s->colspec, s->charges, s->n, g, m, lm, s->pot, s->z_partials, s->stats);
     FE_LAUNCH("fft_rows_inv_kernel");
   }
   const UpdateParams prm{s->n, s->row_begin, s->row_end, g, exaggeration, momentum,

@@ -188,7 +188,6 @@ int session_create(TsneSession** out, int n, int grid, int* d_row_ptr, int* d_co
     s->krow = a.take<float2>(spec);
     s->colspec = a.take<float2>(4 * spec);
     s->pot = a.take<float4>(cells);
-    s->twiddle = a.take<float2>(m / 2);
     s->ro_keys = a.take<unsigned int>(n);
     s->ro_keys_sorted = a.take<unsigned int>(n);
     s->ro_idx = a.take<int>(n);
@@ -218,14 +217,7 @@ int session_create(TsneSession** out, int n, int grid, int* d_row_ptr, int* d_co
       }
     }
   }
-  std::vector<float2> tw(m / 2);
-  for (int k = 0; k < m / 2; ++k) {
-    const double ang = -2.0 * M_PI * static_cast<double>(k) / static_cast<double>(m);
-    tw[k] = make_float2(static_cast<float>(std::cos(ang)), static_cast<float>(std::sin(ang)));
-  }
-  if (check_cuda(cudaMemcpyAsync(s->twiddle, tw.data(), sizeof(float2) * tw.size(),
-                                 cudaMemcpyHostToDevice, s->stream), "H2D twiddles") ||
-      check_cuda(cudaMemsetAsync(s->stats, 0, sizeof(LayoutStats), s->stream), "memset stats") ||
+  if (check_cuda(cudaMemsetAsync(s->stats, 0, sizeof(LayoutStats), s->stream), "memset stats") ||
       check_cuda(cudaMemcpyAsync(&s->stats->lagrange, &s->interp, sizeof(int), cudaMemcpyHostToDevice, s->stream),
                  "H2D interpolation") ||
       check_cuda(cudaMemsetAsync(s->charges, 0, sizeof(ChargeCell) * cells, s->stream), "memset charges") ||

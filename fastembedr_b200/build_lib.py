@@ -24,7 +24,7 @@ INCLUDE = os.path.join(ROOT, "include")
 LIB = os.path.join(PKG, "libfastembedr_b200.so")
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 
-SOURCES = ["common.cu", "nccl_loader.cu", "tsne_affinity.cu", "tsne_kernels.cu", "tsne_session.cu",
+SOURCES = ["common.cu", "host_copy.cu", "nccl_loader.cu", "tsne_affinity.cu", "tsne_kernels.cu", "tsne_session.cu",
            "tsne_reorder.cu", "tsne_shard.cu", "multi_device.cu", "umap.cu", "umap_graph.cu", "umap_noalloc.cu", "umap_session.cu", "landmark.cu", "pca.cu", "knn.cu", "capi.cu"]
 HEADERS = ["fe_common.cuh", "nccl_loader.cuh", "rank_group.h", "tsne.cuh", "umap.cuh"]
 

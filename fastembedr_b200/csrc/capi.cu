@@ -60,8 +60,7 @@ struct DeviceCopy {
 
 int copy_to_device(const void* host, size_t bytes, DeviceCopy& dst, cudaStream_t stream, const char* what) {
   FE_CUDA(cudaMalloc(&dst.p, bytes ? bytes : 1), what);
-  FE_CUDA(cudaMemcpyAsync(dst.p, host, bytes, cudaMemcpyHostToDevice, stream), what);
-  return 0;
+  return fe::h2d_copy(dst.p, host, bytes, stream, what);
 }
 
 // Shared by every openTSNE entry point (the reference's
@@ -260,10 +259,10 @@ int umap_host_run(const int* heads, const int* tails, const float* eps, long lon
       FE_TRY(arena.commit("COO UMAP workspace"));
     }
   }
-  FE_CUDA(cudaMemcpyAsync(d_heads, heads, e * sizeof(int), cudaMemcpyHostToDevice, stream), "H2D heads");
-  FE_CUDA(cudaMemcpyAsync(d_tails, tails, e * sizeof(int), cudaMemcpyHostToDevice, stream), "H2D tails");
-  FE_CUDA(cudaMemcpyAsync(d_eps, eps, e * sizeof(float), cudaMemcpyHostToDevice, stream), "H2D epochs_per_sample");
-  FE_CUDA(cudaMemcpyAsync(d_layout, init, sizeof(float2) * n, cudaMemcpyHostToDevice, stream), "H2D init");
+  FE_TRY(fe::h2d_copy(d_heads, heads, e * sizeof(int), stream, "H2D heads"));
+  FE_TRY(fe::h2d_copy(d_tails, tails, e * sizeof(int), stream, "H2D tails"));
+  FE_TRY(fe::h2d_copy(d_eps, eps, e * sizeof(float), stream, "H2D epochs_per_sample"));
+  FE_TRY(fe::h2d_copy(d_layout, init, sizeof(float2) * n, stream, "H2D init"));
   FE_CUDA(cudaMemsetAsync(d_count, 0, sizeof(long long), stream), "memset count");
   fe::UmapRun r;
   r.params = fe::UmapParams{n, n_epochs, nsr, hash_key_is_tail, seed, lr, a, b, rep};

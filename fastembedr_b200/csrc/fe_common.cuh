@@ -101,6 +101,11 @@ int knn_exact(const void* data, bool data_double, bool data_on_device, bool col_
 // SM count of the current device (cached per device).
 int sm_count();
 
+// Host -> device copy of a caller's buffer (pageable or pinned) that returns
+// once the data is on the device; large pageable sources are staged through
+// a pinned pool by several host threads (host_copy.cu).
+int h2d_copy(void* dst, const void* src, std::size_t bytes, cudaStream_t stream, const char* what);
+
 // Environment helpers.
 int env_int(const char* name, int fallback);         // positive values only
 int env_int_nonneg(const char* name, int fallback);  // zero allowed

@@ -305,7 +305,7 @@ int knn_exact(const void* data, bool data_double, bool data_on_device, bool col_
   }
   const void* src = data;
   if (!data_on_device) {
-    FE_CUDA(cudaMemcpyAsync(raw, data, static_cast<size_t>(n) * p * elt, cudaMemcpyHostToDevice, st), "H2D KNN data");
+    FE_TRY(h2d_copy(raw, data, static_cast<size_t>(n) * p * elt, st, "H2D KNN data"));
     src = raw;
   }
   if (data_double) {

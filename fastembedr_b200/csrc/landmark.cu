@@ -481,10 +481,8 @@ int landmark_tsne(const int* device_indices, const float* device_distances, int 
       cudaStreamDestroy(s);
     }
   } guard{st};
-  FE_CUDA(cudaMemcpyAsync(d_ref, reference_data, ref_items * sizeof(float), cudaMemcpyHostToDevice, st),
-          "H2D landmark reference data");
-  FE_CUDA(cudaMemcpyAsync(d_query, query_data, query_items * sizeof(float), cudaMemcpyHostToDevice, st),
-          "H2D landmark query data");
+  FE_TRY(h2d_copy(d_ref, reference_data, ref_items * sizeof(float), st, "H2D landmark reference data"));
+  FE_TRY(h2d_copy(d_query, query_data, query_items * sizeof(float), st, "H2D landmark query data"));
   FE_CUDA(cudaMemcpyAsync(d_layout_cm, reference_layout, 2 * static_cast<size_t>(n_reference) * sizeof(float),
                           cudaMemcpyHostToDevice, st),
           "H2D landmark reference layout");

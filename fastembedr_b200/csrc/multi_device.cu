@@ -144,10 +144,8 @@ void rank_main(const MultiDeviceTsne& job, int rank, Shared* sh) {
       if (rc == 0) rc = check_cuda(cudaMemcpyPeerAsync(d_dist.p, dev, job.distances, job.caller_device,
                                                        dist_bytes, stream), "peer copy distances");
     } else if (rc == 0) {
-      rc = check_cuda(cudaMemcpyAsync(d_idx.p, job.indices, items * sizeof(int), cudaMemcpyHostToDevice, stream),
-                      "H2D indices");
-      if (rc == 0) rc = check_cuda(cudaMemcpyAsync(d_dist.p, job.distances, dist_bytes, cudaMemcpyHostToDevice,
-                                                   stream), "H2D distances");
+      rc = h2d_copy(d_idx.p, job.indices, items * sizeof(int), stream, "H2D indices");
+      if (rc == 0) rc = h2d_copy(d_dist.p, job.distances, dist_bytes, stream, "H2D distances");
     }
     idx_dev = static_cast<const int*>(d_idx.p);
     dist_dev = d_dist.p;

@@ -302,9 +302,7 @@ int pca_start_layout(const void* values, bool values_double, int n, int p, cudaS
       FE_TRY(a.commit("device PCA initialization"));
     }
   }
-  FE_CUDA(cudaMemcpyAsync(d_raw, values, items * (values_double ? sizeof(double) : sizeof(float)),
-                          cudaMemcpyHostToDevice, st),
-          "H2D PCA data");
+  FE_TRY(h2d_copy(d_raw, values, items * (values_double ? sizeof(double) : sizeof(float)), st, "H2D PCA data"));
   FE_CUDA(cudaMemsetAsync(d_part, 0, static_cast<size_t>(chunks) * tiles * tiles * kPcaTile * kPcaTile * sizeof(double),
                           st),
           "memset PCA partials");

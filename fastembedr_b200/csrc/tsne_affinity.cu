@@ -338,8 +338,8 @@ int upload_csr(const int* row_ptr, const int* col, const float* val, int n, cuda
   FE_TRY(d_c.alloc(nnz, "cudaMalloc(col)"));
   FE_TRY(d_v.alloc(nnz, "cudaMalloc(val)"));
   FE_CUDA(cudaMemcpyAsync(d_rp.p, row_ptr, sizeof(int) * (n + 1), cudaMemcpyHostToDevice, stream), "H2D row_ptr");
-  FE_CUDA(cudaMemcpyAsync(d_c.p, col, sizeof(int) * nnz, cudaMemcpyHostToDevice, stream), "H2D col");
-  FE_CUDA(cudaMemcpyAsync(d_v.p, val, sizeof(float) * nnz, cudaMemcpyHostToDevice, stream), "H2D val");
+  FE_TRY(h2d_copy(d_c.p, col, sizeof(int) * nnz, stream, "H2D col"));
+  FE_TRY(h2d_copy(d_v.p, val, sizeof(float) * nnz, stream, "H2D val"));
   FE_CUDA(cudaStreamSynchronize(stream), "cudaStreamSynchronize(csr upload)");
   *out_row_ptr = d_rp.release();
   *out_col = d_c.release();

@@ -120,9 +120,8 @@ int fe_b200_umap_create(const int* indices, const float* distances, int n, int k
       const size_t items = static_cast<size_t>(n) * k;
       FE_CUDA(cudaMalloc(&d_idx, items * sizeof(int)), "cudaMalloc(UMAP indices)");
       FE_CUDA(cudaMalloc(&d_dist, items * sizeof(float)), "cudaMalloc(UMAP distances)");
-      FE_CUDA(cudaMemcpyAsync(d_idx, indices, items * sizeof(int), cudaMemcpyHostToDevice, s->stream), "H2D");
-      FE_CUDA(cudaMemcpyAsync(d_dist, distances, items * sizeof(float), cudaMemcpyHostToDevice, s->stream),
-              "H2D");
+      FE_TRY(fe::h2d_copy(d_idx, indices, items * sizeof(int), s->stream, "H2D UMAP indices"));
+      FE_TRY(fe::h2d_copy(d_dist, distances, items * sizeof(float), s->stream, "H2D UMAP distances"));
       idx_dev = static_cast<const int*>(d_idx);
       dist_dev = static_cast<const float*>(d_dist);
     }

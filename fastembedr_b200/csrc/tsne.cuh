@@ -267,7 +267,6 @@ struct TsneSession {
   int interp = 0;  // 0 bilinear (the reference's), 1 Lagrange 3-node boxes (FIt-SNE)
   int update_blocks = 0;
   int update_threads = 256;
-  int cols_per_block = 1;
 
   // Optional per-kernel CUDA-event timing (bench / profiling).
   bool profile = false;

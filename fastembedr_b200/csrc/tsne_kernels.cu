@@ -29,6 +29,7 @@
 //                          the last block derives the next grid geometry
 #include "tsne.cuh"
 
+#include <algorithm>
 #include <cfloat>
 #include <climits>
 
@@ -43,79 +44,169 @@ __device__ __forceinline__ float2 csub(float2 a, float2 b) { return make_float2(
 __device__ __forceinline__ float2 conjf2(float2 a) { return make_float2(a.x, -a.y); }
 __device__ __forceinline__ float2 cscale(float2 a, float s) { return make_float2(a.x * s, a.y * s); }
 
-// In-place FFT of `count` length-m sequences laid out back to back in shared
-// memory (m a power of two, count * m <= 8192, blockDim.x = 256), Stockham
-// radix 4 with a final radix-2 pass when log2 m is odd: every pass reads each
+// ---- shared-memory FFT
+//
+// In-place FFT of COUNT length-M sequences laid out back to back in shared
+// memory, M = 2^LOG_M known at compile time (the three FFT kernels are
+// instantiated for every grid side, 4 to 1024), so loop trips, shifts and
+// masks are constants and every thread's loads are issued together.  Stockham
+// radix 4, with a final radix-2 pass when LOG_M is odd: every pass reads each
 // element once into registers, waits at one barrier, applies the twiddles
-// exp(-+2 pi i q k / (4 ns)) and a 4-point DFT, and writes each element once
-// to its Stockham position, so the output is in natural order without a
-// bit-reversal pass.  Twiddles come from sincospif (the FP pipe) rather than a
-// table in memory.  The inverse is unnormalised.
-constexpr int kFftMaxBatch = 8;  // four-element groups per thread and pass
+// w^q (q = 1, 2, 3; w = exp(-+2 pi i k / (4 ns))) and a 4-point DFT, and writes
+// each element once to its Stockham position, so the output is in natural
+// order without a bit-reversal pass.  The inverse is unnormalised.
+//
+// Twiddles: a per-block table in shared memory, filled once per launch with
+// sincospif (arguments k / 2^j are exact in float): radix-4 pass p >= 1 (ns =
+// 4^p) owns entries [(4^p - 4) / 3, (4^(p+1) - 4) / 3), entry k holding
+// exp(-2 pi i k / (4 ns)), so the lanes of a warp read consecutive entries;
+// w^2 and w^3 are complex products.  The radix-2 pass reads exp(-2 pi i j / M),
+// j < M / 2, after them.  The inverse conjugates.
+//
+// Element i of the data buffer lives at sw(i): the low four index bits are
+// XORed with 5 * ((i >> 4) & 3), so that the strided writes of the first two
+// passes (ns = 1: stride 4; ns = 4: runs of 4 at stride 16) and the unit-
+// stride reads and writes of every pass hit 16 different 8-byte bank pairs in
+// each half-warp.  sw permutes each aligned run of 16 elements, and adding a
+// multiple of 64 commutes with it.
+constexpr int kFftBatch = 4;        // four-element groups per thread and pass: row passes
+constexpr int kFftBatchCols = 2;    // column pass (twice the threads, so it needs no spills)
 
-__device__ __forceinline__ float2 twiddle_pi(float turns_times_two) {
-  float sn, cs;
-  sincospif(turns_times_two, &sn, &cs);
-  return make_float2(cs, sn);
+__device__ __forceinline__ int sw(int i) { return i ^ (((i >> 4) & 3) * 5); }
+
+// Columns per block of the column pass: one once a transform fills a block,
+// several for short ones (measured 1.9x faster than 4 per block at G = 256).
+constexpr int fft_cols_per_block(int m) { return m >= 256 ? 1 : (2048 / m < 16 ? 2048 / m : 16); }
+
+// Threads for a block holding `count` length-m sequences: enough for `batch`
+// groups per thread and pass, and at least 256 (fewer only when there are
+// fewer groups) so that short transforms keep eight warps.
+constexpr int fft_threads_for(int count, int m, int batch) {
+  const int groups = count * m / 4;
+  const int need = (groups + batch - 1) / batch;
+  const int floor_threads = groups < 64 ? 64 : (groups < 256 ? groups : 256);
+  const int t = need > floor_threads ? need : floor_threads;
+  return (t + 31) / 32 * 32;
 }
 
-__device__ void block_fft(float2* buf, int count, int m, int log_m, bool inverse) {
-  const int quarter = m >> 2;
-  const int lq = log_m - 2;
-  const int total4 = count * quarter;
-  const float sgn = inverse ? 2.0f : -2.0f;
-  int ns = 1;
-  for (int pass = 0; pass < (log_m >> 1); ++pass) {
-    float2 x[kFftMaxBatch][4];
+constexpr int fft_tw4_entries(int log_m) { return ((1 << (2 * (log_m / 2))) - 4) / 3; }
+constexpr int fft_table_entries(int log_m) { return fft_tw4_entries(log_m) + ((log_m & 1) ? (1 << (log_m - 1)) : 0); }
+constexpr int fft_data_entries(int count, int m) { return (count * m + 15) / 16 * 16; }
+
+template <int LOG_M, int COUNT, int BATCH = kFftBatch>
+struct FftShape {
+  static constexpr int M = 1 << LOG_M;
+  static constexpr int THREADS = fft_threads_for(COUNT, M, BATCH);
+  static constexpr int DATA = fft_data_entries(COUNT, M);
+  static constexpr int TABLE = fft_table_entries(LOG_M);
+  static constexpr size_t SMEM = static_cast<size_t>(DATA + TABLE) * sizeof(float2);
+  static_assert(THREADS <= 1024, "FFT block too large");
+  static_assert((COUNT * M / 4 + THREADS - 1) / THREADS <= BATCH, "groups per thread");
+};
+
+template <int LOG_M, int THREADS>
+__device__ __forceinline__ void fft_fill_twiddles(float2* __restrict__ tw) {
+  constexpr int TW4 = fft_tw4_entries(LOG_M);
+  constexpr int TOTAL = fft_table_entries(LOG_M);
+  for (int i = threadIdx.x; i < TOTAL; i += THREADS) {
+    float turns;
+    if (i < TW4) {
+      int p = 1, off = 0;
+      while (off + (1 << (2 * p)) <= i) {
+        off += 1 << (2 * p);
+        ++p;
+      }
+      turns = static_cast<float>(i - off) / static_cast<float>(4 << (2 * p));
+    } else {
+      turns = static_cast<float>(i - TW4) / static_cast<float>(1 << LOG_M);
+    }
+    float sn, cs;
+    sincospif(-2.0f * turns, &sn, &cs);
+    tw[i] = make_float2(cs, sn);
+  }
+}
+
+template <int LOG_M, int COUNT, int THREADS>
+__device__ __forceinline__ void block_fft(float2* __restrict__ buf, const float2* __restrict__ tw, bool inverse) {
+  constexpr int M = 1 << LOG_M;
+  constexpr int QUARTER = M / 4;
+  constexpr int LQ = LOG_M - 2;
+  constexpr int GROUPS = COUNT * QUARTER;
+  constexpr int BATCHES = (GROUPS + THREADS - 1) / THREADS;
+  constexpr int PASSES = LOG_M / 2;
 #pragma unroll
-    for (int b = 0; b < kFftMaxBatch; ++b) {
-      const int t = static_cast<int>(threadIdx.x) + b * static_cast<int>(blockDim.x);
-      if (t < total4) {
-        const float2* src = buf + ((t >> lq) << log_m) + (t & (quarter - 1));
+  for (int pass = 0; pass < PASSES; ++pass) {
+    const int ns = 1 << (2 * pass);
+    const int tw_off = (ns - 4) / 3;
+    float2 x[BATCHES][4];
 #pragma unroll
-        for (int q = 0; q < 4; ++q) x[b][q] = src[q * quarter];
+    for (int b = 0; b < BATCHES; ++b) {
+      const int t = static_cast<int>(threadIdx.x) + b * THREADS;
+      if (GROUPS % THREADS == 0 || t < GROUPS) {
+        const int src = ((t >> LQ) << LOG_M) + (t & (QUARTER - 1));
+        if (QUARTER % 64 == 0) {
+          const int s0 = sw(src);
+#pragma unroll
+          for (int q = 0; q < 4; ++q) x[b][q] = buf[s0 + q * QUARTER];
+        } else {
+#pragma unroll
+          for (int q = 0; q < 4; ++q) x[b][q] = buf[sw(src + q * QUARTER)];
+        }
       }
     }
     __syncthreads();
 #pragma unroll
-    for (int b = 0; b < kFftMaxBatch; ++b) {
-      const int t = static_cast<int>(threadIdx.x) + b * static_cast<int>(blockDim.x);
-      if (t < total4) {
-        const int j = t & (quarter - 1);
+    for (int b = 0; b < BATCHES; ++b) {
+      const int t = static_cast<int>(threadIdx.x) + b * THREADS;
+      if (GROUPS % THREADS == 0 || t < GROUPS) {
+        const int j = t & (QUARTER - 1);
         const int k = j & (ns - 1);
-        if (ns > 1) {
-          const float inv_span = 1.0f / static_cast<float>(4 * ns);
-#pragma unroll
-          for (int q = 1; q < 4; ++q) {
-            x[b][q] = cmul(x[b][q], twiddle_pi(sgn * static_cast<float>(q * k) * inv_span));
-          }
+        if (pass > 0) {
+          float2 w1 = tw[tw_off + k];
+          if (inverse) w1.y = -w1.y;
+          const float2 w2 = cmul(w1, w1);
+          x[b][1] = cmul(x[b][1], w1);
+          x[b][2] = cmul(x[b][2], w2);
+          x[b][3] = cmul(x[b][3], cmul(w1, w2));
         }
         const float2 a0 = cadd(x[b][0], x[b][2]);
         const float2 a1 = csub(x[b][0], x[b][2]);
         const float2 a2 = cadd(x[b][1], x[b][3]);
         const float2 d = csub(x[b][1], x[b][3]);
         const float2 a3 = inverse ? make_float2(-d.y, d.x) : make_float2(d.y, -d.x);  // +-i d
-        float2* dst = buf + ((t >> lq) << log_m) + ((j - k) << 2) + k;
-        dst[0] = cadd(a0, a2);
-        dst[ns] = cadd(a1, a3);
-        dst[2 * ns] = csub(a0, a2);
-        dst[3 * ns] = csub(a1, a3);
+        const float2 y[4] = {cadd(a0, a2), cadd(a1, a3), csub(a0, a2), csub(a1, a3)};
+        const int dst = ((t >> LQ) << LOG_M) + ((j - k) << 2) + k;
+        if (ns % 64 == 0) {
+          const int d0 = sw(dst);
+#pragma unroll
+          for (int q = 0; q < 4; ++q) buf[d0 + q * ns] = y[q];
+        } else {
+#pragma unroll
+          for (int q = 0; q < 4; ++q) buf[sw(dst + q * ns)] = y[q];
+        }
       }
     }
     __syncthreads();
-    ns <<= 2;
   }
-  if (log_m & 1) {
-    // Last pass, radix 2 with span m / 2: each thread owns the pair (j, j + m/2).
-    const int half = m >> 1;
-    const float inv_m = 1.0f / static_cast<float>(m);
-    for (int t = threadIdx.x; t < count * half; t += blockDim.x) {
-      const int j = t & (half - 1);
-      float2* base = buf + ((t >> (log_m - 1)) << log_m);
-      const float2 a = base[j];
-      const float2 b = cmul(base[j + half], twiddle_pi(sgn * static_cast<float>(j) * inv_m));
-      base[j] = cadd(a, b);
-      base[j + half] = csub(a, b);
+  if (LOG_M & 1) {
+    // Last pass, radix 2 with span M / 2: each thread owns the pair (j, j + M/2).
+    constexpr int HALF = M / 2;
+    constexpr int TW4 = fft_tw4_entries(LOG_M);
+#pragma unroll
+    for (int t0 = 0; t0 < COUNT * HALF; t0 += THREADS) {
+      const int t = t0 + static_cast<int>(threadIdx.x);
+      if ((COUNT * HALF) % THREADS == 0 || t < COUNT * HALF) {
+        const int j = t & (HALF - 1);
+        const int base = (t >> (LOG_M - 1)) << LOG_M;
+        float2 w = tw[TW4 + j];
+        if (inverse) w.y = -w.y;
+        const int i0 = sw(base + j);
+        const int i1 = HALF % 64 == 0 ? i0 + HALF : sw(base + j + HALF);
+        const float2 a = buf[i0];
+        const float2 b = cmul(buf[i1], w);
+        buf[i0] = cadd(a, b);
+        buf[i1] = csub(a, b);
+      }
     }
     __syncthreads();
   }
@@ -608,37 +699,43 @@ __device__ __forceinline__ float3 read_charge(const ChargeCell& c, const ChargeS
 // ------------------------------------------------------------------ FFT passes
 
 // Row r of the three charge planes and kernel row dy = r.  Packs
-// (m + i mx), (my + i Kq), (Kq2) into three complex length-M FFTs.
-__global__ void fft_rows_fwd_kernel(const ChargeCell* __restrict__ charges,
-                                    const LayoutStats* __restrict__ stats, int n, int g, int m,
-                                    int log_m, float2* __restrict__ rowspec, float2* __restrict__ krow) {
+// (m + i mx), (my + i Kq), (Kq2) into three complex length-M FFTs (buffer
+// elements [0, M), [M, 2M), [2M, 3M), stored through sw).  M = 2G.
+template <int LOG_M>
+__global__ void __launch_bounds__(FftShape<LOG_M, 3>::THREADS, 2)
+    fft_rows_fwd_kernel(const ChargeCell* __restrict__ charges, const LayoutStats* __restrict__ stats,
+                        float2* __restrict__ rowspec, float2* __restrict__ krow) {
+  using S = FftShape<LOG_M, 3>;
+  constexpr int M = S::M, G = M / 2, ROW_LEN = G + 1;
   extern __shared__ float2 smem[];
-  float2* z0 = smem;
-  float2* z1 = smem + m;
-  float2* z2 = smem + 2 * m;
+  float2* tw = smem + S::DATA;
   const int r = blockIdx.x;
   const GridGeom q = stats->geom;
   const ChargeScales sc = stats->scales;
-  for (int x = threadIdx.x; x < m; x += blockDim.x) {
-    float3 c = make_float3(0.f, 0.f, 0.f);
-    if (x < g) c = read_charge(charges[static_cast<size_t>(r) * g + x], sc);
-    float kq = 0.f, kq2 = 0.f;
-    if (x <= g - 1) {
-      kernel_values(x, r, q.spacing, &kq, &kq2);
-    } else if (x >= g + 1) {
-      kernel_values(x - m, r, q.spacing, &kq, &kq2);
+  fft_fill_twiddles<LOG_M, S::THREADS>(tw);
+#pragma unroll
+  for (int x0 = 0; x0 < M; x0 += S::THREADS) {
+    const int x = x0 + static_cast<int>(threadIdx.x);
+    if (M % S::THREADS == 0 || x < M) {
+      float3 c = make_float3(0.f, 0.f, 0.f);
+      if (x < G) c = read_charge(charges[static_cast<size_t>(r) * G + x], sc);
+      float kq = 0.f, kq2 = 0.f;
+      if (x <= G - 1) {
+        kernel_values(x, r, q.spacing, &kq, &kq2);
+      } else if (x >= G + 1) {
+        kernel_values(x - M, r, q.spacing, &kq, &kq2);
+      }
+      smem[sw(x)] = make_float2(c.x, c.y);
+      smem[sw(M + x)] = make_float2(c.z, kq);
+      smem[sw(2 * M + x)] = make_float2(kq2, 0.f);
     }
-    z0[x] = make_float2(c.x, c.y);
-    z1[x] = make_float2(c.z, kq);
-    z2[x] = make_float2(kq2, 0.f);
   }
   __syncthreads();
-  block_fft(smem, 3, m, log_m, false);
-  const int row_len = g + 1;
-  for (int k = threadIdx.x; k <= g; k += blockDim.x) {
-    const int km = (m - k) & (m - 1);
-    const float2 a = z0[k], ac = conjf2(z0[km]);
-    const float2 b = z1[k], bc = conjf2(z1[km]);
+  block_fft<LOG_M, 3, S::THREADS>(smem, tw, false);
+  for (int k = threadIdx.x; k <= G; k += S::THREADS) {
+    const int km = (M - k) & (M - 1);
+    const float2 a = smem[sw(k)], ac = conjf2(smem[sw(km)]);
+    const float2 b = smem[sw(M + k)], bc = conjf2(smem[sw(M + km)]);
     const float2 sum_a = cadd(a, ac), dif_a = csub(a, ac);
     const float2 sum_b = cadd(b, bc), dif_b = csub(b, bc);
     // X = (Z + Z*)/2, Y = (Z - Z*)/(2i)
@@ -646,113 +743,159 @@ __global__ void fft_rows_fwd_kernel(const ChargeCell* __restrict__ charges,
     const float2 xmx = make_float2(0.5f * dif_a.y, -0.5f * dif_a.x);
     const float2 xmy = cscale(sum_b, 0.5f);
     const float kqx = 0.5f * dif_b.y;
-    const float kq2x = z2[k].x;
-    float2* out = rowspec + 3 * (static_cast<size_t>(r) * row_len + k);
+    const float kq2x = smem[sw(2 * M + k)].x;
+    float2* out = rowspec + 3 * (static_cast<size_t>(r) * ROW_LEN + k);
     out[0] = xm;
     out[1] = xmx;
     out[2] = xmy;
-    krow[static_cast<size_t>(r) * row_len + k] = make_float2(kqx, kq2x);
+    krow[static_cast<size_t>(r) * ROW_LEN + k] = make_float2(kqx, kq2x);
   }
 }
 
-// Columns [k0, k0 + tk) of the half spectrum: y-FFT of three charge planes and
+// Columns [k0, k0 + TK) of the half spectrum: y-FFT of three charge planes and
 // of the real, even kernel columns (Kq + i Kq2 packs two real spectra), product,
-// inverse y-FFT, keep rows [0, G).
-__global__ void fft_cols_kernel(const float2* __restrict__ rowspec, const float2* __restrict__ krow,
-                                int g, int m, int log_m, int tk, float2* __restrict__ colspec) {
+// inverse y-FFT, keep rows [0, G).  Columns past G (the last block's tail) are
+// transformed as zeros and not stored.
+template <int LOG_M>
+__global__ void __launch_bounds__(FftShape<LOG_M, 4 * fft_cols_per_block(1 << LOG_M), kFftBatchCols>::THREADS,
+                                  FftShape<LOG_M, 4 * fft_cols_per_block(1 << LOG_M), kFftBatchCols>::THREADS > 512 ? 1 : 2)
+    fft_cols_kernel(const float2* __restrict__ rowspec, const float2* __restrict__ krow,
+                    float2* __restrict__ colspec) {
+  constexpr int M = 1 << LOG_M, G = M / 2, ROW_LEN = G + 1;
+  constexpr int TK = fft_cols_per_block(M);
+  using S = FftShape<LOG_M, 4 * TK, kFftBatchCols>;
   extern __shared__ float2 smem[];
-  const int row_len = g + 1;
-  const int k0 = blockIdx.x * tk;
-  const int cols = min(tk, row_len - k0);
-  // Buffer (c, p): column c, plane p in {0: m, 1: mx, 2: my, 3: kernel pack}.
-  for (int t = threadIdx.x; t < cols * m; t += blockDim.x) {
-    const int c = t >> log_m;
-    const int r = t & (m - 1);
-    const int k = k0 + c;
-    float2* b = smem + (static_cast<size_t>(c) * 4 << log_m);
-    float2 v0 = make_float2(0.f, 0.f), v1 = v0, v2 = v0, kk = v0;
-    if (r < g) {
-      const float2* src = rowspec + 3 * (static_cast<size_t>(r) * row_len + k);
-      v0 = src[0];
-      v1 = src[1];
-      v2 = src[2];
+  float2* tw = smem + S::DATA;
+  const int k0 = blockIdx.x * TK;
+  fft_fill_twiddles<LOG_M, S::THREADS>(tw);
+  // Sequence 4c + p: column c, plane p in {0: m, 1: mx, 2: my, 3: kernel pack}.
+#pragma unroll
+  for (int t0 = 0; t0 < TK * M; t0 += S::THREADS) {
+    const int t = t0 + static_cast<int>(threadIdx.x);
+    if ((TK * M) % S::THREADS == 0 || t < TK * M) {
+      const int c = t >> LOG_M;
+      const int r = t & (M - 1);
+      const int k = k0 + c;
+      const int b = (c * 4) << LOG_M;
+      float2 v0 = make_float2(0.f, 0.f), v1 = v0, v2 = v0, kk = v0;
+      if (k < ROW_LEN) {
+        if (r < G) {
+          const float2* src = rowspec + 3 * (static_cast<size_t>(r) * ROW_LEN + k);
+          v0 = src[0];
+          v1 = src[1];
+          v2 = src[2];
+        }
+        const int dy = r <= G - 1 ? r : (r >= G + 1 ? M - r : -1);
+        if (dy >= 0) kk = krow[static_cast<size_t>(dy) * ROW_LEN + k];
+      }
+      smem[sw(b + r)] = v0;
+      smem[sw(b + M + r)] = v1;
+      smem[sw(b + 2 * M + r)] = v2;
+      smem[sw(b + 3 * M + r)] = kk;
     }
-    int dy = -1;
-    if (r <= g - 1) dy = r;
-    else if (r >= g + 1) dy = m - r;
-    if (dy >= 0) kk = krow[static_cast<size_t>(dy) * row_len + k];
-    b[r] = v0;
-    b[m + r] = v1;
-    b[2 * m + r] = v2;
-    b[3 * m + r] = kk;
   }
   __syncthreads();
-  block_fft(smem, cols * 4, m, log_m, false);
-  for (int t = threadIdx.x; t < cols * m; t += blockDim.x) {
-    const int c = t >> log_m;
-    const int r = t & (m - 1);
-    float2* b = smem + (static_cast<size_t>(c) * 4 << log_m);
-    const float2 kk = b[3 * m + r];
-    const float kq = kk.x, kq2 = kk.y;
-    const float2 mm = b[r];
-    b[3 * m + r] = cscale(mm, kq);        // phi_q
-    b[r] = cscale(mm, kq2);               // phi_q2
-    b[m + r] = cscale(b[m + r], kq2);     // phi_xq2
-    b[2 * m + r] = cscale(b[2 * m + r], kq2);  // phi_yq2
+  block_fft<LOG_M, 4 * TK, S::THREADS>(smem, tw, false);
+#pragma unroll
+  for (int t0 = 0; t0 < TK * M; t0 += S::THREADS) {
+    const int t = t0 + static_cast<int>(threadIdx.x);
+    if ((TK * M) % S::THREADS == 0 || t < TK * M) {
+      const int c = t >> LOG_M;
+      const int r = t & (M - 1);
+      const int b = (c * 4) << LOG_M;
+      const float2 kk = smem[sw(b + 3 * M + r)];
+      const float kq = kk.x, kq2 = kk.y;
+      const float2 mm = smem[sw(b + r)];
+      smem[sw(b + 3 * M + r)] = cscale(mm, kq);                        // phi_q
+      smem[sw(b + r)] = cscale(mm, kq2);                               // phi_q2
+      smem[sw(b + M + r)] = cscale(smem[sw(b + M + r)], kq2);          // phi_xq2
+      smem[sw(b + 2 * M + r)] = cscale(smem[sw(b + 2 * M + r)], kq2);  // phi_yq2
+    }
   }
   __syncthreads();
-  block_fft(smem, cols * 4, m, log_m, true);
-  for (int t = threadIdx.x; t < cols * g; t += blockDim.x) {
-    const int c = t / g;
-    const int r = t - c * g;
-    const int k = k0 + c;
-    const float2* b = smem + (static_cast<size_t>(c) * 4 << log_m);
-    float2* out = colspec + 4 * (static_cast<size_t>(r) * row_len + k);
-    out[0] = b[r];
-    out[1] = b[m + r];
-    out[2] = b[2 * m + r];
-    out[3] = b[3 * m + r];
+  block_fft<LOG_M, 4 * TK, S::THREADS>(smem, tw, true);
+#pragma unroll
+  for (int t0 = 0; t0 < TK * G; t0 += S::THREADS) {
+    const int t = t0 + static_cast<int>(threadIdx.x);
+    if ((TK * G) % S::THREADS == 0 || t < TK * G) {
+      const int c = t >> (LOG_M - 1);
+      const int r = t & (G - 1);
+      const int k = k0 + c;
+      if (k < ROW_LEN) {
+        const int b = (c * 4) << LOG_M;
+        float4* out = reinterpret_cast<float4*>(colspec + 4 * (static_cast<size_t>(r) * ROW_LEN + k));
+        const float2 o0 = smem[sw(b + r)], o1 = smem[sw(b + M + r)];
+        const float2 o2 = smem[sw(b + 2 * M + r)], o3 = smem[sw(b + 3 * M + r)];
+        out[0] = make_float4(o0.x, o0.y, o1.x, o1.y);
+        out[1] = make_float4(o2.x, o2.y, o3.x, o3.y);
+      }
+    }
   }
 }
 
 // Output row r: inverse x-FFTs of (phi_q2 + i phi_xq2) and (phi_yq2 + i phi_q)
 // from their half spectra, potentials, this row's share of Z, and clearing of
-// the charges for the next splat.  The last block folds Z.
-__global__ void fft_rows_inv_kernel(const float2* __restrict__ colspec, ChargeCell* __restrict__ charges,
-                                    int n, int g, int m, int log_m, float4* __restrict__ pot, double* __restrict__ z_partials,
-                                    LayoutStats* __restrict__ stats) {
+// the charges for the next splat.  The row's masses are read (and its charge
+// cells cleared) before the transform so that those loads are in flight
+// during it.  The last block folds Z.
+template <int LOG_M>
+__global__ void __launch_bounds__(FftShape<LOG_M, 2>::THREADS, 4)
+    fft_rows_inv_kernel(const float2* __restrict__ colspec, ChargeCell* __restrict__ charges, int n,
+                        float4* __restrict__ pot, double* __restrict__ z_partials,
+                        LayoutStats* __restrict__ stats) {
+  using S = FftShape<LOG_M, 2>;
+  constexpr int M = S::M, G = M / 2, ROW_LEN = G + 1;
+  constexpr int CELLS = (G + S::THREADS - 1) / S::THREADS;
   extern __shared__ float2 smem[];
-  float2* z0 = smem;
-  float2* z1 = smem + m;
+  float2* tw = smem + S::DATA;
   const int r = blockIdx.x;
-  const int row_len = g + 1;
-  const double inv_scale_m = 1.0 / stats->scales.m;
-  for (int k = threadIdx.x; k < m; k += blockDim.x) {
-    const bool mirror = k > g;
-    const int kk = mirror ? m - k : k;
-    const float2* src = colspec + 4 * (static_cast<size_t>(r) * row_len + kk);
-    float2 a = src[0], b = src[1], c = src[2], d = src[3];
-    if (mirror) {
-      a = conjf2(a);
-      b = conjf2(b);
-      c = conjf2(c);
-      d = conjf2(d);
+  unsigned long long mass_q[CELLS];
+#pragma unroll
+  for (int i = 0; i < CELLS; ++i) {
+    const int x = static_cast<int>(threadIdx.x) + i * S::THREADS;
+    mass_q[i] = 0ull;
+    if (G % S::THREADS == 0 || x < G) {
+      ChargeCell* cell = charges + static_cast<size_t>(r) * G + x;
+      mass_q[i] = cell->m;
+      *cell = ChargeCell{0ull, 0ull, 0ull, 0ull};
     }
-    z0[k] = make_float2(a.x - b.y, a.y + b.x);
-    z1[k] = make_float2(c.x - d.y, c.y + d.x);
+  }
+  fft_fill_twiddles<LOG_M, S::THREADS>(tw);
+#pragma unroll
+  for (int k0 = 0; k0 < M; k0 += S::THREADS) {
+    const int k = k0 + static_cast<int>(threadIdx.x);
+    if (M % S::THREADS == 0 || k < M) {
+      const bool mirror = k > G;
+      const int kk = mirror ? M - k : k;
+      const float4* src = reinterpret_cast<const float4*>(colspec + 4 * (static_cast<size_t>(r) * ROW_LEN + kk));
+      const float4 ab = src[0], cd = src[1];
+      float2 a = make_float2(ab.x, ab.y), b = make_float2(ab.z, ab.w);
+      float2 c = make_float2(cd.x, cd.y), d = make_float2(cd.z, cd.w);
+      if (mirror) {
+        a = conjf2(a);
+        b = conjf2(b);
+        c = conjf2(c);
+        d = conjf2(d);
+      }
+      smem[sw(k)] = make_float2(a.x - b.y, a.y + b.x);
+      smem[sw(M + k)] = make_float2(c.x - d.y, c.y + d.x);
+    }
   }
   __syncthreads();
-  block_fft(smem, 2, m, log_m, true);
-  const float scale = 1.0f / (static_cast<float>(m) * static_cast<float>(m));
+  block_fft<LOG_M, 2, S::THREADS>(smem, tw, true);
+  const double inv_scale_m = 1.0 / stats->scales.m;
+  const float scale = 1.0f / (static_cast<float>(M) * static_cast<float>(M));
   double zpart = 0.0;
-  for (int x = threadIdx.x; x < g; x += blockDim.x) {
-    const float2 a = z0[x], b = z1[x];
-    const float4 p = make_float4(a.x * scale, a.y * scale, b.x * scale, b.y * scale);
-    const size_t cell = static_cast<size_t>(r) * g + x;
-    pot[cell] = p;
-    const double mass = static_cast<double>(static_cast<long long>(charges[cell].m)) * inv_scale_m;
-    zpart += mass * static_cast<double>(p.w);
-    charges[cell] = ChargeCell{0ull, 0ull, 0ull, 0ull};
+#pragma unroll
+  for (int i = 0; i < CELLS; ++i) {
+    const int x = static_cast<int>(threadIdx.x) + i * S::THREADS;
+    if (G % S::THREADS == 0 || x < G) {
+      const float2 a = smem[sw(x)], b = smem[sw(M + x)];
+      const float4 p = make_float4(a.x * scale, a.y * scale, b.x * scale, b.y * scale);
+      pot[static_cast<size_t>(r) * G + x] = p;
+      const double mass = static_cast<double>(static_cast<long long>(mass_q[i])) * inv_scale_m;
+      zpart += mass * static_cast<double>(p.w);
+    }
   }
   __shared__ double s_part[32];
   __shared__ bool s_last;
@@ -762,7 +905,7 @@ __global__ void fft_rows_inv_kernel(const float2* __restrict__ colspec, ChargeCe
   __syncthreads();
   if (threadIdx.x == 0) {
     double v = 0.0;
-    for (int w = 0; w < static_cast<int>(blockDim.x >> 5); ++w) v += s_part[w];
+    for (int w = 0; w < S::THREADS / 32; ++w) v += s_part[w];
     z_partials[r] = v;
     __threadfence();
     const unsigned int ticket = atomicAdd(&stats->fft_counter, 1u);
@@ -772,7 +915,7 @@ __global__ void fft_rows_inv_kernel(const float2* __restrict__ colspec, ChargeCe
   if (!s_last) return;
   __threadfence();
   double acc = 0.0;
-  for (int b = threadIdx.x; b < static_cast<int>(gridDim.x); b += blockDim.x) {
+  for (int b = threadIdx.x; b < static_cast<int>(gridDim.x); b += S::THREADS) {
     acc += static_cast<const volatile double*>(z_partials)[b];
   }
   acc = warp_sum(acc);
@@ -781,11 +924,65 @@ __global__ void fft_rows_inv_kernel(const float2* __restrict__ colspec, ChargeCe
   __syncthreads();
   if (threadIdx.x == 0) {
     double z = 0.0;
-    for (int w = 0; w < static_cast<int>(blockDim.x >> 5); ++w) z += s_part[w];
+    for (int w = 0; w < S::THREADS / 32; ++w) z += s_part[w];
     z -= static_cast<double>(n);
     stats->z = z;
     stats->inv_z = static_cast<float>(1.0 / fmax(z, static_cast<double>(FLT_MIN)));
     stats->fft_counter = 0u;
+  }
+}
+
+// Launch and attribute helpers over the instantiated transform lengths.
+#define FE_FFT_LOG_M_CASES(X) X(3) X(4) X(5) X(6) X(7) X(8) X(9) X(10) X(11)
+
+template <int LOG_M>
+int fft_configure() {
+  constexpr int TK = fft_cols_per_block(1 << LOG_M);
+  FE_CUDA(cudaFuncSetAttribute(fft_rows_fwd_kernel<LOG_M>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               static_cast<int>(FftShape<LOG_M, 3>::SMEM)),
+          "cudaFuncSetAttribute(fft_rows_fwd_kernel)");
+  FE_CUDA(cudaFuncSetAttribute(fft_cols_kernel<LOG_M>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               static_cast<int>(FftShape<LOG_M, 4 * TK, kFftBatchCols>::SMEM)),
+          "cudaFuncSetAttribute(fft_cols_kernel)");
+  FE_CUDA(cudaFuncSetAttribute(fft_rows_inv_kernel<LOG_M>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               static_cast<int>(FftShape<LOG_M, 2>::SMEM)),
+          "cudaFuncSetAttribute(fft_rows_inv_kernel)");
+  return 0;
+}
+
+// pass 0: rows forward, 1: columns, 2: rows inverse.
+template <int LOG_M>
+int fft_launch(TsneSession* s, int pass) {
+  constexpr int M = 1 << LOG_M, G = M / 2;
+  constexpr int TK = fft_cols_per_block(M);
+  if (pass == 0) {
+    using S = FftShape<LOG_M, 3>;
+    fft_rows_fwd_kernel<LOG_M><<<G, S::THREADS, S::SMEM, s->stream>>>(s->charges, s->stats, s->rowspec, s->krow);
+    FE_LAUNCH("fft_rows_fwd_kernel");
+  } else if (pass == 1) {
+    using S = FftShape<LOG_M, 4 * TK, kFftBatchCols>;
+    fft_cols_kernel<LOG_M><<<(G + 1 + TK - 1) / TK, S::THREADS, S::SMEM, s->stream>>>(s->rowspec, s->krow,
+                                                                                   s->colspec);
+    FE_LAUNCH("fft_cols_kernel");
+  } else {
+    using S = FftShape<LOG_M, 2>;
+    fft_rows_inv_kernel<LOG_M><<<G, S::THREADS, S::SMEM, s->stream>>>(s->colspec, s->charges, s->n, s->pot,
+                                                                     s->z_partials, s->stats);
+    FE_LAUNCH("fft_rows_inv_kernel");
+  }
+  return 0;
+}
+
+int fft_launch_pass(TsneSession* s, int pass) {
+  switch (s->log_fft) {
+#define FE_FFT_LAUNCH_CASE(L) \
+  case L:                     \
+    return fft_launch<L>(s, pass);
+    FE_FFT_LOG_M_CASES(FE_FFT_LAUNCH_CASE)
+#undef FE_FFT_LAUNCH_CASE
+    default:
+      set_error("t-SNE FFT length outside the instantiated range (grid 4 to 1024)");
+      return 1;
   }
 }
 
@@ -1282,13 +1479,21 @@ void grad_update_launch_shape(int rows, int* blocks, int* threads) {
 }
 
 int configure_kernels(TsneSession* s) {
-  const int m = s->fft;
-  const size_t cols_smem = static_cast<size_t>(s->cols_per_block) * 4 * m * sizeof(float2);
-  const size_t rows_smem = 3 * static_cast<size_t>(m) * sizeof(float2);
-  FE_CUDA(cudaFuncSetAttribute(fft_cols_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               static_cast<int>(cols_smem)), "cudaFuncSetAttribute(fft_cols_kernel)");
-  FE_CUDA(cudaFuncSetAttribute(fft_rows_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               static_cast<int>(rows_smem)), "cudaFuncSetAttribute(fft_rows_fwd_kernel)");
+  if (s->fft != 2 * s->grid) {
+    set_error("t-SNE FFT length must be twice the grid side");
+    return 1;
+  }
+  switch (s->log_fft) {
+#define FE_FFT_CONFIGURE_CASE(L) \
+  case L:                        \
+    FE_TRY(fft_configure<L>());  \
+    break;
+    FE_FFT_LOG_M_CASES(FE_FFT_CONFIGURE_CASE)
+#undef FE_FFT_CONFIGURE_CASE
+    default:
+      set_error("t-SNE FFT length outside the instantiated range (grid 4 to 1024)");
+      return 1;
+  }
   FE_CUDA(cudaFuncSetAttribute(staged_grad_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                static_cast<int>(kStageCap * sizeof(float2))),
           "cudaFuncSetAttribute(staged_grad_kernel)");
@@ -1329,8 +1534,7 @@ struct ProfileScope {
 
 int launch_iteration(TsneSession* s, GradMode mode, float exaggeration, float momentum,
                      float learning_rate, float min_gain, float max_step_norm) {
-  const int g = s->grid, m = s->fft, lm = s->log_fft;
-  const int row_len = g + 1;
+  const int g = s->grid;
   {
     ProfileScope ps(s, kKindSplat);
     const unsigned blocks = static_cast<unsigned>((s->n + kSplatThreads - 1) / kSplatThreads);
@@ -1350,23 +1554,15 @@ int launch_iteration(TsneSession* s, GradMode mode, float exaggeration, float mo
   }
   {
     ProfileScope ps(s, kKindFftRows);
-    fft_rows_fwd_kernel<<<g, 256, 3 * m * sizeof(float2), s->stream>>>(
-        s->charges, s->stats, s->n, g, m, lm, s->rowspec, s->krow);
-    FE_LAUNCH("fft_rows_fwd_kernel");
+    FE_TRY(fft_launch_pass(s, 0));
   }
   {
     ProfileScope ps(s, kKindFftCols);
-    const int tk = s->cols_per_block;
-    const int blocks = (row_len + tk - 1) / tk;
-    fft_cols_kernel<<<blocks, 256, static_cast<size_t>(tk) * 4 * m * sizeof(float2), s->stream>>>(
-        s->rowspec, s->krow, g, m, lm, tk, s->colspec);
-    FE_LAUNCH("fft_cols_kernel");
+    FE_TRY(fft_launch_pass(s, 1));
   }
   {
     ProfileScope ps(s, kKindFftRowsInv);
-    fft_rows_inv_kernel<<<g, 256, 2 * m * sizeof(float2), s->stream>>>(
-        s->colspec, s->charges, s->n, g, m, lm, s->pot, s->z_partials, s->stats);
-    FE_LAUNCH("fft_rows_inv_kernel");
+    FE_TRY(fft_launch_pass(s, 2));
   }
   const UpdateParams prm{s->n, s->row_begin, s->row_end, g, exaggeration, momentum,
                          learning_rate, min_gain, max_step_norm, static_cast<int>(mode)};

@@ -146,11 +146,6 @@ int session_create(TsneSession** out, int n, int grid, int* d_row_ptr, int* d_co
   // Fused gradient/update kernel: a warp per block of 32 rows, persistent
   // blocks of 8 warps, 8 blocks per SM.
   grad_update_launch_shape(n, &s->update_blocks, &s->update_threads);
-  const int m = s->fft;
-  // One spectrum column per block of the column FFT pass once the transform
-  // is long enough to occupy a block (G >= 128: G + 1 blocks, measured 1.9x
-  // faster than 4 columns per block at G = 256); several for short ones.
-  s->cols_per_block = m >= 256 ? 1 : std::max(1, std::min(16, 2048 / m));
   if (configure_kernels(s)) {
     if (s->own_stream) cudaStreamDestroy(s->stream);
     delete s;

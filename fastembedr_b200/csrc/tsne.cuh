@@ -263,6 +263,7 @@ struct TsneSession {
   float2* krow = nullptr;
   float2* colspec = nullptr;
   float4* pot = nullptr;
+  float2* twiddle = nullptr;  // FFT twiddles (fft_twiddle_table)
 
   int interp = 0;  // 0 bilinear (the reference's), 1 Lagrange 3-node boxes (FIt-SNE)
   int update_blocks = 0;
@@ -475,6 +476,10 @@ int launch_permute_in(TsneSession* s, const float2* in, float2* out);
 // ---- kernels (tsne_kernels.cu) ----
 // Raises per-kernel dynamic shared-memory limits for this session's FFT size.
 int configure_kernels(TsneSession* s);
+// FFT twiddle table for transforms of length 2^log_m (entries, and the table
+// itself computed in double and rounded to float; layout in tsne_kernels.cu).
+int fft_twiddle_entries(int log_m);
+void fft_twiddle_table(int log_m, float2* out);
 // Grid and block size of the fused gradient/update kernel for `rows` rows.
 void grad_update_launch_shape(int rows, int* blocks, int* threads);
 int launch_stats(TsneSession* s, int center);

@@ -30,6 +30,7 @@
 #include "tsne.cuh"
 
 #include <algorithm>
+#include <cmath>
 #include <cfloat>
 #include <climits>
 
@@ -56,12 +57,13 @@ __device__ __forceinline__ float2 cscale(float2 a, float s) { return make_float2
 // each element once to its Stockham position, so the output is in natural
 // order without a bit-reversal pass.  The inverse is unnormalised.
 //
-// Twiddles: a per-block table in shared memory, filled once per launch with
-// sincospif (arguments k / 2^j are exact in float): radix-4 pass p >= 1 (ns =
-// 4^p) owns entries [(4^p - 4) / 3, (4^(p+1) - 4) / 3), entry k holding
-// exp(-2 pi i k / (4 ns)), so the lanes of a warp read consecutive entries;
-// w^2 and w^3 are complex products.  The radix-2 pass reads exp(-2 pi i j / M),
-// j < M / 2, after them.  The inverse conjugates.
+// Twiddles: a table computed once per session on the host in double and
+// rounded to float (fft_twiddle_table), copied into shared memory by every
+// block.  Radix-4 pass p >= 1 (ns = 4^p) owns entries [4^p - 4, 4^(p+1) - 4):
+// entry (q - 1) * ns + k holds w^q = exp(-2 pi i q k / (4 ns)), q = 1, 2, 3,
+// so the lanes of a warp read consecutive entries and no twiddle is a product
+// of rounded ones.  The radix-2 pass reads exp(-2 pi i j / M), j < M / 2,
+// after them.  The inverse conjugates.
 //
 // Element i of the data buffer lives at sw(i): the low four index bits are
 // XORed with 5 * ((i >> 4) & 3), so that the strided writes of the first two
@@ -89,7 +91,7 @@ constexpr int fft_threads_for(int count, int m, int batch) {
   return (t + 31) / 32 * 32;
 }
 
-constexpr int fft_tw4_entries(int log_m) { return ((1 << (2 * (log_m / 2))) - 4) / 3; }
+constexpr int fft_tw4_entries(int log_m) { return (1 << (2 * (log_m / 2))) - 4; }
 constexpr int fft_table_entries(int log_m) { return fft_tw4_entries(log_m) + ((log_m & 1) ? (1 << (log_m - 1)) : 0); }
 constexpr int fft_data_entries(int count, int m) { return (count * m + 15) / 16 * 16; }
 
@@ -105,24 +107,11 @@ struct FftShape {
 };
 
 template <int LOG_M, int THREADS>
-__device__ __forceinline__ void fft_fill_twiddles(float2* __restrict__ tw) {
-  constexpr int TW4 = fft_tw4_entries(LOG_M);
-  constexpr int TOTAL = fft_table_entries(LOG_M);
-  for (int i = threadIdx.x; i < TOTAL; i += THREADS) {
-    float turns;
-    if (i < TW4) {
-      int p = 1, off = 0;
-      while (off + (1 << (2 * p)) <= i) {
-        off += 1 << (2 * p);
-        ++p;
-      }
-      turns = static_cast<float>(i - off) / static_cast<float>(4 << (2 * p));
-    } else {
-      turns = static_cast<float>(i - TW4) / static_cast<float>(1 << LOG_M);
-    }
-    float sn, cs;
-    sincospif(-2.0f * turns, &sn, &cs);
-    tw[i] = make_float2(cs, sn);
+__device__ __forceinline__ void fft_load_twiddles(const float2* __restrict__ table, float2* __restrict__ tw) {
+#pragma unroll
+  for (int i0 = 0; i0 < fft_table_entries(LOG_M); i0 += THREADS) {
+    const int i = i0 + static_cast<int>(threadIdx.x);
+    if (i < fft_table_entries(LOG_M)) tw[i] = __ldg(table + i);
   }
 }
 
@@ -137,7 +126,7 @@ __device__ __forceinline__ void block_fft(float2* __restrict__ buf, const float2
 #pragma unroll
   for (int pass = 0; pass < PASSES; ++pass) {
     const int ns = 1 << (2 * pass);
-    const int tw_off = (ns - 4) / 3;
+    const int tw_off = ns - 4;
     float2 x[BATCHES][4];
 #pragma unroll
     for (int b = 0; b < BATCHES; ++b) {
@@ -162,12 +151,12 @@ __device__ __forceinline__ void block_fft(float2* __restrict__ buf, const float2
         const int j = t & (QUARTER - 1);
         const int k = j & (ns - 1);
         if (pass > 0) {
-          float2 w1 = tw[tw_off + k];
-          if (inverse) w1.y = -w1.y;
-          const float2 w2 = cmul(w1, w1);
-          x[b][1] = cmul(x[b][1], w1);
-          x[b][2] = cmul(x[b][2], w2);
-          x[b][3] = cmul(x[b][3], cmul(w1, w2));
+#pragma unroll
+          for (int q = 1; q < 4; ++q) {
+            float2 w = tw[tw_off + (q - 1) * ns + k];
+            if (inverse) w.y = -w.y;
+            x[b][q] = cmul(x[b][q], w);
+          }
         }
         const float2 a0 = cadd(x[b][0], x[b][2]);
         const float2 a1 = csub(x[b][0], x[b][2]);
@@ -698,13 +687,18 @@ __device__ __forceinline__ float3 read_charge(const ChargeCell& c, const ChargeS
 
 // ------------------------------------------------------------------ FFT passes
 
-// Row r of the three charge planes and kernel row dy = r.  Packs
-// (m + i mx), (my + i Kq), (Kq2) into three complex length-M FFTs (buffer
-// elements [0, M), [M, 2M), [2M, 3M), stored through sw).  M = 2G.
+// Row r of the three charge planes and kernel row dy = r as three complex
+// length-M FFTs (buffer elements [0, M), [M, 2M), [2M, 3M), stored through
+// sw; M = 2G): (mx + i my), (m), (Kq + i Kq2).  Two real rows packed into one
+// complex transform share its rounding error, which scales with the larger of
+// the two, so only rows of like magnitude are paired: the moments mx, my are
+// the masses times coordinates of tens of units, and at a converged layout
+// the repulsion is a small difference of their convolutions.
 template <int LOG_M>
 __global__ void __launch_bounds__(FftShape<LOG_M, 3>::THREADS, 2)
     fft_rows_fwd_kernel(const ChargeCell* __restrict__ charges, const LayoutStats* __restrict__ stats,
-                        float2* __restrict__ rowspec, float2* __restrict__ krow) {
+                        const float2* __restrict__ twiddles, float2* __restrict__ rowspec,
+                        float2* __restrict__ krow) {
   using S = FftShape<LOG_M, 3>;
   constexpr int M = S::M, G = M / 2, ROW_LEN = G + 1;
   extern __shared__ float2 smem[];
@@ -712,7 +706,7 @@ __global__ void __launch_bounds__(FftShape<LOG_M, 3>::THREADS, 2)
   const int r = blockIdx.x;
   const GridGeom q = stats->geom;
   const ChargeScales sc = stats->scales;
-  fft_fill_twiddles<LOG_M, S::THREADS>(tw);
+  fft_load_twiddles<LOG_M, S::THREADS>(twiddles, tw);
 #pragma unroll
   for (int x0 = 0; x0 < M; x0 += S::THREADS) {
     const int x = x0 + static_cast<int>(threadIdx.x);
@@ -725,9 +719,9 @@ __global__ void __launch_bounds__(FftShape<LOG_M, 3>::THREADS, 2)
       } else if (x >= G + 1) {
         kernel_values(x - M, r, q.spacing, &kq, &kq2);
       }
-      smem[sw(x)] = make_float2(c.x, c.y);
-      smem[sw(M + x)] = make_float2(c.z, kq);
-      smem[sw(2 * M + x)] = make_float2(kq2, 0.f);
+      smem[sw(x)] = make_float2(c.y, c.z);
+      smem[sw(M + x)] = make_float2(c.x, 0.f);
+      smem[sw(2 * M + x)] = make_float2(kq, kq2);
     }
   }
   __syncthreads();
@@ -735,15 +729,14 @@ __global__ void __launch_bounds__(FftShape<LOG_M, 3>::THREADS, 2)
   for (int k = threadIdx.x; k <= G; k += S::THREADS) {
     const int km = (M - k) & (M - 1);
     const float2 a = smem[sw(k)], ac = conjf2(smem[sw(km)]);
-    const float2 b = smem[sw(M + k)], bc = conjf2(smem[sw(M + km)]);
+    const float2 b = smem[sw(2 * M + k)], bc = conjf2(smem[sw(2 * M + km)]);
     const float2 sum_a = cadd(a, ac), dif_a = csub(a, ac);
-    const float2 sum_b = cadd(b, bc), dif_b = csub(b, bc);
-    // X = (Z + Z*)/2, Y = (Z - Z*)/(2i)
-    const float2 xm = cscale(sum_a, 0.5f);
-    const float2 xmx = make_float2(0.5f * dif_a.y, -0.5f * dif_a.x);
-    const float2 xmy = cscale(sum_b, 0.5f);
-    const float kqx = 0.5f * dif_b.y;
-    const float kq2x = smem[sw(2 * M + k)].x;
+    // X = (Z + Z*)/2, Y = (Z - Z*)/(2i); the kernel spectra are real (even kernels)
+    const float2 xmx = cscale(sum_a, 0.5f);
+    const float2 xmy = make_float2(0.5f * dif_a.y, -0.5f * dif_a.x);
+    const float2 xm = smem[sw(M + k)];
+    const float kqx = 0.5f * (b.x + bc.x);
+    const float kq2x = 0.5f * (b.y - bc.y);
     float2* out = rowspec + 3 * (static_cast<size_t>(r) * ROW_LEN + k);
     out[0] = xm;
     out[1] = xmx;
@@ -760,14 +753,14 @@ template <int LOG_M>
 __global__ void __launch_bounds__(FftShape<LOG_M, 4 * fft_cols_per_block(1 << LOG_M), kFftBatchCols>::THREADS,
                                   FftShape<LOG_M, 4 * fft_cols_per_block(1 << LOG_M), kFftBatchCols>::THREADS > 512 ? 1 : 2)
     fft_cols_kernel(const float2* __restrict__ rowspec, const float2* __restrict__ krow,
-                    float2* __restrict__ colspec) {
+                    const float2* __restrict__ twiddles, float2* __restrict__ colspec) {
   constexpr int M = 1 << LOG_M, G = M / 2, ROW_LEN = G + 1;
   constexpr int TK = fft_cols_per_block(M);
   using S = FftShape<LOG_M, 4 * TK, kFftBatchCols>;
   extern __shared__ float2 smem[];
   float2* tw = smem + S::DATA;
   const int k0 = blockIdx.x * TK;
-  fft_fill_twiddles<LOG_M, S::THREADS>(tw);
+  fft_load_twiddles<LOG_M, S::THREADS>(twiddles, tw);
   // Sequence 4c + p: column c, plane p in {0: m, 1: mx, 2: my, 3: kernel pack}.
 #pragma unroll
   for (int t0 = 0; t0 < TK * M; t0 += S::THREADS) {
@@ -833,16 +826,17 @@ __global__ void __launch_bounds__(FftShape<LOG_M, 4 * fft_cols_per_block(1 << LO
   }
 }
 
-// Output row r: inverse x-FFTs of (phi_q2 + i phi_xq2) and (phi_yq2 + i phi_q)
-// from their half spectra, potentials, this row's share of Z, and clearing of
-// the charges for the next splat.  The row's masses are read (and its charge
+// Output row r: inverse x-FFTs of (phi_xq2 + i phi_yq2) and (phi_q2 + i phi_q)
+// from their half spectra (pairs of like magnitude, as in the forward rows),
+// potentials, this row's share of Z, and clearing of the charges for the next
+// splat.  The row's masses are read (and its charge
 // cells cleared) before the transform so that those loads are in flight
 // during it.  The last block folds Z.
 template <int LOG_M>
 __global__ void __launch_bounds__(FftShape<LOG_M, 2>::THREADS, 4)
     fft_rows_inv_kernel(const float2* __restrict__ colspec, ChargeCell* __restrict__ charges, int n,
-                        float4* __restrict__ pot, double* __restrict__ z_partials,
-                        LayoutStats* __restrict__ stats) {
+                        const float2* __restrict__ twiddles, float4* __restrict__ pot,
+                        double* __restrict__ z_partials, LayoutStats* __restrict__ stats) {
   using S = FftShape<LOG_M, 2>;
   constexpr int M = S::M, G = M / 2, ROW_LEN = G + 1;
   constexpr int CELLS = (G + S::THREADS - 1) / S::THREADS;
@@ -860,7 +854,7 @@ __global__ void __launch_bounds__(FftShape<LOG_M, 2>::THREADS, 4)
       *cell = ChargeCell{0ull, 0ull, 0ull, 0ull};
     }
   }
-  fft_fill_twiddles<LOG_M, S::THREADS>(tw);
+  fft_load_twiddles<LOG_M, S::THREADS>(twiddles, tw);
 #pragma unroll
   for (int k0 = 0; k0 < M; k0 += S::THREADS) {
     const int k = k0 + static_cast<int>(threadIdx.x);
@@ -877,8 +871,8 @@ __global__ void __launch_bounds__(FftShape<LOG_M, 2>::THREADS, 4)
         c = conjf2(c);
         d = conjf2(d);
       }
-      smem[sw(k)] = make_float2(a.x - b.y, a.y + b.x);
-      smem[sw(M + k)] = make_float2(c.x - d.y, c.y + d.x);
+      smem[sw(k)] = make_float2(b.x - c.y, b.y + c.x);
+      smem[sw(M + k)] = make_float2(a.x - d.y, a.y + d.x);
     }
   }
   __syncthreads();
@@ -890,8 +884,8 @@ __global__ void __launch_bounds__(FftShape<LOG_M, 2>::THREADS, 4)
   for (int i = 0; i < CELLS; ++i) {
     const int x = static_cast<int>(threadIdx.x) + i * S::THREADS;
     if (G % S::THREADS == 0 || x < G) {
-      const float2 a = smem[sw(x)], b = smem[sw(M + x)];
-      const float4 p = make_float4(a.x * scale, a.y * scale, b.x * scale, b.y * scale);
+      const float2 xy = smem[sw(x)], qq = smem[sw(M + x)];
+      const float4 p = make_float4(qq.x * scale, xy.x * scale, xy.y * scale, qq.y * scale);
       pot[static_cast<size_t>(r) * G + x] = p;
       const double mass = static_cast<double>(static_cast<long long>(mass_q[i])) * inv_scale_m;
       zpart += mass * static_cast<double>(p.w);
@@ -932,6 +926,30 @@ __global__ void __launch_bounds__(FftShape<LOG_M, 2>::THREADS, 4)
   }
 }
 
+}  // namespace
+
+int fft_twiddle_entries(int log_m) { return fft_table_entries(log_m); }
+
+void fft_twiddle_table(int log_m, float2* out) {
+  const double two_pi = 6.283185307179586476925286766559;
+  int e = 0;
+  for (int pass = 1; pass < log_m / 2; ++pass) {  // radix-4 passes with twiddles
+    const int ns = 1 << (2 * pass);
+    for (int q = 1; q < 4; ++q) {
+      for (int k = 0; k < ns; ++k) {
+        const double ang = -two_pi * static_cast<double>(q * k) / static_cast<double>(4 * ns);
+        out[e++] = make_float2(static_cast<float>(std::cos(ang)), static_cast<float>(std::sin(ang)));
+      }
+    }
+  }
+  for (int j = 0; e < fft_table_entries(log_m); ++j) {
+    const double ang = -two_pi * static_cast<double>(j) / static_cast<double>(1 << log_m);
+    out[e++] = make_float2(static_cast<float>(std::cos(ang)), static_cast<float>(std::sin(ang)));
+  }
+}
+
+namespace {
+
 // Launch and attribute helpers over the instantiated transform lengths.
 #define FE_FFT_LOG_M_CASES(X) X(3) X(4) X(5) X(6) X(7) X(8) X(9) X(10) X(11)
 
@@ -957,17 +975,18 @@ int fft_launch(TsneSession* s, int pass) {
   constexpr int TK = fft_cols_per_block(M);
   if (pass == 0) {
     using S = FftShape<LOG_M, 3>;
-    fft_rows_fwd_kernel<LOG_M><<<G, S::THREADS, S::SMEM, s->stream>>>(s->charges, s->stats, s->rowspec, s->krow);
+    fft_rows_fwd_kernel<LOG_M><<<G, S::THREADS, S::SMEM, s->stream>>>(s->charges, s->stats, s->twiddle, s->rowspec,
+                                                                          s->krow);
     FE_LAUNCH("fft_rows_fwd_kernel");
   } else if (pass == 1) {
     using S = FftShape<LOG_M, 4 * TK, kFftBatchCols>;
     fft_cols_kernel<LOG_M><<<(G + 1 + TK - 1) / TK, S::THREADS, S::SMEM, s->stream>>>(s->rowspec, s->krow,
-                                                                                   s->colspec);
+                                                                                   s->twiddle, s->colspec);
     FE_LAUNCH("fft_cols_kernel");
   } else {
     using S = FftShape<LOG_M, 2>;
-    fft_rows_inv_kernel<LOG_M><<<G, S::THREADS, S::SMEM, s->stream>>>(s->colspec, s->charges, s->n, s->pot,
-                                                                     s->z_partials, s->stats);
+    fft_rows_inv_kernel<LOG_M><<<G, S::THREADS, S::SMEM, s->stream>>>(s->colspec, s->charges, s->n, s->twiddle,
+                                                                     s->pot, s->z_partials, s->stats);
     FE_LAUNCH("fft_rows_inv_kernel");
   }
   return 0;

@@ -183,6 +183,7 @@ int session_create(TsneSession** out, int n, int grid, int* d_row_ptr, int* d_co
     s->krow = a.take<float2>(spec);
     s->colspec = a.take<float2>(4 * spec);
     s->pot = a.take<float4>(cells);
+    s->twiddle = a.take<float2>(fft_twiddle_entries(s->log_fft));
     s->ro_keys = a.take<unsigned int>(n);
     s->ro_keys_sorted = a.take<unsigned int>(n);
     s->ro_idx = a.take<int>(n);
@@ -212,7 +213,12 @@ int session_create(TsneSession** out, int n, int grid, int* d_row_ptr, int* d_co
       }
     }
   }
-  if (check_cuda(cudaMemsetAsync(s->stats, 0, sizeof(LayoutStats), s->stream), "memset stats") ||
+  std::vector<float2> tw(fft_twiddle_entries(s->log_fft));
+  fft_twiddle_table(s->log_fft, tw.data());
+  if (check_cuda(cudaMemcpyAsync(s->twiddle, tw.data(), sizeof(float2) * tw.size(), cudaMemcpyHostToDevice,
+                                 s->stream), "H2D FFT twiddles") ||
+      check_cuda(cudaStreamSynchronize(s->stream), "H2D FFT twiddles") ||
+      check_cuda(cudaMemsetAsync(s->stats, 0, sizeof(LayoutStats), s->stream), "memset stats") ||
       check_cuda(cudaMemcpyAsync(&s->stats->lagrange, &s->interp, sizeof(int), cudaMemcpyHostToDevice, s->stream),
                  "H2D interpolation") ||
       check_cuda(cudaMemsetAsync(s->charges, 0, sizeof(ChargeCell) * cells, s->stream), "memset charges") ||

@@ -27,6 +27,7 @@ _SIGNATURES = {
     "fastembedr_cuda_available": (ctypes.c_bool, []),
     "fastembedr_cuda_embedding_last_error": (ctypes.c_char_p, []),
     "fe_b200_version": (ctypes.c_char_p, []),
+    "fe_b200_release_memory": (I, []),
     "fastembedr_cuda_opentsne_fft_from_knn": (I, _TSNE_KNN_ARGS),
     "fastembedr_cuda_opentsne_fft_from_knn_float": (I, _TSNE_KNN_ARGS),
     "fastembedr_cuda_opentsne_fft_from_device_knn_float": (I, _TSNE_KNN_ARGS),

@@ -47,6 +47,12 @@ def version() -> str:
     return _lib.load().fe_b200_version().decode()
 
 
+def release_memory() -> None:
+    """Returns the device memory the library keeps between calls (a pool per
+    GPU, up to FASTEMBEDR_B200_RETAIN_MB) to the driver (fe_b200_release_memory)."""
+    check(_lib.load().fe_b200_release_memory(), "fe_b200_release_memory")
+
+
 # ------------------------------------------------------------------ parameter policy
 
 

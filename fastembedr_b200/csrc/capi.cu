@@ -9,7 +9,9 @@
 #include "umap.cuh"
 
 #include <cfloat>
+#include <chrono>
 #include <cmath>
+#include <cstdio>
 #include <cstdlib>
 #include <cstring>
 #include <string>
@@ -54,14 +56,55 @@ int resolve_grid(int n, int requested) {
 struct DeviceCopy {
   void* p = nullptr;
   ~DeviceCopy() {
-    if (p) cudaFree(p);
+    if (p) fe::dev_free(p);
   }
 };
 
 int copy_to_device(const void* host, size_t bytes, DeviceCopy& dst, cudaStream_t stream, const char* what) {
-  FE_CUDA(cudaMalloc(&dst.p, bytes ? bytes : 1), what);
+  FE_CUDA(fe::dev_malloc(&dst.p, bytes ? bytes : 1), what);
   return fe::h2d_copy(dst.p, host, bytes, stream, what);
 }
+
+// FASTEMBEDR_B200_TRACE=1: wall time of each phase of a call, printed to
+// stderr when the call ends (the stream is synchronised at every mark, so a
+// traced call is slower; without the variable nothing is added).  The last
+// line covers the teardown after the final mark, measured in the destructor.
+struct PhaseTrace {
+  const char* name;
+  cudaStream_t stream;
+  bool on;
+  std::chrono::steady_clock::time_point t0, last;
+  std::string lines;
+  double alloc_ms = 0.0, free_ms = 0.0;
+  long long alloc_calls = 0;
+  PhaseTrace(const char* n, cudaStream_t s) : name(n), stream(s), on(fe::env_flag("FASTEMBEDR_B200_TRACE", false)) {
+    t0 = last = std::chrono::steady_clock::now();
+    if (on) fe::alloc_time_totals(&alloc_ms, &free_ms, &alloc_calls);
+  }
+  void mark(const char* phase) {
+    if (!on) return;
+    cudaStreamSynchronize(stream);
+    const auto now = std::chrono::steady_clock::now();
+    double a = 0.0, f = 0.0;
+    long long c = 0;
+    fe::alloc_time_totals(&a, &f, &c);
+    char buf[160];
+    std::snprintf(buf, sizeof(buf), " (allocations %lld: %.3f ms, frees %.3f ms)", c - alloc_calls, a - alloc_ms,
+                  f - free_ms);
+    alloc_ms = a;
+    free_ms = f;
+    alloc_calls = c;
+    lines += std::string("[fastembedr_b200 trace] ") + name + " " + phase + ": " +
+             std::to_string(std::chrono::duration<double, std::milli>(now - last).count()) + " ms" + buf + "\n";
+    last = now;
+  }
+  ~PhaseTrace() {
+    if (!on) return;
+    const auto now = std::chrono::steady_clock::now();
+    std::fprintf(stderr, "%s[fastembedr_b200 trace] %s total: %.3f ms\n", lines.c_str(), name,
+                 std::chrono::duration<double, std::milli>(now - t0).count());
+  }
+};
 
 // Shared by every openTSNE entry point (the reference's
 // fastembedr_cuda_opentsne_fft_from_knn_impl, src/embedding_cuda_kernels.cpp:5453-6008).
@@ -107,14 +150,14 @@ int opentsne_impl(const int* indices, const void* distances, bool dist_double, c
     cudaStream_t ps = nullptr;
     FE_CUDA(cudaStreamCreateWithFlags(&ps, cudaStreamNonBlocking), "cudaStreamCreate(PCA)");
     float2* d_start = nullptr;
-    int rc = fe::check_cuda(cudaMalloc(&d_start, sizeof(float2) * static_cast<size_t>(n)), "cudaMalloc(PCA start)");
+    int rc = fe::check_cuda(fe::dev_malloc(&d_start, sizeof(float2) * static_cast<size_t>(n)), "cudaMalloc(PCA start)");
     if (rc == 0) rc = fe::pca_start_layout(pca_values, pca_double, n, pca_p, ps, d_start);
     if (rc == 0) {
       pca_host.resize(2 * static_cast<size_t>(n));
       rc = fe::check_cuda(cudaMemcpy(pca_host.data(), d_start, sizeof(float2) * static_cast<size_t>(n),
                                      cudaMemcpyDeviceToHost), "D2H PCA start");
     }
-    if (d_start != nullptr) cudaFree(d_start);
+    if (d_start != nullptr) fe::dev_free(d_start);
     cudaStreamDestroy(ps);
     if (rc != 0) return 1;
     init = pca_host.data();
@@ -156,6 +199,7 @@ int opentsne_impl(const int* indices, const void* distances, bool dist_double, c
       cudaStreamDestroy(s);
     }
   } guard{stream};
+  PhaseTrace trace("opentsne", stream);
 
   const size_t items = static_cast<size_t>(n) * k;
   int* row_ptr = nullptr;
@@ -172,21 +216,25 @@ int opentsne_impl(const int* indices, const void* distances, bool dist_double, c
                             stream, "H2D openTSNE distances"));
       idx_dev = static_cast<const int*>(d_idx.p);
       dist_dev = d_dist.p;
+      trace.mark("H2D KNN");
     }
     FE_TRY(fe::build_p_device(idx_dev, dist_dev, dist_double, n, k, index_offset, perplexity, stream,
                               &row_ptr, &col, &val, &nnz));
+    trace.mark("P build");
   }
+  trace.mark("KNN copies freed");
   fe::TsneSession* s = nullptr;
   if (fe::session_create(&s, n, resolve_grid(n, 0), row_ptr, col, val, nnz, stream)) {
-    cudaFree(row_ptr);
-    cudaFree(col);
-    cudaFree(val);
+    fe::dev_free(row_ptr);
+    fe::dev_free(col);
+    fe::dev_free(val);
     return 1;
   }
   struct SessionGuard {
     fe::TsneSession* s;
     ~SessionGuard() { fe::session_destroy(s); }
   } sguard{s};
+  trace.mark("session create");
   if (has_init) {
     FE_TRY(fe::session_set_layout(s, init, true, true));
   } else if (pca) {
@@ -197,10 +245,14 @@ int opentsne_impl(const int* indices, const void* distances, bool dist_double, c
   } else {
     FE_TRY(fe::session_random_layout(s, seed));
   }
+  trace.mark("start layout");
   FE_TRY(fe::session_iterate(s, early_exaggeration_iter, early_exaggeration, initial_momentum, lr_early,
                              min_gain, clip));
+  trace.mark("early iterations");
   FE_TRY(fe::session_iterate(s, n_iter, exaggeration, final_momentum, lr_normal, min_gain, clip));
+  trace.mark("iterations");
   FE_TRY(fe::session_get_layout(s, out, true));
+  trace.mark("D2H layout");
   return 0;
 }
 
@@ -400,6 +452,11 @@ extern "C" {
 
 const char* fe_b200_version(void) { return "fastembedr_b200 0.1.0 (sm_100a)"; }
 
+int fe_b200_release_memory(void) {
+  fe::clear_error();
+  return fe::release_retained_memory();
+}
+
 bool fastembedr_cuda_available(void) {
   int count = 0;
   if (cudaGetDeviceCount(&count) != cudaSuccess || count <= 0) {
@@ -568,9 +625,9 @@ int fe_b200_tsne_create(const int* indices, const float* distances, int n, int k
   if (rc == 0) rc = fe::session_create(&s, n, resolve_grid(n, grid_size), row_ptr, col, val, nnz, nullptr);
   if (rc != 0) {
     if (s == nullptr) {
-      if (row_ptr) cudaFree(row_ptr);
-      if (col) cudaFree(col);
-      if (val) cudaFree(val);
+      if (row_ptr) fe::dev_free(row_ptr);
+      if (col) fe::dev_free(col);
+      if (val) fe::dev_free(val);
     }
     cudaStreamDestroy(stream);
     return 1;
@@ -602,9 +659,9 @@ int fe_b200_tsne_create_csr(const int* row_ptr, const int* col, const float* val
   FE_TRY(fe::upload_csr(row_ptr, col, val, n, nullptr, &d_rp, &d_col, &d_val, &nnz));
   fe::TsneSession* s = nullptr;
   if (fe::session_create(&s, n, resolve_grid(n, grid_size), d_rp, d_col, d_val, nnz, nullptr)) {
-    cudaFree(d_rp);
-    cudaFree(d_col);
-    cudaFree(d_val);
+    fe::dev_free(d_rp);
+    fe::dev_free(d_col);
+    fe::dev_free(d_val);
     return 1;
   }
   if (fe::session_set_layout(s, init, true, true)) {
@@ -751,7 +808,7 @@ int fe_b200_pca_start(const void* values, int values_double, int n, int p, float
   cudaStream_t st = nullptr;
   FE_CUDA(cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking), "cudaStreamCreate(PCA)");
   float2* d = nullptr;
-  int rc = fe::check_cuda(cudaMalloc(&d, sizeof(float2) * static_cast<size_t>(n)), "cudaMalloc(PCA start)");
+  int rc = fe::check_cuda(fe::dev_malloc(&d, sizeof(float2) * static_cast<size_t>(n)), "cudaMalloc(PCA start)");
   if (rc == 0) rc = fe::pca_start_layout(values, values_double != 0, n, p, st, d);
   if (rc == 0) {
     rc = fe::check_cuda(cudaMemcpyAsync(out, d, sizeof(float2) * static_cast<size_t>(n), cudaMemcpyDeviceToHost, st),
@@ -759,7 +816,7 @@ int fe_b200_pca_start(const void* values, int values_double, int n, int p, float
   }
   if (rc == 0) rc = fe::check_cuda(cudaStreamSynchronize(st), "cudaStreamSynchronize(PCA start)");
   cudaStreamSynchronize(st);
-  if (d != nullptr) cudaFree(d);
+  if (d != nullptr) fe::dev_free(d);
   cudaStreamDestroy(st);
   return rc;
 }

@@ -101,6 +101,20 @@ int knn_exact(const void* data, bool data_double, bool data_on_device, bool col_
 // SM count of the current device (cached per device).
 int sm_count();
 
+// Device memory of the library (common.cu): cudaMalloc / cudaFree semantics
+// (dev_free waits for the device), served by a per-device pool that retains
+// freed blocks for the next call unless FASTEMBEDR_B200_RETAIN_MB=0.
+cudaError_t dev_malloc_bytes(void** p, std::size_t bytes);
+cudaError_t dev_free(void* p);
+template <typename T>
+inline cudaError_t dev_malloc(T** p, std::size_t bytes) {
+  return dev_malloc_bytes(reinterpret_cast<void**>(p), bytes);
+}
+std::size_t pool_spare_bytes();   // retained and unused bytes on the current device
+// Host time spent in dev_malloc / dev_free since the process started.
+void alloc_time_totals(double* alloc_ms, double* free_ms, long long* alloc_calls);
+int release_retained_memory();    // return every device's retained memory to the driver
+
 // Host -> device copy of a caller's buffer (pageable or pinned) that returns
 // once the data is on the device; large pageable sources are staged through
 // a pinned pool by several host threads (host_copy.cu).

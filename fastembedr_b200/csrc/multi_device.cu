@@ -71,7 +71,7 @@ class HostBarrier {
 struct RankBuf {
   void* p = nullptr;
   ~RankBuf() {
-    if (p) cudaFree(p);
+    if (p) fe::dev_free(p);
   }
 };
 
@@ -136,8 +136,8 @@ void rank_main(const MultiDeviceTsne& job, int rank, Shared* sh) {
   const int* idx_dev = job.indices;
   const void* dist_dev = job.distances;
   if (rc == 0 && (!job.on_device || dev != job.caller_device)) {
-    rc = check_cuda(cudaMalloc(&d_idx.p, items * sizeof(int)), "cudaMalloc(indices)");
-    if (rc == 0) rc = check_cuda(cudaMalloc(&d_dist.p, dist_bytes), "cudaMalloc(distances)");
+    rc = check_cuda(fe::dev_malloc(&d_idx.p, items * sizeof(int)), "cudaMalloc(indices)");
+    if (rc == 0) rc = check_cuda(fe::dev_malloc(&d_dist.p, dist_bytes), "cudaMalloc(distances)");
     if (rc == 0 && job.on_device) {
       rc = check_cuda(cudaMemcpyPeerAsync(d_idx.p, dev, job.indices, job.caller_device, items * sizeof(int),
                                           stream), "peer copy indices");
@@ -157,9 +157,9 @@ void rank_main(const MultiDeviceTsne& job, int rank, Shared* sh) {
   if (rc == 0) {
     rc = session_create(&s, job.n, job.grid, row_ptr, col, val, nnz, stream);
     if (rc != 0) {
-      cudaFree(row_ptr);
-      cudaFree(col);
-      cudaFree(val);
+      fe::dev_free(row_ptr);
+      fe::dev_free(col);
+      fe::dev_free(val);
     }
   }
   if (rc == 0) {

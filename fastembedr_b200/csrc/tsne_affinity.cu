@@ -165,10 +165,10 @@ template <typename T>
 struct DevBuf {
   T* p = nullptr;
   ~DevBuf() {
-    if (p) cudaFree(p);
+    if (p) fe::dev_free(p);
   }
   int alloc(size_t count, const char* what) {
-    return check_cuda(cudaMalloc(reinterpret_cast<void**>(&p), sizeof(T) * (count ? count : 1)), what);
+    return check_cuda(fe::dev_malloc(reinterpret_cast<void**>(&p), sizeof(T) * (count ? count : 1)), what);
   }
   T* release() {
     T* q = p;
@@ -278,10 +278,10 @@ int build_p_device(const int* d_idx, const void* d_dist, bool dist_is_double, in
   }
   const float norm = static_cast<float>(0.5 / total_mass);
   // Release the first-stage buffers before the second sort.
-  cudaFree(keys.release());
-  cudaFree(vals.release());
-  cudaFree(flags.release());
-  cudaFree(pos.release());
+  fe::dev_free(keys.release());
+  fe::dev_free(vals.release());
+  fe::dev_free(flags.release());
+  fe::dev_free(pos.release());
 
   const long long m2 = 2 * u;
   DevBuf<unsigned long long> k2, k2s;
@@ -290,10 +290,10 @@ int build_p_device(const int* d_idx, const void* d_dist, bool dist_is_double, in
   FE_TRY(v2.alloc(m2, "cudaMalloc(directed values)"));
   expand_pairs_kernel<<<blocks_for(u, 256), 256, 0, stream>>>(ukeys.p, uvals.p, u, norm, k2.p, v2.p);
   FE_LAUNCH("expand_pairs_kernel");
-  cudaFree(ukeys.release());
-  cudaFree(uvals.release());
-  cudaFree(keys_sorted.release());
-  cudaFree(vals_sorted.release());
+  fe::dev_free(ukeys.release());
+  fe::dev_free(uvals.release());
+  fe::dev_free(keys_sorted.release());
+  fe::dev_free(vals_sorted.release());
   FE_TRY(k2s.alloc(m2, "cudaMalloc(sorted directed keys)"));
   FE_TRY(v2s.alloc(m2, "cudaMalloc(sorted directed values)"));
   FE_CUDA(cub::DeviceRadixSort::SortPairs(nullptr, temp_bytes, k2.p, k2s.p, v2.p, v2s.p,

@@ -407,13 +407,13 @@ int session_reorder(TsneSession* s, bool by_layout) {
     }
     FE_TRY(memory_preflight(static_cast<size_t>(total) * 32, "padded P preflight"));
     const size_t groups = std::max<size_t>(1, static_cast<size_t>(total));
-    FE_CUDA(cudaMalloc(&s->csr4_col, sizeof(int4) * groups), "cudaMalloc(P cols)");
-    FE_CUDA(cudaMalloc(&s->csr4_val, sizeof(float4) * groups), "cudaMalloc(P vals)");
+    FE_CUDA(fe::dev_malloc(&s->csr4_col, sizeof(int4) * groups), "cudaMalloc(P cols)");
+    FE_CUDA(fe::dev_malloc(&s->csr4_val, sizeof(float4) * groups), "cudaMalloc(P vals)");
     // Staged row blocks address entries and union lists with 32-bit offsets.
     if (s->stage_enabled && static_cast<long long>(total) * 4 < INT_MAX &&
         memory_preflight(static_cast<size_t>(total) * 24, "staged P preflight") == 0) {
-      FE_CUDA(cudaMalloc(&s->stage_col16, sizeof(uint2) * groups), "cudaMalloc(staged P cols)");
-      FE_CUDA(cudaMalloc(&s->stage_union, sizeof(int4) * groups), "cudaMalloc(staged unions)");
+      FE_CUDA(fe::dev_malloc(&s->stage_col16, sizeof(uint2) * groups), "cudaMalloc(staged P cols)");
+      FE_CUDA(fe::dev_malloc(&s->stage_union, sizeof(int4) * groups), "cudaMalloc(staged unions)");
     } else {
       clear_error();
       s->stage_enabled = false;

@@ -4,8 +4,10 @@
 #include "tsne.cuh"
 
 #include <algorithm>
-#include <cstdlib>
+#include <chrono>
 #include <cmath>
+#include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <utility>
 #include <vector>
@@ -242,18 +244,27 @@ int session_create(TsneSession** out, int n, int grid, int* d_row_ptr, int* d_co
 void session_destroy(TsneSession* s) {
   if (s == nullptr) return;
   if (s->stream) cudaStreamSynchronize(s->stream);
+  const bool trace = env_flag("FASTEMBEDR_B200_TRACE", false);
+  const auto t0 = std::chrono::steady_clock::now();
   drop_graphs(s);
   shard_release(s);
   for (cudaEvent_t e : s->events) cudaEventDestroy(e);
-  if (s->row_ptr) cudaFree(s->row_ptr);
-  if (s->col) cudaFree(s->col);
-  if (s->val) cudaFree(s->val);
-  if (s->csr4_col) cudaFree(s->csr4_col);
-  if (s->csr4_val) cudaFree(s->csr4_val);
-  if (s->stage_col16) cudaFree(s->stage_col16);
-  if (s->stage_union) cudaFree(s->stage_union);
+  const auto t1 = std::chrono::steady_clock::now();
+  if (s->row_ptr) fe::dev_free(s->row_ptr);
+  if (s->col) fe::dev_free(s->col);
+  if (s->val) fe::dev_free(s->val);
+  if (s->csr4_col) fe::dev_free(s->csr4_col);
+  if (s->csr4_val) fe::dev_free(s->csr4_val);
+  if (s->stage_col16) fe::dev_free(s->stage_col16);
+  if (s->stage_union) fe::dev_free(s->stage_union);
   s->arena.release();
   if (s->own_stream && s->stream) cudaStreamDestroy(s->stream);
+  if (trace) {
+    const auto t2 = std::chrono::steady_clock::now();
+    std::fprintf(stderr, "[fastembedr_b200 trace] session destroy: graphs and events %.3f ms, device memory %.3f ms\n",
+                 std::chrono::duration<double, std::milli>(t1 - t0).count(),
+                 std::chrono::duration<double, std::milli>(t2 - t1).count());
+  }
   delete s;
 }
 

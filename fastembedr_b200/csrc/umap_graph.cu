@@ -34,8 +34,8 @@
 namespace fe {
 
 UmapDenseGraph::~UmapDenseGraph() {
-  if (nbr) cudaFree(nbr);
-  if (w) cudaFree(w);
+  if (nbr) fe::dev_free(nbr);
+  if (w) fe::dev_free(w);
 }
 
 namespace {
@@ -44,13 +44,13 @@ template <typename T>
 struct Buf {
   T* p = nullptr;
   ~Buf() {
-    if (p) cudaFree(p);
+    if (p) fe::dev_free(p);
   }
   int alloc(size_t count, const char* what) {
-    return check_cuda(cudaMalloc(reinterpret_cast<void**>(&p), sizeof(T) * (count ? count : 1)), what);
+    return check_cuda(fe::dev_malloc(reinterpret_cast<void**>(&p), sizeof(T) * (count ? count : 1)), what);
   }
   void free() {
-    if (p) cudaFree(p);
+    if (p) fe::dev_free(p);
     p = nullptr;
   }
   T* release() {
@@ -448,8 +448,8 @@ int umap_graph_build(const int* d_idx, const void* d_dist, bool dist_is_double, 
   keys.free();
   vals.free();
 
-  FE_CUDA(cudaMalloc(reinterpret_cast<void**>(&g->nbr), sizeof(int) * slots), "cudaMalloc(UMAP graph slots)");
-  FE_CUDA(cudaMalloc(reinterpret_cast<void**>(&g->w), sizeof(float) * slots), "cudaMalloc(UMAP graph weights)");
+  FE_CUDA(fe::dev_malloc(reinterpret_cast<void**>(&g->nbr), sizeof(int) * slots), "cudaMalloc(UMAP graph slots)");
+  FE_CUDA(fe::dev_malloc(reinterpret_cast<void**>(&g->w), sizeof(float) * slots), "cudaMalloc(UMAP graph weights)");
   fill_empty_kernel<<<grid_for(slots, 256), 256, 0, stream>>>(g->nbr, g->w, slots, width);
   FE_LAUNCH("fill_empty_kernel");
   FE_TRY(inc_flag.alloc(m, "cudaMalloc(UMAP incoming flags)"));

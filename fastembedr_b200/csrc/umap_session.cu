@@ -53,7 +53,7 @@ struct fe_b200_umap {
       const fe::NcclApi* api = fe::nccl_api();
       if (api) api->CommDestroy(static_cast<ncclComm_t>(comm));
     }
-    if (shard_mem) cudaFree(shard_mem);
+    if (shard_mem) fe::dev_free(shard_mem);
     arena.release();
     if (stream) cudaStreamDestroy(stream);
   }
@@ -111,15 +111,15 @@ int fe_b200_umap_create(const int* indices, const float* distances, int n, int k
     struct Free {
       void** p;
       ~Free() {
-        if (*p) cudaFree(*p);
+        if (*p) fe::dev_free(*p);
       }
     } fi{&d_idx}, fd{&d_dist};
     const int* idx_dev = indices;
     const float* dist_dev = distances;
     if (!inputs_on_device) {
       const size_t items = static_cast<size_t>(n) * k;
-      FE_CUDA(cudaMalloc(&d_idx, items * sizeof(int)), "cudaMalloc(UMAP indices)");
-      FE_CUDA(cudaMalloc(&d_dist, items * sizeof(float)), "cudaMalloc(UMAP distances)");
+      FE_CUDA(fe::dev_malloc(&d_idx, items * sizeof(int)), "cudaMalloc(UMAP indices)");
+      FE_CUDA(fe::dev_malloc(&d_dist, items * sizeof(float)), "cudaMalloc(UMAP distances)");
       FE_TRY(fe::h2d_copy(d_idx, indices, items * sizeof(int), s->stream, "H2D UMAP indices"));
       FE_TRY(fe::h2d_copy(d_dist, distances, items * sizeof(float), s->stream, "H2D UMAP distances"));
       idx_dev = static_cast<const int*>(d_idx);
@@ -233,11 +233,11 @@ int umap_shard_impl(fe_b200_umap* s, const unsigned char* id, ncclComm_t lent, i
   plan.take<char>(select_bytes);
   FE_TRY(fe::memory_preflight(plan.planned(), "UMAP shard preflight"));
   char* mem = nullptr;
-  FE_CUDA(cudaMalloc(&mem, plan.planned()), "cudaMalloc(UMAP shard)");
+  FE_CUDA(fe::dev_malloc(&mem, plan.planned()), "cudaMalloc(UMAP shard)");
   struct Free {
     char** p;
     ~Free() {
-      if (*p) cudaFree(*p);
+      if (*p) fe::dev_free(*p);
     }
   } release{&mem};
   size_t off = 0;

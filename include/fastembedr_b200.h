@@ -191,6 +191,16 @@ int fastembedr_cuda_raft_tsvd_pca_init(const double* values, int n, int p, int n
 /* Version string of this backend. */
 const char* fe_b200_version(void);
 
+/* Device memory retained between calls.  Every call draws its device buffers
+ * from one memory pool per GPU that keeps freed blocks mapped for the next
+ * call, up to FASTEMBEDR_B200_RETAIN_MB (default 32768; 0 = plain
+ * cudaMalloc/cudaFree, nothing retained): unmapping the several GB of a
+ * large call took the driver from milliseconds to more than half a second.
+ * This returns every GPU's retained, unused memory to the driver (for a
+ * caller about to need it elsewhere).  Returns 0, or 1 with fe_b200 /
+ * fastembedr_cuda last-error text set. */
+int fe_b200_release_memory(void);
+
 /* ---- t-SNE sessions: device-resident state across calls ---- */
 typedef struct fe_b200_tsne fe_b200_tsne;
 

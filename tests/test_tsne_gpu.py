@@ -371,3 +371,28 @@ def test_staged_attraction_is_bit_identical_to_gathers(monkeypatch):
     assert outs["0"][4] == 0
     for a, b in zip(outs["1"][:4], outs["0"][:4]):
         assert np.array_equal(a, b)
+
+
+def test_phase_trace_reports_every_phase(tsne_golden):
+    """FASTEMBEDR_B200_TRACE=1 prints the wall time of each phase of an openTSNE
+    call to stderr (run in a child process so the variable stays local)."""
+    import subprocess
+    import sys
+    import tempfile
+
+    g = tsne_golden
+    code = ("import numpy as np, sys; sys.path.insert(0, '.');"
+            "from fastembedr_b200 import api;"
+            "d = np.load(sys.argv[1]);"
+            "api.opentsne_knn(d['idx'], d['dist'], perplexity=float(d['perplexity']), init=d['init'],"
+            " early_exaggeration_iter=5, n_iter=5)")
+    with tempfile.TemporaryDirectory() as tmp:
+        path = os.path.join(tmp, "knn.npz")
+        np.savez(path, idx=g["idx"], dist=g["dist"], init=g["init"], perplexity=g["perplexity"])
+        env = dict(os.environ, FASTEMBEDR_B200_TRACE="1")
+        root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+        r = subprocess.run([sys.executable, "-c", code, path], cwd=root, env=env, capture_output=True, text=True,
+                           timeout=300)
+    assert r.returncode == 0, r.stderr[-2000:]
+    for phase in ("H2D KNN", "P build", "session create", "early iterations", "iterations", "D2H layout", "total"):
+        assert f"opentsne {phase}" in r.stderr, phase

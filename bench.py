@@ -957,11 +957,23 @@ def main():
         tdist.init_process_group("nccl", init_method="env://", timeout=datetime.timedelta(seconds=300),
                                  device_id=torch.device("cuda", local))
     try:
-        return bench_umap(args) if umap else bench_ours(args)
-    finally:
-        if world > 1:
-            tdist.barrier()
-            tdist.destroy_process_group()
+        rc = bench_umap(args) if umap else bench_ours(args)
+    except BaseException:
+        if world == 1:
+            raise
+        # A failure on one rank: report it now and leave without further
+        # collectives (a barrier here would wait for ranks that are still in
+        # the bench's own collectives); the others end at the process-group
+        # timeout.
+        import traceback
+
+        traceback.print_exc()
+        sys.stderr.flush()
+        os._exit(1)
+    if world > 1:
+        tdist.barrier()
+        tdist.destroy_process_group()
+    return rc
 
 
 if __name__ == "__main__":

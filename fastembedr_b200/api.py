@@ -234,7 +234,9 @@ def knn_exact(data, k: int, exclude_self: bool = True, device_output: bool = Fal
     check(rc, "fe_b200_knn_exact")
     if device_output:
         return d_idx, d_dist
-    return (d_idx.t().cpu().numpy() - 1).astype(np.int32), d_dist.t().cpu().numpy()
+    # (n, k) row-major host arrays, like every other KNN in this package
+    return (np.ascontiguousarray(d_idx.t().cpu().numpy() - 1, dtype=np.int32),
+            np.ascontiguousarray(d_dist.t().cpu().numpy()))
 
 
 def landmark_tsne_transform(indices, distances, reference_data, query_data, reference_layout,

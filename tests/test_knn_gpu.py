@@ -32,6 +32,9 @@ def _compare(idx, dist, ridx, rdist, rtol=1e-6):
 def test_knn_matches_numpy_exact(n, p, k):
     x, _ = S.gaussian_mixture(S.MixtureSpec(n=n, dim=p, components=6, seed=n))
     idx, dist = api.knn_exact(x, k)
+    # row-major (n, k), as every KNN of this package (torch.distributed
+    # broadcasts and the column-major helpers need contiguous arrays)
+    assert idx.flags.c_contiguous and dist.flags.c_contiguous
     ridx, rdist = S.exact_knn_numpy(x, k)
     frac = _compare(idx, dist, ridx, rdist)
     print(f"n={n} p={p} k={k}: {frac:.6f} of entries identical")

@@ -361,8 +361,10 @@ __global__ void __launch_bounds__(512) layout_stats_kernel(const float2* __restr
 
 // ------------------------------------------------------------------ splat
 
+// The scales are powers of two within float's range, so v * scale is exact in
+// float as in double, and both conversions round the same value.
 __device__ __forceinline__ long long to_fixed(float v, double scale) {
-  return __double2ll_rn(static_cast<double>(v) * scale);
+  return __float2ll_rn(v * static_cast<float>(scale));
 }
 
 constexpr int kSplatThreads = 256;
@@ -462,13 +464,10 @@ __global__ void __launch_bounds__(kSplatThreads) splat_kernel(float2* __restrict
   const bool own = key >= 0;
   int x_lo = own ? c.x0 : INT_MAX, y_lo = own ? c.y0 : INT_MAX;
   int x_hi = own ? c.x0 + 1 : INT_MIN, y_hi = own ? c.y0 + 1 : INT_MIN;
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    x_lo = min(x_lo, __shfl_xor_sync(0xffffffffu, x_lo, o));
-    y_lo = min(y_lo, __shfl_xor_sync(0xffffffffu, y_lo, o));
-    x_hi = max(x_hi, __shfl_xor_sync(0xffffffffu, x_hi, o));
-    y_hi = max(y_hi, __shfl_xor_sync(0xffffffffu, y_hi, o));
-  }
+  x_lo = __reduce_min_sync(0xffffffffu, x_lo);
+  y_lo = __reduce_min_sync(0xffffffffu, y_lo);
+  x_hi = __reduce_max_sync(0xffffffffu, x_hi);
+  y_hi = __reduce_max_sync(0xffffffffu, y_hi);
   if (lane == 0) {
     s_box[0][wid] = x_lo;
     s_box[1][wid] = y_lo;
@@ -607,13 +606,10 @@ __global__ void __launch_bounds__(kSplatThreads) splat_lagrange_kernel(float2* _
   const bool own = key >= 0;
   int x_lo = own ? 3 * c.bx : INT_MAX, y_lo = own ? 3 * c.by : INT_MAX;
   int x_hi = own ? 3 * c.bx + 2 : INT_MIN, y_hi = own ? 3 * c.by + 2 : INT_MIN;
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    x_lo = min(x_lo, __shfl_xor_sync(0xffffffffu, x_lo, o));
-    y_lo = min(y_lo, __shfl_xor_sync(0xffffffffu, y_lo, o));
-    x_hi = max(x_hi, __shfl_xor_sync(0xffffffffu, x_hi, o));
-    y_hi = max(y_hi, __shfl_xor_sync(0xffffffffu, y_hi, o));
-  }
+  x_lo = __reduce_min_sync(0xffffffffu, x_lo);
+  y_lo = __reduce_min_sync(0xffffffffu, y_lo);
+  x_hi = __reduce_max_sync(0xffffffffu, x_hi);
+  y_hi = __reduce_max_sync(0xffffffffu, y_hi);
   if (lane == 0) {
     s_box[0][wid] = x_lo;
     s_box[1][wid] = y_lo;

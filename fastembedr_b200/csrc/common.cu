@@ -130,11 +130,28 @@ cudaError_t dev_malloc_bytes(void** p, std::size_t bytes) {
 cudaError_t dev_free(void* p) {
   if (p == nullptr) return cudaSuccess;
   AllocClock clock(g_free_ns);
+  if (retain_bytes() == 0) return cudaFree(p);
+  // The block goes back to the pool of the device that holds it, after that
+  // device is idle, whichever device the caller has current (as cudaFree).
+  cudaPointerAttributes attr{};
+  int current = 0;
+  if (cudaPointerGetAttributes(&attr, p) != cudaSuccess || cudaGetDevice(&current) != cudaSuccess) {
+    cudaGetLastError();
+    return cudaFree(p);
+  }
+  const bool switch_device = attr.type == cudaMemoryTypeDevice && attr.device != current;
+  if (switch_device && cudaSetDevice(attr.device) != cudaSuccess) return cudaFree(p);
+  cudaError_t code;
   DevicePool* dp = current_pool();
-  if (dp == nullptr) return cudaFree(p);
-  const cudaError_t sync = cudaDeviceSynchronize();
-  const cudaError_t code = cudaFreeAsync(p, dp->stream);
-  return sync != cudaSuccess ? sync : code;
+  if (dp == nullptr) {
+    code = cudaFree(p);
+  } else {
+    const cudaError_t sync = cudaDeviceSynchronize();
+    code = cudaFreeAsync(p, dp->stream);
+    if (sync != cudaSuccess) code = sync;
+  }
+  if (switch_device) cudaSetDevice(current);
+  return code;
 }
 
 std::size_t pool_spare_bytes() {

@@ -67,3 +67,25 @@ def test_layout_does_not_depend_on_the_allocator(knn_20k):
         assert r.returncode == 0, r.stderr[-2000:]
         plain = np.load(out)
     assert np.array_equal(pooled, plain)
+
+
+def test_session_closed_with_another_device_current(knn_20k):
+    """A session's buffers go back to the pool of the GPU that holds them even
+    when the caller has another GPU current when it closes the session (as
+    cudaFree would); that GPU's pool then serves a new session."""
+    import torch
+
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    idx, dist, init = knn_20k
+    with torch.cuda.device(1):
+        s = api.TsneSession.from_knn(idx, dist, perplexity=30.0, init=init)
+        s.iterate(4, 12.0, 0.8, float(np.float32(idx.shape[0] / 12.0)))
+        want = s.layout()
+    with torch.cuda.device(0):
+        s.close()
+    with torch.cuda.device(1):
+        with api.TsneSession.from_knn(idx, dist, perplexity=30.0, init=init) as s2:
+            s2.iterate(4, 12.0, 0.8, float(np.float32(idx.shape[0] / 12.0)))
+            assert np.array_equal(s2.layout(), want)
+        api.release_memory()

@@ -371,6 +371,12 @@ cudaGraphExec_t chunk_graph(TsneSession* s, int iters, const float key[5]) {
   const cudaError_t inst = cudaGraphInstantiate(&e.exec, g, 0);
   cudaGraphDestroy(g);
   if (check_cuda(inst, "cudaGraphInstantiate")) return nullptr;
+  // Upload now (at prepare time when called from session_prepare) rather
+  // than on the first launch.
+  if (check_cuda(cudaGraphUpload(e.exec, s->stream), "cudaGraphUpload")) {
+    cudaGraphExecDestroy(e.exec);
+    return nullptr;
+  }
   e.iters = iters;
   e.cur = saved_cur;
   std::memcpy(e.params, key, sizeof(e.params));

@@ -22,7 +22,21 @@
 namespace fe {
 namespace {
 
-constexpr unsigned long long kNoKey = ~0ull;
+// Edge keys pack (row, col) as row << sh | col with sh = bits(n), so both
+// radix sorts run over 2 sh bits (40 at n = 1M) instead of 64; the key with
+// every one of those bits set marks a dropped entry and sorts last (a valid
+// key is at most (n - 1) << sh | (n - 1) < 2^(2 sh) - 1).
+struct KeyPack {
+  int sh;
+  unsigned long long none;
+  unsigned long long mask;
+};
+
+inline KeyPack key_pack(int n) {
+  int sh = 1;
+  while (sh < 31 && (1ll << sh) <= static_cast<long long>(n)) ++sh;
+  return KeyPack{sh, (1ull << (2 * sh)) - 1ull, (1ull << sh) - 1ull};
+}
 
 template <typename DistT>
 __device__ __forceinline__ bool entry_valid(int nb, float d, int n) {
@@ -33,7 +47,7 @@ __device__ __forceinline__ bool entry_valid(int nb, float d, int n) {
 // so consecutive threads read consecutive addresses.
 template <typename DistT>
 __global__ void row_affinity_kernel(const int* __restrict__ idx, const DistT* __restrict__ dist,
-                                    int n, int k, int offset, float log_perp,
+                                    int n, int k, int offset, float log_perp, KeyPack kp,
                                     unsigned long long* __restrict__ keys,
                                     float* __restrict__ vals) {
   const int row = blockIdx.x * blockDim.x + threadIdx.x;
@@ -83,23 +97,23 @@ __global__ void row_affinity_kernel(const int* __restrict__ idx, const DistT* __
     const float d = static_cast<float>(dist[j * nn + row]);
     const size_t slot = j * nn + row;
     if (!entry_valid<DistT>(nb, d, n) || nb == row) {
-      keys[slot] = kNoKey;
+      keys[slot] = kp.none;
       vals[slot] = 0.0f;
       continue;
     }
     const unsigned int a = static_cast<unsigned int>(min(row, nb));
     const unsigned int b = static_cast<unsigned int>(max(row, nb));
-    keys[slot] = (static_cast<unsigned long long>(a) << 32) | b;
+    keys[slot] = (static_cast<unsigned long long>(a) << kp.sh) | b;
     vals[slot] = expf(-used_beta * (d * d)) * inv_sum_p;
   }
 }
 
-__global__ void mark_heads_kernel(const unsigned long long* __restrict__ keys, long long m,
+__global__ void mark_heads_kernel(const unsigned long long* __restrict__ keys, long long m, KeyPack kp,
                                   int* __restrict__ flags) {
   const long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x;
   if (i >= m) return;
   const unsigned long long key = keys[i];
-  flags[i] = (key != kNoKey && (i == 0 || keys[i - 1] != key)) ? 1 : 0;
+  flags[i] = (key != kp.none && (i == 0 || keys[i - 1] != key)) ? 1 : 0;
 }
 
 // Sums each run of equal keys in double (src/tsne_neighbors.cpp:601-617).
@@ -131,34 +145,34 @@ __global__ void reduce_runs_kernel(const unsigned long long* __restrict__ keys,
 }
 
 __global__ void expand_pairs_kernel(const unsigned long long* __restrict__ ukeys,
-                                    const float* __restrict__ uvals, long long u, float norm,
+                                    const float* __restrict__ uvals, long long u, float norm, KeyPack kp,
                                     unsigned long long* __restrict__ keys2,
                                     float* __restrict__ vals2) {
   const long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x;
   if (i >= u) return;
   const unsigned long long key = ukeys[i];
-  const unsigned long long a = key >> 32, b = key & 0xffffffffull;
+  const unsigned long long a = key >> kp.sh, b = key & kp.mask;
   const float v = uvals[i] * norm;
-  keys2[2 * i] = (a << 32) | b;
-  keys2[2 * i + 1] = (b << 32) | a;
+  keys2[2 * i] = (a << kp.sh) | b;
+  keys2[2 * i + 1] = (b << kp.sh) | a;
   vals2[2 * i] = v;
   vals2[2 * i + 1] = v;
 }
 
 // row_start[r] = first entry of row r in the (row, col)-sorted list.
-__global__ void row_bounds_kernel(const unsigned long long* __restrict__ keys, long long m, int n,
+__global__ void row_bounds_kernel(const unsigned long long* __restrict__ keys, long long m, int n, KeyPack kp,
                                   int* __restrict__ row_start) {
   const long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x;
   if (i > m) return;
-  const int r = i < m ? static_cast<int>(keys[i] >> 32) : n;
-  const int rp = i == 0 ? -1 : static_cast<int>(keys[i - 1] >> 32);
+  const int r = i < m ? static_cast<int>(keys[i] >> kp.sh) : n;
+  const int rp = i == 0 ? -1 : static_cast<int>(keys[i - 1] >> kp.sh);
   for (int t = rp + 1; t <= r; ++t) row_start[t] = static_cast<int>(i);
 }
 
-__global__ void split_keys_kernel(const unsigned long long* __restrict__ keys, long long m,
+__global__ void split_keys_kernel(const unsigned long long* __restrict__ keys, long long m, KeyPack kp,
                                   int* __restrict__ col) {
   const long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x;
-  if (i < m) col[i] = static_cast<int>(keys[i] & 0xffffffffull);
+  if (i < m) col[i] = static_cast<int>(keys[i] & kp.mask);
 }
 
 template <typename T>
@@ -182,14 +196,14 @@ inline unsigned blocks_for(long long m, int threads) {
 }
 
 // Sorted (row, col) entry list -> CSR; the values array is adopted as is.
-int assemble_csr(const unsigned long long* d_keys, float* d_vals, long long m, int n,
+int assemble_csr(const unsigned long long* d_keys, float* d_vals, long long m, int n, KeyPack kp,
                  cudaStream_t stream, int** out_row_ptr, int** out_col) {
   DevBuf<int> row_ptr, col;
   FE_TRY(row_ptr.alloc(n + 1, "cudaMalloc(row_ptr)"));
   FE_TRY(col.alloc(m, "cudaMalloc(P col)"));
-  row_bounds_kernel<<<blocks_for(m + 1, 256), 256, 0, stream>>>(d_keys, m, n, row_ptr.p);
+  row_bounds_kernel<<<blocks_for(m + 1, 256), 256, 0, stream>>>(d_keys, m, n, kp, row_ptr.p);
   FE_LAUNCH("row_bounds_kernel");
-  split_keys_kernel<<<blocks_for(m, 256), 256, 0, stream>>>(d_keys, m, col.p);
+  split_keys_kernel<<<blocks_for(m, 256), 256, 0, stream>>>(d_keys, m, kp, col.p);
   FE_LAUNCH("split_keys_kernel");
   FE_CUDA(cudaStreamSynchronize(stream), "cudaStreamSynchronize(P assemble)");
   *out_row_ptr = row_ptr.release();
@@ -213,12 +227,13 @@ int build_p_device(const int* d_idx, const void* d_dist, bool dist_is_double, in
   FE_TRY(keys.alloc(m, "cudaMalloc(edge keys)"));
   FE_TRY(vals.alloc(m, "cudaMalloc(edge values)"));
   const float log_perp = static_cast<float>(std::log(static_cast<double>(perplexity)));
+  const KeyPack kp = key_pack(n);
   if (dist_is_double) {
     row_affinity_kernel<double><<<blocks_for(n, 128), 128, 0, stream>>>(
-        d_idx, static_cast<const double*>(d_dist), n, k, index_offset, log_perp, keys.p, vals.p);
+        d_idx, static_cast<const double*>(d_dist), n, k, index_offset, log_perp, kp, keys.p, vals.p);
   } else {
     row_affinity_kernel<float><<<blocks_for(n, 128), 128, 0, stream>>>(
-        d_idx, static_cast<const float*>(d_dist), n, k, index_offset, log_perp, keys.p, vals.p);
+        d_idx, static_cast<const float*>(d_dist), n, k, index_offset, log_perp, kp, keys.p, vals.p);
   }
   FE_LAUNCH("row_affinity_kernel");
 
@@ -226,13 +241,13 @@ int build_p_device(const int* d_idx, const void* d_dist, bool dist_is_double, in
   FE_TRY(vals_sorted.alloc(m, "cudaMalloc(sorted values)"));
   size_t temp_bytes = 0;
   FE_CUDA(cub::DeviceRadixSort::SortPairs(nullptr, temp_bytes, keys.p, keys_sorted.p, vals.p,
-                                          vals_sorted.p, static_cast<int>(m), 0, 64, stream),
+                                          vals_sorted.p, static_cast<int>(m), 0, 2 * kp.sh, stream),
           "cub::DeviceRadixSort(sizing)");
   {
     DevBuf<unsigned char> temp;
     FE_TRY(temp.alloc(temp_bytes, "cudaMalloc(sort temp)"));
     FE_CUDA(cub::DeviceRadixSort::SortPairs(temp.p, temp_bytes, keys.p, keys_sorted.p, vals.p,
-                                            vals_sorted.p, static_cast<int>(m), 0, 64, stream),
+                                            vals_sorted.p, static_cast<int>(m), 0, 2 * kp.sh, stream),
             "cub::DeviceRadixSort(pair keys)");
     FE_CUDA(cudaStreamSynchronize(stream), "cudaStreamSynchronize(pair sort)");
   }
@@ -240,7 +255,7 @@ int build_p_device(const int* d_idx, const void* d_dist, bool dist_is_double, in
   DevBuf<int> flags, pos;
   FE_TRY(flags.alloc(m, "cudaMalloc(head flags)"));
   FE_TRY(pos.alloc(m, "cudaMalloc(head positions)"));
-  mark_heads_kernel<<<blocks_for(m, 256), 256, 0, stream>>>(keys_sorted.p, m, flags.p);
+  mark_heads_kernel<<<blocks_for(m, 256), 256, 0, stream>>>(keys_sorted.p, m, kp, flags.p);
   FE_LAUNCH("mark_heads_kernel");
   FE_CUDA(cub::DeviceScan::ExclusiveSum(nullptr, temp_bytes, flags.p, pos.p, static_cast<int>(m), stream),
           "cub::DeviceScan(sizing)");
@@ -288,7 +303,7 @@ int build_p_device(const int* d_idx, const void* d_dist, bool dist_is_double, in
   DevBuf<float> v2, v2s;
   FE_TRY(k2.alloc(m2, "cudaMalloc(directed keys)"));
   FE_TRY(v2.alloc(m2, "cudaMalloc(directed values)"));
-  expand_pairs_kernel<<<blocks_for(u, 256), 256, 0, stream>>>(ukeys.p, uvals.p, u, norm, k2.p, v2.p);
+  expand_pairs_kernel<<<blocks_for(u, 256), 256, 0, stream>>>(ukeys.p, uvals.p, u, norm, kp, k2.p, v2.p);
   FE_LAUNCH("expand_pairs_kernel");
   fe::dev_free(ukeys.release());
   fe::dev_free(uvals.release());
@@ -297,17 +312,17 @@ int build_p_device(const int* d_idx, const void* d_dist, bool dist_is_double, in
   FE_TRY(k2s.alloc(m2, "cudaMalloc(sorted directed keys)"));
   FE_TRY(v2s.alloc(m2, "cudaMalloc(sorted directed values)"));
   FE_CUDA(cub::DeviceRadixSort::SortPairs(nullptr, temp_bytes, k2.p, k2s.p, v2.p, v2s.p,
-                                          static_cast<int>(m2), 0, 64, stream),
+                                          static_cast<int>(m2), 0, 2 * kp.sh, stream),
           "cub::DeviceRadixSort(sizing)");
   {
     DevBuf<unsigned char> temp;
     FE_TRY(temp.alloc(temp_bytes, "cudaMalloc(sort temp)"));
     FE_CUDA(cub::DeviceRadixSort::SortPairs(temp.p, temp_bytes, k2.p, k2s.p, v2.p, v2s.p,
-                                            static_cast<int>(m2), 0, 64, stream),
+                                            static_cast<int>(m2), 0, 2 * kp.sh, stream),
             "cub::DeviceRadixSort(directed keys)");
     FE_CUDA(cudaStreamSynchronize(stream), "cudaStreamSynchronize(directed sort)");
   }
-  FE_TRY(assemble_csr(k2s.p, v2s.p, m2, n, stream, out_row_ptr, out_col));
+  FE_TRY(assemble_csr(k2s.p, v2s.p, m2, n, kp, stream, out_row_ptr, out_col));
   *out_val = v2s.release();
   *out_nnz = m2;
   return 0;

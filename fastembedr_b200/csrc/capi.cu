@@ -329,6 +329,12 @@ int umap_host_run(const int* heads, const int* tails, const float* eps, long lon
   r.stream = stream;
   r.edge_blocks = fe::umap_edge_blocks(n_edges);
   r.use_graphs = fe::env_flag("FASTEMBEDR_CUDA_GRAPH_CAPTURE", true);
+  struct CompactionGuard {
+    fe::UmapCompaction c;
+    ~CompactionGuard() { fe::umap_compaction_free(&c); }
+  } compaction;
+  FE_TRY(fe::umap_compaction_alloc(n_edges, &compaction.c));
+  r.compact = compaction.c;
   FE_TRY(fe::umap_run_epochs(&r, epoch_begin, epoch_end));
   FE_CUDA(cudaMemcpyAsync(out, d_layout, sizeof(float2) * n, cudaMemcpyDeviceToHost, stream), "D2H layout");
   if (positive_samples != nullptr) {
@@ -424,6 +430,12 @@ int umap_fused_impl(const int* idx, const void* dist, bool dist_double, bool on_
   r.stream = stream;
   r.edge_blocks = fe::umap_edge_blocks(n_edges);
   r.use_graphs = fe::env_flag("FASTEMBEDR_CUDA_GRAPH_CAPTURE", true);
+  struct CompactionGuard {
+    fe::UmapCompaction c;
+    ~CompactionGuard() { fe::umap_compaction_free(&c); }
+  } compaction;
+  FE_TRY(fe::umap_compaction_alloc(n_edges, &compaction.c));
+  r.compact = compaction.c;
   FE_TRY(fe::umap_run_epochs(&r, 0, n_epochs));
   FE_CUDA(cudaMemcpyAsync(out, layout, sizeof(float2) * n, cudaMemcpyDeviceToHost, stream), "D2H fused umap layout");
   FE_CUDA(cudaStreamSynchronize(stream), "cudaStreamSynchronize(fused umap)");

@@ -37,6 +37,9 @@
 
 #include "nccl_loader.cuh"
 
+#include <cub/cub.cuh>
+#include <thrust/iterator/counting_iterator.h>
+
 #include <cfloat>
 #include <cmath>
 
@@ -110,11 +113,13 @@ __device__ __forceinline__ int negative_vertex(unsigned int n, unsigned int seed
 
 __device__ __forceinline__ float clip4(float v) { return v < -4.0f ? -4.0f : (v > 4.0f ? 4.0f : v); }
 
-template <int Mode>
+template <int Mode, bool Compact>
 __global__ void __launch_bounds__(256) umap_epoch_kernel(const int* __restrict__ heads,
                                                          const int* __restrict__ tails,
                                                          const float* __restrict__ periods,
                                                          long long edge_begin, long long edge_end,
+                                                         const int* __restrict__ active,
+                                                         const int* __restrict__ active_count,
                                                          float2* layout, const float2* __restrict__ frozen,
                                                          float2* __restrict__ delta, UmapParams p,
                                                          int epoch, long long* positive_count) {
@@ -126,13 +131,18 @@ __global__ void __launch_bounds__(256) umap_epoch_kernel(const int* __restrict__
   const int lane = threadIdx.x & 31;
   long long local_pos = 0;
   const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
-  // Whole warps iterate together so the head-run reduction sees full warps.
-  const long long base0 = edge_begin + static_cast<long long>(blockIdx.x) * blockDim.x + (threadIdx.x & ~31);
-  for (long long base = base0; base < edge_end; base += stride) {
-    const long long gid = base + lane;
+  // Items: the edges [edge_begin, edge_end), or with Compact the firing edge
+  // ids listed in active[0, *active_count) (in edge order).  Whole warps
+  // iterate together so the head-run reduction sees full warps.
+  const long long n_items = Compact ? static_cast<long long>(*active_count) : edge_end - edge_begin;
+  const long long base0 = static_cast<long long>(blockIdx.x) * blockDim.x + (threadIdx.x & ~31);
+  for (long long base = base0; base < n_items; base += stride) {
+    const long long item = base + lane;
+    const long long gid = item < n_items ? (Compact ? static_cast<long long>(__ldcs(active + item)) : edge_begin + item)
+                                         : -1;
     int h = -1, t = -1;
     float gx_h = 0.f, gy_h = 0.f;
-    if (gid < edge_end) {
+    if (gid >= 0) {
       h = __ldcs(heads + gid);
       t = __ldcs(tails + gid);
       const float per = __ldcs(periods + gid);
@@ -317,11 +327,34 @@ int gather_layout(UmapRun* r) {
                          "ncclAllGather(UMAP layout rows)");
 }
 
+// Edges whose schedule applies at least one positive sample in `epoch`
+// (the only edges the epoch kernel does work for).
+struct FiresInEpoch {
+  const float* periods;
+  int epoch;
+  __device__ bool operator()(const int& e) const { return positive_samples(__ldg(periods + e), epoch) > 0; }
+};
+
 template <int Mode>
 int launch_edges(UmapRun* r, int epoch, long long e0, long long e1) {
-  umap_epoch_kernel<Mode><<<r->edge_blocks, 256, 0, r->stream>>>(
-      r->heads, r->tails, r->periods, e0, e1, r->layout, r->layout, Mode == kUmapDelta ? r->delta : nullptr,
-      r->params, epoch, r->positive_count);
+  // Edge-granularity Hogwild keeps the whole-list scan: packing the firing
+  // edges puts about four times as many of them in flight at once, and this
+  // mode, the one that follows the CPU replay's order, measurably lost kNN
+  // preservation with it (0.00743 against 0.00773-0.00790 at 70k).
+  const UmapCompaction& c = r->compact;
+  if (c.active != nullptr && Mode != kUmapInplace && e1 > e0) {
+    std::size_t bytes = c.temp_bytes;
+    FE_CUDA(cub::DeviceSelect::If(c.temp, bytes, thrust::make_counting_iterator<int>(static_cast<int>(e0)), c.active,
+                                  c.count, static_cast<int>(e1 - e0), FiresInEpoch{r->periods, epoch}, r->stream),
+            "cub::DeviceSelect(firing edges)");
+    umap_epoch_kernel<Mode, true><<<r->edge_blocks, 256, 0, r->stream>>>(
+        r->heads, r->tails, r->periods, e0, e1, c.active, c.count, r->layout, r->layout,
+        Mode == kUmapDelta ? r->delta : nullptr, r->params, epoch, r->positive_count);
+  } else {
+    umap_epoch_kernel<Mode, false><<<r->edge_blocks, 256, 0, r->stream>>>(
+        r->heads, r->tails, r->periods, e0, e1, nullptr, nullptr, r->layout, r->layout,
+        Mode == kUmapDelta ? r->delta : nullptr, r->params, epoch, r->positive_count);
+  }
   FE_LAUNCH("umap_epoch_kernel");
   return 0;
 }
@@ -386,6 +419,33 @@ int umap_run_epochs(UmapRun* r, int epoch_begin, int epoch_end) {
     FE_CUDA(launch, "cudaGraphLaunch(umap)");
   }
   return 0;
+}
+
+int umap_compaction_alloc(long long n_edges, UmapCompaction* c) {
+  *c = UmapCompaction{};
+  if (!env_flag("FASTEMBEDR_B200_UMAP_COMPACT", true) || n_edges < 1) return 0;
+  if (n_edges >= (1ll << 31) - 1) return 0;  // 32-bit edge ids in the list; scan the whole list instead
+  std::size_t bytes = 0;
+  FE_CUDA(cub::DeviceSelect::If(nullptr, bytes, thrust::make_counting_iterator<int>(0), static_cast<int*>(nullptr),
+                                static_cast<int*>(nullptr), static_cast<int>(n_edges), FiresInEpoch{nullptr, 0}),
+          "cub::DeviceSelect(sizing)");
+  UmapCompaction out;
+  out.temp_bytes = bytes;
+  if (dev_malloc(&out.active, sizeof(int) * static_cast<std::size_t>(n_edges)) != cudaSuccess ||
+      dev_malloc(&out.count, sizeof(int)) != cudaSuccess || dev_malloc(&out.temp, bytes) != cudaSuccess) {
+    cudaGetLastError();
+    umap_compaction_free(&out);
+    return 0;  // no room for the list: scan the whole list (same results)
+  }
+  *c = out;
+  return 0;
+}
+
+void umap_compaction_free(UmapCompaction* c) {
+  dev_free(c->active);
+  dev_free(c->count);
+  dev_free(c->temp);
+  *c = UmapCompaction{};
 }
 
 int umap_edge_blocks(long long n_edges) {

@@ -32,6 +32,22 @@ struct UmapParams {
   int own_end = 0x7fffffff;
 };
 
+// Per-epoch compaction of the edge list to the edges that fire in that epoch
+// (umap_compaction_alloc).  A warp then carries 32 firing edges instead of the
+// ~9 of 32 consecutive edges that fire on average, so four times as many
+// dependent sample chains are in flight per SM; edges keep their order.
+struct UmapCompaction {
+  int* active = nullptr;       // firing edge ids of the current range, in order
+  int* count = nullptr;        // how many
+  void* temp = nullptr;        // CUB select scratch
+  std::size_t temp_bytes = 0;
+};
+
+// Buffers for runs over up to n_edges edges (dev_malloc); compaction stays off
+// (all pointers null) when FASTEMBEDR_B200_UMAP_COMPACT=0.
+int umap_compaction_alloc(long long n_edges, UmapCompaction* c);
+void umap_compaction_free(UmapCompaction* c);
+
 struct UmapRun {
   UmapParams params;
   int mode = kUmapInplace;
@@ -45,6 +61,7 @@ struct UmapRun {
   cudaStream_t stream = nullptr;
   int edge_blocks = 1;
   bool use_graphs = true;
+  UmapCompaction compact;  // all null: every epoch scans the whole edge list
   // Sharded runs: after each epoch the owned rows (blocks of rows_per_rank,
   // layout padded to shard_ranks * rows_per_rank rows) are all-gathered.
   void* comm = nullptr;  // ncclComm_t

@@ -47,8 +47,12 @@ struct fe_b200_umap {
   int* own_heads = nullptr;
   int* own_tails = nullptr;
   float* own_periods = nullptr;
+  // Firing-edge lists of the epochs (made at the first run, for every edge).
+  fe::UmapCompaction compact;
+  bool compact_tried = false;
   ~fe_b200_umap() {
     if (stream) cudaStreamSynchronize(stream);
+    fe::umap_compaction_free(&compact);
     if (comm && own_comm) {
       const fe::NcclApi* api = fe::nccl_api();
       if (api) api->CommDestroy(static_cast<ncclComm_t>(comm));
@@ -193,6 +197,11 @@ int fe_b200_umap_run(fe_b200_umap* s, int epoch_begin, int epoch_end, int n_epoc
   r.stream = s->stream;
   r.edge_blocks = fe::umap_edge_blocks(std::max(1ll, r.n_edges));
   r.use_graphs = fe::env_flag("FASTEMBEDR_CUDA_GRAPH_CAPTURE", true);
+  if (!s->compact_tried) {
+    s->compact_tried = true;
+    FE_TRY(fe::umap_compaction_alloc(s->n_edges, &s->compact));
+  }
+  r.compact = s->compact;
   return fe::umap_run_epochs(&r, epoch_begin, epoch_end);
 }
 

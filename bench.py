@@ -12,7 +12,8 @@ configuration the headline metric (t-SNE iterations/s at N = 1M) is quoted on.
 Our arm (--impl ours) prints one JSON line with
   value      iterations/s with P, layout and optimizer state resident in HBM
   e2e        iterations/s of the full C-ABI call (fastembedr_cuda_opentsne_fft_from_knn_float)
-             from pinned host KNN to host layout: H2D, P build, 750 iterations, D2H
+             from pageable host KNN, as the reference's R wrapper passes it, to host layout:
+             H2D, P build, 750 iterations, D2H (the same call from pinned buffers beside it)
   roofline   the fused gradient/update kernel: algorithmic bytes per launch over its
              CUDA-event duration, against MEASURED_PEAKS.json's HBM copy bandwidth
   cpu_baseline  the reference's own CPU loop (oracle/_ref) on the first iterations of the
@@ -902,11 +903,12 @@ def umap_measure(workload: str, steps: int, warmup: int, skip_e2e: bool, skip_cp
         "negative_samples_per_second": neg / (elapsed_ms / 1000.0),
         "epochs_per_second": steps / (elapsed_ms / 1000.0),
         "edges_scanned_per_second": info["n_edges"] * steps / (elapsed_ms / 1000.0),
-        "roofline": {"kernel": "umap_epoch_kernel (+ sanitize)", "bound": "hbm", "achieved": achieved,
+        "roofline": {"kernel": "umap_epoch_kernel over the epoch's firing edges (+ their CUB select and the "
+                               "sanitize)", "bound": "hbm", "achieved": achieved,
                      "peak": hbm, "peak_kind": peak_kind, "unit": "GB/s", "frac": achieved / hbm,
                      "algorithmic_bytes_per_launch": alg_bytes, "avg_launch_ms": epoch_s * 1000.0,
                      "traffic": profile_traffic("umap_epoch_kernel", workload)},
-        "gpu_launches": 2 * steps,
+        "gpu_launches": 2 * steps,  # epoch kernel + sanitize per epoch (the CUB select's kernels are CUB's)
         "clocks": clocks.summary(), "e2e": e2e, "cpu_baseline": cpu,
     }
     if ref_gpu is not None:
